@@ -1,0 +1,100 @@
+"""The CPU oracle is pinned against fixtures produced by the reference itself.
+
+tests/golden/make_golden.py ran the reference LAPrune code (CPU/PyTorch path)
+on seeded inputs from laprune_b200.synthetic; these tests regenerate the same
+inputs, check their checksums, and require the oracle to reproduce the
+reference's outputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from laprune_b200 import synthetic as syn
+
+
+def _check_sums(fix, tensors):
+    got = np.array([syn.checksum(t) for t in tensors])
+    np.testing.assert_allclose(got, fix["checksums"], rtol=1e-9, atol=1e-6,
+                               err_msg="synthetic input generator drifted")
+
+
+def test_cfg1_scores_and_topk(golden_dir):
+    fix = np.load(golden_dir / "cfg1_scoring.npz")
+    c = syn.config1(0)
+    _check_sums(fix, [c["C"], c["codes"], c["q"]])
+    s = oracle.scores_per_kv_head(c["C"].numpy(), c["q"].float().numpy(), c["codes"].numpy(), c["G"])
+    ref = fix["scores"]
+    scale = np.abs(ref).max()
+    assert np.abs(s - ref).max() <= 1e-5 * scale
+    gs = oracle.group_sum(s, 4)
+    top = oracle.topk_rows(gs, 0, gs.shape[1], c["k"])
+    for h in range(8):
+        ov = oracle.topk_overlap(top[h], fix["topk"][h], gs[h], fix["kth"][h], tol=1e-4)
+        assert ov == 1.0
+
+
+def test_cfg2_encode_codes(golden_dir):
+    fix = np.load(golden_dir / "cfg2_encode.npz")
+    c = syn.config2(0)
+    _check_sums(fix, [c["C"], c["keys"], c["code_cache"], c["q"]])
+    B, Hkv, Tn, D = c["keys"].shape
+    x = c["keys"].permute(1, 0, 2, 3).reshape(Hkv * B * Tn, D).float().numpy()
+    cbi = np.repeat(np.arange(Hkv, dtype=np.int32), B * Tn)
+    codes = oracle.encode_greedy(x, c["C"].numpy(), cbi)
+    ref = fix["codes"].transpose(1, 0, 2, 3).reshape(Hkv * B * Tn, 32)
+    rows_equal = (codes == ref).all(1)
+    # Disagreements may only start at a near-tie of the fp32 distances.
+    for n in np.nonzero(~rows_equal)[0]:
+        m = int(np.nonzero(codes[n] != ref[n])[0][0])
+        dist = oracle.encode_stage_dists(x[n], c["C"].numpy()[cbi[n]], ref[n][:m], m)
+        assert abs(dist[codes[n][m]] - dist[ref[n][m]]) < 1e-4
+    assert rows_equal.mean() >= 0.99
+
+
+def test_cfg2_scores_sample(golden_dir):
+    fix = np.load(golden_dir / "cfg2_encode.npz")
+    c = syn.config2(0)
+    cache = c["code_cache"].clone()
+    p0 = c["pos0"]
+    cache[:, :, p0:p0 + 64] = torch.from_numpy(fix["codes"])
+    sample = fix["sample"]
+    for b in range(4):
+        s = oracle.scores_per_kv_head(c["C"].numpy(), c["q"][b].float().numpy(),
+                                      np.ascontiguousarray(cache[b][:, sample].numpy()), 4)
+        ref = fix["scores"][b]
+        assert np.abs(s - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_cfg3_decode_step(golden_dir):
+    fix = np.load(golden_dir / "cfg3_decode.npz")
+    c = syn.config3(0)
+    _check_sums(fix, [c["C"], c["codes"], c["keys"], c["vals"], c["q"]])
+    gs, top, keep, out = oracle.decode_step_group(
+        c["C"].numpy(), c["q"].float().numpy(), c["codes"].numpy(),
+        c["keys"].float().numpy(), c["vals"].float().numpy(), c["k"], c["sink"], c["local"], 4)
+    for h in range(8):
+        assert oracle.topk_overlap(top[h], fix["topk"][h], gs[h], fix["kth"][h], tol=1e-4) == 1.0
+    assert np.abs(out - fix["out"]).max() <= 1e-4
+
+
+def test_small_shared(golden_dir):
+    fix = np.load(golden_dir / "small_shared.npz")
+    sm = syn.small_shared(7)
+    _check_sums(fix, [sm["cb"], sm["codes_full"], sm["q"], sm["x"]])
+    codes = sm["codes_full"].numpy()[:, :sm["T"]]           # strided view
+    s = oracle.score_gqa(oracle.lut(sm["q"].float().numpy(), sm["cb"].numpy()), codes, 4)
+    assert np.abs(s - fix["scores"]).max() <= 1e-5 * np.abs(fix["scores"]).max()
+    enc = oracle.encode_greedy(sm["x"].numpy(), sm["cb"].numpy())
+    assert (enc == fix["codes_enc"]).all(1).mean() >= 0.99
+
+
+@pytest.mark.parametrize("sink", [0, 4])
+def test_reference_decode_hook(golden_dir, sink):
+    fix = np.load(golden_dir / "decode_hook.npz")
+    dh = syn.decode_hook_case(11)
+    _check_sums(fix, [dh["cb"], dh["codes"], dh["keys"], dh["vals"], dh["q"]])
+    out = oracle.decode_hook_reference(dh["cb"].numpy(), dh["q"].numpy(), dh["codes"].numpy(),
+                                       dh["keys"].numpy(), dh["vals"].numpy(), dh["T"], sink, 64)
+    ref = fix[f"out_sink{sink}"]
+    assert np.abs(out - ref).max() <= 1e-4
