@@ -1,0 +1,405 @@
+"""Benchmark of the LAPrune sparse-decode hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (applied to every sparse layer of a
+Llama-3.1-8B decode token): per layer, B=1, T=131072 cached tokens, 32 query
+/ 8 KV heads, head_dim 128, per-KV-head fp32 codebooks [8,32,256,128], uint8
+codes [8,T,32], bf16 K/V [8,T,128]; LUT build -> scoring of the candidate
+window [4, T-64) -> top-2048 per KV head on GQA-summed scores -> union with 4
+sink + 64 local tokens -> GQA K/V gather -> split-K flash-decode.  One STEP is
+one decode token through the 30 sparse layers (layers 2..31), each layer with
+its own resident caches (≈18 GB, far above the 126 MB L2), inputs seeded
+synthetic.  Dense layers 0-1, projections and MLP are not part of this path.
+
+Prints ONE JSON line (rank 0).  Under torchrun (N>1) every rank runs its own
+independent copy of the workload (weak scaling, no collective on the data
+path); timings are max-reduced over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s Llama-3.1-8B @128k ctx; LUT-score HBM GB/s vs peak"
+UNIT = "tok/s (sparse-attention hot path, 30 layers)"
+T_CTX, HQ, HKV, D, M, K = 131072, 32, 8, 128, 32, 256
+TOPK, SINK, LOCAL = 2048, 4, 64
+N_LAYERS = 30
+WORKLOAD = ("cfg3 x 30 sparse layers: Llama-3.1-8B LAPrune sparse decode step per token, B=1, "
+            "T=131072, Hq=32/Hkv=8, D=128, M=32, K=256, top-2048 per KV head (GQA-summed) "
+            "+ 4 sink + 64 local, bf16 K/V, fp32 per-KV-head codebooks")
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _profile_traffic():
+    """Per-launch DRAM traffic of the scorer from the committed ncu summary
+    (a line 'traffic_bytes_per_launch: <int>'), scaled by the summary's own
+    note when it was captured on a smaller case; None if absent."""
+    p = ROOT / "profiles" / "score_kernel_cfg3.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, period_ms: int = 50):
+        self.proc = None
+        self.gpu = gpu_index
+        self.period = period_ms
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", str(self.period)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def _dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference algorithm on the host cores (oracle port)
+# ---------------------------------------------------------------------------
+
+def _cpu_layer_sample(cfg):
+    """One bounded sample of a layer step on the CPU: the full pipeline
+    (LUT, scoring, group sum, top-k, keep set, attention) for ONE KV head of
+    a T=131072 layer.  Returns the fraction of a full 8-head layer step."""
+    import numpy as np
+    import oracle
+    h = cfg["h"]
+    C, q, codes, keys, vals = cfg["C"], cfg["q"], cfg["codes"], cfg["keys"], cfg["vals"]
+    T = codes.shape[1]
+    s = oracle.score_gqa(oracle.lut(q[h * 4:(h + 1) * 4], C[h]), codes[h:h + 1], 4)
+    gs = oracle.group_sum(s, 4)
+    top = oracle.topk_rows(gs, SINK, T - LOCAL, TOPK)
+    keep = oracle.keep_positions(top, T, SINK, LOCAL)
+    oracle.sparse_attention(q[h * 4:(h + 1) * 4], keys[h:h + 1], vals[h:h + 1],
+                            np.repeat(keep, 4, axis=0), 4)
+    return 1.0 / HKV
+
+
+def _cpu_inputs(seed: int = 0, heads: int = 2):
+    """Host inputs for `heads` KV heads of one T=131072 layer (fp32 K/V)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    C = rng.standard_normal((heads, M, K, D), dtype=np.float32) * 0.05
+    codes = rng.integers(0, 256, (heads, T_CTX, M), dtype=np.uint8)
+    keys = rng.standard_normal((heads, T_CTX, D), dtype=np.float32)
+    vals = rng.standard_normal((heads, T_CTX, D), dtype=np.float32)
+    q = rng.standard_normal((heads * 4, D), dtype=np.float32)
+    return {"C": C, "codes": codes, "keys": keys, "vals": vals, "q": q, "h": 0, "heads": heads}
+
+
+SAMPLE_DESC = ("one KV head of one T=131072 layer per sample (full pipeline: LUT build, scoring, "
+               "GQA sum, top-2048, keep set, attention of 4 query heads), fp32, scaled to "
+               "8 KV heads x 30 layers")
+
+
+def cpu_baseline(seconds: float = 10.0):
+    """Time the oracle restatement of the reference path on the host cores
+    for about `seconds`; value in the bench unit (tokens through 30 layers)."""
+    import oracle
+    oracle.set_num_threads(os.cpu_count() or 1)
+    cfg = _cpu_inputs(0)
+    _cpu_layer_sample(cfg)  # warm
+    done, t0 = 0.0, time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < seconds:
+        cfg["h"] = n % cfg["heads"]
+        done += _cpu_layer_sample(cfg)
+        n += 1
+    el = time.perf_counter() - t0
+    return {"value": done / el / N_LAYERS, "unit": UNIT, "cores": oracle.num_threads(),
+            "kind": "port", "sample": f"{n} samples in {el:.1f} s; " + SAMPLE_DESC}
+
+
+def run_reference(args):
+    ws, rank, _ = _dist_env()
+    if rank != 0:
+        return 0
+    import oracle
+    oracle.set_num_threads(os.cpu_count() or 1)
+    cfg = _cpu_inputs(0)
+    for i in range(args.warmup):
+        cfg["h"] = i % cfg["heads"]
+        _cpu_layer_sample(cfg)
+    done = 0.0
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        cfg["h"] = i % cfg["heads"]
+        done += _cpu_layer_sample(cfg)
+    el = time.perf_counter() - t0
+    value = done / el / N_LAYERS
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "parallelism": "host cores",
+                   "step": "each step is one bounded sample: " + SAMPLE_DESC},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+                         "sample": SAMPLE_DESC},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args):
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from laprune_b200 import _lib, ops
+
+    world, rank, local = _dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", init_method="env://",
+                                timeout=__import__("datetime").timedelta(seconds=300))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = _lib.load()
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+
+    layers = []
+    for li in range(N_LAYERS):
+        C = torch.randn((HKV, M, K, D), generator=g, device=dev) * 0.05
+        codes = torch.randint(0, 256, (HKV, T_CTX, M), generator=g, device=dev, dtype=torch.uint8)
+        keys = torch.randn((HKV, T_CTX, D), generator=g, device=dev).to(torch.bfloat16)
+        vals = torch.randn((HKV, T_CTX, D), generator=g, device=dev).to(torch.bfloat16)
+        q = torch.randn((HQ, D), generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty((1, HQ, D), dtype=torch.bfloat16, device=dev)
+        layers.append({"C": C, "codes": codes, "keys": keys, "vals": vals, "q": q, "out": out})
+    for L in layers:
+        L["args"] = ops.build_args(L["q"], L["C"], L["codes"], L["keys"], L["vals"], topk=TOPK,
+                                   sink=SINK, local=LOCAL, out=L["out"])
+    need = max(lib.lp_sparse_decode_workspace_size(ctypes.byref(L["args"])) for L in layers)
+    ws = ops.workspace(need, dev, tag="bench")
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def step(events=None):
+        for li, L in enumerate(layers):
+            a = L["args"]
+            if events is not None:
+                a.stage_events = ctypes.cast(events[li], ctypes.c_void_p)
+            else:
+                a.stage_events = None
+            rc = lib.lp_sparse_decode(ctypes.byref(a), ws.data_ptr(), ws.numel(), sh)
+            if rc != 0:
+                _lib.check(rc)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+
+    # per-stage events on sampled steps
+    sample_every = max(1, args.steps // 8)
+    ev_sets = {}
+    for s in range(0, args.steps, sample_every):
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(N_LAYERS)]
+        ev_sets[s] = (evs, [ops.event_array(e) for e in evs])
+
+    sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for s in range(args.steps):
+        step(ev_sets[s][1] if s in ev_sets else None)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    elapsed_ms = t_start.elapsed_time(t_end)
+
+    stage_ms = [0.0] * 4
+    nsamp = 0
+    for s, (evs, _) in ev_sets.items():
+        for li in range(N_LAYERS):
+            e = evs[li]
+            for j in range(4):
+                stage_ms[j] += e[j].elapsed_time(e[j + 1])
+            nsamp += 1
+    stage_ms = [x / max(1, nsamp) for x in stage_ms]
+
+    ok = all(bool(torch.isfinite(L["out"]).all()) for L in layers)
+    errs = ops.device_errors(ws, dev)
+
+    # ---- end to end through the public API: host q in, host out back ----
+    q_host = torch.empty((N_LAYERS, HQ, D), dtype=torch.bfloat16).pin_memory()
+    q_host.copy_(torch.stack([L["q"].cpu() for L in layers]))
+    out_host = torch.empty((N_LAYERS, HQ, D), dtype=torch.bfloat16).pin_memory()
+    q_dev = torch.empty((N_LAYERS, HQ, D), dtype=torch.bfloat16, device=dev)
+    out_dev = torch.empty((N_LAYERS, HQ, D), dtype=torch.bfloat16, device=dev)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        for li, L in enumerate(layers):
+            ops.sparse_decode(q_dev[li], L["C"], L["codes"], L["keys"], L["vals"], topk=TOPK,
+                              sink=SINK, local=LOCAL, out=out_dev[li:li + 1], ws=ws)
+        out_host.copy_(out_dev, non_blocking=True)
+
+    for _ in range(max(1, min(args.warmup, 3))):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_end)
+
+    # max over ranks
+    t = torch.tensor([elapsed_ms, e2e_ms] + stage_ms, device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+    stage_ms = [float(x) for x in t[2:]]
+
+    if rank == 0:
+        tok_s = world * args.steps / (elapsed_ms / 1e3)
+        e2e_tok_s = world * args.steps / (e2e_ms / 1e3)
+        peak, peak_kind = _peaks()
+        ncand = T_CTX - SINK - LOCAL
+        score_bytes = HKV * ncand * M                  # uint8 codes streamed per launch
+        lut_bytes = HKV * M * K * D * 4                 # fp32 codebooks read per launch
+        gather_bytes = HKV * (TOPK + SINK + LOCAL) * D * 2 * 2
+        score_s = stage_ms[1] / 1e3
+        achieved = score_bytes / score_s / 1e9
+        step_bytes = N_LAYERS * (score_bytes + lut_bytes + gather_bytes)
+        line = {
+            "metric": METRIC, "value": tok_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (scores) / bf16 (K,V,q,out)",
+            "data": "synthetic (seeded, generated on device)",
+            "config": {
+                "workload": WORKLOAD, "global_batch": world, "seq_len": T_CTX,
+                "parallelism": f"replicas x{world} (independent sequences per GPU)",
+                "l2": "inputs larger than L2: 30 resident layer instances (~18 GB) cycled per step",
+                "layer_steps_per_s": tok_s * N_LAYERS,
+                "step_algorithmic_bytes": step_bytes,
+                "step_hbm_gbs": step_bytes / (elapsed_ms / args.steps / 1e3) / 1e9,
+                "stage_us": {"lut_build": stage_ms[0] * 1e3, "score": stage_ms[1] * 1e3,
+                             "select": stage_ms[2] * 1e3, "attention": stage_ms[3] * 1e3},
+                "outputs_finite": ok, "device_error_bits": errs,
+            },
+            "roofline": {"bound": "hbm", "kernel": "score_kernel (LUT scorer + histogram)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": score_bytes,
+                         "traffic": _profile_traffic()},
+            "clocks": clocks,
+            "e2e": {"value": e2e_tok_s, "unit": UNIT,
+                    "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
+                    "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+                    "api": "laprune_b200.ops.sparse_decode per layer, q from pinned host, out to pinned host"},
+            "gpu_launches": args.steps * N_LAYERS * 4,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,137 @@
+/*
+ * laprune_b200.h -- C ABI of the B200 (sm_100a) implementation of LAPrune's
+ * sparse-decode hot path.
+ *
+ * Conventions
+ *   - Every entry point returns an int status (LP_OK == 0).  On failure the
+ *     message is available from lp_last_error() (thread-local); the Python
+ *     binding raises RuntimeError with that text, mirroring the reference's
+ *     TORCH_CHECK messages where an entry point replaces a reference one.
+ *   - Pointers are device pointers unless stated otherwise; sizes and strides
+ *     are plain integers (strides in ELEMENTS of the pointed-to type unless
+ *     stated as bytes).  No framework types cross this boundary.
+ *   - `stream` is a cudaStream_t passed as void*; every kernel is launched on
+ *     it and nothing synchronises the host, so calls are stream-ordered and
+ *     can be captured in CUDA graphs (except where noted).
+ *   - The caller owns every buffer, including `workspace` (size from the
+ *     matching *_workspace_size function, 256-byte aligned, device memory).
+ *     A workspace must not be shared by calls that may run concurrently.
+ */
+#ifndef LAPRUNE_B200_H
+#define LAPRUNE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define LP_OK 0
+#define LP_ERR_INVALID 1     /* bad argument (shape, dtype, stride, size)      */
+#define LP_ERR_CUDA 2        /* a CUDA runtime call or kernel launch failed    */
+#define LP_ERR_UNSUPPORTED 3 /* valid but not implemented on this path         */
+#define LP_ERR_WORKSPACE 4   /* workspace missing, too small or misaligned     */
+
+/* element types */
+#define LP_F32 0
+#define LP_F16 1
+#define LP_BF16 2
+#define LP_F64 3
+#define LP_U8 4
+#define LP_I8 5
+#define LP_I64 6
+#define LP_I32 7
+
+/* selection modes of the fused pipeline */
+#define LP_SELECT_KV_GROUP 0   /* top-k per KV head on GQA-summed scores      */
+#define LP_SELECT_QUERY_HEAD 1 /* top-k per query head (reference decode hook) */
+
+/* device-side error bits reported through lp_read_device_errors */
+#define LP_DEVERR_WAIT_TIMEOUT 1u  /* a bounded wait gave up                    */
+#define LP_DEVERR_TIE_OVERFLOW 2u  /* informational: exact slow select path ran */
+
+const char* lp_last_error(void);
+int lp_version(void);
+/* sizeof(lp_sparse_decode_args), for bindings to verify their struct layout */
+size_t lp_sizeof_sparse_decode_args(void);
+
+/* ======================================================================
+ * Fused hot path
+ * ====================================================================== */
+
+/* Arguments of the sparse decode step (one decode token, one layer).
+ * Geometry: B sequences, Hkv KV heads, G query heads per KV head
+ * (Hq = Hkv*G), head_dim D, M codebooks of K entries.                     */
+typedef struct lp_sparse_decode_args {
+    /* query rows q[b][hq][0..D) at q + b*q_stride_b + hq*q_stride_h (elements) */
+    const void* q;
+    int32_t q_dtype; /* LP_BF16 | LP_F16 | LP_F32 */
+    int32_t _pad0;
+    int64_t q_stride_b, q_stride_h;
+    /* fp32 codebooks, contiguous [Hkv][M][K][D] (cb_per_kv_head=1) or
+     * [M][K][D] shared by every KV head (cb_per_kv_head=0) */
+    const float* codebooks;
+    int32_t cb_per_kv_head;
+    int32_t _pad1;
+    /* uint8 codes[b][hkv][t][m] at codes + b*sb + hkv*sh + t*st + m (bytes) */
+    const uint8_t* codes;
+    int64_t codes_stride_b, codes_stride_h, codes_stride_t;
+    /* K/V cache [b][hkv][t][0..D) (elements), dtype LP_BF16 | LP_F16 */
+    const void* keys;
+    const void* vals;
+    int32_t kv_dtype;
+    int32_t _pad2;
+    int64_t k_stride_b, k_stride_h, k_stride_t;
+    int64_t v_stride_b, v_stride_h, v_stride_t;
+    int32_t B, Hkv, G, D, M, K;
+    int32_t T_codes;  /* tokens with codes (candidate scoring range ends here) */
+    int32_t T_total;  /* tokens attended to (K/V rows valid in [0,T_total))   */
+    int32_t sink;     /* leading sink tokens always kept                      */
+    int32_t local;    /* trailing local window always kept                    */
+    int32_t topk;     /* tokens selected per selection unit                   */
+    int32_t select_mode; /* LP_SELECT_KV_GROUP | LP_SELECT_QUERY_HEAD          */
+    float scale;      /* softmax scale; <= 0 selects 1/sqrt(D)                */
+    int32_t out_dtype; /* LP_BF16 | LP_F16 | LP_F32                           */
+    /* attention output out[b][hq][0..D) at out + b*out_stride_b + hq*out_stride_h;
+     * NULL skips the attention stage (scoring + selection only) */
+    void* out;
+    int64_t out_stride_b, out_stride_h;
+    /* optional fp32 per-query-head scores [B][Hq][T_codes] (contiguous); only
+     * the candidate window is written.  NULL: not produced. */
+    float* head_scores;
+    /* optional selected indices [units][topk] in ascending order, int32;
+     * units = B*Hkv (KV_GROUP) or B*Hkv*G (QUERY_HEAD).  NULL: not produced. */
+    int32_t* topk_out;
+    /* optional array of 5 cudaEvent_t recorded on `stream` before the LUT
+     * build and after the LUT build, scoring, selection and attention stages
+     * (for live per-kernel timing).  NULL: no events. */
+    void** stage_events;
+} lp_sparse_decode_args;
+
+/* Workspace bytes needed by lp_sparse_decode for this geometry. */
+size_t lp_sparse_decode_workspace_size(const lp_sparse_decode_args* a);
+
+/* LUT build (q . C_m[k], fp32) -> candidate-window scoring -> exact top-k
+ * (ties: lower index first) -> union with sink and local window -> GQA K/V
+ * gather -> split-K flash-decode.  Reference path this replaces:
+ *   laprune/llm/aq_kv.py:633-699 (approx_inner_product_multihead_gqa),
+ *   laprune/llm/modifiers/aq_evaluation.py:146-253 (_decode_attention:
+ *   candidate window :185-205, keep set :206-237, gather :239-250,
+ *   SDPA :251),
+ *   aq_kernels/aq_lut_gqa.cu:460-534 (aq_lut_gather_grouped) and
+ *   :536-664 (gqa_gather_kv / gqa_gather_kv_with_tail). */
+int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Reads and clears the device-side error bits accumulated in `workspace`
+ * by earlier calls (synchronises `stream`). */
+int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
+                          uint32_t* bits_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LAPRUNE_B200_H */

@@ -1,0 +1,80 @@
+"""ctypes binding of the C ABI declared in include/laprune_b200.h.
+
+The library is built in-tree by ``python -m laprune_b200.build``.  There is no
+fallback: if the library is missing or cannot be loaded, importing the CUDA
+entry points raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+_LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblaprune_b200.so"
+
+LP_OK, LP_ERR_INVALID, LP_ERR_CUDA, LP_ERR_UNSUPPORTED, LP_ERR_WORKSPACE = 0, 1, 2, 3, 4
+LP_F32, LP_F16, LP_BF16, LP_F64, LP_U8, LP_I8, LP_I64, LP_I32 = range(8)
+LP_SELECT_KV_GROUP, LP_SELECT_QUERY_HEAD = 0, 1
+LP_DEVERR_WAIT_TIMEOUT, LP_DEVERR_TIE_OVERFLOW = 1, 2
+
+_c_i32, _c_i64, _c_p, _c_f = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float
+
+
+class SparseDecodeArgs(ctypes.Structure):
+    """Mirror of lp_sparse_decode_args."""
+    _fields_ = [
+        ("q", _c_p), ("q_dtype", _c_i32), ("_pad0", _c_i32),
+        ("q_stride_b", _c_i64), ("q_stride_h", _c_i64),
+        ("codebooks", _c_p), ("cb_per_kv_head", _c_i32), ("_pad1", _c_i32),
+        ("codes", _c_p), ("codes_stride_b", _c_i64), ("codes_stride_h", _c_i64), ("codes_stride_t", _c_i64),
+        ("keys", _c_p), ("vals", _c_p), ("kv_dtype", _c_i32), ("_pad2", _c_i32),
+        ("k_stride_b", _c_i64), ("k_stride_h", _c_i64), ("k_stride_t", _c_i64),
+        ("v_stride_b", _c_i64), ("v_stride_h", _c_i64), ("v_stride_t", _c_i64),
+        ("B", _c_i32), ("Hkv", _c_i32), ("G", _c_i32), ("D", _c_i32), ("M", _c_i32), ("K", _c_i32),
+        ("T_codes", _c_i32), ("T_total", _c_i32), ("sink", _c_i32), ("local", _c_i32),
+        ("topk", _c_i32), ("select_mode", _c_i32),
+        ("scale", _c_f), ("out_dtype", _c_i32),
+        ("out", _c_p), ("out_stride_b", _c_i64), ("out_stride_h", _c_i64),
+        ("head_scores", _c_p), ("topk_out", _c_p), ("stage_events", _c_p),
+    ]
+
+
+# name -> (restype, argtypes) of every exported entry point
+SIGNATURES = {
+    "lp_last_error": (ctypes.c_char_p, []),
+    "lp_version": (ctypes.c_int, []),
+    "lp_sizeof_sparse_decode_args": (ctypes.c_size_t, []),
+    "lp_sparse_decode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SparseDecodeArgs)]),
+    "lp_sparse_decode": (ctypes.c_int, [ctypes.POINTER(SparseDecodeArgs), _c_p, ctypes.c_size_t, _c_p]),
+    "lp_read_device_errors": (ctypes.c_int, [_c_p, ctypes.c_size_t, _c_p, ctypes.POINTER(ctypes.c_uint32)]),
+}
+
+_lib = None
+
+
+def library_path() -> Path:
+    return _LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load the CUDA library (raises if it is not built)."""
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            raise ImportError(
+                f"laprune_b200 CUDA library not found at {_LIB_PATH}; "
+                "build it with `python -m laprune_b200.build`")
+        lib = ctypes.CDLL(str(_LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if lib.lp_sizeof_sparse_decode_args() != ctypes.sizeof(SparseDecodeArgs):
+            raise ImportError("lp_sparse_decode_args layout mismatch between the binding and the library")
+        _lib = lib
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != LP_OK:
+        msg = load().lp_last_error()
+        raise RuntimeError(msg.decode() if msg else f"laprune_b200 error {status}")

@@ -1,0 +1,422 @@
+// pipeline.cu -- C-ABI entry points of the fused sparse-decode hot path.
+#include <algorithm>
+#include <mutex>
+#include <string>
+
+#include "attention.cuh"
+#include "lut_build.cuh"
+#include "score.cuh"
+#include "select.cuh"
+
+namespace lp {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(LP_ERR_CUDA, std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
+    return LP_OK;
+}
+
+int sm_count(int device) {
+    static int cache[64] = {0};
+    if (device < 0 || device >= 64) return 148;
+    if (!cache[device]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) n = 148;
+        cache[device] = n;
+    }
+    return cache[device];
+}
+
+// Opt-in to > 48 KB dynamic shared memory, once per (kernel, device).
+template <typename F>
+static int smem_opt_in(F* kernel, int bytes, int device, bool* done_flags) {
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 0 || device >= 64) device = 0;
+    if (!done_flags[device]) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess)
+            return fail(LP_ERR_CUDA, std::string("cudaFuncSetAttribute(max dynamic smem): ") + cudaGetErrorString(e));
+        done_flags[device] = true;
+    }
+    return LP_OK;
+}
+
+// ----------------------------------------------------------------------------
+// geometry / workspace plan
+// ----------------------------------------------------------------------------
+struct Plan {
+    int U, Usel, Uatt, HG;
+    bool heads;      // per-head tables (query-head selection or head scores requested)
+    bool per_head;   // selection per query head
+    int c0, c1, ncand;
+    int n_sink, local_start, n_local, n_rows;
+    int score_threads, score_ctas_per_unit, score_chunk;
+    int sel_ctas_per_unit, sel_words_per_cta;
+    int rows_per, nsplit;
+    int64_t bm_words;
+    // workspace regions
+    uint32_t* err;
+    float* lut;
+    float* bounds;
+    float* sel_scores;
+    uint32_t* bitmap;
+    float2* tie_buf;
+    int4* info;
+    float* part;
+    uint32_t* zero;  // hist | tie_count | done_sel | done_att
+    int64_t zero_words;
+    uint32_t* hist;
+    uint32_t* tie_count;
+    uint32_t* done_sel;
+    uint32_t* done_att;
+    size_t bytes;
+};
+
+static constexpr int kScoreStages = 4;
+static constexpr int kGroupThreads = 256;
+static constexpr int kHeadsThreads = 256;
+
+static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int device) {
+    LP_CHECK(a != nullptr, "args must not be NULL");
+    LP_CHECK(a->B > 0 && a->Hkv > 0 && a->G > 0, "B, Hkv and G must be positive");
+    LP_CHECK(a->M == 32 && a->K == 256, "the fused scorer supports M=32 codebooks of K=256 entries");
+    LP_CHECK(a->D > 0 && a->D % 4 == 0 && a->D <= 512, "D must be a positive multiple of 4 (<= 512)");
+    LP_CHECK(a->T_codes >= 0 && a->T_total > 0 && a->T_codes <= a->T_total,
+             "need 0 <= T_codes <= T_total and T_total > 0");
+    LP_CHECK(a->sink >= 0 && a->local >= 0, "sink and local must be non-negative");
+    LP_CHECK(a->select_mode == LP_SELECT_KV_GROUP || a->select_mode == LP_SELECT_QUERY_HEAD,
+             "select_mode must be LP_SELECT_KV_GROUP or LP_SELECT_QUERY_HEAD");
+    Plan& p = *P;
+    p.per_head = a->select_mode == LP_SELECT_QUERY_HEAD;
+    p.heads = p.per_head || a->head_scores != nullptr;
+    LP_CHECK(!p.heads || a->G <= 4, "per-query-head scoring supports G <= 4 query heads per KV head");
+    p.U = a->B * a->Hkv;
+    p.Usel = p.per_head ? p.U * a->G : p.U;
+    p.HG = p.per_head ? 1 : a->G;
+    p.Uatt = p.Usel;
+    LP_CHECK(p.HG <= 8, "at most 8 query heads per KV head are attended per unit");
+
+    // candidate window and keep set (aq_evaluation.py:189-193, 210-237)
+    const int T = a->T_total;
+    const int sink_end = a->sink > 0 ? std::min(a->sink, a->T_codes) : 0;
+    const int local_start0 = std::max(T - std::max(a->local, 0), 0);
+    const int cand_end = a->local > 0 ? std::min(a->T_codes, local_start0) : a->T_codes;
+    p.c0 = sink_end;
+    p.c1 = std::max(sink_end, cand_end);
+    p.ncand = p.c1 - p.c0;
+    LP_CHECK(a->topk >= 0 && a->topk <= p.ncand,
+             "topk must be in [0, number of candidates] (candidates = [sink, min(T_codes, T_total-local)))");
+    int sb = a->sink > 0 ? std::min(a->sink, T) : 0;
+    int start = a->local > 0 ? std::max(T - a->local, 0) : T;
+    if (start <= 0) sb = 0;
+    else if (start < sb) start = sb;
+    p.n_sink = sb;
+    p.local_start = start;
+    p.n_local = T - start;
+    p.n_rows = p.n_sink + a->topk + p.n_local;
+    if (p.n_rows == 0) {  // reference keeps the last token (aq_evaluation.py:234-235)
+        p.local_start = T - 1;
+        p.n_local = 1;
+        p.n_rows = 1;
+    }
+    LP_CHECK(p.c0 >= p.n_sink || p.ncand == 0, "internal: candidate window overlaps the sink tokens");
+
+    const int sms = sm_count(device);
+    p.score_threads = p.heads ? kHeadsThreads : kGroupThreads;
+    const int target = p.heads ? sms : 2 * sms;
+    p.score_ctas_per_unit = std::max(1, target / p.U);
+    int chunk = (p.ncand + p.score_ctas_per_unit - 1) / std::max(1, p.score_ctas_per_unit);
+    chunk = std::max(p.score_threads, (chunk + p.score_threads - 1) / p.score_threads * p.score_threads);
+    p.score_chunk = chunk;
+    p.score_ctas_per_unit = std::max(1, (p.ncand + chunk - 1) / chunk);
+
+    const int nwords_cand = p.ncand > 0 ? ((p.c1 + 31) >> 5) - (p.c0 >> 5) : 0;
+    p.sel_ctas_per_unit = std::max(1, std::min(std::max(1, 2 * sms / p.Usel), std::max(1, nwords_cand / 8)));
+    p.sel_words_per_cta = std::max(1, (nwords_cand + p.sel_ctas_per_unit - 1) / p.sel_ctas_per_unit);
+    p.sel_ctas_per_unit = std::max(1, (nwords_cand + p.sel_words_per_cta - 1) / p.sel_words_per_cta);
+
+    const int split_target = std::max(1, 2 * sms / p.Uatt);
+    p.rows_per = std::min(kAttnRows, std::max(1, (p.n_rows + split_target - 1) / split_target));
+    p.nsplit = (p.n_rows + p.rows_per - 1) / p.rows_per;
+
+    p.bm_words = (a->T_codes + 31) / 32 + 1;
+
+    Carver c(ws);
+    p.err = c.take<uint32_t>(64);
+    p.lut = c.take<float>((size_t)p.U * 256 * 32 * (p.heads ? 4 : 1));
+    p.bounds = c.take<float>((size_t)p.U * (p.heads ? a->G : 1) * 32 * 2);
+    p.sel_scores = c.take<float>((size_t)p.Usel * std::max(1, a->T_codes));
+    p.bitmap = c.take<uint32_t>((size_t)p.Usel * p.bm_words);
+    p.tie_buf = c.take<float2>((size_t)p.Usel * kTieCap);
+    p.info = c.take<int4>((size_t)p.Usel);
+    p.part = c.take<float>((size_t)p.Uatt * p.nsplit * p.HG * (2 + 128));
+    p.zero_words = (int64_t)p.Usel * kNB + p.Usel + p.Usel + p.Uatt;
+    p.zero = c.take<uint32_t>((size_t)p.zero_words);
+    p.hist = p.zero;
+    p.tie_count = p.hist + (int64_t)p.Usel * kNB;
+    p.done_sel = p.tie_count + p.Usel;
+    p.done_att = p.done_sel + p.Usel;
+    p.bytes = c.used();
+    return LP_OK;
+}
+
+template <typename QT>
+static int launch_lut(const lp_sparse_decode_args* a, const Plan& p, cudaStream_t st) {
+    LutBuildParams lp_{};
+    lp_.q = a->q;
+    lp_.q_stride_b = a->q_stride_b;
+    lp_.q_stride_h = a->q_stride_h;
+    lp_.cb = a->codebooks;
+    lp_.cb_per_kv_head = a->cb_per_kv_head;
+    lp_.Hkv = a->Hkv;
+    lp_.G = a->G;
+    lp_.D = a->D;
+    lp_.M = a->M;
+    lp_.K = a->K;
+    lp_.lut = p.lut;
+    lp_.bounds = p.bounds;
+    lp_.zero = p.zero;
+    lp_.zero_words = p.zero_words;
+    dim3 grid(a->M, p.U);
+    if (p.heads)
+        lut_build_kernel<QT, true><<<grid, 256, 4 * a->D * sizeof(float), st>>>(lp_);
+    else
+        lut_build_kernel<QT, false><<<grid, 256, a->D * sizeof(float), st>>>(lp_);
+    return check_launch("lut_build_kernel");
+}
+
+template <typename QT, typename KT, typename OT>
+static int launch_attn(const lp_sparse_decode_args* a, const Plan& p, cudaStream_t st) {
+    AttnParams ap{};
+    ap.q = a->q;
+    ap.q_stride_b = a->q_stride_b;
+    ap.q_stride_h = a->q_stride_h;
+    ap.keys = a->keys;
+    ap.vals = a->vals;
+    ap.k_stride_b = a->k_stride_b;
+    ap.k_stride_h = a->k_stride_h;
+    ap.k_stride_t = a->k_stride_t;
+    ap.v_stride_b = a->v_stride_b;
+    ap.v_stride_h = a->v_stride_h;
+    ap.v_stride_t = a->v_stride_t;
+    ap.bitmap = p.bitmap;
+    ap.bm_stride = p.bm_words;
+    ap.Hkv = a->Hkv;
+    ap.G = a->G;
+    ap.HG = p.HG;
+    ap.c0 = p.c0;
+    ap.c1 = p.c1;
+    ap.n_sink = p.n_sink;
+    ap.k = a->topk;
+    ap.local_start = p.local_start;
+    ap.n_local = p.n_local;
+    ap.n_rows = p.n_rows;
+    ap.T_total = a->T_total;
+    ap.nsplit = p.nsplit;
+    const float scale = a->scale > 0.f ? a->scale : 1.0f / sqrtf((float)a->D);
+    ap.scale_log2 = scale * 1.4426950408889634f;
+    ap.part = p.part;
+    ap.done = p.done_att;
+    ap.out = a->out;
+    ap.out_stride_b = a->out_stride_b;
+    ap.out_stride_h = a->out_stride_h;
+    dim3 grid(p.nsplit, p.Uatt);
+    sparse_attn_kernel<QT, KT, OT, 256><<<grid, 256, 0, st>>>(ap);
+    return check_launch("sparse_attn_kernel");
+}
+
+template <typename QT, typename KT>
+static int launch_attn_out(const lp_sparse_decode_args* a, const Plan& p, cudaStream_t st) {
+    switch (a->out_dtype) {
+        case LP_BF16: return launch_attn<QT, KT, __nv_bfloat16>(a, p, st);
+        case LP_F16: return launch_attn<QT, KT, __half>(a, p, st);
+        case LP_F32: return launch_attn<QT, KT, float>(a, p, st);
+    }
+    return fail(LP_ERR_INVALID, "out_dtype must be LP_BF16, LP_F16 or LP_F32");
+}
+
+template <typename QT>
+static int launch_attn_kv(const lp_sparse_decode_args* a, const Plan& p, cudaStream_t st) {
+    switch (a->kv_dtype) {
+        case LP_BF16: return launch_attn_out<QT, __nv_bfloat16>(a, p, st);
+        case LP_F16: return launch_attn_out<QT, __half>(a, p, st);
+    }
+    return fail(LP_ERR_INVALID, "kv_dtype must be LP_BF16 or LP_F16");
+}
+
+static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+}  // namespace lp
+
+using namespace lp;
+
+extern "C" {
+
+const char* lp_last_error(void) { return g_last_error.c_str(); }
+
+int lp_version(void) { return 1; }
+
+size_t lp_sizeof_sparse_decode_args(void) { return sizeof(lp_sparse_decode_args); }
+
+size_t lp_sparse_decode_workspace_size(const lp_sparse_decode_args* a) {
+    Plan p{};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (make_plan(a, nullptr, &p, dev) != LP_OK) return 0;
+    return p.bytes;
+}
+
+int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+    int dev = 0;
+    LP_CUDA(cudaGetDevice(&dev));
+    Plan p{};
+    int rc = make_plan(a, workspace, &p, dev);
+    if (rc != LP_OK) return rc;
+    if (!workspace || workspace_bytes < p.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return fail(LP_ERR_WORKSPACE, "workspace missing, misaligned (256 B) or smaller than lp_sparse_decode_workspace_size()");
+    LP_CHECK(a->q && a->codebooks && a->codes, "q, codebooks and codes must not be NULL");
+    LP_CHECK(a->q_dtype == LP_BF16 || a->q_dtype == LP_F16 || a->q_dtype == LP_F32,
+             "q_dtype must be LP_BF16, LP_F16 or LP_F32");
+    LP_CHECK(aligned16(a->codebooks), "codebooks must be 16-byte aligned");
+    LP_CHECK(aligned16(a->codes) && a->codes_stride_b % 16 == 0 && a->codes_stride_h % 16 == 0,
+             "codes base and batch/head strides must be 16-byte aligned");
+    LP_CHECK(a->codes_stride_t == 32, "codes rows must be contiguous 32-byte rows (stride_t == M == 32)");
+    if (a->out) {
+        LP_CHECK(a->keys && a->vals, "keys and vals must not be NULL when out is requested");
+        LP_CHECK(a->D == 128, "the attention stage supports head_dim D=128");
+        const int esz = 2;
+        LP_CHECK(aligned16(a->keys) && aligned16(a->vals), "keys/vals must be 16-byte aligned");
+        LP_CHECK((a->k_stride_b * esz) % 16 == 0 && (a->k_stride_h * esz) % 16 == 0 &&
+                     (a->k_stride_t * esz) % 16 == 0 && (a->v_stride_b * esz) % 16 == 0 &&
+                     (a->v_stride_h * esz) % 16 == 0 && (a->v_stride_t * esz) % 16 == 0,
+                 "K/V strides must be multiples of 16 bytes");
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaEvent_t* ev = reinterpret_cast<cudaEvent_t*>(a->stage_events);
+    auto mark = [&](int i) -> int {
+        if (ev && ev[i]) {
+            cudaError_t e = cudaEventRecord(ev[i], st);
+            if (e != cudaSuccess) return fail(LP_ERR_CUDA, std::string("cudaEventRecord: ") + cudaGetErrorString(e));
+        }
+        return LP_OK;
+    };
+    if ((rc = mark(0)) != LP_OK) return rc;
+
+    // 1. tables
+    switch (a->q_dtype) {
+        case LP_BF16: rc = launch_lut<__nv_bfloat16>(a, p, st); break;
+        case LP_F16: rc = launch_lut<__half>(a, p, st); break;
+        default: rc = launch_lut<float>(a, p, st); break;
+    }
+    if (rc != LP_OK) return rc;
+    if ((rc = mark(1)) != LP_OK) return rc;
+
+    // 2. scores + histogram
+    if (p.ncand > 0) {
+        ScoreParams sp{};
+        sp.lut = p.lut;
+        sp.bounds = p.bounds;
+        sp.codes = a->codes;
+        sp.codes_stride_b = a->codes_stride_b;
+        sp.codes_stride_h = a->codes_stride_h;
+        sp.Hkv = a->Hkv;
+        sp.G = a->G;
+        sp.c0 = p.c0;
+        sp.c1 = p.c1;
+        sp.chunk = p.score_chunk;
+        sp.sel_scores = p.sel_scores;
+        sp.sel_stride = std::max(1, a->T_codes);
+        sp.head_scores = a->head_scores;
+        sp.hs_stride = a->T_codes;
+        sp.hist = p.hist;
+        sp.sel_per_head = p.per_head ? 1 : 0;
+        sp.err = p.err;
+        dim3 grid(p.score_ctas_per_unit, p.U);
+        if (p.heads) {
+            using S = ScoreSmem<true, kHeadsThreads, kScoreStages>;
+            static bool opt[64] = {false};
+            rc = smem_opt_in(score_kernel<true, kHeadsThreads, kScoreStages>, S::kTotal, dev, opt);
+            if (rc != LP_OK) return rc;
+            score_kernel<true, kHeadsThreads, kScoreStages><<<grid, kHeadsThreads, S::kTotal, st>>>(sp);
+        } else {
+            using S = ScoreSmem<false, kGroupThreads, kScoreStages>;
+            static bool opt[64] = {false};
+            rc = smem_opt_in(score_kernel<false, kGroupThreads, kScoreStages>, S::kTotal, dev, opt);
+            if (rc != LP_OK) return rc;
+            score_kernel<false, kGroupThreads, kScoreStages><<<grid, kGroupThreads, S::kTotal, st>>>(sp);
+        }
+        rc = check_launch("score_kernel");
+        if (rc != LP_OK) return rc;
+        if ((rc = mark(2)) != LP_OK) return rc;
+
+        // 3. selection
+        SelectParams sel{};
+        sel.sel_scores = p.sel_scores;
+        sel.sel_stride = std::max(1, a->T_codes);
+        sel.bounds = p.bounds;
+        sel.Gb = p.heads ? a->G : 1;
+        sel.per_head = p.per_head ? 1 : 0;
+        sel.hist = p.hist;
+        sel.bitmap = p.bitmap;
+        sel.bm_stride = p.bm_words;
+        sel.tie_buf = p.tie_buf;
+        sel.tie_count = p.tie_count;
+        sel.done = p.done_sel;
+        sel.info = p.info;
+        sel.c0 = p.c0;
+        sel.c1 = p.c1;
+        sel.k = a->topk;
+        sel.words_per_cta = p.sel_words_per_cta;
+        sel.err = p.err;
+        const int sel_smem = kTieCap * 8;
+        static bool opt_sel[64] = {false};
+        rc = smem_opt_in(select_kernel<256>, sel_smem, dev, opt_sel);
+        if (rc != LP_OK) return rc;
+        select_kernel<256><<<dim3(p.sel_ctas_per_unit, p.Usel), 256, sel_smem, st>>>(sel);
+        rc = check_launch("select_kernel");
+        if (rc != LP_OK) return rc;
+        if (a->topk_out && a->topk > 0) {
+            compact_kernel<256><<<p.Usel, 256, 0, st>>>(p.bitmap, p.bm_words, p.c0, p.c1, a->topk, a->topk_out);
+            rc = check_launch("compact_kernel");
+            if (rc != LP_OK) return rc;
+        }
+    } else {
+        if ((rc = mark(2)) != LP_OK) return rc;
+    }
+    if ((rc = mark(3)) != LP_OK) return rc;
+
+    // 4. attention over the kept rows
+    if (a->out) {
+        switch (a->q_dtype) {
+            case LP_BF16: rc = launch_attn_kv<__nv_bfloat16>(a, p, st); break;
+            case LP_F16: rc = launch_attn_kv<__half>(a, p, st); break;
+            default: rc = launch_attn_kv<float>(a, p, st); break;
+        }
+        if (rc != LP_OK) return rc;
+    }
+    if ((rc = mark(4)) != LP_OK) return rc;
+    return LP_OK;
+}
+
+int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream, uint32_t* bits_out) {
+    LP_CHECK(workspace && workspace_bytes >= 256 && bits_out, "workspace and bits_out must not be NULL");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    uint32_t v = 0;
+    LP_CUDA(cudaMemcpyAsync(&v, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    LP_CUDA(cudaStreamSynchronize(st));
+    LP_CUDA(cudaMemsetAsync(workspace, 0, sizeof(uint32_t), st));
+    *bits_out = v;
+    return LP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,223 @@
+"""Torch-facing wrappers of the fused sparse-decode hot path.
+
+These functions take CUDA tensors, allocate outputs, and call the C ABI of
+``include/laprune_b200.h`` on the current CUDA stream.  They never fall back
+to a CPU or PyTorch implementation: a non-CUDA input or a missing library is
+an error.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import SparseDecodeArgs
+
+_DTYPE = {torch.float32: _lib.LP_F32, torch.float16: _lib.LP_F16, torch.bfloat16: _lib.LP_BF16}
+
+_ws_lock = threading.Lock()
+_ws_cache: dict = {}
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def workspace(nbytes: int, device: torch.device, tag: str = "decode") -> torch.Tensor:
+    """A cached, zero-initialised device workspace of at least ``nbytes``.
+
+    One workspace per (device, tag, stream); calls sharing it must be
+    stream-ordered (the default for calls issued from one stream).
+    """
+    dev = torch.device(device)
+    key = (dev.index, tag, torch.cuda.current_stream(dev).cuda_stream)
+    with _ws_lock:
+        ws = _ws_cache.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
+            _ws_cache[key] = ws
+        return ws
+
+
+@dataclass
+class SparseDecodeResult:
+    out: Optional[torch.Tensor]
+    topk: Optional[torch.Tensor]
+    head_scores: Optional[torch.Tensor]
+
+
+def _window(T_codes: int, T_total: int, sink: int, local: int):
+    sink_end = min(sink, T_codes) if sink > 0 else 0
+    local_start = max(T_total - max(local, 0), 0)
+    cand_end = min(T_codes, local_start) if local > 0 else T_codes
+    return sink_end, max(sink_end, cand_end)
+
+
+def num_candidates(T_codes: int, T_total: int, sink: int, local: int) -> int:
+    lo, hi = _window(T_codes, T_total, sink, local)
+    return hi - lo
+
+
+def build_args(q, codebooks, codes, keys=None, vals=None, *, topk: int, T_codes=None, T_total=None,
+               sink: int = 4, local: int = 64, select: str = "kv_group", scale=None,
+               out=None, head_scores=None, topk_out=None) -> SparseDecodeArgs:
+    """Validate tensors and fill the C argument struct (no launch)."""
+    if q.dim() == 2:
+        q = q.unsqueeze(0)
+    if codes.dim() == 3:
+        codes = codes.unsqueeze(0)
+    if keys is not None and keys.dim() == 3:
+        keys = keys.unsqueeze(0)
+    if vals is not None and vals.dim() == 3:
+        vals = vals.unsqueeze(0)
+    for name, t in (("q", q), ("codebooks", codebooks), ("codes", codes), ("keys", keys), ("vals", vals)):
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor")
+    B, Hq, D = q.shape
+    _, Hkv, cap, M = codes.shape
+    if codes.dtype != torch.uint8:
+        raise RuntimeError("codes must be uint8")
+    if Hq % Hkv != 0:
+        raise RuntimeError(f"Invalid GQA score heads: Hq={Hq}, Hkv={Hkv}")
+    G = Hq // Hkv
+    if codebooks.dtype != torch.float32 or not codebooks.is_contiguous():
+        raise RuntimeError("codebooks must be contiguous fp32 [Hkv,M,K,D] or [M,K,D]")
+    per_kv = codebooks.dim() == 4
+    if per_kv and codebooks.shape[0] != Hkv:
+        raise RuntimeError("per-KV-head codebooks must have Hkv sets")
+    Mc, K, Dc = codebooks.shape[-3:]
+    if Mc != M or Dc != D:
+        raise RuntimeError(f"AQ shape mismatch: codebook={tuple(codebooks.shape)}, q={tuple(q.shape)}, codes={tuple(codes.shape)}")
+    if q.stride(-1) != 1 or codes.stride(-1) != 1:
+        raise RuntimeError("q and codes must be contiguous in their last dimension")
+    T_codes = cap if T_codes is None else int(T_codes)
+    T_total = (keys.shape[2] if keys is not None else T_codes) if T_total is None else int(T_total)
+    if not 0 <= T_codes <= cap:
+        raise RuntimeError(f"T_codes={T_codes} exceeds the code cache capacity {cap}")
+    if keys is not None and (T_total > keys.shape[2] or T_total > vals.shape[2]):
+        raise RuntimeError(f"T_total={T_total} exceeds the K/V cache capacity {keys.shape[2]}")
+    if keys is not None and (keys.shape[:2] != (B, Hkv) or vals.shape != keys.shape or keys.shape[3] != D):
+        raise RuntimeError("expected K/V [B,Hkv,T,D] matching q and codes")
+    a = SparseDecodeArgs()
+    a.q = q.data_ptr()
+    a.q_dtype = _DTYPE[q.dtype]
+    a.q_stride_b, a.q_stride_h = q.stride(0), q.stride(1)
+    a.codebooks = codebooks.data_ptr()
+    a.cb_per_kv_head = int(per_kv)
+    a.codes = codes.data_ptr()
+    a.codes_stride_b, a.codes_stride_h, a.codes_stride_t = codes.stride(0), codes.stride(1), codes.stride(2)
+    if keys is not None:
+        if keys.dtype not in (torch.bfloat16, torch.float16) or vals.dtype != keys.dtype:
+            raise RuntimeError("keys/vals must both be bf16 or both fp16")
+        if keys.stride(-1) != 1 or vals.stride(-1) != 1:
+            raise RuntimeError("K/V head dimension must be contiguous")
+        a.keys, a.vals = keys.data_ptr(), vals.data_ptr()
+        a.kv_dtype = _DTYPE[keys.dtype]
+        a.k_stride_b, a.k_stride_h, a.k_stride_t = keys.stride(0), keys.stride(1), keys.stride(2)
+        a.v_stride_b, a.v_stride_h, a.v_stride_t = vals.stride(0), vals.stride(1), vals.stride(2)
+    a.B, a.Hkv, a.G, a.D, a.M, a.K = B, Hkv, G, D, M, K
+    a.T_codes, a.T_total, a.sink, a.local = T_codes, T_total, int(sink), int(local)
+    a.topk = int(topk)
+    if select not in ("kv_group", "query_head"):
+        raise RuntimeError("select must be 'kv_group' or 'query_head'")
+    a.select_mode = _lib.LP_SELECT_KV_GROUP if select == "kv_group" else _lib.LP_SELECT_QUERY_HEAD
+    a.scale = float(scale) if scale is not None else 0.0
+    if out is not None:
+        if out.dim() == 2:
+            out = out.unsqueeze(0)
+        a.out = out.data_ptr()
+        a.out_dtype = _DTYPE[out.dtype]
+        a.out_stride_b, a.out_stride_h = out.stride(0), out.stride(1)
+    if head_scores is not None:
+        a.head_scores = head_scores.data_ptr()
+    if topk_out is not None:
+        a.topk_out = topk_out.data_ptr()
+    return a
+
+
+def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
+                  keys: Optional[torch.Tensor] = None, vals: Optional[torch.Tensor] = None, *,
+                  topk: int, T_codes: Optional[int] = None, T_total: Optional[int] = None,
+                  sink: int = 4, local: int = 64, select: str = "kv_group",
+                  scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                  out_dtype: Optional[torch.dtype] = None, return_topk: bool = False,
+                  return_head_scores: bool = False, attention: bool = True,
+                  ws: Optional[torch.Tensor] = None, stage_events=None) -> SparseDecodeResult:
+    """One sparse decode step of one layer (see lp_sparse_decode).
+
+    q [B,Hq,D] (or [Hq,D]); codebooks fp32 [Hkv,M,K,D] or [M,K,D]; codes uint8
+    [B,Hkv,cap,M]; keys/vals [B,Hkv,cap,D] bf16/fp16.  Returns the attention
+    output [B,Hq,D] (``out_dtype``, default the K/V dtype), and optionally the
+    selected indices ([B*Hkv, topk] or [B*Hq, topk], ascending int32) and the
+    fp32 per-query-head scores [B,Hq,T_codes] (candidate window only).
+    """
+    squeeze = q.dim() == 2
+    q3 = q.unsqueeze(0) if squeeze else q
+    B, Hq, D = q3.shape
+    Hkv = codes.shape[-3]
+    dev = q.device
+    T_codes_v = codes.shape[-2] if T_codes is None else int(T_codes)
+    o = None
+    if attention:
+        if keys is None or vals is None:
+            raise RuntimeError("keys and vals are required for the attention stage")
+        if out is None:
+            out = torch.empty((B, Hq, D), dtype=out_dtype or keys.dtype, device=dev)
+        o = out
+    units = B * Hkv if select == "kv_group" else B * Hq
+    tk = torch.empty((units, max(topk, 1)), dtype=torch.int32, device=dev) if return_topk else None
+    hs = torch.zeros((B, Hq, T_codes_v), dtype=torch.float32, device=dev) if return_head_scores else None
+    a = build_args(q3, codebooks, codes, keys, vals, topk=topk, T_codes=T_codes, T_total=T_total,
+                   sink=sink, local=local, select=select, scale=scale, out=o, head_scores=hs,
+                   topk_out=tk)
+    ev_arr = None
+    if stage_events is not None:
+        ev_arr = event_array(stage_events)
+        a.stage_events = ctypes.cast(ev_arr, ctypes.c_void_p)
+    lib = _lib.load()
+    need = lib.lp_sparse_decode_workspace_size(ctypes.byref(a))
+    if need == 0:
+        _lib.check(_lib.LP_ERR_INVALID)
+    if ws is None:
+        ws = workspace(need, dev)
+    with torch.cuda.device(dev):
+        _lib.check(lib.lp_sparse_decode(ctypes.byref(a), ws.data_ptr(), ws.numel(), _stream_handle(dev)))
+    if o is not None and squeeze:
+        o = o[0]
+    return SparseDecodeResult(out=o, topk=tk[:, :topk] if tk is not None else None, head_scores=hs)
+
+
+def event_array(events) -> ctypes.Array:
+    """ctypes array of raw cudaEvent_t handles of torch.cuda.Event objects
+    (each event is created on the current device if it was not yet)."""
+    handles = []
+    for e in events:
+        if e is None:
+            handles.append(None)
+            continue
+        if not e.cuda_event:
+            e.record()  # lazily creates the underlying cudaEvent_t
+        handles.append(e.cuda_event)
+    return (ctypes.c_void_p * len(handles))(*handles)
+
+
+def device_errors(ws: Optional[torch.Tensor] = None, device=None) -> int:
+    """Read and clear the device-side error bits of a workspace."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if ws is None:
+        key = (dev.index, "decode", torch.cuda.current_stream(dev).cuda_stream)
+        ws = _ws_cache.get(key)
+        if ws is None:
+            return 0
+    bits = ctypes.c_uint32(0)
+    _lib.check(_lib.load().lp_read_device_errors(ws.data_ptr(), ws.numel(), _stream_handle(dev),
+                                                 ctypes.byref(bits)))
+    return int(bits.value)

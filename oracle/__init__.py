@@ -215,6 +215,14 @@ def encode_stage_dists(x_row, codebooks, prefix_codes, m: int) -> np.ndarray:
     return out
 
 
+def _gather_rows(src, head: int, rows) -> np.ndarray:
+    """fp32 copy of src[head][rows] for a numpy array or a (CPU) torch tensor."""
+    if hasattr(src, "float") and hasattr(src, "numpy"):  # torch tensor, any float dtype
+        import torch
+        return src[head][torch.from_numpy(np.asarray(rows, dtype=np.int64))].float().numpy()
+    return np.asarray(src[head][rows], dtype=np.float32)
+
+
 def sparse_attention(q, keys, vals, idx, G: int, scale: float | None = None) -> np.ndarray:
     """fp32 softmax(q K[idx]^T * scale) V[idx] per query head.
 
@@ -232,8 +240,8 @@ def sparse_attention(q, keys, vals, idx, G: int, scale: float | None = None) -> 
     kg = np.empty((H, n, D), dtype=np.float32)
     vg = np.empty((H, n, D), dtype=np.float32)
     for h in range(H):
-        kg[h] = np.asarray(keys[h // G][idx[h]], dtype=np.float32)
-        vg[h] = np.asarray(vals[h // G][idx[h]], dtype=np.float32)
+        kg[h] = _gather_rows(keys, h // G, idx[h])
+        vg[h] = _gather_rows(vals, h // G, idx[h])
     local = np.broadcast_to(np.arange(n, dtype=np.int32), (H, n)).copy()
     out = np.empty((H, D), dtype=np.float32)
     _load().orc_sparse_attention(_p(q, _f32p), _p(kg, _f32p), _p(vg, _f32p),
