@@ -20,6 +20,12 @@
 //     one FADD per (token, m).
 //   * HEADS tables hold the G <= 4 query heads of a KV group interleaved
 //     (16 bytes per (k, m)); one 128-bit conflict-free gather per (token, m).
+//   * Table entries are staged into shared memory as int32 fixed point with
+//     a power-of-two scale 2^S chosen from the table bound (every entry
+//     below 2^25 / 2^23 in magnitude, so 32 / 128 terms cannot overflow), and
+//     the gathered entries are summed EXACTLY in integers.  The score is
+//     therefore independent of the (rotated) summation order: tokens with
+//     identical code rows get identical scores, and ties are real ties.
 //   * The selection score of every candidate token is written (fp32) and
 //     counted into a per-unit histogram over the hard score bound [lo, hi]
 //     derived from the table's per-m min/max, for the radix select that
@@ -80,6 +86,26 @@ __device__ __forceinline__ BinParams bin_params(const float* bounds, int u, int 
     return bp;
 }
 
+// Power-of-two fixed-point scale of a unit's tables: S such that every
+// entry |v| < 2^(limit_bits - S).  Derived from the per-(head, m) min/max so
+// every CTA of the unit computes the same S.
+__device__ __forceinline__ int fixed_shift(const float* bounds, int u, int Gb, int M, int limit_bits) {
+    float mx = 0.f;
+    for (int g = 0; g < Gb; ++g) {
+        const float* bd = bounds + ((int64_t)u * Gb + g) * M * 2;
+        for (int i = 0; i < 2 * M; ++i) mx = fmaxf(mx, fabsf(bd[i]));
+    }
+    if (!(mx > 0.f) || !isfinite(mx)) return 0;
+    int e;
+    frexpf(mx, &e);  // mx < 2^e
+    int S = limit_bits - e;
+    return S < -100 ? -100 : (S > 100 ? 100 : S);
+}
+
+__device__ __forceinline__ int to_fixed(float v, float scale) {
+    return __float2int_rn(__fmul_rn(v, scale));
+}
+
 // Shared-memory footprint of the scorer.
 template <bool HEADS, int THREADS, int STAGES>
 struct ScoreSmem {
@@ -132,21 +158,25 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
             bulk_g2s(s_lut, lut_g, S::kLutBytes, s_lut_bar);
         }
     }
+    const int Gb = HEADS ? p.G : 1;
+    const int S_fx = fixed_shift(p.bounds, u, Gb, 32, HEADS ? 23 : 25);
+    const float to_fx = ldexpf(1.f, S_fx), from_fx = ldexpf(1.f, -S_fx);
     if (!HEADS) {
-        // [k][m] (32 floats per k) -> [k][m'] with m' and m'+32 both LUT[m'][k]
+        // [k][m] (32 floats per k) -> int32 [k][m'] with m' and m'+32 both LUT[m'][k]
         const float4* g4 = reinterpret_cast<const float4*>(lut_g);
-        float4* d4 = reinterpret_cast<float4*>(s_lut);
+        int4* d4 = reinterpret_cast<int4*>(s_lut);
         for (int f = tid; f < 256 * 8; f += THREADS) {
             const float4 v = __ldg(g4 + f);
+            const int4 iv = make_int4(to_fixed(v.x, to_fx), to_fixed(v.y, to_fx), to_fixed(v.z, to_fx),
+                                      to_fixed(v.w, to_fx));
             const int k = f >> 3, m4 = f & 7;
-            d4[k * 16 + m4] = v;
-            d4[k * 16 + 8 + m4] = v;
+            d4[k * 16 + m4] = iv;
+            d4[k * 16 + 8 + m4] = iv;
         }
     }
     for (int i = tid; i < S::kHistHeads * kNB; i += THREADS) s_hist[i] = 0u;
 
     // selection-unit bin parameters
-    const int Gb = HEADS ? p.G : 1;
     BinParams bp[S::kHistHeads];
     if (HEADS && p.sel_per_head) {
 #pragma unroll
@@ -177,6 +207,15 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
         for (int j = 0; j < issued; ++j) mbar_wait(&s_bar[j], 0u, nullptr);
         return;
     }
+    if (HEADS) {
+        float4* l4 = reinterpret_cast<float4*>(s_lut);
+        for (int i = tid; i < S::kLutBytes / 16; i += THREADS) {
+            const float4 v = l4[i];
+            reinterpret_cast<int4*>(l4)[i] = make_int4(to_fixed(v.x, to_fx), to_fixed(v.y, to_fx),
+                                                       to_fixed(v.z, to_fx), to_fixed(v.w, to_fx));
+        }
+        __syncthreads();
+    }
 
     for (int i = 0; i < ntiles; ++i) {
         const int slot = i % STAGES;
@@ -190,20 +229,21 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
         if (t < t_end) {
             const uint32_t* row = reinterpret_cast<const uint32_t*>(s_ring + slot * THREADS * 32 + tid * 32);
             if (!HEADS) {
-                float acc = 0.f;
+                int iacc = 0;
 #pragma unroll
                 for (int w = 0; w < 8; ++w) {
                     const uint32_t cw = row[(w + L) & 7u];
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
                         const uint32_t a = __byte_perm(cw, off[s], sel[s]);
-                        acc += *reinterpret_cast<const float*>(s_lut + a + 16 * w);
+                        iacc += *reinterpret_cast<const int*>(s_lut + a + 16 * w);
                     }
                 }
+                const float acc = __fmul_rn(__int2float_rn(iacc), from_fx);
                 p.sel_scores[(int64_t)u * p.sel_stride + t] = acc;
                 atomicAdd(&s_hist[score_bin(acc, bp[0].lo, bp[0].inv_w, kNB)], 1u);
             } else {
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                int i0 = 0, i1 = 0, i2 = 0, i3 = 0;
 #pragma unroll
                 for (int w = 0; w < 8; ++w) {
                     const uint32_t wi = (w + L) & 7u;
@@ -212,13 +252,17 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
                         const uint32_t code = __byte_perm(cw, 0u, sel[s]);
-                        const float4 v = *reinterpret_cast<const float4*>(s_lut + (code << 9) + rot + off[s]);
-                        a0 += v.x;
-                        a1 += v.y;
-                        a2 += v.z;
-                        a3 += v.w;
+                        const int4 v = *reinterpret_cast<const int4*>(s_lut + (code << 9) + rot + off[s]);
+                        i0 += v.x;
+                        i1 += v.y;
+                        i2 += v.z;
+                        i3 += v.w;
                     }
                 }
+                const float a0 = __fmul_rn(__int2float_rn(i0), from_fx);
+                const float a1 = __fmul_rn(__int2float_rn(i1), from_fx);
+                const float a2 = __fmul_rn(__int2float_rn(i2), from_fx);
+                const float a3 = __fmul_rn(__int2float_rn(i3), from_fx);
                 const float hs[4] = {a0, a1, a2, a3};
                 if (p.head_scores) {
 #pragma unroll
@@ -234,7 +278,7 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
                         }
                     }
                 } else {
-                    const float sum = ((a0 + a1) + a2) + a3;
+                    const float sum = __fmul_rn(__int2float_rn(((i0 + i1) + i2) + i3), from_fx);
                     p.sel_scores[(int64_t)u * p.sel_stride + t] = sum;
                     atomicAdd(&s_hist[score_bin(sum, bp[0].lo, bp[0].inv_w, kNB)], 1u);
                 }
