@@ -117,25 +117,41 @@ __global__ void __launch_bounds__(THREADS) sparse_attn_kernel(AttnParams p) {
         const uint32_t* bm = p.bitmap + (int64_t)u * p.bm_stride;
         const int wlo = p.c0 >> 5, whi = (p.c1 + 31) >> 5;
         const int nwords = whi - wlo;
+        // each thread owns a contiguous run of words; runs are scanned in
+        // rounds of WB words held in registers (loads issued together)
+        constexpr int WB = 16;
         const int per = (nwords + THREADS - 1) / THREADS;
         const int wa = wlo + tid * per, wb = min(whi, wa + per);
-        int cnt = 0;
-        for (int w = wa; w < wb; ++w) cnt += __popc(bm[w]);
-        int before;
-        Scan(scan_tmp).ExclusiveSum(cnt, before);
-        if (before < j1 && before + cnt > j0) {
-            int rank = before;
-            for (int w = wa; w < wb && rank < j1; ++w) {
-                uint32_t bits = bm[w];
-                const int c = __popc(bits);
-                if (rank + c <= j0) { rank += c; continue; }
-                while (bits) {
-                    const int bit = __ffs(bits) - 1;
-                    bits &= bits - 1;
-                    if (rank >= j0 && rank < j1) s_rows[p.n_sink + rank - r0] = w * 32 + bit;
-                    ++rank;
+        int base_round = 0;  // selected tokens before this round (block-wide)
+        for (int r = 0; r < per; r += WB) {
+            uint32_t words[WB];
+            int cnt = 0;
+#pragma unroll
+            for (int j = 0; j < WB; ++j) {
+                const int w = wa + r + j;
+                words[j] = (r + j < per && w < wb) ? __ldcg(bm + w) : 0u;
+            }
+#pragma unroll
+            for (int j = 0; j < WB; ++j) cnt += __popc(words[j]);
+            int before, total;
+            Scan(scan_tmp).ExclusiveSum(cnt, before, total);
+            __syncthreads();
+            int rank = base_round + before;
+            if (rank < j1 && rank + cnt > j0) {
+#pragma unroll
+                for (int j = 0; j < WB; ++j) {
+                    uint32_t bits = words[j];
+                    const int c = __popc(bits);
+                    if (rank + c <= j0 || rank >= j1) { rank += c; continue; }
+                    while (bits) {
+                        const int bit = __ffs(bits) - 1;
+                        bits &= bits - 1;
+                        if (rank >= j0 && rank < j1) s_rows[p.n_sink + rank - r0] = (wa + r + j) * 32 + bit;
+                        ++rank;
+                    }
                 }
             }
+            base_round += total;
         }
     }
     // queries (fp32)
@@ -171,7 +187,7 @@ __global__ void __launch_bounds__(THREADS) sparse_attn_kernel(AttnParams p) {
             a = fmaf(qv.w, kv.w, a);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-            if (lane == 0) s_p[g][r] = a * p.scale_log2;
+            if (lane == g) s_p[g][r] = a * p.scale_log2;
         }
     }
     __syncthreads();
@@ -221,18 +237,59 @@ __global__ void __launch_bounds__(THREADS) sparse_attn_kernel(AttnParams p) {
     __threadfence();
     const float* pu = p.part + (int64_t)u * p.nsplit * p.HG * (2 + D);
     OT* ob = reinterpret_cast<OT*>(p.out) + (int64_t)b * p.out_stride_b;
-    for (int o = tid; o < p.HG * D; o += THREADS) {
-        const int g = o / D, d = o - g * D;
-        float M = -INFINITY;
-        for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, __ldcg(pu + ((int64_t)s * p.HG + g) * (2 + D)));
-        float L = 0.f, acc = 0.f;
-        for (int s = 0; s < p.nsplit; ++s) {
-            const float* ps = pu + ((int64_t)s * p.HG + g) * (2 + D);
-            const float f = exp2f(__ldcg(ps) - M);
-            L = fmaf(__ldcg(ps + 1), f, L);
-            acc = fmaf(__ldcg(ps + 2 + d), f, acc);
+    // slice weights 2^(m_s - M) / L per head, computed once into shared memory
+    float* s_w = &s_p[0][0];  // reuse: needs nsplit * HG floats (<= 8 * R)
+    const bool wfit = p.nsplit * p.HG <= 8 * R;
+    if (wfit) {
+        for (int g = warp; g < p.HG; g += NW) {
+            float M = -INFINITY;
+            for (int s = lane; s < p.nsplit; s += 32) M = fmaxf(M, __ldcg(pu + ((int64_t)s * p.HG + g) * (2 + D)));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            float L = 0.f;
+            for (int s = lane; s < p.nsplit; s += 32) {
+                const float* ps = pu + ((int64_t)s * p.HG + g) * (2 + D);
+                const float f = exp2f(__ldcg(ps) - M);
+                s_w[g * p.nsplit + s] = f;
+                L = fmaf(__ldcg(ps + 1), f, L);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+            __syncwarp();
+            const float invL = 1.f / L;
+            for (int s = lane; s < p.nsplit; s += 32) s_w[g * p.nsplit + s] *= invL;
         }
-        ob[(int64_t)(hkv * p.G + g0 + g) * p.out_stride_h + d] = from_f32<OT>(acc / L);
+        __syncthreads();
+        for (int o = tid; o < p.HG * D; o += THREADS) {
+            const int g = o / D, d = o - g * D;
+            const float* pg = pu + (int64_t)g * (2 + D) + 2 + d;
+            const int64_t sstride = (int64_t)p.HG * (2 + D);
+            float acc = 0.f;
+            int s = 0;
+            for (; s + 8 <= p.nsplit; s += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = __ldcg(pg + (s + j) * sstride);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc = fmaf(v[j], s_w[g * p.nsplit + s + j], acc);
+            }
+            for (; s < p.nsplit; ++s) acc = fmaf(__ldcg(pg + s * sstride), s_w[g * p.nsplit + s], acc);
+            ob[(int64_t)(hkv * p.G + g0 + g) * p.out_stride_h + d] = from_f32<OT>(acc);
+        }
+    } else {
+        for (int o = tid; o < p.HG * D; o += THREADS) {
+            const int g = o / D, d = o - g * D;
+            float M = -INFINITY;
+            for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, __ldcg(pu + ((int64_t)s * p.HG + g) * (2 + D)));
+            float L = 0.f, acc = 0.f;
+            for (int s = 0; s < p.nsplit; ++s) {
+                const float* ps = pu + ((int64_t)s * p.HG + g) * (2 + D);
+                const float f = exp2f(__ldcg(ps) - M);
+                L = fmaf(__ldcg(ps + 1), f, L);
+                acc = fmaf(__ldcg(ps + 2 + d), f, acc);
+            }
+            ob[(int64_t)(hkv * p.G + g0 + g) * p.out_stride_h + d] = from_f32<OT>(acc / L);
+        }
     }
 }
 

@@ -60,7 +60,7 @@ struct Plan {
     bool per_head;   // selection per query head
     int c0, c1, ncand;
     int n_sink, local_start, n_local, n_rows;
-    int score_threads, score_ctas_per_unit, score_chunk;
+    int score_ctas;
     int sel_ctas_per_unit, sel_words_per_cta;
     int rows_per, nsplit;
     int64_t bm_words;
@@ -82,9 +82,9 @@ struct Plan {
     size_t bytes;
 };
 
-static constexpr int kScoreStages = 4;
-static constexpr int kGroupThreads = 256;
-static constexpr int kHeadsThreads = 256;
+static constexpr int kScoreThreads = 512;
+static constexpr int kGroupStages = 8;
+static constexpr int kHeadsStages = 4;
 
 static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int device) {
     LP_CHECK(a != nullptr, "args must not be NULL");
@@ -132,13 +132,11 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     LP_CHECK(p.c0 >= p.n_sink || p.ncand == 0, "internal: candidate window overlaps the sink tokens");
 
     const int sms = sm_count(device);
-    p.score_threads = p.heads ? kHeadsThreads : kGroupThreads;
-    const int target = p.heads ? sms : 2 * sms;
-    p.score_ctas_per_unit = std::max(1, target / p.U);
-    int chunk = (p.ncand + p.score_ctas_per_unit - 1) / std::max(1, p.score_ctas_per_unit);
-    chunk = std::max(p.score_threads, (chunk + p.score_threads - 1) / p.score_threads * p.score_threads);
-    p.score_chunk = chunk;
-    p.score_ctas_per_unit = std::max(1, (p.ncand + chunk - 1) / chunk);
+    {
+        const int tiles_per_unit = (p.ncand + kScoreThreads - 1) / kScoreThreads;
+        const int64_t want = std::min<int64_t>((int64_t)sms, (int64_t)p.U * std::max(1, tiles_per_unit));
+        p.score_ctas = (int)std::max<int64_t>((int64_t)p.U, want);
+    }
 
     const int nwords_cand = p.ncand > 0 ? ((p.c1 + 31) >> 5) - (p.c0 >> 5) : 0;
     p.sel_ctas_per_unit = std::max(1, std::min(std::max(1, 2 * sms / p.Usel), std::max(1, nwords_cand / 8)));
@@ -154,7 +152,7 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     Carver c(ws);
     p.err = c.take<uint32_t>(64);
     p.lut = c.take<float>((size_t)p.U * 256 * 32 * (p.heads ? 4 : 1));
-    p.bounds = c.take<float>((size_t)p.U * (p.heads ? a->G : 1) * 32 * 2);
+    p.bounds = c.take<float>((size_t)p.U * (p.heads ? a->G : 1) * 32 * kLutParts * 2);
     p.sel_scores = c.take<float>((size_t)p.Usel * std::max(1, a->T_codes));
     p.bitmap = c.take<uint32_t>((size_t)p.Usel * p.bm_words);
     p.tie_buf = c.take<float2>((size_t)p.Usel * kTieCap);
@@ -187,11 +185,11 @@ static int launch_lut(const lp_sparse_decode_args* a, const Plan& p, cudaStream_
     lp_.bounds = p.bounds;
     lp_.zero = p.zero;
     lp_.zero_words = p.zero_words;
-    dim3 grid(a->M, p.U);
+    dim3 grid(a->M * kLutParts, p.U);
     if (p.heads)
-        lut_build_kernel<QT, true><<<grid, 256, 4 * a->D * sizeof(float), st>>>(lp_);
+        lut_build_kernel<QT, true><<<grid, kLutThreads, 4 * a->D * sizeof(float), st>>>(lp_);
     else
-        lut_build_kernel<QT, false><<<grid, 256, a->D * sizeof(float), st>>>(lp_);
+        lut_build_kernel<QT, false><<<grid, kLutThreads, a->D * sizeof(float), st>>>(lp_);
     return check_launch("lut_build_kernel");
 }
 
@@ -331,9 +329,9 @@ int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t wor
         sp.codes_stride_h = a->codes_stride_h;
         sp.Hkv = a->Hkv;
         sp.G = a->G;
+        sp.U = p.U;
         sp.c0 = p.c0;
         sp.c1 = p.c1;
-        sp.chunk = p.score_chunk;
         sp.sel_scores = p.sel_scores;
         sp.sel_stride = std::max(1, a->T_codes);
         sp.head_scores = a->head_scores;
@@ -341,20 +339,34 @@ int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t wor
         sp.hist = p.hist;
         sp.sel_per_head = p.per_head ? 1 : 0;
         sp.err = p.err;
-        dim3 grid(p.score_ctas_per_unit, p.U);
+        // programmatic dependent launch: the scorer starts streaming codes
+        // while the table build finishes (it waits before reading tables)
+        cudaLaunchConfig_t cfg{};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.gridDim = dim3(p.score_ctas);
+        cfg.blockDim = dim3(kScoreThreads);
+        cfg.stream = st;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t le;
         if (p.heads) {
-            using S = ScoreSmem<true, kHeadsThreads, kScoreStages>;
+            using S = ScoreSmem<true, kScoreThreads, kHeadsStages>;
             static bool opt[64] = {false};
-            rc = smem_opt_in(score_kernel<true, kHeadsThreads, kScoreStages>, S::kTotal, dev, opt);
+            rc = smem_opt_in(score_kernel<true, kScoreThreads, kHeadsStages>, S::kTotal, dev, opt);
             if (rc != LP_OK) return rc;
-            score_kernel<true, kHeadsThreads, kScoreStages><<<grid, kHeadsThreads, S::kTotal, st>>>(sp);
+            cfg.dynamicSmemBytes = S::kTotal;
+            le = cudaLaunchKernelEx(&cfg, score_kernel<true, kScoreThreads, kHeadsStages>, sp);
         } else {
-            using S = ScoreSmem<false, kGroupThreads, kScoreStages>;
+            using S = ScoreSmem<false, kScoreThreads, kGroupStages>;
             static bool opt[64] = {false};
-            rc = smem_opt_in(score_kernel<false, kGroupThreads, kScoreStages>, S::kTotal, dev, opt);
+            rc = smem_opt_in(score_kernel<false, kScoreThreads, kGroupStages>, S::kTotal, dev, opt);
             if (rc != LP_OK) return rc;
-            score_kernel<false, kGroupThreads, kScoreStages><<<grid, kGroupThreads, S::kTotal, st>>>(sp);
+            cfg.dynamicSmemBytes = S::kTotal;
+            le = cudaLaunchKernelEx(&cfg, score_kernel<false, kScoreThreads, kGroupStages>, sp);
         }
+        if (le != cudaSuccess) return fail(LP_ERR_CUDA, std::string("score_kernel launch: ") + cudaGetErrorString(le));
         rc = check_launch("score_kernel");
         if (rc != LP_OK) return rc;
         if ((rc = mark(2)) != LP_OK) return rc;

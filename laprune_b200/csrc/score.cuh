@@ -32,6 +32,7 @@
 //     follows.
 #pragma once
 #include "common.cuh"
+#include "lut_build.cuh"
 
 namespace lp {
 
@@ -42,9 +43,8 @@ struct ScoreParams {
     const float* bounds;   // [U][Gb][32][2]
     const uint8_t* codes;  // codes[b][hkv][t][32] (row stride 32 bytes)
     int64_t codes_stride_b, codes_stride_h;  // bytes
-    int Hkv, G;
+    int Hkv, G, U;
     int c0, c1;            // candidate window [c0, c1)
-    int chunk;             // tokens per CTA (multiple of the tile)
     float* sel_scores;     // [Usel][sel_stride]
     int64_t sel_stride;
     float* head_scores;    // HEADS: optional per-query-head scores [B][Hq][hs_stride]
@@ -65,11 +65,16 @@ __device__ __forceinline__ BinParams bin_params(const float* bounds, int u, int 
                                                 int g_count, int M) {
     float lo = 0.f, hi = 0.f;
     for (int g = g_first; g < g_first + g_count; ++g) {
-        const float* bd = bounds + ((int64_t)u * Gb + g) * M * 2;
+        const float* bd = bounds + ((int64_t)u * Gb + g) * M * kLutParts * 2;
         float l = 0.f, h = 0.f;
         for (int m = 0; m < M; ++m) {
-            l = __fadd_rn(l, bd[2 * m]);
-            h = __fadd_rn(h, bd[2 * m + 1]);
+            float mn = bd[(m * kLutParts) * 2], mx = bd[(m * kLutParts) * 2 + 1];
+            for (int q = 1; q < kLutParts; ++q) {
+                mn = fminf(mn, bd[(m * kLutParts + q) * 2]);
+                mx = fmaxf(mx, bd[(m * kLutParts + q) * 2 + 1]);
+            }
+            l = __fadd_rn(l, mn);
+            h = __fadd_rn(h, mx);
         }
         lo = __fadd_rn(lo, l);
         hi = __fadd_rn(hi, h);
@@ -91,11 +96,12 @@ __device__ __forceinline__ BinParams bin_params(const float* bounds, int u, int 
 // every CTA of the unit computes the same S.
 __device__ __forceinline__ int fixed_shift(const float* bounds, int u, int Gb, int M, int limit_bits) {
     float mx = 0.f;
-    for (int g = 0; g < Gb; ++g) {
-        const float* bd = bounds + ((int64_t)u * Gb + g) * M * 2;
-        for (int i = 0; i < 2 * M; ++i) mx = fmaxf(mx, fabsf(bd[i]));
+    const float* bd = bounds + (int64_t)u * Gb * M * kLutParts * 2;
+    for (int i = 0; i < Gb * M * kLutParts * 2; ++i) {
+        const float v = fabsf(bd[i]);
+        if (isfinite(v)) mx = fmaxf(mx, v);
     }
-    if (!(mx > 0.f) || !isfinite(mx)) return 0;
+    if (!(mx > 0.f)) return 0;
     int e;
     frexpf(mx, &e);  // mx < 2^e
     int S = limit_bits - e;
@@ -110,15 +116,33 @@ __device__ __forceinline__ int to_fixed(float v, float scale) {
 template <bool HEADS, int THREADS, int STAGES>
 struct ScoreSmem {
     static constexpr int kLutBytes = HEADS ? 256 * 32 * 16 : 256 * 64 * 4;
-    static constexpr int kRingBytes = STAGES * THREADS * 32;
+    static constexpr int kTileBytes = THREADS * 32;  // one code row per thread
+    static constexpr int kRingBytes = STAGES * kTileBytes;
     static constexpr int kHistHeads = HEADS ? 4 : 1;
     static constexpr int kHistBytes = kHistHeads * kNB * 4;
     static constexpr int kBarBytes = (STAGES + 1) * 8;
     static constexpr int kTotal = kLutBytes + kRingBytes + kHistBytes + kBarBytes + 128;
 };
 
+// CTA -> (unit, token range).  The nctas CTAs are spread over the U units as
+// evenly as possible (units u < nctas % U get one more CTA).
+__device__ __forceinline__ void score_cta_range(int cta, int nctas, int U, int c0, int ncand,
+                                                int* unit, int* t_begin, int* t_end) {
+    const int base = nctas / U, extra = nctas % U;
+    int u, j, n;
+    if (cta < extra * (base + 1)) {
+        u = cta / (base + 1); j = cta - u * (base + 1); n = base + 1;
+    } else {
+        const int i = cta - extra * (base + 1);
+        u = extra + i / base; j = i - (u - extra) * base; n = base;
+    }
+    *unit = u;
+    *t_begin = c0 + (int)((int64_t)ncand * j / n);
+    *t_end = c0 + (int)((int64_t)ncand * (j + 1) / n);
+}
+
 template <bool HEADS, int THREADS, int STAGES>
-__global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
+__global__ void __launch_bounds__(THREADS, 1) score_kernel(ScoreParams p) {
     using S = ScoreSmem<HEADS, THREADS, STAGES>;
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* s_lut = smem;
@@ -128,12 +152,10 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
     uint64_t* s_lut_bar = s_bar + STAGES;
 
     const int tid = threadIdx.x, lane = tid & 31;
-    const int u = blockIdx.y;
+    int u, t_begin, t_end;
+    score_cta_range(blockIdx.x, gridDim.x, p.U, p.c0, p.c1 - p.c0, &u, &t_begin, &t_end);
     const int b = u / p.Hkv, hkv = u - b * p.Hkv;
-    const int t_begin = p.c0 + blockIdx.x * p.chunk;
-    const int t_end = min(p.c1, t_begin + p.chunk);
-    if (t_begin >= t_end) return;
-    const int ntiles = (t_end - t_begin + THREADS - 1) / THREADS;
+    const int ntiles = t_end > t_begin ? (t_end - t_begin + THREADS - 1) / THREADS : 0;
     const uint8_t* src = p.codes + (int64_t)b * p.codes_stride_b + (int64_t)hkv * p.codes_stride_h;
     const float* lut_g = p.lut + (int64_t)u * (HEADS ? 256 * 32 * 4 : 256 * 32);
 
@@ -142,21 +164,26 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
         fence_barrier_init();
     }
     __syncthreads();
+    // Code tiles do not depend on the table-build kernel: start streaming them
+    // before waiting for it (programmatic dependent launch).
     uint64_t policy = 0;
+    const int npre = ntiles < STAGES ? ntiles : STAGES;
     if (tid == 0) {
         policy = policy_evict_first();
-        const int npre = ntiles < STAGES ? ntiles : STAGES;
         for (int i = 0; i < npre; ++i) {
             const int t0 = t_begin + i * THREADS;
             const int n = min(THREADS, t_end - t0);
             mbar_arrive_expect_tx(&s_bar[i], (uint32_t)n * 32u);
-            bulk_g2s_stream(s_ring + i * THREADS * 32, src + (int64_t)t0 * 32, (uint32_t)n * 32u,
+            bulk_g2s_stream(s_ring + i * S::kTileBytes, src + (int64_t)t0 * 32, (uint32_t)n * 32u,
                             &s_bar[i], policy);
         }
-        if (HEADS) {
-            mbar_arrive_expect_tx(s_lut_bar, S::kLutBytes);
-            bulk_g2s(s_lut, lut_g, S::kLutBytes, s_lut_bar);
-        }
+    }
+    for (int i = tid; i < S::kHistHeads * kNB; i += THREADS) s_hist[i] = 0u;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    if (HEADS && tid == 0) {
+        mbar_arrive_expect_tx(s_lut_bar, S::kLutBytes);
+        bulk_g2s(s_lut, lut_g, S::kLutBytes, s_lut_bar);
     }
     const int Gb = HEADS ? p.G : 1;
     const int S_fx = fixed_shift(p.bounds, u, Gb, 32, HEADS ? 23 : 25);
@@ -165,8 +192,9 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
         // [k][m] (32 floats per k) -> int32 [k][m'] with m' and m'+32 both LUT[m'][k]
         const float4* g4 = reinterpret_cast<const float4*>(lut_g);
         int4* d4 = reinterpret_cast<int4*>(s_lut);
+#pragma unroll 4
         for (int f = tid; f < 256 * 8; f += THREADS) {
-            const float4 v = __ldg(g4 + f);
+            const float4 v = __ldcg(g4 + f);
             const int4 iv = make_int4(to_fixed(v.x, to_fx), to_fixed(v.y, to_fx), to_fixed(v.z, to_fx),
                                       to_fixed(v.w, to_fx));
             const int k = f >> 3, m4 = f & 7;
@@ -174,7 +202,6 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
             d4[k * 16 + 8 + m4] = iv;
         }
     }
-    for (int i = tid; i < S::kHistHeads * kNB; i += THREADS) s_hist[i] = 0u;
 
     // selection-unit bin parameters
     BinParams bp[S::kHistHeads];
@@ -200,7 +227,7 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
             sel[s] = 0x5504u | (bs << 4);  // [0][0][code][off] = code*256 + off
         }
     }
-    int issued = ntiles < STAGES ? ntiles : STAGES;
+    int issued = npre;
     bool ok = true;
     if (HEADS) ok = mbar_wait(s_lut_bar, 0, p.err);
     if (__syncthreads_or(!ok)) {
@@ -227,7 +254,7 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
         }
         const int t = t_begin + i * THREADS + tid;
         if (t < t_end) {
-            const uint32_t* row = reinterpret_cast<const uint32_t*>(s_ring + slot * THREADS * 32 + tid * 32);
+            const uint32_t* row = reinterpret_cast<const uint32_t*>(s_ring + slot * S::kTileBytes + tid * 32);
             if (!HEADS) {
                 int iacc = 0;
 #pragma unroll
@@ -290,7 +317,7 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams p) {
             const int t0 = t_begin + j * THREADS;
             const int n = min(THREADS, t_end - t0);
             mbar_arrive_expect_tx(&s_bar[slot], (uint32_t)n * 32u);
-            bulk_g2s_stream(s_ring + slot * THREADS * 32, src + (int64_t)t0 * 32, (uint32_t)n * 32u,
+            bulk_g2s_stream(s_ring + slot * S::kTileBytes, src + (int64_t)t0 * 32, (uint32_t)n * 32u,
                             &s_bar[slot], policy);
             ++issued;
         }

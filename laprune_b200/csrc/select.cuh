@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(THREADS) select_kernel(SelectParams p) {
     const int g0 = p.per_head ? usel - bu * p.Gb : 0;
     const BinParams bp = bin_params(p.bounds, bu, p.Gb, g0, p.per_head ? 1 : p.Gb, 32);
 
-    for (int i = tid; i < kNB; i += THREADS) s_hist[i] = p.hist[(int64_t)usel * kNB + i];
+    for (int i = tid; i < kNB; i += THREADS) s_hist[i] = __ldcg(p.hist + (int64_t)usel * kNB + i);
     if (tid == 0) { s_bstar = kNB; s_above = 0; }
     __syncthreads();
     if (p.k > 0) find_threshold_bin<THREADS>(s_hist, p.k, &s_bstar, &s_above);
@@ -105,10 +105,21 @@ __global__ void __launch_bounds__(THREADS) select_kernel(SelectParams p) {
     const int wlo = p.c0 >> 5, whi = (p.c1 + 31) >> 5;
     const int wb = wlo + blockIdx.x * p.words_per_cta;
     const int we = min(whi, wb + p.words_per_cta);
-    for (int w = wb + warp; w < we; w += NWARP) {
+    constexpr int BATCH = 8;  // words per warp whose scores are loaded together
+    for (int w0 = wb + warp; w0 < we; w0 += NWARP * BATCH) {
+      float sv[BATCH];
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j) {
+        const int t = (w0 + j * NWARP) * 32 + lane;
+        sv[j] = (w0 + j * NWARP < we && t >= p.c0 && t < p.c1) ? __ldcg(sc + t) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j) {
+        const int w = w0 + j * NWARP;
+        if (w >= we) break;
         const int t = w * 32 + lane;
         const bool valid = t >= p.c0 && t < p.c1;
-        const float s = valid ? sc[t] : 0.f;
+        const float s = sv[j];
         const int bin = score_bin(s, bp.lo, bp.inv_w, kNB);
         const bool sel = valid && bin > bstar;
         const bool tie = valid && bin == bstar;
@@ -125,6 +136,7 @@ __global__ void __launch_bounds__(THREADS) select_kernel(SelectParams p) {
                     p.tie_buf[(int64_t)usel * kTieCap + pos] = make_float2(s, __int_as_float(t));
             }
         }
+      }
     }
 
     // completion: the last CTA of this unit resolves bin b*
