@@ -92,6 +92,18 @@ __global__ void __launch_bounds__(kLutThreads) lut_build_kernel(LutBuildParams p
         for (int64_t i = start; i < p.zero_words; i += nthreads) p.zero[i] = 0u;
     }
 
+    const float* cbm = p.cb + (int64_t)(p.cb_per_kv_head ? hkv : 0) * p.M * p.K * p.D +
+                       (int64_t)m * p.K * p.D;
+    const int kper = (p.K + kLutParts - 1) / kLutParts;
+    const int kbeg = part * kper, kend = min(p.K, kbeg + kper);
+    // pull this CTA's whole codebook slice toward L2 before anything else
+    if (tid == 0 && kend > kbeg) {
+        const uint32_t bytes = (uint32_t)((kend - kbeg) * p.D * sizeof(float));
+        if ((bytes & 15u) == 0 && (((uintptr_t)(cbm + (int64_t)kbeg * p.D)) & 15u) == 0)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(cbm + (int64_t)kbeg * p.D), "r"(bytes)
+                         : "memory");
+    }
+
     const QT* qb = reinterpret_cast<const QT*>(p.q) + (int64_t)b * p.q_stride_b;
     for (int d = tid; d < p.D; d += blockDim.x) {
         if (HEADS) {
@@ -107,10 +119,6 @@ __global__ void __launch_bounds__(kLutThreads) lut_build_kernel(LutBuildParams p
     }
     __syncthreads();
 
-    const float* cbm = p.cb + (int64_t)(p.cb_per_kv_head ? hkv : 0) * p.M * p.K * p.D +
-                       (int64_t)m * p.K * p.D;
-    const int kper = (p.K + kLutParts - 1) / kLutParts;
-    const int kbeg = part * kper, kend = min(p.K, kbeg + kper);
     const int nchunk = (p.D + 127) / 128;
 
     float vmin[GQ], vmax[GQ];

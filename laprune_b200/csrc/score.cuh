@@ -61,23 +61,29 @@ struct BinParams {
     float lo, inv_w;
 };
 
-__device__ __forceinline__ BinParams bin_params(const float* bounds, int u, int Gb, int g_first,
-                                                int g_count, int M) {
+// Executed by ONE full warp (lane m handles codebook m; M == 32): the hard
+// score bound of a selection unit summed over g in [g_first, g_first+g_count)
+// and the bin scale.  The reduction tree is fixed, so every kernel that calls
+// this gets bit-identical bins.
+__device__ __forceinline__ BinParams bin_params_warp(const float* bounds, int u, int Gb, int g_first,
+                                                     int g_count) {
+    const int lane = threadIdx.x & 31;
     float lo = 0.f, hi = 0.f;
     for (int g = g_first; g < g_first + g_count; ++g) {
-        const float* bd = bounds + ((int64_t)u * Gb + g) * M * kLutParts * 2;
-        float l = 0.f, h = 0.f;
-        for (int m = 0; m < M; ++m) {
-            float mn = bd[(m * kLutParts) * 2], mx = bd[(m * kLutParts) * 2 + 1];
-            for (int q = 1; q < kLutParts; ++q) {
-                mn = fminf(mn, bd[(m * kLutParts + q) * 2]);
-                mx = fmaxf(mx, bd[(m * kLutParts + q) * 2 + 1]);
-            }
-            l = __fadd_rn(l, mn);
-            h = __fadd_rn(h, mx);
+        const float* bd = bounds + (((int64_t)u * Gb + g) * 32 + lane) * kLutParts * 2;
+        float mn = bd[0], mx = bd[1];
+#pragma unroll
+        for (int q = 1; q < kLutParts; ++q) {
+            mn = fminf(mn, bd[2 * q]);
+            mx = fmaxf(mx, bd[2 * q + 1]);
         }
-        lo = __fadd_rn(lo, l);
-        hi = __fadd_rn(hi, h);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            mn = __fadd_rn(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = __fadd_rn(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        lo = __fadd_rn(lo, mn);
+        hi = __fadd_rn(hi, mx);
     }
     // widen by a relative margin so rounding of the scores cannot leave the
     // range (values outside are clamped anyway; this only keeps bins even)
@@ -91,20 +97,25 @@ __device__ __forceinline__ BinParams bin_params(const float* bounds, int u, int 
     return bp;
 }
 
-// Power-of-two fixed-point scale of a unit's tables: S such that every
-// entry |v| < 2^(limit_bits - S).  Derived from the per-(head, m) min/max so
-// every CTA of the unit computes the same S.
-__device__ __forceinline__ int fixed_shift(const float* bounds, int u, int Gb, int M, int limit_bits) {
+// Executed by ONE full warp: power-of-two fixed-point scale of a unit's
+// tables, S such that every entry |v| < 2^(limit_bits - S).
+__device__ __forceinline__ int fixed_shift_warp(const float* bounds, int u, int Gb, int limit_bits) {
+    const int lane = threadIdx.x & 31;
     float mx = 0.f;
-    const float* bd = bounds + (int64_t)u * Gb * M * kLutParts * 2;
-    for (int i = 0; i < Gb * M * kLutParts * 2; ++i) {
-        const float v = fabsf(bd[i]);
-        if (isfinite(v)) mx = fmaxf(mx, v);
+    for (int g = 0; g < Gb; ++g) {
+        const float* bd = bounds + (((int64_t)u * Gb + g) * 32 + lane) * kLutParts * 2;
+#pragma unroll
+        for (int i = 0; i < 2 * kLutParts; ++i) {
+            const float v = fabsf(bd[i]);
+            if (isfinite(v)) mx = fmaxf(mx, v);
+        }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (!(mx > 0.f)) return 0;
     int e;
     frexpf(mx, &e);  // mx < 2^e
-    int S = limit_bits - e;
+    const int S = limit_bits - e;
     return S < -100 ? -100 : (S > 100 ? 100 : S);
 }
 
@@ -186,7 +197,24 @@ __global__ void __launch_bounds__(THREADS, 1) score_kernel(ScoreParams p) {
         bulk_g2s(s_lut, lut_g, S::kLutBytes, s_lut_bar);
     }
     const int Gb = HEADS ? p.G : 1;
-    const int S_fx = fixed_shift(p.bounds, u, Gb, 32, HEADS ? 23 : 25);
+    // per-unit constants, computed by warp 0 and broadcast
+    __shared__ BinParams s_bp[4];
+    __shared__ int s_shift;
+    if (tid < 32) {
+        const int sh = fixed_shift_warp(p.bounds, u, Gb, HEADS ? 23 : 25);
+        if (HEADS && p.sel_per_head) {
+            for (int g = 0; g < p.G; ++g) {
+                const BinParams b_ = bin_params_warp(p.bounds, u, Gb, g, 1);
+                if (tid == 0) s_bp[g] = b_;
+            }
+        } else {
+            const BinParams b_ = bin_params_warp(p.bounds, u, Gb, 0, Gb);
+            if (tid == 0) s_bp[0] = b_;
+        }
+        if (tid == 0) s_shift = sh;
+    }
+    __syncthreads();
+    const int S_fx = s_shift;
     const float to_fx = ldexpf(1.f, S_fx), from_fx = ldexpf(1.f, -S_fx);
     if (!HEADS) {
         // [k][m] (32 floats per k) -> int32 [k][m'] with m' and m'+32 both LUT[m'][k]
@@ -205,13 +233,8 @@ __global__ void __launch_bounds__(THREADS, 1) score_kernel(ScoreParams p) {
 
     // selection-unit bin parameters
     BinParams bp[S::kHistHeads];
-    if (HEADS && p.sel_per_head) {
 #pragma unroll
-        for (int g = 0; g < S::kHistHeads; ++g)
-            bp[g] = bin_params(p.bounds, u, Gb, g < p.G ? g : 0, 1, 32);
-    } else {
-        bp[0] = bin_params(p.bounds, u, Gb, 0, Gb, 32);
-    }
+    for (int g = 0; g < S::kHistHeads; ++g) bp[g] = s_bp[(HEADS && p.sel_per_head && g < p.G) ? g : 0];
 
     // per-lane constants of the rotated gather
     const uint32_t L = (uint32_t)lane >> 2;

@@ -90,11 +90,15 @@ __global__ void __launch_bounds__(THREADS) select_kernel(SelectParams p) {
     constexpr int NWARP = THREADS / 32;
     const int bu = p.per_head ? usel / p.Gb : usel;
     const int g0 = p.per_head ? usel - bu * p.Gb : 0;
-    const BinParams bp = bin_params(p.bounds, bu, p.Gb, g0, p.per_head ? 1 : p.Gb, 32);
-
+    __shared__ BinParams s_bp;
+    if (tid < 32) {
+        const BinParams b_ = bin_params_warp(p.bounds, bu, p.Gb, g0, p.per_head ? 1 : p.Gb);
+        if (tid == 0) s_bp = b_;
+    }
     for (int i = tid; i < kNB; i += THREADS) s_hist[i] = __ldcg(p.hist + (int64_t)usel * kNB + i);
     if (tid == 0) { s_bstar = kNB; s_above = 0; }
     __syncthreads();
+    const BinParams bp = s_bp;
     if (p.k > 0) find_threshold_bin<THREADS>(s_hist, p.k, &s_bstar, &s_above);
     __syncthreads();
     const int bstar = s_bstar;
