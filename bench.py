@@ -52,7 +52,7 @@ def _profile_traffic():
     """Per-launch DRAM traffic of the scorer from the committed ncu summary
     (a line 'traffic_bytes_per_launch: <int>'), scaled by the summary's own
     note when it was captured on a smaller case; None if absent."""
-    p = ROOT / "profiles" / "score_kernel_cfg3.md"
+    p = ROOT / "profiles" / "fused_kernel_cfg3.md"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -246,13 +246,11 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
 
-    def step(events=None):
+    def step(events=None, phases=None):
         for li, L in enumerate(layers):
             a = L["args"]
-            if events is not None:
-                a.stage_events = ctypes.cast(events[li], ctypes.c_void_p)
-            else:
-                a.stage_events = None
+            a.stage_events = ctypes.cast(events[li], ctypes.c_void_p) if events is not None else None
+            a.phase_ns = phases[li].data_ptr() if phases is not None else None
             rc = lib.lp_sparse_decode(ctypes.byref(a), ws.data_ptr(), ws.numel(), sh)
             if rc != 0:
                 _lib.check(rc)
@@ -271,7 +269,8 @@ def run_ours(args):
     ev_sets = {}
     for s in range(0, args.steps, sample_every):
         evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(N_LAYERS)]
-        ev_sets[s] = (evs, [ops.event_array(e) for e in evs])
+        ph = [torch.zeros(8, dtype=torch.int64, device=dev) for _ in range(N_LAYERS)]
+        ev_sets[s] = (evs, [ops.event_array(e) for e in evs], ph)
 
     sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
     sampler.start()
@@ -282,22 +281,35 @@ def run_ours(args):
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
     for s in range(args.steps):
-        step(ev_sets[s][1] if s in ev_sets else None)
+        if s in ev_sets:
+            step(ev_sets[s][1], ev_sets[s][2])
+        else:
+            step()
     t_end.record(stream)
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
     elapsed_ms = t_start.elapsed_time(t_end)
 
+    # per-launch kernel time (events around each layer's launch, sampled
+    # steps) and the fused kernel's phase split (device global timer)
     stage_ms = [0.0] * 4
-    nsamp = 0
-    for s, (evs, _) in ev_sets.items():
+    phase_us = [0.0] * 7
+    nsamp = nph = 0
+    for s, (evs, _, ph) in ev_sets.items():
         for li in range(N_LAYERS):
             e = evs[li]
             for j in range(4):
                 stage_ms[j] += e[j].elapsed_time(e[j + 1])
             nsamp += 1
+            t = ph[li].cpu().tolist()
+            if all(x > 0 for x in t):
+                for j in range(7):
+                    phase_us[j] += (t[j + 1] - t[j]) / 1e3
+                nph += 1
     stage_ms = [x / max(1, nsamp) for x in stage_ms]
+    phase_us = [x / max(1, nph) for x in phase_us]
+    kernel_ms = sum(stage_ms)
 
     ok = all(bool(torch.isfinite(L["out"]).all()) for L in layers)
     errs = ops.device_errors(ws, dev)
@@ -331,11 +343,11 @@ def run_ours(args):
     e2e_ms = e_start.elapsed_time(e_end)
 
     # max over ranks
-    t = torch.tensor([elapsed_ms, e2e_ms] + stage_ms, device=dev, dtype=torch.float64)
+    t = torch.tensor([elapsed_ms, e2e_ms, kernel_ms] + stage_ms, device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_ms = float(t[0]), float(t[1])
-    stage_ms = [float(x) for x in t[2:]]
+    elapsed_ms, e2e_ms, kernel_ms = float(t[0]), float(t[1]), float(t[2])
+    stage_ms = [float(x) for x in t[3:]]
 
     if rank == 0:
         tok_s = world * args.steps / (elapsed_ms / 1e3)
@@ -345,9 +357,9 @@ def run_ours(args):
         score_bytes = HKV * ncand * M                  # uint8 codes streamed per launch
         lut_bytes = HKV * M * K * D * 4                 # fp32 codebooks read per launch
         gather_bytes = HKV * (TOPK + SINK + LOCAL) * D * 2 * 2
-        score_s = stage_ms[1] / 1e3
-        achieved = score_bytes / score_s / 1e9
-        step_bytes = N_LAYERS * (score_bytes + lut_bytes + gather_bytes)
+        launch_bytes = score_bytes + lut_bytes + gather_bytes
+        achieved = launch_bytes / (kernel_ms / 1e3) / 1e9
+        step_bytes = N_LAYERS * launch_bytes
         line = {
             "metric": METRIC, "value": tok_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
@@ -360,21 +372,26 @@ def run_ours(args):
                 "layer_steps_per_s": tok_s * N_LAYERS,
                 "step_algorithmic_bytes": step_bytes,
                 "step_hbm_gbs": step_bytes / (elapsed_ms / args.steps / 1e3) / 1e9,
-                "stage_us": {"lut_build": stage_ms[0] * 1e3, "score": stage_ms[1] * 1e3,
-                             "select": stage_ms[2] * 1e3, "attention": stage_ms[3] * 1e3},
+                "kernel_us_per_layer": kernel_ms * 1e3,
+                "fused_phase_us": {"A_lut": phase_us[0], "barrier_A": phase_us[1], "B_score": phase_us[2],
+                                   "barrier_B": phase_us[3], "C_select": phase_us[4],
+                                   "barrier_C+D_ties": phase_us[5], "E_attention": phase_us[6]},
                 "outputs_finite": ok, "device_error_bits": errs,
             },
-            "roofline": {"bound": "hbm", "kernel": "score_kernel (LUT scorer + histogram)",
+            "roofline": {"bound": "hbm",
+                         "kernel": "sparse_decode_fused_kernel (LUT build + scorer + select + attention)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_launch": score_bytes,
+                         "algorithmic_bytes_per_launch": launch_bytes,
+                         "bytes_split": {"codebooks_fp32": lut_bytes, "codes_u8": score_bytes,
+                                         "kv_rows_bf16": gather_bytes},
                          "traffic": _profile_traffic()},
             "clocks": clocks,
             "e2e": {"value": e2e_tok_s, "unit": UNIT,
                     "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
                     "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
                     "api": "laprune_b200.ops.sparse_decode per layer, q from pinned host, out to pinned host"},
-            "gpu_launches": args.steps * N_LAYERS * 4,
+            "gpu_launches": args.steps * N_LAYERS,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)

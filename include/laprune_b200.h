@@ -108,7 +108,16 @@ typedef struct lp_sparse_decode_args {
      * build and after the LUT build, scoring, selection and attention stages
      * (for live per-kernel timing).  NULL: no events. */
     void** stage_events;
+    /* LP_FLAG_* bits */
+    int32_t flags;
+    int32_t _pad3;
+    /* optional uint64[8] of device global-timer stamps (ns) at the phase
+     * boundaries of the fused single-kernel path (diagnostics).  NULL: none. */
+    uint64_t* phase_ns;
 } lp_sparse_decode_args;
+
+/* flags of lp_sparse_decode_args */
+#define LP_FLAG_NO_FUSED 1 /* use the multi-kernel path even when the fused kernel applies */
 
 /* Workspace bytes needed by lp_sparse_decode for this geometry. */
 size_t lp_sparse_decode_workspace_size(const lp_sparse_decode_args* a);

@@ -15,6 +15,7 @@ LP_OK, LP_ERR_INVALID, LP_ERR_CUDA, LP_ERR_UNSUPPORTED, LP_ERR_WORKSPACE = 0, 1,
 LP_F32, LP_F16, LP_BF16, LP_F64, LP_U8, LP_I8, LP_I64, LP_I32 = range(8)
 LP_SELECT_KV_GROUP, LP_SELECT_QUERY_HEAD = 0, 1
 LP_DEVERR_WAIT_TIMEOUT, LP_DEVERR_TIE_OVERFLOW = 1, 2
+LP_FLAG_NO_FUSED = 1
 
 _c_i32, _c_i64, _c_p, _c_f = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float
 
@@ -35,6 +36,7 @@ class SparseDecodeArgs(ctypes.Structure):
         ("scale", _c_f), ("out_dtype", _c_i32),
         ("out", _c_p), ("out_stride_b", _c_i64), ("out_stride_h", _c_i64),
         ("head_scores", _c_p), ("topk_out", _c_p), ("stage_events", _c_p),
+        ("flags", _c_i32), ("_pad3", _c_i32), ("phase_ns", _c_p),
     ]
 
 

@@ -7,7 +7,7 @@
 #include <stdint.h>
 #include <string>
 
-#include "../../include/laprune_b200.h"
+#include "laprune_b200.h"
 
 namespace lp {
 

@@ -1,0 +1,736 @@
+// fused_step.cuh -- the whole sparse decode step of one layer in ONE
+// persistent cooperative kernel (one CTA per SM).
+//
+// Reference path replaced: laprune/llm/aq_kv.py:633-699 (LUT build +
+// grouped scorer), laprune/llm/modifiers/aq_evaluation.py:185-253 (candidate
+// window, top-k, keep set, GQA gather, SDPA) -- here with per-KV-head
+// selection on GQA-summed scores (the benchmark configs).
+//
+// Why one kernel: at decode sizes every stage after the two HBM streams is a
+// short chain of dependent L2 round trips (histogram -> threshold -> bitmap
+// -> ties -> row list -> gather -> merge).  Separate kernels pay a launch
+// ramp, a tail and a global round trip for every intermediate; here the
+// intermediates stay in shared memory and the stages are separated by
+// three grid barriers.
+//
+// Phases (CTA c owns one selection unit u = (b, kv head) for phases B-E):
+//   A  LUT build: the CTAs split the U*32*256 codeword rows evenly and write
+//      LUT_sum[u][k][m] = q_sum . C_m[k] (fp32) to L2.  The code tiles of
+//      phase B are already streaming into the CTA's TMA ring.        | barrier
+//   B  score: the unit's table is staged as int32 fixed point (exact sums,
+//      order-independent), the per-m bounds are recomputed from the table in
+//      shared memory (identical in every CTA of the unit), the CTA's code
+//      words stream through the ring, scores stay in shared memory (and go
+//      to global for the rare exact slow path), histogram -> global.  | barrier
+//   C  select: bin b* of the k-th score from the unit histogram; bitmap
+//      words of the CTA's own tokens (ballots) and tie-bin tokens appended
+//      to the unit's tie buffer.                                       | barrier
+//   D  ties: every CTA of the unit sorts the (small) tie buffer itself and
+//      overlays the winners on the bitmap in shared memory -- no barrier.
+//      If any unit overflowed the tie buffer, unit leaders run the exact
+//      radix select on the global scores and one more barrier follows.
+//   E  attention: the CTA's slice of kept rows (ascending token order) is
+//      recovered by a prefix popcount of (bitmap | overlay); K/V rows are
+//      gathered once per KV head (16-byte cp.async) and attended by all G
+//      query heads; the last CTA of the unit merges the slice states.
+//
+// Every wait (TMA ring, grid barrier) is bounded; on timeout the CTA records
+// LP_DEVERR_WAIT_TIMEOUT, drains its own copies and exits.
+#pragma once
+#include <cub/block/block_scan.cuh>
+#include "attention.cuh"
+#include "lut_build.cuh"
+#include "score.cuh"
+#include "select.cuh"
+
+namespace lp {
+
+constexpr int kFThreads = 512;
+constexpr int kFStages = 6;
+constexpr int kFTile = kFThreads * 32;           // 16 KB of code rows per stage
+constexpr int kFScoreCap = 11264;                // tokens per CTA kept in smem
+constexpr int kFMaxWords = 8192;                 // bitmap words per unit in smem overlay
+constexpr int kFMaxRows = 128;                   // kept rows per CTA in phase E
+
+struct FusedParams {
+    const void* q;
+    int64_t q_stride_b, q_stride_h;
+    const float* cb;
+    int cb_per_kv_head;
+    const uint8_t* codes;
+    int64_t codes_stride_b, codes_stride_h;
+    const void* keys;
+    const void* vals;
+    int64_t k_stride_b, k_stride_h, k_stride_t;
+    int64_t v_stride_b, v_stride_h, v_stride_t;
+    int Hkv, G, U;
+    int c0, c1, k;
+    int n_sink, local_start, n_local, n_rows, T_total;
+    float scale_log2;
+    void* out;
+    int64_t out_stride_b, out_stride_h;
+    int32_t* topk_out;
+    // workspace
+    float* lut;          // [U][256][32]
+    float* sel_scores;   // [U][sel_stride]
+    int64_t sel_stride;
+    uint32_t* hist;      // [U][kNB]           (zeroed in phase A)
+    uint32_t* bitmap;    // [U][bm_stride]
+    int64_t bm_stride;
+    float2* tie_buf;     // [U][kTieCap]
+    uint32_t* tie_count; // [U]                 (zeroed in phase A)
+    uint32_t* done_att;  // [U]                 (zeroed in phase A)
+    float* part;         // [U][max_split][G][2+128]
+    int max_split;
+    uint32_t* bar;       // grid barrier word (self-resetting)
+    uint32_t* err;
+    unsigned long long* phase_ns;  // optional [8] globaltimer stamps (CTA 0)
+};
+
+struct FusedSmem {
+    static constexpr int kLut = 256 * 64 * 4;          // 64 KB (phase B table; reused)
+    static constexpr int kRing = kFStages * kFTile;    // 96 KB (phase B ring; reused in E)
+    static constexpr int kHist = kNB * 4;              // 8 KB
+    static constexpr int kScores = kFScoreCap * 4;     // 48 KB
+    static constexpr int kBars = kFStages * 8;
+    static constexpr int kTotal = kLut + kRing + kHist + kScores + kBars + 128;
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid-wide barrier for a cooperative launch.  The barrier word flips its
+// top bit once per barrier (CTA 0 adds 2^31 - (n-1), the others 1), so it
+// needs no reset between barriers or calls.  Bounded: returns false on
+// timeout (after recording the error bit).
+__device__ __forceinline__ bool grid_barrier(uint32_t* bar, uint32_t* err) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t n = gridDim.x;
+        const uint32_t inc = blockIdx.x == 0 ? (0x80000000u - (n - 1u)) : 1u;
+        __threadfence();
+        const uint32_t old = atomicAdd(bar, inc);
+        int ok = 1;
+        const long long t0 = clock64();
+        while (((ld_acquire_u32(bar) ^ old) & 0x80000000u) == 0u) {
+            if (clock64() - t0 > kWaitCycles) {
+                atomicOr(err, LP_DEVERR_WAIT_TIMEOUT);
+                ok = 0;
+                break;
+            }
+        }
+        __threadfence();
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+// CTA -> (unit, index within unit, CTAs of the unit)
+__device__ __forceinline__ void fused_cta_unit(int cta, int nctas, int U, int* u, int* j, int* n) {
+    const int base = nctas / U, extra = nctas % U;
+    if (cta < extra * (base + 1)) {
+        *u = cta / (base + 1); *j = cta - *u * (base + 1); *n = base + 1;
+    } else {
+        const int i = cta - extra * (base + 1);
+        *u = extra + i / base; *j = i - (*u - extra) * base; *n = base;
+    }
+}
+
+template <typename QT, typename KT, typename OT>
+__global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(FusedParams p) {
+    using S = FusedSmem;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    unsigned char* s_lut = smem;
+    unsigned char* s_ring = smem + S::kLut;
+    uint32_t* s_hist = reinterpret_cast<uint32_t*>(s_ring + S::kRing);
+    float* s_scores = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(s_hist) + S::kHist);
+    uint64_t* s_bar = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(s_scores) + S::kScores);
+
+    __shared__ float s_qsum[2][128];
+    __shared__ float s_mmin[kFThreads / 32][32], s_mmax[kFThreads / 32][32];
+    __shared__ BinParams s_bp;
+    __shared__ int s_shift, s_bstar, s_above, s_flag;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = kFThreads / 32;
+    const bool stamp = p.phase_ns != nullptr && blockIdx.x == 0 && tid == 0;
+    if (stamp) p.phase_ns[0] = global_ns();
+
+    int u, cj, cn;
+    fused_cta_unit(blockIdx.x, gridDim.x, p.U, &u, &cj, &cn);
+    const int b = u / p.Hkv, hkv = u - b * p.Hkv;
+    // the CTA's tokens: a run of whole bitmap words of the candidate window
+    const int wlo = p.c0 >> 5, whi = (p.c1 + 31) >> 5;
+    const int nwu = whi - wlo;
+    const int w_begin = wlo + (int)((int64_t)nwu * cj / cn);
+    const int w_end = wlo + (int)((int64_t)nwu * (cj + 1) / cn);
+    const int t_begin = max(p.c0, w_begin * 32);
+    const int t_end = min(p.c1, w_end * 32);
+    const int ntok = max(0, t_end - t_begin);
+    const int ntiles = (ntok + kFThreads - 1) / kFThreads;
+    const bool keep_smem = ntok <= kFScoreCap;
+    const uint8_t* src = p.codes + (int64_t)b * p.codes_stride_b + (int64_t)hkv * p.codes_stride_h;
+
+    if (tid == 0) {
+        for (int s = 0; s < kFStages; ++s) mbar_init(&s_bar[s], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    // ---- start streaming the phase-B code tiles right away ----
+    uint64_t policy = 0;
+    const int npre = ntiles < kFStages ? ntiles : kFStages;
+    if (tid == 0) {
+        policy = policy_evict_first();
+        for (int i = 0; i < npre; ++i) {
+            const int t0 = t_begin + i * kFThreads;
+            const int nn = min(kFThreads, t_end - t0);
+            mbar_arrive_expect_tx(&s_bar[i], (uint32_t)nn * 32u);
+            bulk_g2s_stream(s_ring + i * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[i], policy);
+        }
+    }
+    int issued = npre;
+    auto drain = [&](int from) {
+        for (int j = from; j < issued; ++j) mbar_wait(&s_bar[j % kFStages], (uint32_t)(j / kFStages) & 1u, nullptr);
+    };
+
+    // ================= phase A: LUT build =================
+    {
+        // zero the per-call state used after barrier A
+        const int64_t nz = (int64_t)p.U * kNB;
+        for (int64_t i = (int64_t)blockIdx.x * kFThreads + tid; i < nz; i += (int64_t)gridDim.x * kFThreads)
+            p.hist[i] = 0u;
+        for (int i = blockIdx.x * kFThreads + tid; i < p.U; i += gridDim.x * kFThreads) {
+            p.tie_count[i] = 0u;
+            p.done_att[i] = 0u;
+        }
+        const int64_t total = (int64_t)p.U * 32 * 256;       // codeword rows
+        // rows per CTA rounded to a multiple of 8 so a warp batch of 8 rows
+        // never straddles a (unit, m) block of 256 rows
+        const int64_t per = ((total + gridDim.x - 1) / gridDim.x + 7) & ~(int64_t)7;
+        const int64_t f_begin = (int64_t)blockIdx.x * per;
+        const int64_t f_end = min(total, f_begin + per);
+        // q_sum of the (at most two) units this CTA touches
+        const int ua = (int)(f_begin / 8192);
+        for (int i = tid; i < 2 * 128; i += kFThreads) {
+            const int slot = i >> 7, d = i & 127;
+            const int uu = ua + slot;
+            float acc = 0.f;
+            if (uu < p.U) {
+                const int bb = uu / p.Hkv, hh = uu - bb * p.Hkv;
+                const QT* qb = reinterpret_cast<const QT*>(p.q) + (int64_t)bb * p.q_stride_b;
+                for (int g = 0; g < p.G; ++g) acc += to_f32(qb[(int64_t)(hh * p.G + g) * p.q_stride_h + d]);
+            }
+            s_qsum[slot][d] = acc;
+        }
+        __syncthreads();
+        for (int64_t f0 = f_begin + warp * 8; f0 < f_end; f0 += NW * 8) {
+            const int uu = (int)(f0 / 8192);
+            const int m = (int)((f0 >> 8) & 31);
+            const int k0 = (int)(f0 & 255);
+            const int hh = uu % p.Hkv;
+            const float* rows = p.cb + (int64_t)(p.cb_per_kv_head ? hh : 0) * (32 * 256 * 128) +
+                                ((int64_t)m * 256 + k0) * 128 + lane * 4;
+            float4 cv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                cv[j] = (f0 + j < f_end) ? __ldg(reinterpret_cast<const float4*>(rows + j * 128))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 qv = *reinterpret_cast<const float4*>(&s_qsum[uu - ua][lane * 4]);
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float a = qv.x * cv[j].x;
+                a = fmaf(qv.y, cv[j].y, a);
+                a = fmaf(qv.z, cv[j].z, a);
+                a = fmaf(qv.w, cv[j].w, a);
+                v[j] = a;
+            }
+            const float tot = transpose_reduce8(v, lane);
+            const int kk = k0 + ((lane >> 2) & 7);
+            if ((lane & 3) == 0 && f0 + ((lane >> 2) & 7) < f_end)
+                p.lut[((int64_t)uu * 256 + kk) * 32 + m] = tot;
+        }
+    }
+    if (stamp) p.phase_ns[1] = global_ns();
+    if (!grid_barrier(p.bar, p.err)) { drain(0); return; }
+    if (stamp) p.phase_ns[2] = global_ns();
+
+    // ================= phase B: score =================
+    BinParams bp;
+    float from_fx;
+    {
+        // stage the unit table: fp32 -> per-m bounds -> int32 fixed point (dup layout)
+        const float4* g4 = reinterpret_cast<const float4*>(p.lut + (int64_t)u * 256 * 32);
+        float4 v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = __ldcg(g4 + tid + j * kFThreads);
+        // thread's m group is (tid & 7); reduce min/max per m over k
+        float mn[4], mx[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float a0 = (&v[0].x)[e], a1 = (&v[1].x)[e], a2 = (&v[2].x)[e], a3 = (&v[3].x)[e];
+            mn[e] = fminf(fminf(a0, a1), fminf(a2, a3));
+            mx[e] = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+        }
+#pragma unroll
+        for (int o = 8; o <= 16; o <<= 1)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                mn[e] = fminf(mn[e], __shfl_xor_sync(0xffffffffu, mn[e], o));
+                mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], o));
+            }
+        if (lane < 8) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                s_mmin[warp][lane * 4 + e] = mn[e];
+                s_mmax[warp][lane * 4 + e] = mx[e];
+            }
+        }
+        __syncthreads();
+        if (tid < 32) {
+            // lane = m: reduce over warps, then sum over m with a fixed tree
+            float a = s_mmin[0][lane], c = s_mmax[0][lane];
+            for (int w = 1; w < NW; ++w) { a = fminf(a, s_mmin[w][lane]); c = fmaxf(c, s_mmax[w][lane]); }
+            float amax = fmaxf(fabsf(a), fabsf(c));
+            float lo = a, hi = c;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                lo = __fadd_rn(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+                hi = __fadd_rn(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            }
+            if (lane == 0) {
+                const float span = __fsub_rn(hi, lo);
+                const float pad = __fmul_rn(fmaxf(fabsf(lo), fabsf(hi)), 1e-5f);
+                BinParams q_;
+                q_.lo = __fsub_rn(lo, pad);
+                const float h2 = __fadd_rn(hi, pad);
+                q_.inv_w = (span > 0.f) ? __fdiv_rn((float)kNB, __fsub_rn(h2, q_.lo)) : 0.f;
+                s_bp = q_;
+                int sh = 0;
+                if (amax > 0.f && isfinite(amax)) {
+                    int e;
+                    frexpf(amax, &e);
+                    sh = max(-100, min(100, 25 - e));
+                }
+                s_shift = sh;
+            }
+        }
+        for (int i = tid; i < kNB; i += kFThreads) s_hist[i] = 0u;
+        __syncthreads();
+        bp = s_bp;
+        const float to_fx = ldexpf(1.f, s_shift);
+        from_fx = ldexpf(1.f, -s_shift);
+        int4* d4 = reinterpret_cast<int4*>(s_lut);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int f = tid + j * kFThreads;
+            const int4 iv = make_int4(to_fixed(v[j].x, to_fx), to_fixed(v[j].y, to_fx), to_fixed(v[j].z, to_fx),
+                                      to_fixed(v[j].w, to_fx));
+            const int kk = f >> 3, m4 = f & 7;
+            d4[kk * 16 + m4] = iv;
+            d4[kk * 16 + 8 + m4] = iv;
+        }
+        __syncthreads();
+
+        const uint32_t L = (uint32_t)lane >> 2;
+        uint32_t off[4], sel[4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const uint32_t bs = (uint32_t)(s + lane) & 3u;
+            off[s] = 16u * L + 4u * bs;
+            sel[s] = 0x5504u | (bs << 4);
+        }
+        float* gsc = p.sel_scores + (int64_t)u * p.sel_stride;
+        for (int i = 0; i < ntiles; ++i) {
+            const int slot = i % kFStages;
+            const bool ok = mbar_wait(&s_bar[slot], (uint32_t)(i / kFStages) & 1u, p.err);
+            if (__syncthreads_or(!ok)) { drain(i); return; }
+            const int lt = i * kFThreads + tid;
+            const int t = t_begin + lt;
+            if (t < t_end) {
+                const uint32_t* row = reinterpret_cast<const uint32_t*>(s_ring + slot * kFTile + tid * 32);
+                int iacc = 0;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) {
+                    const uint32_t cw = row[(w + L) & 7u];
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        const uint32_t a = __byte_perm(cw, off[s], sel[s]);
+                        iacc += *reinterpret_cast<const int*>(s_lut + a + 16 * w);
+                    }
+                }
+                const float sc = __fmul_rn(__int2float_rn(iacc), from_fx);
+                if (keep_smem) s_scores[lt] = sc;
+                gsc[t] = sc;
+                atomicAdd(&s_hist[score_bin(sc, bp.lo, bp.inv_w, kNB)], 1u);
+            }
+            __syncthreads();
+            if (tid == 0 && i + kFStages < ntiles) {
+                const int j = i + kFStages;
+                const int t0 = t_begin + j * kFThreads;
+                const int nn = min(kFThreads, t_end - t0);
+                mbar_arrive_expect_tx(&s_bar[slot], (uint32_t)nn * 32u);
+                bulk_g2s_stream(s_ring + slot * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[slot],
+                                policy);
+                ++issued;
+            }
+        }
+        for (int i = tid; i < kNB; i += kFThreads) {
+            const uint32_t c = s_hist[i];
+            if (c) atomicAdd(&p.hist[(int64_t)u * kNB + i], c);
+        }
+    }
+    if (stamp) p.phase_ns[3] = global_ns();
+    if (!grid_barrier(p.bar, p.err)) return;
+    if (stamp) p.phase_ns[4] = global_ns();
+
+    // ================= phase C: select (threshold bin, bitmap, ties) =================
+    uint32_t* bm = p.bitmap + (int64_t)u * p.bm_stride;
+    {
+        for (int i = tid; i < kNB; i += kFThreads) s_hist[i] = __ldcg(p.hist + (int64_t)u * kNB + i);
+        if (tid == 0) { s_bstar = kNB; s_above = 0; }
+        __syncthreads();
+        if (p.k > 0) find_threshold_bin<kFThreads>(s_hist, p.k, &s_bstar, &s_above);
+        __syncthreads();
+        const int bstar = s_bstar;
+        const float* gsc = p.sel_scores + (int64_t)u * p.sel_stride;
+        for (int w = w_begin + warp; w < w_end; w += NW) {
+            const int t = w * 32 + lane;
+            const bool valid = t >= p.c0 && t < p.c1;
+            float s = 0.f;
+            if (valid) s = keep_smem ? s_scores[t - t_begin] : __ldcg(gsc + t);
+            const int bin = score_bin(s, bp.lo, bp.inv_w, kNB);
+            const bool sel_ = valid && bin > bstar;
+            const bool tie = valid && bin == bstar;
+            const uint32_t bits = __ballot_sync(0xffffffffu, sel_);
+            if (lane == 0) bm[w] = bits;
+            const uint32_t tmask = __ballot_sync(0xffffffffu, tie);
+            if (tmask) {
+                uint32_t base = 0;
+                if (lane == 0) base = atomicAdd(&p.tie_count[u], (uint32_t)__popc(tmask));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                if (tie) {
+                    const uint32_t pos = base + __popc(tmask & ((1u << lane) - 1u));
+                    if (pos < (uint32_t)kTieCap)
+                        p.tie_buf[(int64_t)u * kTieCap + pos] = make_float2(s, __int_as_float(t));
+                }
+            }
+        }
+    }
+    if (stamp) p.phase_ns[5] = global_ns();
+    if (!grid_barrier(p.bar, p.err)) return;
+
+    // ================= phase D: ties (redundant per CTA, no barrier) =================
+    // overlay of the tie winners on the unit bitmap, in shared memory
+    uint32_t* s_over = reinterpret_cast<uint32_t*>(s_ring);          // [nwu] words (<= kFMaxWords)
+    float* s_tk = reinterpret_cast<float*>(s_lut);                  // tie sort keys  [kTieCap]
+    int* s_ti = reinterpret_cast<int*>(s_lut + kTieCap * 4);        // tie sort index [kTieCap]
+    {
+        const int need = p.k - s_above;
+        if (tid == 0) {
+            int any = 0;
+            for (int uu = 0; uu < p.U; ++uu) any |= __ldcg(p.tie_count + uu) > (uint32_t)kTieCap;
+            s_flag = any;
+        }
+        for (int i = tid; i < nwu; i += kFThreads) s_over[i] = 0u;
+        __syncthreads();
+        const bool overflow_any = s_flag != 0;
+        const int ntie = (int)__ldcg(p.tie_count + u);
+        if (ntie <= kTieCap && need > 0) {
+            int n = 1;
+            while (n < ntie) n <<= 1;
+            for (int i = tid; i < n; i += kFThreads) {
+                if (i < ntie) {
+                    const float2 e = __ldcg(p.tie_buf + (int64_t)u * kTieCap + i);
+                    s_tk[i] = e.x;
+                    s_ti[i] = __float_as_int(e.y);
+                } else {
+                    s_tk[i] = -INFINITY;
+                    s_ti[i] = 0x7fffffff;
+                }
+            }
+            for (int size = 2; size <= n; size <<= 1) {
+                for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                    __syncthreads();
+                    for (int i = tid; i < (n >> 1); i += kFThreads) {
+                        const int a = 2 * i - (i & (stride - 1));
+                        const int c = a + stride;
+                        const bool up = (a & size) == 0;
+                        const float ka = s_tk[a], kc = s_tk[c];
+                        const int ia = s_ti[a], ic = s_ti[c];
+                        if (sel_before(kc, ic, ka, ia) == up) {
+                            s_tk[a] = kc; s_tk[c] = ka;
+                            s_ti[a] = ic; s_ti[c] = ia;
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            for (int i = tid; i < need; i += kFThreads) {
+                const int t = s_ti[i];
+                atomicOr(&s_over[(t >> 5) - wlo], 1u << (t & 31));
+            }
+        }
+        if (overflow_any) {
+            // exact slow path by the unit leader on the global scores, then a
+            // grid-uniform extra barrier (every CTA saw the same flag)
+            if (cj == 0 && ntie > kTieCap && need > 0) {
+                if (tid == 0) atomicOr(p.err, LP_DEVERR_TIE_OVERFLOW);
+                uint32_t* h256 = reinterpret_cast<uint32_t*>(s_lut);
+                __shared__ uint32_t s_prefix, s_mask;
+                __shared__ int s_remaining;
+                const float* gsc = p.sel_scores + (int64_t)u * p.sel_stride;
+                if (tid == 0) { s_prefix = 0; s_mask = 0; s_remaining = need; }
+                for (int shift = 24; shift >= 0; shift -= 8) {
+                    for (int i = tid; i < 256; i += kFThreads) h256[i] = 0;
+                    __syncthreads();
+                    const uint32_t prefix = s_prefix, mask = s_mask;
+                    for (int t = p.c0 + tid; t < p.c1; t += kFThreads) {
+                        const float s = __ldcg(gsc + t);
+                        if (score_bin(s, bp.lo, bp.inv_w, kNB) != s_bstar) continue;
+                        const uint32_t key = ordered_key(s);
+                        if ((key & mask) != prefix) continue;
+                        atomicAdd(&h256[(key >> shift) & 255u], 1u);
+                    }
+                    __syncthreads();
+                    if (tid == 0) {
+                        const int rem = s_remaining;
+                        int acc = 0;
+                        for (int d = 255; d >= 0; --d) {
+                            const int c = (int)h256[d];
+                            if (acc + c >= rem) {
+                                s_prefix = prefix | ((uint32_t)d << shift);
+                                s_mask = mask | (255u << shift);
+                                s_remaining = rem - acc;
+                                break;
+                            }
+                            acc += c;
+                        }
+                    }
+                    __syncthreads();
+                }
+                const uint32_t kstar = s_prefix;
+                const int take_eq = s_remaining;
+                using Scan = cub::BlockScan<int, kFThreads>;
+                __shared__ typename Scan::TempStorage tmp;
+                __shared__ int s_eq_base;
+                if (tid == 0) s_eq_base = 0;
+                __syncthreads();
+                for (int base = p.c0; base < p.c1; base += kFThreads) {
+                    const int t = base + tid;
+                    int gt = 0, eq = 0;
+                    if (t < p.c1) {
+                        const float s = __ldcg(gsc + t);
+                        if (score_bin(s, bp.lo, bp.inv_w, kNB) == s_bstar) {
+                            const uint32_t key = ordered_key(s);
+                            gt = key > kstar;
+                            eq = key == kstar;
+                        }
+                    }
+                    int rank, total;
+                    Scan(tmp).ExclusiveSum(eq, rank, total);
+                    if (gt || (eq && s_eq_base + rank < take_eq)) atomicOr(&bm[t >> 5], 1u << (t & 31));
+                    __syncthreads();
+                    if (tid == 0) s_eq_base += total;
+                    __syncthreads();
+                }
+            }
+            if (!grid_barrier(p.bar, p.err)) return;
+        }
+    }
+    if (stamp) p.phase_ns[6] = global_ns();
+
+    // ================= phase E: attention over the CTA's slice of kept rows =================
+    {
+        constexpr int D = 128;
+        KT* s_k = reinterpret_cast<KT*>(s_ring + kFMaxWords * 4);                 // [rows][128]
+        KT* s_v = s_k + kFMaxRows * D;                                           // [rows][128]
+        int* s_rows = reinterpret_cast<int*>(s_hist);                           // [kFMaxRows]
+        float* s_q = reinterpret_cast<float*>(s_lut + 2 * kTieCap * 4);          // [G][128]
+        float* s_p = s_q + 8 * D;                                                // [G][kFMaxRows]
+        float* s_ml = s_p + 8 * kFMaxRows;                                       // [G][2]
+        float* s_w = reinterpret_cast<float*>(s_lut + 48 * 1024);                // [G][cn] merge weights
+        __shared__ int s_last;
+        using Scan = cub::BlockScan<int, kFThreads>;
+        __shared__ typename Scan::TempStorage scan_tmp;
+
+        const int rows_per = (p.n_rows + cn - 1) / cn;
+        const int r0 = cj * rows_per;
+        const int r1 = min(p.n_rows, r0 + rows_per);
+        const int nr = max(0, r1 - r0);
+        for (int i = tid; i < kFMaxRows; i += kFThreads) s_rows[i] = 0;
+        __syncthreads();
+        for (int r = r0 + tid; r < min(r1, p.n_sink); r += kFThreads) s_rows[r - r0] = r;
+        for (int r = max(r0, p.n_sink + p.k) + tid; r < r1; r += kFThreads)
+            s_rows[r - r0] = p.local_start + (r - p.n_sink - p.k);
+        const int j0 = max(r0, p.n_sink) - p.n_sink;
+        const int j1 = min(r1, p.n_sink + p.k) - p.n_sink;
+        if (j0 < j1) {
+            constexpr int WB = 16;
+            const int per = (nwu + kFThreads - 1) / kFThreads;
+            const int wa = tid * per;  // relative word index
+            int base_round = 0;
+            for (int r = 0; r < per; r += WB) {
+                uint32_t words[WB];
+                int cnt = 0;
+#pragma unroll
+                for (int j = 0; j < WB; ++j) {
+                    const int w = wa + r + j;
+                    words[j] = (r + j < per && w < nwu) ? (__ldcg(bm + wlo + w) | s_over[w]) : 0u;
+                    cnt += __popc(words[j]);
+                }
+                int before, total;
+                Scan(scan_tmp).ExclusiveSum(cnt, before, total);
+                __syncthreads();
+                int rank = base_round + before;
+                if (rank < j1 && rank + cnt > j0) {
+#pragma unroll
+                    for (int j = 0; j < WB; ++j) {
+                        uint32_t bits = words[j];
+                        const int c = __popc(bits);
+                        if (rank + c <= j0 || rank >= j1) { rank += c; continue; }
+                        while (bits) {
+                            const int bit = __ffs(bits) - 1;
+                            bits &= bits - 1;
+                            if (rank >= j0 && rank < j1) {
+                                const int tok = (wlo + wa + r + j) * 32 + bit;
+                                s_rows[p.n_sink + rank - r0] = tok;
+                                if (p.topk_out) p.topk_out[(int64_t)u * p.k + rank] = tok;
+                            }
+                            ++rank;
+                        }
+                    }
+                }
+                base_round += total;
+            }
+        }
+        const QT* qb = reinterpret_cast<const QT*>(p.q) + (int64_t)b * p.q_stride_b;
+        for (int i = tid; i < p.G * D; i += kFThreads) {
+            const int g = i / D, d = i - g * D;
+            s_q[g * D + d] = to_f32(qb[(int64_t)(hkv * p.G + g) * p.q_stride_h + d]);
+        }
+        __syncthreads();
+        // gather
+        const KT* kb = reinterpret_cast<const KT*>(p.keys) + (int64_t)b * p.k_stride_b + (int64_t)hkv * p.k_stride_h;
+        const KT* vb = reinterpret_cast<const KT*>(p.vals) + (int64_t)b * p.v_stride_b + (int64_t)hkv * p.v_stride_h;
+        constexpr int CH = D * (int)sizeof(KT) / 16;
+        constexpr int EPC = 16 / (int)sizeof(KT);
+        for (int c = tid; c < nr * CH; c += kFThreads) {
+            const int r = c / CH, part = c - r * CH;
+            const int64_t t = min(max(s_rows[r], 0), p.T_total - 1);
+            cp_async16(s_k + r * D + part * EPC, kb + t * p.k_stride_t + part * EPC);
+            cp_async16(s_v + r * D + part * EPC, vb + t * p.v_stride_t + part * EPC);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        // logits (log2 domain)
+        for (int r = warp; r < nr; r += NW) {
+            const float4 kv = Vec4<KT>::load(s_k + r * D + lane * 4);
+            for (int g = 0; g < p.G; ++g) {
+                const float4 qv = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
+                float a = qv.x * kv.x;
+                a = fmaf(qv.y, kv.y, a);
+                a = fmaf(qv.z, kv.z, a);
+                a = fmaf(qv.w, kv.w, a);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                if (lane == g) s_p[g * kFMaxRows + r] = a * p.scale_log2;
+            }
+        }
+        __syncthreads();
+        for (int g = warp; g < p.G; g += NW) {
+            float mx = -INFINITY;
+            for (int r = lane; r < nr; r += 32) mx = fmaxf(mx, s_p[g * kFMaxRows + r]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            float sum = 0.f;
+            for (int r = lane; r < nr; r += 32) {
+                const float e = exp2f(s_p[g * kFMaxRows + r] - mx);
+                s_p[g * kFMaxRows + r] = e;
+                sum += e;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) { s_ml[2 * g] = mx; s_ml[2 * g + 1] = sum; }
+        }
+        __syncthreads();
+        float* part = p.part + ((int64_t)u * p.max_split + cj) * p.G * (2 + D);
+        for (int o = tid; o < p.G * (D / 2); o += kFThreads) {
+            const int g = o / (D / 2), dp = o - g * (D / 2);
+            float ax = 0.f, ay = 0.f;
+            for (int r = 0; r < nr; ++r) {
+                const float2 vv = Vec4<KT>::load2(s_v + r * D + 2 * dp);
+                const float w = s_p[g * kFMaxRows + r];
+                ax = fmaf(w, vv.x, ax);
+                ay = fmaf(w, vv.y, ay);
+            }
+            float* pg = part + g * (2 + D);
+            pg[2 + 2 * dp] = ax;
+            pg[3 + 2 * dp] = ay;
+            if (dp == 0) { pg[0] = nr > 0 ? s_ml[2 * g] : -INFINITY; pg[1] = nr > 0 ? s_ml[2 * g + 1] : 0.f; }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            const uint32_t ticket = atomicAdd(&p.done_att[u], 1u);
+            s_last = (ticket == (uint32_t)cn - 1u);
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        // merge the cn slice states of the unit
+        const float* pu = p.part + (int64_t)u * p.max_split * p.G * (2 + D);
+        const int64_t sstride = (int64_t)p.G * (2 + D);
+        for (int g = warp; g < p.G; g += NW) {
+            float M = -INFINITY;
+            for (int s = lane; s < cn; s += 32) M = fmaxf(M, __ldcg(pu + s * sstride + g * (2 + D)));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            float Lsum = 0.f;
+            for (int s = lane; s < cn; s += 32) {
+                const float* ps = pu + s * sstride + g * (2 + D);
+                const float f = exp2f(__ldcg(ps) - M);
+                s_w[g * cn + s] = f;
+                Lsum = fmaf(__ldcg(ps + 1), f, Lsum);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
+            __syncwarp();
+            const float invL = 1.f / Lsum;
+            for (int s = lane; s < cn; s += 32) s_w[g * cn + s] *= invL;
+        }
+        __syncthreads();
+        OT* ob = reinterpret_cast<OT*>(p.out) + (int64_t)b * p.out_stride_b;
+        for (int o = tid; o < p.G * D; o += kFThreads) {
+            const int g = o / D, d = o - g * D;
+            const float* pg = pu + g * (2 + D) + 2 + d;
+            float acc = 0.f;
+            int s = 0;
+            for (; s + 8 <= cn; s += 8) {
+                float vv[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) vv[j] = __ldcg(pg + (s + j) * sstride);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc = fmaf(vv[j], s_w[g * cn + s + j], acc);
+            }
+            for (; s < cn; ++s) acc = fmaf(__ldcg(pg + s * sstride), s_w[g * cn + s], acc);
+            ob[(int64_t)(hkv * p.G + g) * p.out_stride_h + d] = from_f32<OT>(acc);
+        }
+        if (stamp) p.phase_ns[7] = global_ns();
+    }
+}
+
+}  // namespace lp

@@ -4,6 +4,7 @@
 #include <string>
 
 #include "attention.cuh"
+#include "fused_step.cuh"
 #include "lut_build.cuh"
 #include "score.cuh"
 #include "select.cuh"
@@ -64,6 +65,8 @@ struct Plan {
     int sel_ctas_per_unit, sel_words_per_cta;
     int rows_per, nsplit;
     int64_t bm_words;
+    bool fused;       // single cooperative kernel path
+    int fused_ctas, fused_max_split;
     // workspace regions
     uint32_t* err;
     float* lut;
@@ -79,6 +82,7 @@ struct Plan {
     uint32_t* tie_count;
     uint32_t* done_sel;
     uint32_t* done_att;
+    uint32_t* bar;
     size_t bytes;
 };
 
@@ -149,6 +153,19 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
 
     p.bm_words = (a->T_codes + 31) / 32 + 1;
 
+    // the fused single-kernel path (cooperative, one CTA per SM)
+    p.fused_ctas = sms;
+    {
+        const int cn_min = p.U > 0 ? p.fused_ctas / p.U : 0;
+        const int nwu = p.ncand > 0 ? ((p.c1 + 31) >> 5) - (p.c0 >> 5) : 0;
+        const int ntok_max = cn_min > 0 ? (nwu + cn_min - 1) / cn_min * 32 : 0;
+        p.fused = !(a->flags & LP_FLAG_NO_FUSED) && !p.per_head && !p.heads && a->out != nullptr &&
+                  a->D == 128 && a->G <= 8 && p.U <= p.fused_ctas && p.ncand > 0 && a->topk > 0 &&
+                  nwu <= kFMaxWords && cn_min >= 1 &&
+                  (p.n_rows + cn_min - 1) / cn_min <= kFMaxRows && ntok_max <= (1 << 30);
+        p.fused_max_split = cn_min + 1;
+    }
+
     Carver c(ws);
     p.err = c.take<uint32_t>(64);
     p.lut = c.take<float>((size_t)p.U * 256 * 32 * (p.heads ? 4 : 1));
@@ -157,7 +174,9 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     p.bitmap = c.take<uint32_t>((size_t)p.Usel * p.bm_words);
     p.tie_buf = c.take<float2>((size_t)p.Usel * kTieCap);
     p.info = c.take<int4>((size_t)p.Usel);
-    p.part = c.take<float>((size_t)p.Uatt * p.nsplit * p.HG * (2 + 128));
+    p.part = c.take<float>((size_t)std::max((size_t)p.Uatt * p.nsplit * p.HG, (size_t)p.U * p.fused_max_split * a->G) *
+                           (2 + 128));
+    p.bar = c.take<uint32_t>(64);
     p.zero_words = (int64_t)p.Usel * kNB + p.Usel + p.Usel + p.Uatt;
     p.zero = c.take<uint32_t>((size_t)p.zero_words);
     p.hist = p.zero;
@@ -254,6 +273,94 @@ static int launch_attn_kv(const lp_sparse_decode_args* a, const Plan& p, cudaStr
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
+template <typename QT, typename KT, typename OT>
+static int launch_fused(const lp_sparse_decode_args* a, const Plan& p, cudaStream_t st, int dev) {
+    FusedParams fp{};
+    fp.q = a->q;
+    fp.q_stride_b = a->q_stride_b;
+    fp.q_stride_h = a->q_stride_h;
+    fp.cb = a->codebooks;
+    fp.cb_per_kv_head = a->cb_per_kv_head;
+    fp.codes = a->codes;
+    fp.codes_stride_b = a->codes_stride_b;
+    fp.codes_stride_h = a->codes_stride_h;
+    fp.keys = a->keys;
+    fp.vals = a->vals;
+    fp.k_stride_b = a->k_stride_b;
+    fp.k_stride_h = a->k_stride_h;
+    fp.k_stride_t = a->k_stride_t;
+    fp.v_stride_b = a->v_stride_b;
+    fp.v_stride_h = a->v_stride_h;
+    fp.v_stride_t = a->v_stride_t;
+    fp.Hkv = a->Hkv;
+    fp.G = a->G;
+    fp.U = p.U;
+    fp.c0 = p.c0;
+    fp.c1 = p.c1;
+    fp.k = a->topk;
+    fp.n_sink = p.n_sink;
+    fp.local_start = p.local_start;
+    fp.n_local = p.n_local;
+    fp.n_rows = p.n_rows;
+    fp.T_total = a->T_total;
+    const float scale = a->scale > 0.f ? a->scale : 1.0f / sqrtf((float)a->D);
+    fp.scale_log2 = scale * 1.4426950408889634f;
+    fp.out = a->out;
+    fp.out_stride_b = a->out_stride_b;
+    fp.out_stride_h = a->out_stride_h;
+    fp.topk_out = a->topk_out;
+    fp.lut = p.lut;
+    fp.sel_scores = p.sel_scores;
+    fp.sel_stride = std::max(1, a->T_codes);
+    fp.hist = p.hist;
+    fp.bitmap = p.bitmap;
+    fp.bm_stride = p.bm_words;
+    fp.tie_buf = p.tie_buf;
+    fp.tie_count = p.tie_count;
+    fp.done_att = p.done_att;
+    fp.part = p.part;
+    fp.max_split = p.fused_max_split;
+    fp.bar = p.bar;
+    fp.err = p.err;
+    fp.phase_ns = reinterpret_cast<unsigned long long*>(a->phase_ns);
+    auto kernel = sparse_decode_fused_kernel<QT, KT, OT>;
+    static bool opt[64] = {false};
+    int rc = smem_opt_in(kernel, FusedSmem::kTotal, dev, opt);
+    if (rc != LP_OK) return rc;
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.gridDim = dim3(p.fused_ctas);
+    cfg.blockDim = dim3(kFThreads);
+    cfg.dynamicSmemBytes = FusedSmem::kTotal;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, fp);
+    if (e != cudaSuccess) return fail(LP_ERR_CUDA, std::string("sparse_decode_fused_kernel launch: ") + cudaGetErrorString(e));
+    return LP_OK;
+}
+
+template <typename QT, typename KT>
+static int launch_fused_out(const lp_sparse_decode_args* a, const Plan& p, cudaStream_t st, int dev) {
+    switch (a->out_dtype) {
+        case LP_BF16: return launch_fused<QT, KT, __nv_bfloat16>(a, p, st, dev);
+        case LP_F16: return launch_fused<QT, KT, __half>(a, p, st, dev);
+        case LP_F32: return launch_fused<QT, KT, float>(a, p, st, dev);
+    }
+    return fail(LP_ERR_INVALID, "out_dtype must be LP_BF16, LP_F16 or LP_F32");
+}
+
+template <typename QT>
+static int launch_fused_kv(const lp_sparse_decode_args* a, const Plan& p, cudaStream_t st, int dev) {
+    switch (a->kv_dtype) {
+        case LP_BF16: return launch_fused_out<QT, __nv_bfloat16>(a, p, st, dev);
+        case LP_F16: return launch_fused_out<QT, __half>(a, p, st, dev);
+    }
+    return fail(LP_ERR_INVALID, "kv_dtype must be LP_BF16 or LP_F16");
+}
+
 }  // namespace lp
 
 using namespace lp;
@@ -309,6 +416,18 @@ int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t wor
         return LP_OK;
     };
     if ((rc = mark(0)) != LP_OK) return rc;
+
+    if (p.fused) {
+        switch (a->q_dtype) {
+            case LP_BF16: rc = launch_fused_kv<__nv_bfloat16>(a, p, st, dev); break;
+            case LP_F16: rc = launch_fused_kv<__half>(a, p, st, dev); break;
+            default: rc = launch_fused_kv<float>(a, p, st, dev); break;
+        }
+        if (rc != LP_OK) return rc;
+        for (int i = 1; i <= 4; ++i)
+            if ((rc = mark(i)) != LP_OK) return rc;
+        return LP_OK;
+    }
 
     // 1. tables
     switch (a->q_dtype) {

@@ -150,7 +150,8 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
                   scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                   out_dtype: Optional[torch.dtype] = None, return_topk: bool = False,
                   return_head_scores: bool = False, attention: bool = True,
-                  ws: Optional[torch.Tensor] = None, stage_events=None) -> SparseDecodeResult:
+                  ws: Optional[torch.Tensor] = None, stage_events=None,
+                  fused: Optional[bool] = None, phase_ns: Optional[torch.Tensor] = None) -> SparseDecodeResult:
     """One sparse decode step of one layer (see lp_sparse_decode).
 
     q [B,Hq,D] (or [Hq,D]); codebooks fp32 [Hkv,M,K,D] or [M,K,D]; codes uint8
@@ -158,6 +159,11 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
     output [B,Hq,D] (``out_dtype``, default the K/V dtype), and optionally the
     selected indices ([B*Hkv, topk] or [B*Hq, topk], ascending int32) and the
     fp32 per-query-head scores [B,Hq,T_codes] (candidate window only).
+
+    ``fused=None`` lets the library run the whole step as one cooperative
+    kernel when the geometry allows (KV-group selection with attention);
+    ``fused=False`` forces the multi-kernel path.  ``phase_ns`` (int64 [8]
+    on the device) receives global-timer stamps of the fused kernel phases.
     """
     squeeze = q.dim() == 2
     q3 = q.unsqueeze(0) if squeeze else q
@@ -178,6 +184,10 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
     a = build_args(q3, codebooks, codes, keys, vals, topk=topk, T_codes=T_codes, T_total=T_total,
                    sink=sink, local=local, select=select, scale=scale, out=o, head_scores=hs,
                    topk_out=tk)
+    if fused is False:
+        a.flags |= _lib.LP_FLAG_NO_FUSED
+    if phase_ns is not None:
+        a.phase_ns = phase_ns.data_ptr()
     ev_arr = None
     if stage_events is not None:
         ev_arr = event_array(stage_events)

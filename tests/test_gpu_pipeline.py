@@ -55,13 +55,14 @@ def test_cfg1_scoring_op(golden_dir):
     _check_errors()
 
 
-def test_cfg3_sparse_decode_step(golden_dir):
+@pytest.mark.parametrize("fused", [None, False], ids=["auto", "multi"])
+def test_cfg3_sparse_decode_step(golden_dir, fused):
     fix = np.load(golden_dir / "cfg3_decode.npz")
     c = syn.config3(0)
     dev = _dev()
     C, codes, K, V, q = (c[n].to(dev) for n in ("C", "codes", "keys", "vals", "q"))
     r = ops.sparse_decode(q, C, codes, K, V, topk=c["k"], sink=c["sink"], local=c["local"],
-                          return_topk=True)
+                          return_topk=True, fused=fused)
     torch.cuda.synchronize()
     top = r.topk.cpu().numpy()
     T = codes.shape[1]
@@ -129,14 +130,15 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("fused", [None, False], ids=["auto", "multi"])
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
-def test_pipeline_vs_oracle(case):
+def test_pipeline_vs_oracle(case, fused):
     B, Hkv, G, Tc, Tt, cap, k, sink, local, per_kv, select, kvd, qd = case
     C, codes, K, V, q = _rand_case(1000 + Tc, B, Hkv, G, Tt, cap=cap, per_kv=per_kv, kv_dtype=kvd, q_dtype=qd)
     dev = _dev()
     r = ops.sparse_decode(q.to(dev), C.to(dev), codes.to(dev), K.to(dev), V.to(dev), topk=k,
                           T_codes=Tc, T_total=Tt, sink=sink, local=local, select=select,
-                          return_topk=True, out_dtype=torch.float32)
+                          return_topk=True, out_dtype=torch.float32, fused=fused)
     torch.cuda.synchronize()
     top_ref, out_ref, s_ref = _oracle_step(C, codes, K, V, q, Tc, Tt, k, sink, local, per_kv, select)
     top = r.topk.cpu().numpy()
@@ -158,14 +160,15 @@ def test_pipeline_vs_oracle(case):
     _check_errors()
 
 
-def test_ties_take_lowest_index():
+@pytest.mark.parametrize("fused", [None, False], ids=["auto", "multi"])
+def test_ties_take_lowest_index(fused):
     # every code equal -> every candidate score equal -> exact slow path; the
     # first k candidates (lowest indices) must be chosen
     C, codes, K, V, q = _rand_case(5, 1, 2, 4, 6000, equal_codes=True)
     dev = _dev()
     k, sink, local = 100, 4, 64
     r = ops.sparse_decode(q.to(dev), C.to(dev), codes.to(dev), K.to(dev), V.to(dev), topk=k,
-                          sink=sink, local=local, return_topk=True)
+                          sink=sink, local=local, return_topk=True, fused=fused)
     torch.cuda.synchronize()
     top = r.topk.cpu().numpy()
     for u in range(2):
@@ -174,13 +177,31 @@ def test_ties_take_lowest_index():
     assert bits & 1 == 0 and bits & 2 == 2  # slow exact path ran, no timeout
 
 
-def test_repeat_calls_deterministic():
+@pytest.mark.parametrize("fused", [None, False], ids=["auto", "multi"])
+def test_repeat_calls_deterministic(fused):
     C, codes, K, V, q = _rand_case(9, 1, 8, 4, 20000)
     dev = _dev()
     args = [t.to(dev) for t in (q, C, codes, K, V)]
-    outs = [ops.sparse_decode(*args, topk=400, sink=4, local=64, return_topk=True) for _ in range(3)]
+    outs = [ops.sparse_decode(*args, topk=400, sink=4, local=64, return_topk=True, fused=fused)
+            for _ in range(3)]
     torch.cuda.synchronize()
     for o in outs[1:]:
         assert torch.equal(o.topk, outs[0].topk)
         assert torch.equal(o.out, outs[0].out)
     _check_errors()
+
+
+def test_fused_path_is_taken_for_cfg3_geometry():
+    # the fused kernel stamps its phases; the multi-kernel path does not
+    c = syn.config3(0, T=32768)
+    dev = _dev()
+    args = [c[n].to(dev) for n in ("q", "C", "codes", "keys", "vals")]
+    ns = torch.zeros(8, dtype=torch.int64, device=dev)
+    ops.sparse_decode(*args, topk=512, sink=4, local=64, phase_ns=ns)
+    torch.cuda.synchronize()
+    t = ns.cpu().numpy()
+    assert (t > 0).all() and (np.diff(t) >= 0).all()
+    ns.zero_()
+    ops.sparse_decode(*args, topk=512, sink=4, local=64, phase_ns=ns, fused=False)
+    torch.cuda.synchronize()
+    assert (ns.cpu().numpy() == 0).all()
