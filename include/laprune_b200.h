@@ -14,8 +14,11 @@
  *     it and nothing synchronises the host, so calls are stream-ordered and
  *     can be captured in CUDA graphs (except where noted).
  *   - The caller owns every buffer, including `workspace` (size from the
- *     matching *_workspace_size function, 256-byte aligned, device memory).
- *     A workspace must not be shared by calls that may run concurrently.
+ *     matching *_workspace_size function, 256-byte aligned, device memory,
+ *     ZERO-FILLED before its first use).  Its first 512 bytes hold state
+ *     that persists between calls (device error bits, a grid-barrier word),
+ *     at the same offsets for every geometry; the rest is scratch.  A
+ *     workspace must not be shared by calls that may run concurrently.
  */
 #ifndef LAPRUNE_B200_H
 #define LAPRUNE_B200_H
@@ -135,7 +138,8 @@ int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t wor
                      void* stream);
 
 /* Reads and clears the device-side error bits accumulated in `workspace`
- * by earlier calls (synchronises `stream`). */
+ * by earlier calls (synchronises `stream`); after a wait timeout it also
+ * restores the workspace's grid-barrier word. */
 int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
                           uint32_t* bits_out);
 

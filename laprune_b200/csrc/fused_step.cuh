@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             __syncthreads();
             for (int i = tid; i < need; i += kFThreads) {
                 const int t = s_ti[i];
-                atomicOr(&s_over[(t >> 5) - wlo], 1u << (t & 31));
+                if (t >= p.c0 && t < p.c1) atomicOr(&s_over[(t >> 5) - wlo], 1u << (t & 31));
             }
         }
         if (overflow_any) {

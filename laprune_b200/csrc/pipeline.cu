@@ -167,7 +167,10 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     }
 
     Carver c(ws);
+    // fixed offsets, identical for every geometry: the error word (0) and the
+    // grid-barrier word (256 B), whose value must survive between calls
     p.err = c.take<uint32_t>(64);
+    p.bar = c.take<uint32_t>(64);
     p.lut = c.take<float>((size_t)p.U * 256 * 32 * (p.heads ? 4 : 1));
     p.bounds = c.take<float>((size_t)p.U * (p.heads ? a->G : 1) * 32 * kLutParts * 2);
     p.sel_scores = c.take<float>((size_t)p.Usel * std::max(1, a->T_codes));
@@ -176,7 +179,6 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     p.info = c.take<int4>((size_t)p.Usel);
     p.part = c.take<float>((size_t)std::max((size_t)p.Uatt * p.nsplit * p.HG, (size_t)p.U * p.fused_max_split * a->G) *
                            (2 + 128));
-    p.bar = c.take<uint32_t>(64);
     p.zero_words = (int64_t)p.Usel * kNB + p.Usel + p.Usel + p.Uatt;
     p.zero = c.take<uint32_t>((size_t)p.zero_words);
     p.hist = p.zero;
@@ -546,6 +548,9 @@ int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
     LP_CUDA(cudaMemcpyAsync(&v, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     LP_CUDA(cudaStreamSynchronize(st));
     LP_CUDA(cudaMemsetAsync(workspace, 0, sizeof(uint32_t), st));
+    // a timed-out grid barrier leaves its word mid-count: restore it
+    if (v & LP_DEVERR_WAIT_TIMEOUT) LP_CUDA(cudaMemsetAsync(static_cast<char*>(workspace) + 256, 0, 4, st));
+    LP_CUDA(cudaStreamSynchronize(st));
     *bits_out = v;
     return LP_OK;
 }

@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(THREADS) select_kernel(SelectParams p) {
         __syncthreads();
         for (int i = tid; i < need; i += THREADS) {
             const int t = is[i];
-            atomicOr(&bm[t >> 5], 1u << (t & 31));
+            if (t >= p.c0 && t < p.c1) atomicOr(&bm[t >> 5], 1u << (t & 31));
         }
         return;
     }

@@ -205,3 +205,22 @@ def test_fused_path_is_taken_for_cfg3_geometry():
     ops.sparse_decode(*args, topk=512, sink=4, local=64, phase_ns=ns, fused=False)
     torch.cuda.synchronize()
     assert (ns.cpu().numpy() == 0).all()
+
+
+def test_workspace_shared_across_geometries():
+    # one workspace, alternating shapes: the persistent state (error word,
+    # grid-barrier word) must sit at geometry-independent offsets
+    dev = _dev()
+    ws = torch.zeros(256 << 20, dtype=torch.uint8, device=dev)
+    outs = {}
+    for rep in range(2):
+        for T, Hkv in ((4096, 8), (20000, 2), (777, 4)):
+            C, codes, K, V, q = _rand_case(T, 1, Hkv, 4, T)
+            r = ops.sparse_decode(q.to(dev), C.to(dev), codes.to(dev), K.to(dev), V.to(dev),
+                                  topk=32, sink=4, local=64, return_topk=True, ws=ws)
+            torch.cuda.synchronize()
+            if rep == 0:
+                outs[T] = (r.topk.clone(), r.out.clone())
+            else:
+                assert torch.equal(outs[T][0], r.topk) and torch.equal(outs[T][1], r.out)
+    assert ops.device_errors(ws, dev) & 1 == 0
