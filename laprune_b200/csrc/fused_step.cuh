@@ -80,6 +80,7 @@ struct FusedParams {
     float2* tie_buf;     // [U][kTieCap]
     uint32_t* tie_count; // [U]                 (zeroed in phase A)
     uint32_t* done_att;  // [U]                 (zeroed in phase A)
+    uint32_t* cta_count; // [gridDim.x] selected-above-threshold count of each CTA
     float* part;         // [U][max_split][G][2+128]
     int max_split;
     uint32_t* bar;       // grid barrier word (self-resetting)
@@ -197,6 +198,39 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             const int nn = min(kFThreads, t_end - t0);
             mbar_arrive_expect_tx(&s_bar[i], (uint32_t)nn * 32u);
             bulk_g2s_stream(s_ring + i * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[i], policy);
+        }
+    }
+    // ---- pull this CTA's codebook rows (phase A) and the rest of its code
+    //      range (phase B) toward L2 at once: the HBM streams then run at full
+    //      depth from t=0 while both phases read from L2 ----
+    if (tid == 0) {
+        const int64_t total = (int64_t)p.U * 32 * 256;
+        const int64_t per = ((total + gridDim.x - 1) / gridDim.x + 7) & ~(int64_t)7;
+        int64_t f = (int64_t)blockIdx.x * per;
+        const int64_t fe = min(total, f + per);
+        while (f < fe) {
+            const int64_t uu = f / 8192;
+            const int64_t seg_end = min(fe, (uu + 1) * 8192);
+            const float* base = p.cb + (int64_t)(p.cb_per_kv_head ? (int)(uu % p.Hkv) : 0) * (32 * 256 * 128);
+            const char* a0 = reinterpret_cast<const char*>(base + (f - uu * 8192) * 128);
+            int64_t bytes = (seg_end - f) * 512;
+            while (bytes > 0) {
+                const uint32_t nb = (uint32_t)(bytes < 65536 ? bytes : 65536);
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a0), "r"(nb) : "memory");
+                a0 += nb;
+                bytes -= nb;
+            }
+            f = seg_end;
+        }
+        if (ntiles > npre) {
+            const char* a0 = reinterpret_cast<const char*>(src) + (int64_t)(t_begin + npre * kFThreads) * 32;
+            int64_t bytes = (int64_t)(t_end - (t_begin + npre * kFThreads)) * 32;
+            while (bytes > 0) {
+                const uint32_t nb = (uint32_t)(bytes < 65536 ? bytes : 65536);
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a0), "r"(nb) : "memory");
+                a0 += nb;
+                bytes -= nb;
+            }
         }
     }
     int issued = npre;
@@ -396,26 +430,27 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     if (!grid_barrier(p.bar, p.err)) return;
     if (stamp) p.phase_ns[4] = global_ns();
 
-    // ================= phase C: select (threshold bin, bitmap, ties) =================
+    // ================= phase C: select (threshold bin, own counts, ties) =================
     uint32_t* bm = p.bitmap + (int64_t)u * p.bm_stride;
+    const float* gsc_c = p.sel_scores + (int64_t)u * p.sel_stride;
+    __shared__ int s_cnt_above, s_nsel, s_win_before;
     {
         for (int i = tid; i < kNB; i += kFThreads) s_hist[i] = __ldcg(p.hist + (int64_t)u * kNB + i);
-        if (tid == 0) { s_bstar = kNB; s_above = 0; }
+        if (tid == 0) { s_bstar = kNB; s_above = 0; s_cnt_above = 0; }
         __syncthreads();
         if (p.k > 0) find_threshold_bin<kFThreads>(s_hist, p.k, &s_bstar, &s_above);
         __syncthreads();
         const int bstar = s_bstar;
-        const float* gsc = p.sel_scores + (int64_t)u * p.sel_stride;
+        int my_above = 0;
         for (int w = w_begin + warp; w < w_end; w += NW) {
             const int t = w * 32 + lane;
             const bool valid = t >= p.c0 && t < p.c1;
             float s = 0.f;
-            if (valid) s = keep_smem ? s_scores[t - t_begin] : __ldcg(gsc + t);
+            if (valid) s = keep_smem ? s_scores[t - t_begin] : __ldcg(gsc_c + t);
             const int bin = score_bin(s, bp.lo, bp.inv_w, kNB);
-            const bool sel_ = valid && bin > bstar;
             const bool tie = valid && bin == bstar;
-            const uint32_t bits = __ballot_sync(0xffffffffu, sel_);
-            if (lane == 0) bm[w] = bits;
+            my_above += __popc(__ballot_sync(0xffffffffu, valid && bin > bstar));
+            if (lane == 0) bm[w] = 0u;  // cleared for the exact slow path
             const uint32_t tmask = __ballot_sync(0xffffffffu, tie);
             if (tmask) {
                 uint32_t base = 0;
@@ -428,59 +463,50 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 }
             }
         }
+        if (lane == 0 && my_above) atomicAdd(&s_cnt_above, my_above);
+        __syncthreads();
+        if (tid == 0) p.cta_count[blockIdx.x] = (uint32_t)s_cnt_above;
     }
     if (stamp) p.phase_ns[5] = global_ns();
     if (!grid_barrier(p.bar, p.err)) return;
 
     // ================= phase D: ties (redundant per CTA, no barrier) =================
-    // overlay of the tie winners on the unit bitmap, in shared memory
-    uint32_t* s_over = reinterpret_cast<uint32_t*>(s_ring);          // [nwu] words (<= kFMaxWords)
-    float* s_tk = reinterpret_cast<float*>(s_lut);                  // tie sort keys  [kTieCap]
-    int* s_ti = reinterpret_cast<int*>(s_lut + kTieCap * 4);        // tie sort index [kTieCap]
+    // winners of the CTA's own token range -> bit lt of s_win
+    uint32_t* s_win = s_hist;                                              // [ceil(ntok/32)] words
+    float* s_tk = reinterpret_cast<float*>(s_ring + 64 * 1024);           // tie keys  [kTieCap]
+    int* s_ti = reinterpret_cast<int*>(s_ring + 64 * 1024 + kTieCap * 4);  // tie index [kTieCap]
     {
         const int need = p.k - s_above;
-        if (tid == 0) {
-            int any = 0;
-            for (int uu = 0; uu < p.U; ++uu) any |= __ldcg(p.tie_count + uu) > (uint32_t)kTieCap;
-            s_flag = any;
-        }
-        for (int i = tid; i < nwu; i += kFThreads) s_over[i] = 0u;
-        __syncthreads();
-        const bool overflow_any = s_flag != 0;
+        const bool ovf_mine = tid < p.U && __ldcg(p.tie_count + tid) > (uint32_t)kTieCap;
+        for (int i = tid; i < (ntok + 31) / 32; i += kFThreads) s_win[i] = 0u;
+        if (tid == 0) s_win_before = 0;
+        const bool overflow_any = __syncthreads_or(ovf_mine) != 0;
         const int ntie = (int)__ldcg(p.tie_count + u);
+        if (stamp) p.phase_ns[6] = global_ns();
         if (ntie <= kTieCap && need > 0) {
-            int n = 1;
-            while (n < ntie) n <<= 1;
-            for (int i = tid; i < n; i += kFThreads) {
-                if (i < ntie) {
-                    const float2 e = __ldcg(p.tie_buf + (int64_t)u * kTieCap + i);
-                    s_tk[i] = e.x;
-                    s_ti[i] = __float_as_int(e.y);
-                } else {
-                    s_tk[i] = -INFINITY;
-                    s_ti[i] = 0x7fffffff;
-                }
-            }
-            for (int size = 2; size <= n; size <<= 1) {
-                for (int stride = size >> 1; stride > 0; stride >>= 1) {
-                    __syncthreads();
-                    for (int i = tid; i < (n >> 1); i += kFThreads) {
-                        const int a = 2 * i - (i & (stride - 1));
-                        const int c = a + stride;
-                        const bool up = (a & size) == 0;
-                        const float ka = s_tk[a], kc = s_tk[c];
-                        const int ia = s_ti[a], ic = s_ti[c];
-                        if (sel_before(kc, ic, ka, ia) == up) {
-                            s_tk[a] = kc; s_tk[c] = ka;
-                            s_ti[a] = ic; s_ti[c] = ia;
-                        }
-                    }
-                }
+            for (int i = tid; i < ntie; i += kFThreads) {
+                const float2 e = __ldcg(p.tie_buf + (int64_t)u * kTieCap + i);
+                s_tk[i] = e.x;
+                s_ti[i] = __float_as_int(e.y);
             }
             __syncthreads();
-            for (int i = tid; i < need; i += kFThreads) {
-                const int t = s_ti[i];
-                if (t >= p.c0 && t < p.c1) atomicOr(&s_over[(t >> 5) - wlo], 1u << (t & 31));
+            // rank of each tie entry in selection order (score desc, index asc):
+            // the first `need` ranks win.  O(n^2 / threads) comparisons.
+            for (int i = tid; i < ntie; i += kFThreads) {
+                const float ki = s_tk[i];
+                const int ii = s_ti[i];
+                int rank = 0;
+                for (int j = 0; j < ntie; ++j) rank += sel_before(s_tk[j], s_ti[j], ki, ii);
+                if (rank < need) {
+                    const int lt = ii - t_begin;
+                    if (ii >= t_begin && ii < t_end) atomicOr(&s_win[lt >> 5], 1u << (lt & 31));
+                    if (p.topk_out && ii >= p.c0 && ii < p.c1) {
+                        // owner CTA (within the unit) of token ii
+                        const int x = (ii >> 5) - wlo;
+                        const int owner = (int)(((int64_t)(x + 1) * cn - 1) / nwu);
+                        if (owner < cj) atomicAdd(&s_win_before, 1);
+                    }
+                }
             }
         }
         if (overflow_any) {
@@ -491,16 +517,15 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 uint32_t* h256 = reinterpret_cast<uint32_t*>(s_lut);
                 __shared__ uint32_t s_prefix, s_mask;
                 __shared__ int s_remaining;
-                const float* gsc = p.sel_scores + (int64_t)u * p.sel_stride;
                 if (tid == 0) { s_prefix = 0; s_mask = 0; s_remaining = need; }
                 for (int shift = 24; shift >= 0; shift -= 8) {
                     for (int i = tid; i < 256; i += kFThreads) h256[i] = 0;
                     __syncthreads();
                     const uint32_t prefix = s_prefix, mask = s_mask;
                     for (int t = p.c0 + tid; t < p.c1; t += kFThreads) {
-                        const float s = __ldcg(gsc + t);
-                        if (score_bin(s, bp.lo, bp.inv_w, kNB) != s_bstar) continue;
-                        const uint32_t key = ordered_key(s);
+                        const float sv = __ldcg(gsc_c + t);
+                        if (score_bin(sv, bp.lo, bp.inv_w, kNB) != s_bstar) continue;
+                        const uint32_t key = ordered_key(sv);
                         if ((key & mask) != prefix) continue;
                         atomicAdd(&h256[(key >> shift) & 255u], 1u);
                     }
@@ -532,9 +557,9 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                     const int t = base + tid;
                     int gt = 0, eq = 0;
                     if (t < p.c1) {
-                        const float s = __ldcg(gsc + t);
-                        if (score_bin(s, bp.lo, bp.inv_w, kNB) == s_bstar) {
-                            const uint32_t key = ordered_key(s);
+                        const float sv = __ldcg(gsc_c + t);
+                        if (score_bin(sv, bp.lo, bp.inv_w, kNB) == s_bstar) {
+                            const uint32_t key = ordered_key(sv);
                             gt = key > kstar;
                             eq = key == kstar;
                         }
@@ -548,139 +573,180 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 }
             }
             if (!grid_barrier(p.bar, p.err)) return;
+            if (ntie > kTieCap && need > 0) {
+                // winners of this unit are the bits the leader set
+                for (int w = w_begin + tid; w < w_end; w += kFThreads) {
+                    const uint32_t bits = __ldcg(bm + w);
+                    for (uint32_t b2 = bits; b2; b2 &= b2 - 1) {
+                        const int lt = w * 32 + __ffs(b2) - 1 - t_begin;
+                        if (lt >= 0 && lt < ntok) atomicOr(&s_win[lt >> 5], 1u << (lt & 31));
+                    }
+                }
+                if (p.topk_out) {
+                    int c = 0;
+                    for (int w = wlo + tid; w < w_begin; w += kFThreads) c += __popc(__ldcg(bm + w));
+                    if (c) atomicAdd(&s_win_before, c);
+                }
+            }
         }
+        __syncthreads();
     }
-    if (stamp) p.phase_ns[6] = global_ns();
 
-    // ================= phase E: attention over the CTA's slice of kept rows =================
+    // ================= phase E: attention over the CTA's own kept rows =================
     {
         constexpr int D = 128;
-        KT* s_k = reinterpret_cast<KT*>(s_ring + kFMaxWords * 4);                 // [rows][128]
-        KT* s_v = s_k + kFMaxRows * D;                                           // [rows][128]
-        int* s_rows = reinterpret_cast<int*>(s_hist);                           // [kFMaxRows]
-        float* s_q = reinterpret_cast<float*>(s_lut + 2 * kTieCap * 4);          // [G][128]
-        float* s_p = s_q + 8 * D;                                                // [G][kFMaxRows]
-        float* s_ml = s_p + 8 * kFMaxRows;                                       // [G][2]
-        float* s_w = reinterpret_cast<float*>(s_lut + 48 * 1024);                // [G][cn] merge weights
+        constexpr int R = kFMaxRows;
+        int* s_list = reinterpret_cast<int*>(s_lut);                                 // [<= kFScoreCap]
+        float* s_q = reinterpret_cast<float*>(s_lut + kFScoreCap * 4);              // [8][128]
+        float* s_p = s_q + 8 * D;                                                    // [8][R]
+        float* s_m = s_p + 8 * R;                                                    // [8] running max
+        float* s_l = s_m + 8;                                                        // [8] running sum
+        float* s_al = s_l + 8;                                                       // [8] rescale
+        float* s_w = s_al + 8;                                                       // [8][cn] merge weights
+        KT* s_k = reinterpret_cast<KT*>(s_ring);                                     // [R][128]
+        KT* s_v = s_k + R * D;                                                       // [R][128]
         __shared__ int s_last;
         using Scan = cub::BlockScan<int, kFThreads>;
         __shared__ typename Scan::TempStorage scan_tmp;
 
-        const int rows_per = (p.n_rows + cn - 1) / cn;
-        const int r0 = cj * rows_per;
-        const int r1 = min(p.n_rows, r0 + rows_per);
-        const int nr = max(0, r1 - r0);
-        for (int i = tid; i < kFMaxRows; i += kFThreads) s_rows[i] = 0;
-        __syncthreads();
-        for (int r = r0 + tid; r < min(r1, p.n_sink); r += kFThreads) s_rows[r - r0] = r;
-        for (int r = max(r0, p.n_sink + p.k) + tid; r < r1; r += kFThreads)
-            s_rows[r - r0] = p.local_start + (r - p.n_sink - p.k);
-        const int j0 = max(r0, p.n_sink) - p.n_sink;
-        const int j1 = min(r1, p.n_sink + p.k) - p.n_sink;
-        if (j0 < j1) {
-            constexpr int WB = 16;
-            const int per = (nwu + kFThreads - 1) / kFThreads;
-            const int wa = tid * per;  // relative word index
-            int base_round = 0;
-            for (int r = 0; r < per; r += WB) {
-                uint32_t words[WB];
-                int cnt = 0;
-#pragma unroll
-                for (int j = 0; j < WB; ++j) {
-                    const int w = wa + r + j;
-                    words[j] = (r + j < per && w < nwu) ? (__ldcg(bm + wlo + w) | s_over[w]) : 0u;
-                    cnt += __popc(words[j]);
-                }
-                int before, total;
-                Scan(scan_tmp).ExclusiveSum(cnt, before, total);
-                __syncthreads();
-                int rank = base_round + before;
-                if (rank < j1 && rank + cnt > j0) {
-#pragma unroll
-                    for (int j = 0; j < WB; ++j) {
-                        uint32_t bits = words[j];
-                        const int c = __popc(bits);
-                        if (rank + c <= j0 || rank >= j1) { rank += c; continue; }
-                        while (bits) {
-                            const int bit = __ffs(bits) - 1;
-                            bits &= bits - 1;
-                            if (rank >= j0 && rank < j1) {
-                                const int tok = (wlo + wa + r + j) * 32 + bit;
-                                s_rows[p.n_sink + rank - r0] = tok;
-                                if (p.topk_out) p.topk_out[(int64_t)u * p.k + rank] = tok;
-                            }
-                            ++rank;
-                        }
-                    }
-                }
-                base_round += total;
+        // ---- own selected tokens in ascending order ----
+        const int bstar = s_bstar;
+        {
+            const int per = (ntok + kFThreads - 1) / kFThreads;
+            const int la = tid * per, lb = min(ntok, la + per);
+            int cnt = 0;
+            for (int lt = la; lt < lb; ++lt) {
+                const float sv = keep_smem ? s_scores[lt] : __ldcg(gsc_c + t_begin + lt);
+                cnt += (score_bin(sv, bp.lo, bp.inv_w, kNB) > bstar) || ((s_win[lt >> 5] >> (lt & 31)) & 1u);
             }
+            int pos, total;
+            Scan(scan_tmp).ExclusiveSum(cnt, pos, total);
+            for (int lt = la; lt < lb; ++lt) {
+                const float sv = keep_smem ? s_scores[lt] : __ldcg(gsc_c + t_begin + lt);
+                if ((score_bin(sv, bp.lo, bp.inv_w, kNB) > bstar) || ((s_win[lt >> 5] >> (lt & 31)) & 1u))
+                    s_list[pos++] = t_begin + lt;
+            }
+            if (tid == 0) s_nsel = total;
         }
         const QT* qb = reinterpret_cast<const QT*>(p.q) + (int64_t)b * p.q_stride_b;
         for (int i = tid; i < p.G * D; i += kFThreads) {
             const int g = i / D, d = i - g * D;
             s_q[g * D + d] = to_f32(qb[(int64_t)(hkv * p.G + g) * p.q_stride_h + d]);
         }
+        if (tid < 8) { s_m[tid] = -INFINITY; s_l[tid] = 0.f; }
         __syncthreads();
-        // gather
+        const int nsel = s_nsel;
+        if (p.topk_out && nsel > 0) {
+            // rank offset of this CTA's first selected token within the unit
+            __shared__ int s_off;
+            if (tid == 0) s_off = s_win_before;
+            __syncthreads();
+            const int ubase = blockIdx.x - cj;  // first CTA of the unit
+            int c = 0;
+            for (int j = tid; j < cj; j += kFThreads) c += (int)__ldcg(p.cta_count + ubase + j);
+            if (c) atomicAdd(&s_off, c);
+            __syncthreads();
+            const int off = s_off;
+            for (int i = tid; i < nsel; i += kFThreads)
+                if (off + i < p.k) p.topk_out[(int64_t)u * p.k + off + i] = s_list[i];
+        }
+        const int n_sink_here = cj == 0 ? p.n_sink : 0;
+        const int n_loc_here = cj == cn - 1 ? p.n_local : 0;
+        const int nrows = n_sink_here + nsel + n_loc_here;
+
         const KT* kb = reinterpret_cast<const KT*>(p.keys) + (int64_t)b * p.k_stride_b + (int64_t)hkv * p.k_stride_h;
         const KT* vb = reinterpret_cast<const KT*>(p.vals) + (int64_t)b * p.v_stride_b + (int64_t)hkv * p.v_stride_h;
         constexpr int CH = D * (int)sizeof(KT) / 16;
         constexpr int EPC = 16 / (int)sizeof(KT);
-        for (int c = tid; c < nr * CH; c += kFThreads) {
-            const int r = c / CH, part = c - r * CH;
-            const int64_t t = min(max(s_rows[r], 0), p.T_total - 1);
-            cp_async16(s_k + r * D + part * EPC, kb + t * p.k_stride_t + part * EPC);
-            cp_async16(s_v + r * D + part * EPC, vb + t * p.v_stride_t + part * EPC);
-        }
-        cp_async_commit();
-        cp_async_wait<0>();
-        __syncthreads();
-        // logits (log2 domain)
-        for (int r = warp; r < nr; r += NW) {
-            const float4 kv = Vec4<KT>::load(s_k + r * D + lane * 4);
-            for (int g = 0; g < p.G; ++g) {
-                const float4 qv = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
-                float a = qv.x * kv.x;
-                a = fmaf(qv.y, kv.y, a);
-                a = fmaf(qv.z, kv.z, a);
-                a = fmaf(qv.w, kv.w, a);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-                if (lane == g) s_p[g * kFMaxRows + r] = a * p.scale_log2;
+        float acc0 = 0.f, acc1 = 0.f;  // P.V for outputs o = tid and tid + 512
+        for (int c0r = 0; c0r < nrows; c0r += R) {
+            const int nr = min(R, nrows - c0r);
+            for (int c = tid; c < nr * CH; c += kFThreads) {
+                const int r = c / CH, part = c - r * CH;
+                const int rr = c0r + r;
+                int tok = rr < n_sink_here ? rr
+                        : rr < n_sink_here + nsel ? s_list[rr - n_sink_here]
+                        : p.local_start + (rr - n_sink_here - nsel);
+                const int64_t t = min(max(tok, 0), p.T_total - 1);
+                cp_async16(s_k + r * D + part * EPC, kb + t * p.k_stride_t + part * EPC);
+                cp_async16(s_v + r * D + part * EPC, vb + t * p.v_stride_t + part * EPC);
             }
-        }
-        __syncthreads();
-        for (int g = warp; g < p.G; g += NW) {
-            float mx = -INFINITY;
-            for (int r = lane; r < nr; r += 32) mx = fmaxf(mx, s_p[g * kFMaxRows + r]);
+            cp_async_commit();
+            cp_async_wait<0>();
+            __syncthreads();
+            // logits (log2 domain): warp per row, lane per 4 dims
+            for (int r = warp; r < nr; r += NW) {
+                const float4 kv = Vec4<KT>::load(s_k + r * D + lane * 4);
+                for (int g = 0; g < p.G; ++g) {
+                    const float4 qv = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
+                    float a = qv.x * kv.x;
+                    a = fmaf(qv.y, kv.y, a);
+                    a = fmaf(qv.z, kv.z, a);
+                    a = fmaf(qv.w, kv.w, a);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            float sum = 0.f;
-            for (int r = lane; r < nr; r += 32) {
-                const float e = exp2f(s_p[g * kFMaxRows + r] - mx);
-                s_p[g * kFMaxRows + r] = e;
-                sum += e;
+                    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                    if (lane == g) s_p[g * R + r] = a * p.scale_log2;
+                }
             }
+            __syncthreads();
+            // online softmax update per head
+            for (int g = warp; g < p.G; g += NW) {
+                float mx = -INFINITY;
+                for (int r = lane; r < nr; r += 32) mx = fmaxf(mx, s_p[g * R + r]);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0) { s_ml[2 * g] = mx; s_ml[2 * g + 1] = sum; }
+                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                const float m_old = s_m[g];
+                const float m_new = fmaxf(m_old, mx);
+                float sum = 0.f;
+                for (int r = lane; r < nr; r += 32) {
+                    const float e = exp2f(s_p[g * R + r] - m_new);
+                    s_p[g * R + r] = e;
+                    sum += e;
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                __syncwarp();
+                if (lane == 0) {
+                    const float alpha = exp2f(m_old - m_new);  // 0 on the first chunk
+                    s_al[g] = alpha;
+                    s_l[g] = s_l[g] * alpha + sum;
+                    s_m[g] = m_new;
+                }
+            }
+            __syncthreads();
+            // P.V: thread -> output (g, d), rows unrolled by 2
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int o = tid + h * kFThreads;
+                if (o < p.G * D) {
+                    const int g = o >> 7, d = o & (D - 1);
+                    const float* pg = s_p + g * R;
+                    float x0 = 0.f, x1 = 0.f;
+                    int r = 0;
+                    for (; r + 2 <= nr; r += 2) {
+                        x0 = fmaf(pg[r], to_f32(s_v[r * D + d]), x0);
+                        x1 = fmaf(pg[r + 1], to_f32(s_v[(r + 1) * D + d]), x1);
+                    }
+                    if (r < nr) x0 = fmaf(pg[r], to_f32(s_v[r * D + d]), x0);
+                    if (h == 0) acc0 = fmaf(acc0, s_al[g], x0 + x1);
+                    else acc1 = fmaf(acc1, s_al[g], x0 + x1);
+                }
+            }
+            __syncthreads();
         }
-        __syncthreads();
+        // partial state of this CTA
         float* part = p.part + ((int64_t)u * p.max_split + cj) * p.G * (2 + D);
-        for (int o = tid; o < p.G * (D / 2); o += kFThreads) {
-            const int g = o / (D / 2), dp = o - g * (D / 2);
-            float ax = 0.f, ay = 0.f;
-            for (int r = 0; r < nr; ++r) {
-                const float2 vv = Vec4<KT>::load2(s_v + r * D + 2 * dp);
-                const float w = s_p[g * kFMaxRows + r];
-                ax = fmaf(w, vv.x, ax);
-                ay = fmaf(w, vv.y, ay);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int o = tid + h * kFThreads;
+            if (o < p.G * D) {
+                const int g = o >> 7, d = o & (D - 1);
+                part[g * (2 + D) + 2 + d] = h == 0 ? acc0 : acc1;
+                if (d == 0) {
+                    part[g * (2 + D)] = s_m[g];
+                    part[g * (2 + D) + 1] = s_l[g];
+                }
             }
-            float* pg = part + g * (2 + D);
-            pg[2 + 2 * dp] = ax;
-            pg[3 + 2 * dp] = ay;
-            if (dp == 0) { pg[0] = nr > 0 ? s_ml[2 * g] : -INFINITY; pg[1] = nr > 0 ? s_ml[2 * g + 1] : 0.f; }
         }
         __syncthreads();
         if (tid == 0) {

@@ -83,6 +83,7 @@ struct Plan {
     uint32_t* done_sel;
     uint32_t* done_att;
     uint32_t* bar;
+    uint32_t* cta_count;
     size_t bytes;
 };
 
@@ -161,8 +162,7 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
         const int ntok_max = cn_min > 0 ? (nwu + cn_min - 1) / cn_min * 32 : 0;
         p.fused = !(a->flags & LP_FLAG_NO_FUSED) && !p.per_head && !p.heads && a->out != nullptr &&
                   a->D == 128 && a->G <= 8 && p.U <= p.fused_ctas && p.ncand > 0 && a->topk > 0 &&
-                  nwu <= kFMaxWords && cn_min >= 1 &&
-                  (p.n_rows + cn_min - 1) / cn_min <= kFMaxRows && ntok_max <= (1 << 30);
+                  nwu <= kFMaxWords && cn_min >= 1 && ntok_max <= kFScoreCap;
         p.fused_max_split = cn_min + 1;
     }
 
@@ -179,6 +179,7 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     p.info = c.take<int4>((size_t)p.Usel);
     p.part = c.take<float>((size_t)std::max((size_t)p.Uatt * p.nsplit * p.HG, (size_t)p.U * p.fused_max_split * a->G) *
                            (2 + 128));
+    p.cta_count = c.take<uint32_t>((size_t)p.fused_ctas);
     p.zero_words = (int64_t)p.Usel * kNB + p.Usel + p.Usel + p.Uatt;
     p.zero = c.take<uint32_t>((size_t)p.zero_words);
     p.hist = p.zero;
@@ -320,6 +321,7 @@ static int launch_fused(const lp_sparse_decode_args* a, const Plan& p, cudaStrea
     fp.tie_buf = p.tie_buf;
     fp.tie_count = p.tie_count;
     fp.done_att = p.done_att;
+    fp.cta_count = p.cta_count;
     fp.part = p.part;
     fp.max_split = p.fused_max_split;
     fp.bar = p.bar;
