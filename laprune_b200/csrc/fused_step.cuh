@@ -50,7 +50,7 @@ constexpr int kFStages = 6;
 constexpr int kFTile = kFThreads * 32;           // 16 KB of code rows per stage
 constexpr int kFScoreCap = 11264;                // tokens per CTA kept in smem
 constexpr int kFMaxWords = 8192;                 // bitmap words per unit in smem overlay
-constexpr int kFMaxRows = 128;                   // kept rows per CTA in phase E
+constexpr int kFMaxRows = 192;                   // kept rows per attention chunk in phase E
 
 struct FusedParams {
     const void* q;
@@ -93,7 +93,7 @@ struct FusedSmem {
     static constexpr int kRing = kFStages * kFTile;    // 96 KB (phase B ring; reused in E)
     static constexpr int kHist = kNB * 4;              // 8 KB
     static constexpr int kScores = kFScoreCap * 4;     // 48 KB
-    static constexpr int kBars = kFStages * 8;
+    static constexpr int kBars = 2 * kFStages * 8;  // full + empty barriers
     static constexpr int kTotal = kLut + kRing + kHist + kScores + kBars + 128;
 };
 
@@ -158,8 +158,6 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     float* s_scores = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(s_hist) + S::kHist);
     uint64_t* s_bar = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(s_scores) + S::kScores);
 
-    __shared__ float s_qsum[2][128];
-    __shared__ float s_mmin[kFThreads / 32][32], s_mmax[kFThreads / 32][32];
     __shared__ BinParams s_bp;
     __shared__ int s_shift, s_bstar, s_above, s_flag;
 
@@ -183,8 +181,12 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     const bool keep_smem = ntok <= kFScoreCap;
     const uint8_t* src = p.codes + (int64_t)b * p.codes_stride_b + (int64_t)hkv * p.codes_stride_h;
 
+    uint64_t* s_empty = s_bar + kFStages;  // per-slot "all warps done" barriers
     if (tid == 0) {
-        for (int s = 0; s < kFStages; ++s) mbar_init(&s_bar[s], 1);
+        for (int s = 0; s < kFStages; ++s) {
+            mbar_init(&s_bar[s], 1);
+            mbar_init(&s_empty[s], NW);
+        }
         fence_barrier_init();
     }
     __syncthreads();
@@ -200,9 +202,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             bulk_g2s_stream(s_ring + i * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[i], policy);
         }
     }
-    // ---- pull this CTA's codebook rows (phase A) and the rest of its code
-    //      range (phase B) toward L2 at once: the HBM streams then run at full
-    //      depth from t=0 while both phases read from L2 ----
+    // ---- pull this CTA's whole codebook slice (phase A) toward L2 at once,
+    //      so the codebook stream runs at full depth from t=0 ----
     if (tid == 0) {
         const int64_t total = (int64_t)p.U * 32 * 256;
         const int64_t per = ((total + gridDim.x - 1) / gridDim.x + 7) & ~(int64_t)7;
@@ -221,16 +222,6 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 bytes -= nb;
             }
             f = seg_end;
-        }
-        if (ntiles > npre) {
-            const char* a0 = reinterpret_cast<const char*>(src) + (int64_t)(t_begin + npre * kFThreads) * 32;
-            int64_t bytes = (int64_t)(t_end - (t_begin + npre * kFThreads)) * 32;
-            while (bytes > 0) {
-                const uint32_t nb = (uint32_t)(bytes < 65536 ? bytes : 65536);
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a0), "r"(nb) : "memory");
-                a0 += nb;
-                bytes -= nb;
-            }
         }
     }
     int issued = npre;
@@ -254,7 +245,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         const int64_t per = ((total + gridDim.x - 1) / gridDim.x + 7) & ~(int64_t)7;
         const int64_t f_begin = (int64_t)blockIdx.x * per;
         const int64_t f_end = min(total, f_begin + per);
-        // q_sum of the (at most two) units this CTA touches
+        // q_sum of the (at most two) units this CTA touches (s_hist is free now)
+        float (*s_qsum)[128] = reinterpret_cast<float (*)[128]>(s_hist);
         const int ua = (int)(f_begin / 8192);
         for (int i = tid; i < 2 * 128; i += kFThreads) {
             const int slot = i >> 7, d = i & 127;
@@ -310,6 +302,9 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[j] = __ldcg(g4 + tid + j * kFThreads);
         // thread's m group is (tid & 7); reduce min/max per m over k
+        // (scratch in the score buffer, which is not written yet)
+        float (*s_mmin)[32] = reinterpret_cast<float (*)[32]>(s_scores);
+        float (*s_mmax)[32] = s_mmin + NW;
         float mn[4], mx[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -387,10 +382,17 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             sel[s] = 0x5504u | (bs << 4);
         }
         float* gsc = p.sel_scores + (int64_t)u * p.sel_stride;
+        // Ring protocol: full[s] completes when tile bytes land; every warp
+        // arrives on empty[s] once it has read its rows of the tile; thread 0
+        // refills slot (i-1)%S with tile i-1+S one iteration later, after
+        // empty[(i-1)%S] completed.  No block-wide barrier per tile.
+        __shared__ int s_abort;
+        if (tid == 0) s_abort = 0;
+        __syncthreads();
         for (int i = 0; i < ntiles; ++i) {
             const int slot = i % kFStages;
-            const bool ok = mbar_wait(&s_bar[slot], (uint32_t)(i / kFStages) & 1u, p.err);
-            if (__syncthreads_or(!ok)) { drain(i); return; }
+            if (!mbar_wait(&s_bar[slot], (uint32_t)(i / kFStages) & 1u, p.err)) s_abort = 1;
+            if (*((volatile int*)&s_abort)) break;
             const int lt = i * kFThreads + tid;
             const int t = t_begin + lt;
             if (t < t_end) {
@@ -410,17 +412,24 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 gsc[t] = sc;
                 atomicAdd(&s_hist[score_bin(sc, bp.lo, bp.inv_w, kNB)], 1u);
             }
-            __syncthreads();
-            if (tid == 0 && i + kFStages < ntiles) {
-                const int j = i + kFStages;
-                const int t0 = t_begin + j * kFThreads;
-                const int nn = min(kFThreads, t_end - t0);
-                mbar_arrive_expect_tx(&s_bar[slot], (uint32_t)nn * 32u);
-                bulk_g2s_stream(s_ring + slot * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[slot],
-                                policy);
-                ++issued;
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_empty[slot])) : "memory");
+            if (tid == 0 && i >= 1 && i - 1 + kFStages < ntiles) {
+                const int pi = i - 1, ps = pi % kFStages;
+                if (!mbar_wait(&s_empty[ps], (uint32_t)(pi / kFStages) & 1u, p.err)) {
+                    s_abort = 1;
+                } else {
+                    const int j = pi + kFStages;
+                    const int t0 = t_begin + j * kFThreads;
+                    const int nn = min(kFThreads, t_end - t0);
+                    mbar_arrive_expect_tx(&s_bar[ps], (uint32_t)nn * 32u);
+                    bulk_g2s_stream(s_ring + ps * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[ps],
+                                    policy);
+                    ++issued;
+                }
             }
         }
+        if (__syncthreads_or(s_abort)) { drain(0); return; }
         for (int i = tid; i < kNB; i += kFThreads) {
             const uint32_t c = s_hist[i];
             if (c) atomicAdd(&p.hist[(int64_t)u * kNB + i], c);
@@ -441,6 +450,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         if (p.k > 0) find_threshold_bin<kFThreads>(s_hist, p.k, &s_bstar, &s_above);
         __syncthreads();
         const int bstar = s_bstar;
+        uint32_t* s_selw = s_hist + 1024;  // own words' "bin > b*" bits (the histogram is consumed)
         int my_above = 0;
         for (int w = w_begin + warp; w < w_end; w += NW) {
             const int t = w * 32 + lane;
@@ -449,8 +459,12 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             if (valid) s = keep_smem ? s_scores[t - t_begin] : __ldcg(gsc_c + t);
             const int bin = score_bin(s, bp.lo, bp.inv_w, kNB);
             const bool tie = valid && bin == bstar;
-            my_above += __popc(__ballot_sync(0xffffffffu, valid && bin > bstar));
-            if (lane == 0) bm[w] = 0u;  // cleared for the exact slow path
+            const uint32_t abv = __ballot_sync(0xffffffffu, valid && bin > bstar);
+            my_above += __popc(abv);
+            if (lane == 0) {
+                bm[w] = 0u;  // cleared for the exact slow path
+                s_selw[w - w_begin] = abv;
+            }
             const uint32_t tmask = __ballot_sync(0xffffffffu, tie);
             if (tmask) {
                 uint32_t base = 0;
@@ -472,7 +486,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
 
     // ================= phase D: ties (redundant per CTA, no barrier) =================
     // winners of the CTA's own token range -> bit lt of s_win
-    uint32_t* s_win = s_hist;                                              // [ceil(ntok/32)] words
+    uint32_t* s_win = s_hist + 1536;                                       // [ceil(ntok/32)] words
     float* s_tk = reinterpret_cast<float*>(s_ring + 64 * 1024);           // tie keys  [kTieCap]
     int* s_ti = reinterpret_cast<int*>(s_ring + 64 * 1024 + kTieCap * 4);  // tie index [kTieCap]
     {
@@ -609,23 +623,40 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         using Scan = cub::BlockScan<int, kFThreads>;
         __shared__ typename Scan::TempStorage scan_tmp;
 
-        // ---- own selected tokens in ascending order ----
-        const int bstar = s_bstar;
+        // ---- own selected tokens in ascending order, from the bits of phase C
+        //      (word w of the CTA covers tokens 32*(w_begin+w) .. +31) and the
+        //      tie winners of phase D (bit lt = token t_begin + lt) ----
         {
-            const int per = (ntok + kFThreads - 1) / kFThreads;
-            const int la = tid * per, lb = min(ntok, la + per);
+            const uint32_t* s_selw = s_hist + 1024;
+            const int nw_own = w_end - w_begin;
+            const int shift0 = t_begin - w_begin * 32;  // 0 except for the first CTA (c0 % 32)
+            // winners in word-aligned form
+            auto win_word = [&](int w) -> uint32_t {
+                // bits of tokens 32*(w_begin+w) + i  <->  lt = 32*w + i - shift0
+                const int lt0 = 32 * w - shift0;
+                uint32_t r = 0u;
+                const int wl = lt0 >> 5, sh = lt0 & 31;  // lt0 may be negative for w = 0
+                if (lt0 >= 0) {
+                    r = s_win[wl] >> sh;
+                    if (sh && wl + 1 < (ntok + 31) / 32) r |= s_win[wl + 1] << (32 - sh);
+                } else {
+                    r = s_win[0] << (-lt0);
+                }
+                return r;
+            };
             int cnt = 0;
-            for (int lt = la; lt < lb; ++lt) {
-                const float sv = keep_smem ? s_scores[lt] : __ldcg(gsc_c + t_begin + lt);
-                cnt += (score_bin(sv, bp.lo, bp.inv_w, kNB) > bstar) || ((s_win[lt >> 5] >> (lt & 31)) & 1u);
+            uint32_t wordsel = 0u;
+            const int w = tid;  // one own word per thread (nw_own <= kFScoreCap/32 + 1 <= 512)
+            if (w < nw_own) {
+                wordsel = s_selw[w] | win_word(w);
+                const int tb = (w_begin + w) * 32;
+                if (tb < p.c0) wordsel &= ~0u << (p.c0 - tb);
+                if (tb + 32 > p.c1) wordsel &= (p.c1 - tb) >= 32 ? ~0u : ((1u << (p.c1 - tb)) - 1u);
+                cnt = __popc(wordsel);
             }
             int pos, total;
             Scan(scan_tmp).ExclusiveSum(cnt, pos, total);
-            for (int lt = la; lt < lb; ++lt) {
-                const float sv = keep_smem ? s_scores[lt] : __ldcg(gsc_c + t_begin + lt);
-                if ((score_bin(sv, bp.lo, bp.inv_w, kNB) > bstar) || ((s_win[lt >> 5] >> (lt & 31)) & 1u))
-                    s_list[pos++] = t_begin + lt;
-            }
+            for (uint32_t b2 = wordsel; b2; b2 &= b2 - 1) s_list[pos++] = (w_begin + w) * 32 + __ffs(b2) - 1;
             if (tid == 0) s_nsel = total;
         }
         const QT* qb = reinterpret_cast<const QT*>(p.q) + (int64_t)b * p.q_stride_b;
@@ -650,8 +681,11 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             for (int i = tid; i < nsel; i += kFThreads)
                 if (off + i < p.k) p.topk_out[(int64_t)u * p.k + off + i] = s_list[i];
         }
-        const int n_sink_here = cj == 0 ? p.n_sink : 0;
-        const int n_loc_here = cj == cn - 1 ? p.n_local : 0;
+        // the unit's sink and local-window rows are spread evenly over its CTAs
+        const int sk0 = (int)((int64_t)p.n_sink * cj / cn), sk1 = (int)((int64_t)p.n_sink * (cj + 1) / cn);
+        const int lc0 = (int)((int64_t)p.n_local * cj / cn), lc1 = (int)((int64_t)p.n_local * (cj + 1) / cn);
+        const int n_sink_here = sk1 - sk0;
+        const int n_loc_here = lc1 - lc0;
         const int nrows = n_sink_here + nsel + n_loc_here;
 
         const KT* kb = reinterpret_cast<const KT*>(p.keys) + (int64_t)b * p.k_stride_b + (int64_t)hkv * p.k_stride_h;
@@ -664,9 +698,9 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             for (int c = tid; c < nr * CH; c += kFThreads) {
                 const int r = c / CH, part = c - r * CH;
                 const int rr = c0r + r;
-                int tok = rr < n_sink_here ? rr
+                int tok = rr < n_sink_here ? sk0 + rr
                         : rr < n_sink_here + nsel ? s_list[rr - n_sink_here]
-                        : p.local_start + (rr - n_sink_here - nsel);
+                        : p.local_start + lc0 + (rr - n_sink_here - nsel);
                 const int64_t t = min(max(tok, 0), p.T_total - 1);
                 cp_async16(s_k + r * D + part * EPC, kb + t * p.k_stride_t + part * EPC);
                 cp_async16(s_v + r * D + part * EPC, vb + t * p.v_stride_t + part * EPC);
