@@ -93,7 +93,7 @@ struct FusedSmem {
     static constexpr int kRing = kFStages * kFTile;    // 96 KB (phase B ring; reused in E)
     static constexpr int kHist = kNB * 4;              // 8 KB
     static constexpr int kScores = kFScoreCap * 4;     // 48 KB
-    static constexpr int kBars = 2 * kFStages * 8;  // full + empty barriers
+    static constexpr int kBars = (2 * kFStages + 3) * 8;  // ring full + empty, 3 phase-A stages
     static constexpr int kTotal = kLut + kRing + kHist + kScores + kBars + 128;
 };
 
@@ -181,12 +181,14 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     const bool keep_smem = ntok <= kFScoreCap;
     const uint8_t* src = p.codes + (int64_t)b * p.codes_stride_b + (int64_t)hkv * p.codes_stride_h;
 
-    uint64_t* s_empty = s_bar + kFStages;  // per-slot "all warps done" barriers
+    uint64_t* s_empty = s_bar + kFStages;      // per-slot "all warps done" barriers
+    uint64_t* s_abar = s_bar + 2 * kFStages;   // phase-A codebook stages
     if (tid == 0) {
         for (int s = 0; s < kFStages; ++s) {
             mbar_init(&s_bar[s], 1);
             mbar_init(&s_empty[s], NW);
         }
+        for (int s = 0; s < 3; ++s) mbar_init(&s_abar[s], 1);
         fence_barrier_init();
     }
     __syncthreads();
@@ -202,34 +204,15 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             bulk_g2s_stream(s_ring + i * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[i], policy);
         }
     }
-    // ---- pull this CTA's whole codebook slice (phase A) toward L2 at once,
-    //      so the codebook stream runs at full depth from t=0 ----
-    if (tid == 0) {
-        const int64_t total = (int64_t)p.U * 32 * 256;
-        const int64_t per = ((total + gridDim.x - 1) / gridDim.x + 7) & ~(int64_t)7;
-        int64_t f = (int64_t)blockIdx.x * per;
-        const int64_t fe = min(total, f + per);
-        while (f < fe) {
-            const int64_t uu = f / 8192;
-            const int64_t seg_end = min(fe, (uu + 1) * 8192);
-            const float* base = p.cb + (int64_t)(p.cb_per_kv_head ? (int)(uu % p.Hkv) : 0) * (32 * 256 * 128);
-            const char* a0 = reinterpret_cast<const char*>(base + (f - uu * 8192) * 128);
-            int64_t bytes = (seg_end - f) * 512;
-            while (bytes > 0) {
-                const uint32_t nb = (uint32_t)(bytes < 65536 ? bytes : 65536);
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a0), "r"(nb) : "memory");
-                a0 += nb;
-                bytes -= nb;
-            }
-            f = seg_end;
-        }
-    }
     int issued = npre;
     auto drain = [&](int from) {
         for (int j = from; j < issued; ++j) mbar_wait(&s_bar[j % kFStages], (uint32_t)(j / kFStages) & 1u, nullptr);
     };
 
     // ================= phase A: LUT build =================
+    // The CTA's codeword rows stream HBM -> shared memory through 3 bulk-copy
+    // stages of 64 rows (32 KB); warp w dots rows 4w..4w+3 of a stage with the
+    // summed query and reduces the 4 dot products with a 6-shuffle transpose.
     {
         // zero the per-call state used after barrier A
         const int64_t nz = (int64_t)p.U * kNB;
@@ -240,11 +223,32 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             p.done_att[i] = 0u;
         }
         const int64_t total = (int64_t)p.U * 32 * 256;       // codeword rows
-        // rows per CTA rounded to a multiple of 8 so a warp batch of 8 rows
-        // never straddles a (unit, m) block of 256 rows
         const int64_t per = ((total + gridDim.x - 1) / gridDim.x + 7) & ~(int64_t)7;
-        const int64_t f_begin = (int64_t)blockIdx.x * per;
+        const int64_t f_begin = min(total, (int64_t)blockIdx.x * per);
         const int64_t f_end = min(total, f_begin + per);
+        const int nchunk = (int)((f_end - f_begin + 63) / 64);
+        auto abuf = [&](int c) -> unsigned char* {
+            const int b3 = c % 3;
+            return b3 == 2 ? reinterpret_cast<unsigned char*>(s_scores) : s_lut + b3 * 32768;
+        };
+        auto issue_chunk = [&](int c) {
+            const int64_t r0 = f_begin + (int64_t)c * 64;
+            const int64_t r1 = min(f_end, r0 + 64);
+            uint64_t* bar = &s_abar[c % 3];
+            mbar_arrive_expect_tx(bar, (uint32_t)((r1 - r0) * 512));
+            int64_t f = r0;
+            unsigned char* dst = abuf(c);
+            while (f < r1) {  // at most one unit boundary inside a chunk
+                const int64_t uu = f / 8192;
+                const int64_t seg = min(r1, (uu + 1) * 8192);
+                const float* base = p.cb + (int64_t)(p.cb_per_kv_head ? (int)(uu % p.Hkv) : 0) * (32 * 256 * 128);
+                bulk_g2s(dst, base + (f - uu * 8192) * 128, (uint32_t)((seg - f) * 512), bar);
+                dst += (seg - f) * 512;
+                f = seg;
+            }
+        };
+        if (tid == 0)
+            for (int c = 0; c < 3 && c < nchunk; ++c) issue_chunk(c);
         // q_sum of the (at most two) units this CTA touches (s_hist is free now)
         float (*s_qsum)[128] = reinterpret_cast<float (*)[128]>(s_hist);
         const int ua = (int)(f_begin / 8192);
@@ -260,32 +264,53 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             s_qsum[slot][d] = acc;
         }
         __syncthreads();
-        for (int64_t f0 = f_begin + warp * 8; f0 < f_end; f0 += NW * 8) {
-            const int uu = (int)(f0 / 8192);
-            const int m = (int)((f0 >> 8) & 31);
-            const int k0 = (int)(f0 & 255);
-            const int hh = uu % p.Hkv;
-            const float* rows = p.cb + (int64_t)(p.cb_per_kv_head ? hh : 0) * (32 * 256 * 128) +
-                                ((int64_t)m * 256 + k0) * 128 + lane * 4;
-            float4 cv[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                cv[j] = (f0 + j < f_end) ? __ldg(reinterpret_cast<const float4*>(rows + j * 128))
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float4 qv = *reinterpret_cast<const float4*>(&s_qsum[uu - ua][lane * 4]);
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                float a = qv.x * cv[j].x;
-                a = fmaf(qv.y, cv[j].y, a);
-                a = fmaf(qv.z, cv[j].z, a);
-                a = fmaf(qv.w, cv[j].w, a);
-                v[j] = a;
+        bool okA = true;
+        for (int c = 0; c < nchunk; ++c) {
+            if (!mbar_wait(&s_abar[c % 3], (uint32_t)(c / 3) & 1u, p.err)) okA = false;
+            if (__syncthreads_or(!okA)) {
+                for (int j = c; j < min(nchunk, c + 3); ++j) mbar_wait(&s_abar[j % 3], (uint32_t)(j / 3) & 1u, nullptr);
+                drain(0);
+                return;
             }
-            const float tot = transpose_reduce8(v, lane);
-            const int kk = k0 + ((lane >> 2) & 7);
-            if ((lane & 3) == 0 && f0 + ((lane >> 2) & 7) < f_end)
-                p.lut[((int64_t)uu * 256 + kk) * 32 + m] = tot;
+            const int64_t r0 = f_begin + (int64_t)c * 64;
+            const int64_t fr = r0 + warp * 4;  // first row of this warp (4 rows, same unit and m)
+            if (fr < f_end) {
+                const int uu = (int)(fr / 8192);
+                const int m = (int)((fr >> 8) & 31);
+                const int k0 = (int)(fr & 255);
+                const float* rows = reinterpret_cast<const float*>(abuf(c)) + (warp * 4) * 128 + lane * 4;
+                const float4 qv = *reinterpret_cast<const float4*>(&s_qsum[uu - ua][lane * 4]);
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float4 cv = (fr + j < f_end) ? *reinterpret_cast<const float4*>(rows + j * 128)
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                    float a = qv.x * cv.x;
+                    a = fmaf(qv.y, cv.y, a);
+                    a = fmaf(qv.z, cv.z, a);
+                    a = fmaf(qv.w, cv.w, a);
+                    v[j] = a;
+                }
+                // transpose-reduce of 4 values: lane l ends with row (l >> 3) & 3
+                const bool b4 = lane & 16, b3 = lane & 8;
+                float w2[2];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const float keep = b4 ? v[2 + j] : v[j];
+                    const float send = b4 ? v[j] : v[2 + j];
+                    w2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                }
+                const float keep = b3 ? w2[1] : w2[0];
+                const float send = b3 ? w2[0] : w2[1];
+                float tot = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 4);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+                const int j = (lane >> 3) & 3;
+                if ((lane & 7) == 0 && fr + j < f_end) p.lut[((int64_t)uu * 256 + k0 + j) * 32 + m] = tot;
+            }
+            __syncthreads();  // stage c fully consumed
+            if (tid == 0 && c + 3 < nchunk) issue_chunk(c + 3);
         }
     }
     if (stamp) p.phase_ns[1] = global_ns();
@@ -389,36 +414,56 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         __shared__ int s_abort;
         if (tid == 0) s_abort = 0;
         __syncthreads();
-        for (int i = 0; i < ntiles; ++i) {
-            const int slot = i % kFStages;
-            if (!mbar_wait(&s_bar[slot], (uint32_t)(i / kFStages) & 1u, p.err)) s_abort = 1;
-            if (*((volatile int*)&s_abort)) break;
-            const int lt = i * kFThreads + tid;
-            const int t = t_begin + lt;
-            if (t < t_end) {
-                const uint32_t* row = reinterpret_cast<const uint32_t*>(s_ring + slot * kFTile + tid * 32);
-                int iacc = 0;
+        // two tiles per iteration: two independent gather chains per thread
+        auto score_row = [&](int slot, int lt) {
+            const uint32_t* row = reinterpret_cast<const uint32_t*>(s_ring + slot * kFTile + tid * 32);
+            int iacc = 0;
 #pragma unroll
-                for (int w = 0; w < 8; ++w) {
-                    const uint32_t cw = row[(w + L) & 7u];
+            for (int w = 0; w < 8; ++w) {
+                const uint32_t cw = row[(w + L) & 7u];
 #pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        const uint32_t a = __byte_perm(cw, off[s], sel[s]);
-                        iacc += *reinterpret_cast<const int*>(s_lut + a + 16 * w);
-                    }
+                for (int s = 0; s < 4; ++s) {
+                    const uint32_t a = __byte_perm(cw, off[s], sel[s]);
+                    iacc += *reinterpret_cast<const int*>(s_lut + a + 16 * w);
                 }
-                const float sc = __fmul_rn(__int2float_rn(iacc), from_fx);
-                if (keep_smem) s_scores[lt] = sc;
-                gsc[t] = sc;
-                atomicAdd(&s_hist[score_bin(sc, bp.lo, bp.inv_w, kNB)], 1u);
+            }
+            return __fmul_rn(__int2float_rn(iacc), from_fx);
+        };
+        auto commit_score = [&](int lt, float sc) {
+            if (keep_smem) s_scores[lt] = sc;
+            gsc[t_begin + lt] = sc;
+            atomicAdd(&s_hist[score_bin(sc, bp.lo, bp.inv_w, kNB)], 1u);
+        };
+        for (int i = 0; i < ntiles; i += 2) {
+            const bool two = i + 1 < ntiles;
+            const int s0 = i % kFStages, s1 = (i + 1) % kFStages;
+            if (!mbar_wait(&s_bar[s0], (uint32_t)(i / kFStages) & 1u, p.err)) s_abort = 1;
+            if (two && !mbar_wait(&s_bar[s1], (uint32_t)((i + 1) / kFStages) & 1u, p.err)) s_abort = 1;
+            if (*((volatile int*)&s_abort)) break;
+            const int lt0 = i * kFThreads + tid, lt1 = lt0 + kFThreads;
+            const bool v0 = t_begin + lt0 < t_end, v1 = two && t_begin + lt1 < t_end;
+            if (v1) {
+                const float a0 = score_row(s0, lt0);
+                const float a1 = score_row(s1, lt1);
+                commit_score(lt0, a0);
+                commit_score(lt1, a1);
+            } else if (v0) {
+                commit_score(lt0, score_row(s0, lt0));
             }
             __syncwarp();
-            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_empty[slot])) : "memory");
-            if (tid == 0 && i >= 1 && i - 1 + kFStages < ntiles) {
-                const int pi = i - 1, ps = pi % kFStages;
-                if (!mbar_wait(&s_empty[ps], (uint32_t)(pi / kFStages) & 1u, p.err)) {
-                    s_abort = 1;
-                } else {
+            if (lane == 0) {
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_empty[s0])) : "memory");
+                if (two) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_empty[s1])) : "memory");
+            }
+            if (tid == 0) {
+                // refill the slots of the two tiles consumed in the previous iteration
+                for (int pi = i - 2; pi < i; ++pi) {
+                    if (pi < 0 || pi + kFStages >= ntiles) continue;
+                    const int ps = pi % kFStages;
+                    if (!mbar_wait(&s_empty[ps], (uint32_t)(pi / kFStages) & 1u, p.err)) {
+                        s_abort = 1;
+                        break;
+                    }
                     const int j = pi + kFStages;
                     const int t0 = t_begin + j * kFThreads;
                     const int nn = min(kFThreads, t_end - t0);
@@ -442,10 +487,11 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     // ================= phase C: select (threshold bin, own counts, ties) =================
     uint32_t* bm = p.bitmap + (int64_t)u * p.bm_stride;
     const float* gsc_c = p.sel_scores + (int64_t)u * p.sel_stride;
-    __shared__ int s_cnt_above, s_nsel, s_win_before;
+    __shared__ int s_cnt_above, s_nsel, s_win_before, s_ntie_loc, s_tie_base;
     {
+        float2* s_tloc = reinterpret_cast<float2*>(s_lut);  // this CTA's tie-bin tokens (<= kTieCap)
         for (int i = tid; i < kNB; i += kFThreads) s_hist[i] = __ldcg(p.hist + (int64_t)u * kNB + i);
-        if (tid == 0) { s_bstar = kNB; s_above = 0; s_cnt_above = 0; }
+        if (tid == 0) { s_bstar = kNB; s_above = 0; s_cnt_above = 0; s_ntie_loc = 0; }
         __syncthreads();
         if (p.k > 0) find_threshold_bin<kFThreads>(s_hist, p.k, &s_bstar, &s_above);
         __syncthreads();
@@ -467,19 +513,29 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             }
             const uint32_t tmask = __ballot_sync(0xffffffffu, tie);
             if (tmask) {
-                uint32_t base = 0;
-                if (lane == 0) base = atomicAdd(&p.tie_count[u], (uint32_t)__popc(tmask));
+                int base = 0;
+                if (lane == 0) base = atomicAdd(&s_ntie_loc, __popc(tmask));
                 base = __shfl_sync(0xffffffffu, base, 0);
                 if (tie) {
-                    const uint32_t pos = base + __popc(tmask & ((1u << lane) - 1u));
-                    if (pos < (uint32_t)kTieCap)
-                        p.tie_buf[(int64_t)u * kTieCap + pos] = make_float2(s, __int_as_float(t));
+                    const int pos = base + __popc(tmask & ((1u << lane) - 1u));
+                    if (pos < kTieCap) s_tloc[pos] = make_float2(s, __int_as_float(t));
                 }
             }
         }
         if (lane == 0 && my_above) atomicAdd(&s_cnt_above, my_above);
         __syncthreads();
-        if (tid == 0) p.cta_count[blockIdx.x] = (uint32_t)s_cnt_above;
+        if (tid == 0) {
+            p.cta_count[blockIdx.x] = (uint32_t)s_cnt_above;
+            s_tie_base = s_ntie_loc ? (int)atomicAdd(&p.tie_count[u], (uint32_t)s_ntie_loc) : 0;
+        }
+        __syncthreads();
+        // (a CTA with more than kTieCap ties makes the unit overflow: the
+        // reservation above counts them all, only the copy is capped)
+        const int nloc = min(s_ntie_loc, kTieCap);
+        for (int i = tid; i < nloc; i += kFThreads) {
+            const int pos = s_tie_base + i;
+            if (pos < kTieCap) p.tie_buf[(int64_t)u * kTieCap + pos] = s_tloc[i];
+        }
     }
     if (stamp) p.phase_ns[5] = global_ns();
     if (!grid_barrier(p.bar, p.err)) return;
@@ -708,7 +764,59 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             cp_async_commit();
             cp_async_wait<0>();
             __syncthreads();
-            // logits (log2 domain): warp per row, lane per 4 dims
+            // logits (log2 domain)
+            if (p.G == 4) {
+                // warp handles rows 4w..4w+3 (+64 per pass); lane covers dims 4l..4l+3;
+                // the 16 (row, head) partial dots are reduced by one 16-way transpose
+                float4 qv[4];
+#pragma unroll
+                for (int g = 0; g < 4; ++g) qv[g] = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
+                for (int r0w = warp * 4; r0w < nr; r0w += NW * 4) {
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float4 kv = (r0w + j < nr) ? Vec4<KT>::load(s_k + (r0w + j) * D + lane * 4)
+                                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int g = 0; g < 4; ++g) {
+                            float a = qv[g].x * kv.x;
+                            a = fmaf(qv[g].y, kv.y, a);
+                            a = fmaf(qv[g].z, kv.z, a);
+                            a = fmaf(qv[g].w, kv.w, a);
+                            v[j * 4 + g] = a;
+                        }
+                    }
+                    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+                    float x8[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float keep = b4 ? v[8 + j] : v[j];
+                        const float send = b4 ? v[j] : v[8 + j];
+                        x8[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                    }
+                    float x4[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float keep = b3 ? x8[4 + j] : x8[j];
+                        const float send = b3 ? x8[j] : x8[4 + j];
+                        x4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                    }
+                    float x2[2];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const float keep = b2 ? x4[2 + j] : x4[j];
+                        const float send = b2 ? x4[j] : x4[2 + j];
+                        x2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                    }
+                    const float keep = b1 ? x2[1] : x2[0];
+                    const float send = b1 ? x2[0] : x2[1];
+                    float tot = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+                    tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+                    const int idx = (lane >> 1) & 15;  // = 4 * row + head
+                    const int rr = r0w + (idx >> 2);
+                    if ((lane & 1) == 0 && rr < nr) s_p[(idx & 3) * R + rr] = tot * p.scale_log2;
+                }
+            } else
             for (int r = warp; r < nr; r += NW) {
                 const float4 kv = Vec4<KT>::load(s_k + r * D + lane * 4);
                 for (int g = 0; g < p.G; ++g) {
@@ -748,35 +856,52 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 }
             }
             __syncthreads();
-            // P.V: thread -> output (g, d), rows unrolled by 2
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int o = tid + h * kFThreads;
-                if (o < p.G * D) {
-                    const int g = o >> 7, d = o & (D - 1);
+            // P.V: thread -> (half, head g, dim pair dp); rows interleaved by half
+            {
+                const int npairs = p.G * (D / 2);
+                const int nhalf = npairs <= kFThreads / 2 ? 2 : 1;
+                const int pair = tid % (kFThreads / nhalf);
+                const int half = tid / (kFThreads / nhalf);
+                float x = 0.f, y = 0.f;
+                if (pair < npairs) {
+                    const int g = pair / (D / 2), dp = pair - g * (D / 2);
                     const float* pg = s_p + g * R;
-                    float x0 = 0.f, x1 = 0.f;
-                    int r = 0;
-                    for (; r + 2 <= nr; r += 2) {
-                        x0 = fmaf(pg[r], to_f32(s_v[r * D + d]), x0);
-                        x1 = fmaf(pg[r + 1], to_f32(s_v[(r + 1) * D + d]), x1);
+                    for (int r = half; r < nr; r += nhalf) {
+                        const float2 vv = Vec4<KT>::load2(s_v + r * D + 2 * dp);
+                        x = fmaf(pg[r], vv.x, x);
+                        y = fmaf(pg[r], vv.y, y);
                     }
-                    if (r < nr) x0 = fmaf(pg[r], to_f32(s_v[r * D + d]), x0);
-                    if (h == 0) acc0 = fmaf(acc0, s_al[g], x0 + x1);
-                    else acc1 = fmaf(acc1, s_al[g], x0 + x1);
+                }
+                float* s_red = s_q + 4 * D;  // scratch for the second half (free rows of s_q)
+                if (nhalf == 2 && half == 1 && pair < npairs) {
+                    s_red[2 * pair] = x;
+                    s_red[2 * pair + 1] = y;
+                }
+                __syncthreads();
+                if (half == 0 && pair < npairs) {
+                    if (nhalf == 2) {
+                        x += s_red[2 * pair];
+                        y += s_red[2 * pair + 1];
+                    }
+                    const int g = pair / (D / 2);
+                    acc0 = fmaf(acc0, s_al[g], x);
+                    acc1 = fmaf(acc1, s_al[g], y);
                 }
             }
             __syncthreads();
         }
-        // partial state of this CTA
+        // partial state of this CTA: (half 0, pair) threads own dims 2dp, 2dp+1
         float* part = p.part + ((int64_t)u * p.max_split + cj) * p.G * (2 + D);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int o = tid + h * kFThreads;
-            if (o < p.G * D) {
-                const int g = o >> 7, d = o & (D - 1);
-                part[g * (2 + D) + 2 + d] = h == 0 ? acc0 : acc1;
-                if (d == 0) {
+        {
+            const int npairs = p.G * (D / 2);
+            const int nhalf = npairs <= kFThreads / 2 ? 2 : 1;
+            const int pair = tid % (kFThreads / nhalf);
+            const int half = tid / (kFThreads / nhalf);
+            if (half == 0 && pair < npairs) {
+                const int g = pair / (D / 2), dp = pair - g * (D / 2);
+                part[g * (2 + D) + 2 + 2 * dp] = acc0;
+                part[g * (2 + D) + 3 + 2 * dp] = acc1;
+                if (dp == 0) {
                     part[g * (2 + D)] = s_m[g];
                     part[g * (2 + D) + 1] = s_l[g];
                 }
@@ -794,40 +919,80 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         // merge the cn slice states of the unit
         const float* pu = p.part + (int64_t)u * p.max_split * p.G * (2 + D);
         const int64_t sstride = (int64_t)p.G * (2 + D);
-        for (int g = warp; g < p.G; g += NW) {
-            float M = -INFINITY;
-            for (int s = lane; s < cn; s += 32) M = fmaxf(M, __ldcg(pu + s * sstride + g * (2 + D)));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            float Lsum = 0.f;
-            for (int s = lane; s < cn; s += 32) {
-                const float* ps = pu + s * sstride + g * (2 + D);
-                const float f = exp2f(__ldcg(ps) - M);
-                s_w[g * cn + s] = f;
-                Lsum = fmaf(__ldcg(ps + 1), f, Lsum);
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
-            __syncwarp();
-            const float invL = 1.f / Lsum;
-            for (int s = lane; s < cn; s += 32) s_w[g * cn + s] *= invL;
-        }
-        __syncthreads();
         OT* ob = reinterpret_cast<OT*>(p.out) + (int64_t)b * p.out_stride_b;
-        for (int o = tid; o < p.G * D; o += kFThreads) {
-            const int g = o / D, d = o - g * D;
-            const float* pg = pu + g * (2 + D) + 2 + d;
-            float acc = 0.f;
-            int s = 0;
-            for (; s + 8 <= cn; s += 8) {
-                float vv[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) vv[j] = __ldcg(pg + (s + j) * sstride);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc = fmaf(vv[j], s_w[g * cn + s + j], acc);
+        constexpr int MAXS = 24;
+        if (cn <= MAXS) {
+            // one round trip: every slice value a thread needs is loaded at once
+            float* s_ml2 = s_w;  // [cn][G][2] (m, l)
+            for (int i = tid; i < cn * p.G * 2; i += kFThreads) {
+                const int sl = i / (p.G * 2), rem = i - sl * p.G * 2;
+                s_ml2[i] = __ldcg(pu + sl * sstride + (rem >> 1) * (2 + D) + (rem & 1));
             }
-            for (; s < cn; ++s) acc = fmaf(__ldcg(pg + s * sstride), s_w[g * cn + s], acc);
-            ob[(int64_t)(hkv * p.G + g) * p.out_stride_h + d] = from_f32<OT>(acc);
+            auto merge_out = [&](int o, const float* av) {
+                const int g = o / D, d = o - g * D;
+                float M = -INFINITY;
+                for (int sl = 0; sl < cn; ++sl) M = fmaxf(M, s_ml2[(sl * p.G + g) * 2]);
+                float L = 0.f, acc = 0.f;
+#pragma unroll
+                for (int sl = 0; sl < MAXS; ++sl) {
+                    if (sl < cn) {
+                        const float f = exp2f(s_ml2[(sl * p.G + g) * 2] - M);
+                        L = fmaf(s_ml2[(sl * p.G + g) * 2 + 1], f, L);
+                        acc = fmaf(av[sl], f, acc);
+                    }
+                }
+                ob[(int64_t)(hkv * p.G + g) * p.out_stride_h + d] = from_f32<OT>(acc / L);
+            };
+            auto load_av = [&](int o, float* av) {
+                const int g = o / D, d = o - g * D;
+#pragma unroll
+                for (int sl = 0; sl < MAXS; ++sl)
+                    av[sl] = sl < cn ? __ldcg(pu + sl * sstride + g * (2 + D) + 2 + d) : 0.f;
+            };
+            float av[MAXS];
+            const bool has0 = tid < p.G * D;
+            if (has0) load_av(tid, av);  // issued before the barrier: overlaps the m/l loads
+            __syncthreads();
+            if (has0) merge_out(tid, av);
+            for (int o = tid + kFThreads; o < p.G * D; o += kFThreads) {
+                load_av(o, av);
+                merge_out(o, av);
+            }
+        } else {
+            for (int g = warp; g < p.G; g += NW) {
+                float M = -INFINITY;
+                for (int sl = lane; sl < cn; sl += 32) M = fmaxf(M, __ldcg(pu + sl * sstride + g * (2 + D)));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+                float Lsum = 0.f;
+                for (int sl = lane; sl < cn; sl += 32) {
+                    const float* ps = pu + sl * sstride + g * (2 + D);
+                    const float f = exp2f(__ldcg(ps) - M);
+                    s_w[g * cn + sl] = f;
+                    Lsum = fmaf(__ldcg(ps + 1), f, Lsum);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
+                __syncwarp();
+                const float invL = 1.f / Lsum;
+                for (int sl = lane; sl < cn; sl += 32) s_w[g * cn + sl] *= invL;
+            }
+            __syncthreads();
+            for (int o = tid; o < p.G * D; o += kFThreads) {
+                const int g = o / D, d = o - g * D;
+                const float* pg = pu + g * (2 + D) + 2 + d;
+                float acc = 0.f;
+                int sl = 0;
+                for (; sl + 8 <= cn; sl += 8) {
+                    float vv[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) vv[j] = __ldcg(pg + (sl + j) * sstride);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc = fmaf(vv[j], s_w[g * cn + sl + j], acc);
+                }
+                for (; sl < cn; ++sl) acc = fmaf(__ldcg(pg + sl * sstride), s_w[g * cn + sl], acc);
+                ob[(int64_t)(hkv * p.G + g) * p.out_stride_h + d] = from_f32<OT>(acc);
+            }
         }
         if (p.phase_ns && tid == 0) atomicMax(&p.phase_ns[7], global_ns());
     }
