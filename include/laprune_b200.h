@@ -117,6 +117,17 @@ typedef struct lp_sparse_decode_args {
     /* optional uint64[8] of device global-timer stamps (ns) at the phase
      * boundaries of the fused single-kernel path (diagnostics).  NULL: none. */
     uint64_t* phase_ns;
+    /* optional L2 prefetch of the NEXT call's inputs, issued by the fused
+     * kernel once its own HBM streams are done (while its selection and
+     * attention stages leave HBM idle): region i covers prefetch_count[i]
+     * blocks of prefetch_bytes[i] bytes starting every prefetch_stride[i]
+     * bytes from prefetch_ptr[i] (e.g. the next layer's codebooks and the
+     * [0,T) rows of every KV head of its code cache).  Bytes and addresses
+     * should be multiples of 16.  NULL pointers / zero bytes: nothing. */
+    const void* prefetch_ptr[2];
+    int64_t prefetch_bytes[2];
+    int64_t prefetch_count[2];
+    int64_t prefetch_stride[2];
 } lp_sparse_decode_args;
 
 /* flags of lp_sparse_decode_args */

@@ -37,6 +37,8 @@ class SparseDecodeArgs(ctypes.Structure):
         ("out", _c_p), ("out_stride_b", _c_i64), ("out_stride_h", _c_i64),
         ("head_scores", _c_p), ("topk_out", _c_p), ("stage_events", _c_p),
         ("flags", _c_i32), ("_pad3", _c_i32), ("phase_ns", _c_p),
+        ("prefetch_ptr", _c_p * 2), ("prefetch_bytes", _c_i64 * 2),
+        ("prefetch_count", _c_i64 * 2), ("prefetch_stride", _c_i64 * 2),
     ]
 
 

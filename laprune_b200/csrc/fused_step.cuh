@@ -86,7 +86,30 @@ struct FusedParams {
     uint32_t* bar;       // grid barrier word (self-resetting)
     uint32_t* err;
     unsigned long long* phase_ns;  // optional [8] globaltimer stamps (CTA 0)
+    const char* pf_ptr[2];         // L2 prefetch of the next call's inputs
+    int64_t pf_bytes[2], pf_count[2], pf_stride[2];
 };
+
+// This CTA's share of an L2 prefetch region (count blocks of `bytes` every
+// `stride` bytes), split evenly over the grid in 16-byte granules.
+__device__ __forceinline__ void prefetch_share(const char* ptr, int64_t bytes, int64_t count, int64_t stride) {
+    if (!ptr || bytes <= 0 || count <= 0) return;
+    const int64_t total = bytes * count;
+    const int64_t per = ((total + gridDim.x - 1) / gridDim.x + 15) & ~(int64_t)15;
+    int64_t a = (int64_t)blockIdx.x * per;
+    const int64_t e = min(total, a + per);
+    while (a < e) {
+        const int64_t blk = a / bytes, off = a - blk * bytes;
+        int64_t n = min(e - a, bytes - off);
+        n = min(n, (int64_t)65536);
+        const int64_t n16 = n & ~(int64_t)15;
+        if (n16 > 0) {
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr + blk * stride + off), "r"((uint32_t)n16)
+                         : "memory");
+        }
+        a += n > 0 ? n : 16;
+    }
+}
 
 struct FusedSmem {
     static constexpr int kLut = 256 * 64 * 4;          // 64 KB (phase B table; reused)
@@ -119,8 +142,8 @@ __device__ __forceinline__ bool grid_barrier(uint32_t* bar, uint32_t* err) {
     if (threadIdx.x == 0) {
         const uint32_t n = gridDim.x;
         const uint32_t inc = blockIdx.x == 0 ? (0x80000000u - (n - 1u)) : 1u;
-        __threadfence();
-        const uint32_t old = atomicAdd(bar, inc);
+        uint32_t old;
+        asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(bar), "r"(inc) : "memory");
         int ok = 1;
         const long long t0 = clock64();
         while (((ld_acquire_u32(bar) ^ old) & 0x80000000u) == 0u) {
@@ -159,6 +182,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     uint64_t* s_bar = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(s_scores) + S::kScores);
 
     __shared__ BinParams s_bp;
+    __shared__ __align__(16) float s_qu[8 * 128];  // the unit's G query rows (fp32), loaded at start
     __shared__ int s_shift, s_bstar, s_above, s_flag;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -208,6 +232,11 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     auto drain = [&](int from) {
         for (int j = from; j < issued; ++j) mbar_wait(&s_bar[j % kFStages], (uint32_t)(j / kFStages) & 1u, nullptr);
     };
+
+    for (int i = tid; i < p.G * 128; i += kFThreads) {
+        const int g = i >> 7, d = i & 127;
+        s_qu[i] = to_f32(reinterpret_cast<const QT*>(p.q)[(int64_t)b * p.q_stride_b + (int64_t)(hkv * p.G + g) * p.q_stride_h + d]);
+    }
 
     // ================= phase A: LUT build =================
     // The CTA's codeword rows stream HBM -> shared memory through 3 bulk-copy
@@ -483,6 +512,10 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     if (stamp) p.phase_ns[3] = global_ns();
     if (!grid_barrier(p.bar, p.err)) return;
     if (stamp) p.phase_ns[4] = global_ns();
+    if (tid == 0) {
+        prefetch_share(p.pf_ptr[0], p.pf_bytes[0], p.pf_count[0], p.pf_stride[0]);
+        prefetch_share(p.pf_ptr[1], p.pf_bytes[1], p.pf_count[1], p.pf_stride[1]);
+    }
 
     // ================= phase C: select (threshold bin, own counts, ties) =================
     uint32_t* bm = p.bitmap + (int64_t)u * p.bm_stride;
@@ -667,8 +700,9 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         constexpr int D = 128;
         constexpr int R = kFMaxRows;
         int* s_list = reinterpret_cast<int*>(s_lut);                                 // [<= kFScoreCap]
-        float* s_q = reinterpret_cast<float*>(s_lut + kFScoreCap * 4);              // [8][128]
-        float* s_p = s_q + 8 * D;                                                    // [8][R]
+        float* s_q = s_qu;                                                           // [8][128]
+        float* s_red = reinterpret_cast<float*>(s_lut + kFScoreCap * 4);            // [512] P.V half sums
+        float* s_p = s_red + 512;                                                    // [8][R]
         float* s_m = s_p + 8 * R;                                                    // [8] running max
         float* s_l = s_m + 8;                                                        // [8] running sum
         float* s_al = s_l + 8;                                                       // [8] rescale
@@ -714,11 +748,6 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             Scan(scan_tmp).ExclusiveSum(cnt, pos, total);
             for (uint32_t b2 = wordsel; b2; b2 &= b2 - 1) s_list[pos++] = (w_begin + w) * 32 + __ffs(b2) - 1;
             if (tid == 0) s_nsel = total;
-        }
-        const QT* qb = reinterpret_cast<const QT*>(p.q) + (int64_t)b * p.q_stride_b;
-        for (int i = tid; i < p.G * D; i += kFThreads) {
-            const int g = i / D, d = i - g * D;
-            s_q[g * D + d] = to_f32(qb[(int64_t)(hkv * p.G + g) * p.q_stride_h + d]);
         }
         if (tid < 8) { s_m[tid] = -INFINITY; s_l[tid] = 0.f; }
         __syncthreads();
@@ -866,13 +895,31 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 if (pair < npairs) {
                     const int g = pair / (D / 2), dp = pair - g * (D / 2);
                     const float* pg = s_p + g * R;
-                    for (int r = half; r < nr; r += nhalf) {
+                    float x1 = 0.f, y1 = 0.f;
+                    int r = half;
+                    for (; r + 3 * nhalf < nr; r += 4 * nhalf) {
+                        const float2 v0 = Vec4<KT>::load2(s_v + r * D + 2 * dp);
+                        const float2 v1 = Vec4<KT>::load2(s_v + (r + nhalf) * D + 2 * dp);
+                        const float2 v2 = Vec4<KT>::load2(s_v + (r + 2 * nhalf) * D + 2 * dp);
+                        const float2 v3 = Vec4<KT>::load2(s_v + (r + 3 * nhalf) * D + 2 * dp);
+                        const float p0 = pg[r], p1 = pg[r + nhalf], p2 = pg[r + 2 * nhalf], p3 = pg[r + 3 * nhalf];
+                        x = fmaf(p0, v0.x, x);
+                        y = fmaf(p0, v0.y, y);
+                        x1 = fmaf(p1, v1.x, x1);
+                        y1 = fmaf(p1, v1.y, y1);
+                        x = fmaf(p2, v2.x, x);
+                        y = fmaf(p2, v2.y, y);
+                        x1 = fmaf(p3, v3.x, x1);
+                        y1 = fmaf(p3, v3.y, y1);
+                    }
+                    for (; r < nr; r += nhalf) {
                         const float2 vv = Vec4<KT>::load2(s_v + r * D + 2 * dp);
                         x = fmaf(pg[r], vv.x, x);
                         y = fmaf(pg[r], vv.y, y);
                     }
+                    x += x1;
+                    y += y1;
                 }
-                float* s_red = s_q + 4 * D;  // scratch for the second half (free rows of s_q)
                 if (nhalf == 2 && half == 1 && pair < npairs) {
                     s_red[2 * pair] = x;
                     s_red[2 * pair + 1] = y;

@@ -327,6 +327,12 @@ static int launch_fused(const lp_sparse_decode_args* a, const Plan& p, cudaStrea
     fp.bar = p.bar;
     fp.err = p.err;
     fp.phase_ns = reinterpret_cast<unsigned long long*>(a->phase_ns);
+    for (int i = 0; i < 2; ++i) {
+        fp.pf_ptr[i] = static_cast<const char*>(a->prefetch_ptr[i]);
+        fp.pf_bytes[i] = a->prefetch_bytes[i];
+        fp.pf_count[i] = a->prefetch_count[i];
+        fp.pf_stride[i] = a->prefetch_stride[i];
+    }
     auto kernel = sparse_decode_fused_kernel<QT, KT, OT>;
     static bool opt[64] = {false};
     int rc = smem_opt_in(kernel, FusedSmem::kTotal, dev, opt);

@@ -66,9 +66,22 @@ def num_candidates(T_codes: int, T_total: int, sink: int, local: int) -> int:
     return hi - lo
 
 
+def prefetch_regions(codebooks: torch.Tensor, codes: torch.Tensor, T_codes: Optional[int] = None):
+    """L2-prefetch regions covering one layer's LUT inputs: its codebooks
+    and the valid [0, T_codes) rows of every (batch, KV head) of its code
+    cache.  Pass them as ``prefetch`` of the PREVIOUS call so they are
+    fetched while that call's selection/attention stages leave HBM idle."""
+    c = codes if codes.dim() == 4 else codes.unsqueeze(0)
+    T = c.shape[2] if T_codes is None else int(T_codes)
+    regs = [(codebooks.data_ptr(), codebooks.numel() * codebooks.element_size(), 1, 0)]
+    if c.stride(0) == c.shape[1] * c.stride(1):
+        regs.append((c.data_ptr(), T * c.stride(2), c.shape[0] * c.shape[1], c.stride(1)))
+    return regs
+
+
 def build_args(q, codebooks, codes, keys=None, vals=None, *, topk: int, T_codes=None, T_total=None,
                sink: int = 4, local: int = 64, select: str = "kv_group", scale=None,
-               out=None, head_scores=None, topk_out=None) -> SparseDecodeArgs:
+               out=None, head_scores=None, topk_out=None, prefetch=None) -> SparseDecodeArgs:
     """Validate tensors and fill the C argument struct (no launch)."""
     if q.dim() == 2:
         q = q.unsqueeze(0)
@@ -140,6 +153,12 @@ def build_args(q, codebooks, codes, keys=None, vals=None, *, topk: int, T_codes=
         a.head_scores = head_scores.data_ptr()
     if topk_out is not None:
         a.topk_out = topk_out.data_ptr()
+    for i, reg in enumerate((prefetch or [])[:2]):
+        ptr, nbytes, count, stride = reg
+        a.prefetch_ptr[i] = int(ptr)
+        a.prefetch_bytes[i] = int(nbytes)
+        a.prefetch_count[i] = int(count)
+        a.prefetch_stride[i] = int(stride)
     return a
 
 
@@ -151,7 +170,8 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
                   out_dtype: Optional[torch.dtype] = None, return_topk: bool = False,
                   return_head_scores: bool = False, attention: bool = True,
                   ws: Optional[torch.Tensor] = None, stage_events=None,
-                  fused: Optional[bool] = None, phase_ns: Optional[torch.Tensor] = None) -> SparseDecodeResult:
+                  fused: Optional[bool] = None, phase_ns: Optional[torch.Tensor] = None,
+                  prefetch=None) -> SparseDecodeResult:
     """One sparse decode step of one layer (see lp_sparse_decode).
 
     q [B,Hq,D] (or [Hq,D]); codebooks fp32 [Hkv,M,K,D] or [M,K,D]; codes uint8
@@ -164,6 +184,8 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
     kernel when the geometry allows (KV-group selection with attention);
     ``fused=False`` forces the multi-kernel path.  ``phase_ns`` (int64 [8]
     on the device) receives global-timer stamps of the fused kernel phases.
+    ``prefetch`` (see :func:`prefetch_regions`) names up to two regions of
+    the NEXT call's inputs to pull into L2 during this call's tail.
     """
     squeeze = q.dim() == 2
     q3 = q.unsqueeze(0) if squeeze else q
@@ -183,7 +205,7 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
     hs = torch.zeros((B, Hq, T_codes_v), dtype=torch.float32, device=dev) if return_head_scores else None
     a = build_args(q3, codebooks, codes, keys, vals, topk=topk, T_codes=T_codes, T_total=T_total,
                    sink=sink, local=local, select=select, scale=scale, out=o, head_scores=hs,
-                   topk_out=tk)
+                   topk_out=tk, prefetch=prefetch)
     if fused is False:
         a.flags |= _lib.LP_FLAG_NO_FUSED
     if phase_ns is not None:
