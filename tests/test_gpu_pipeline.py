@@ -228,12 +228,11 @@ def test_workspace_shared_across_geometries():
 
 def test_prefetch_of_next_inputs_does_not_change_results():
     dev = _dev()
-    a = [t.to(dev) for t in _rand_case(21, 1, 8, 4, 30000)]
-    b = [t.to(dev) for t in _rand_case(22, 1, 8, 4, 30000)]
-    q, C, codes, K, V = a
+    C, codes, K, V, q = [t.to(dev) for t in _rand_case(21, 1, 8, 4, 30000)]
+    C2, codes2, _, _, _ = [t.to(dev) for t in _rand_case(22, 1, 8, 4, 30000)]
     r0 = ops.sparse_decode(q, C, codes, K, V, topk=600, sink=4, local=64, return_topk=True)
     r1 = ops.sparse_decode(q, C, codes, K, V, topk=600, sink=4, local=64, return_topk=True,
-                           prefetch=ops.prefetch_regions(b[1], b[2]))
+                           prefetch=ops.prefetch_regions(C2, codes2))
     torch.cuda.synchronize()
     assert torch.equal(r0.topk, r1.topk) and torch.equal(r0.out, r1.out)
     assert ops.device_errors(device=dev) & 1 == 0
