@@ -238,14 +238,9 @@ def run_ours(args):
         q = torch.randn((HQ, D), generator=g, device=dev).to(torch.bfloat16)
         out = torch.empty((1, HQ, D), dtype=torch.bfloat16, device=dev)
         layers.append({"C": C, "codes": codes, "keys": keys, "vals": vals, "q": q, "out": out})
-    # each layer's call prefetches the next layer's codebooks and codes into
-    # L2 while its own selection/attention tail runs (the last layer prefetches
-    # layer 0 of the next token)
-    for li, L in enumerate(layers):
-        nxt = layers[(li + 1) % N_LAYERS]
+    for L in layers:
         L["args"] = ops.build_args(L["q"], L["C"], L["codes"], L["keys"], L["vals"], topk=TOPK,
-                                   sink=SINK, local=LOCAL, out=L["out"],
-                                   prefetch=ops.prefetch_regions(nxt["C"], nxt["codes"]))
+                                   sink=SINK, local=LOCAL, out=L["out"])
     need = max(lib.lp_sparse_decode_workspace_size(ctypes.byref(L["args"])) for L in layers)
     ws = ops.workspace(need, dev, tag="bench")
     stream = torch.cuda.current_stream(dev)
@@ -329,10 +324,8 @@ def run_ours(args):
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
         for li, L in enumerate(layers):
-            nxt = layers[(li + 1) % N_LAYERS]
             ops.sparse_decode(q_dev[li], L["C"], L["codes"], L["keys"], L["vals"], topk=TOPK,
-                              sink=SINK, local=LOCAL, out=out_dev[li:li + 1], ws=ws,
-                              prefetch=ops.prefetch_regions(nxt["C"], nxt["codes"]))
+                              sink=SINK, local=LOCAL, out=out_dev[li:li + 1], ws=ws)
         out_host.copy_(out_dev, non_blocking=True)
 
     for _ in range(max(1, min(args.warmup, 3))):

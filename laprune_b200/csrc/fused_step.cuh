@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     if (stamp) p.phase_ns[3] = global_ns();
     if (!grid_barrier(p.bar, p.err)) return;
     if (stamp) p.phase_ns[4] = global_ns();
-    if (tid == 0) {
+    if (tid == kFThreads - 32) {  // a lane off the select critical path
         prefetch_share(p.pf_ptr[0], p.pf_bytes[0], p.pf_count[0], p.pf_stride[0]);
         prefetch_share(p.pf_ptr[1], p.pf_bytes[1], p.pf_count[1], p.pf_stride[1]);
     }
