@@ -15,9 +15,9 @@
  *     can be captured in CUDA graphs (except where noted).
  *   - The caller owns every buffer, including `workspace` (size from the
  *     matching *_workspace_size function, 256-byte aligned, device memory,
- *     ZERO-FILLED before its first use).  Its first 512 bytes hold state
- *     that persists between calls (device error bits, a grid-barrier word),
- *     at the same offsets for every geometry; the rest is scratch.  A
+ *     ZERO-FILLED before its first use).  Its first 2048 bytes hold state
+ *     that persists between calls (device error bits, barrier words), at
+ *     the same offsets for every geometry; the rest is scratch.  A
  *     workspace must not be shared by calls that may run concurrently.
  */
 #ifndef LAPRUNE_B200_H
@@ -132,6 +132,8 @@ typedef struct lp_sparse_decode_args {
 
 /* flags of lp_sparse_decode_args */
 #define LP_FLAG_NO_FUSED 1 /* use the multi-kernel path even when the fused kernel applies */
+#define LP_FLAG_EXCHANGE_SELECT 2 /* fused kernel: settle the top-k through the tie exchange,
+                                    not the published-candidate union */
 
 /* Workspace bytes needed by lp_sparse_decode for this geometry. */
 size_t lp_sparse_decode_workspace_size(const lp_sparse_decode_args* a);
@@ -150,7 +152,7 @@ int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t wor
 
 /* Reads and clears the device-side error bits accumulated in `workspace`
  * by earlier calls (synchronises `stream`); after a wait timeout it also
- * restores the workspace's grid-barrier word. */
+ * restores the workspace's barrier words. */
 int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
                           uint32_t* bits_out);
 

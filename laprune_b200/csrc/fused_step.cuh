@@ -11,30 +11,36 @@
 // -> ties -> row list -> gather -> merge).  Separate kernels pay a launch
 // ramp, a tail and a global round trip for every intermediate; here the
 // intermediates stay in shared memory and the stages are separated by
-// three grid barriers.
+// four barriers among the CTAs of one unit.  Units never wait for each
+// other, so a unit whose LUT is ready streams its codes while others are
+// still building theirs.
 //
-// Phases (CTA c owns one selection unit u = (b, kv head) for phases B-E):
-//   A  LUT build: the CTAs split the U*32*256 codeword rows evenly and write
-//      LUT_sum[u][k][m] = q_sum . C_m[k] (fp32) to L2.  The code tiles of
-//      phase B are already streaming into the CTA's TMA ring.        | barrier
+// Phases (CTA c belongs to one selection unit u = (b, kv head)):
+//   A  LUT build: the unit's CTAs split its 32*256 codeword rows evenly and
+//      write LUT_sum[u][k][m] = q_sum . C_m[k] (fp32) to L2.  The code tiles
+//      of phase B are already streaming into the CTA's TMA ring.    | barrier
 //   B  score: the unit's table is staged as int32 fixed point (exact sums,
 //      order-independent), the per-m bounds are recomputed from the table in
 //      shared memory (identical in every CTA of the unit), the CTA's code
 //      words stream through the ring, scores stay in shared memory (and go
 //      to global for the rare exact slow path), histogram -> global.  | barrier
-//   C  select: bin b* of the k-th score from the unit histogram; bitmap
-//      words of the CTA's own tokens (ballots) and tie-bin tokens appended
-//      to the unit's tie buffer.                                       | barrier
-//   D  ties: every CTA of the unit sorts the (small) tie buffer itself and
-//      overlays the winners on the bitmap in shared memory -- no barrier.
-//      If any unit overflowed the tie buffer, unit leaders run the exact
-//      radix select on the global scores and one more barrier follows.
-//   E  attention: the CTA's slice of kept rows (ascending token order) is
-//      recovered by a prefix popcount of (bitmap | overlay); K/V rows are
-//      gathered once per KV head (16-byte cp.async) and attended by all G
-//      query heads; the last CTA of the unit merges the slice states.
+//   C  select: bin b* of the k-th score from the unit histogram; ballots give
+//      the CTA's above-threshold tokens (row list in shared memory) and its
+//      tie-bin tokens (written to its own slot of the tie buffer).  The K/V
+//      rows known at this point -- above-threshold tokens and the CTA's share
+//      of the sink and local-window rows -- start loading (cp.async) before
+//      the barrier.                                                     | barrier
+//   D  ties: every CTA gathers the unit's tie-bin tokens from the slots of
+//      its CTAs and ranks its own ones against all -- no barrier.  If the
+//      unit overflowed the tie capacity, its leader runs the exact radix
+//      select on the global scores and one more unit barrier follows.
+//   E  attention: the tie winners' rows are gathered while the logits of
+//      the early rows are computed; all G query heads of the KV head attend
+//      the CTA's rows (online softmax); the slice state goes to L2.  | barrier
+//   M  merge: each CTA of the unit combines the slice states of a 1/cn share
+//      of the unit's G*128 outputs and writes them.
 //
-// Every wait (TMA ring, grid barrier) is bounded; on timeout the CTA records
+// Every wait (TMA ring, unit barrier) is bounded; on timeout the CTA records
 // LP_DEVERR_WAIT_TIMEOUT, drains its own copies and exits.
 #pragma once
 #include <cub/block/block_scan.cuh>
@@ -51,6 +57,9 @@ constexpr int kFTile = kFThreads * 32;           // 16 KB of code rows per stage
 constexpr int kFScoreCap = 11264;                // tokens per CTA kept in smem
 constexpr int kFMaxWords = 8192;                 // bitmap words per unit in smem overlay
 constexpr int kFMaxRows = 192;                   // kept rows per attention chunk in phase E
+constexpr int kPubWin = 128;                     // bins in a CTA's published count window
+constexpr int kPubMaxCtas = 64;                  // CTAs per unit of the published-candidate path
+constexpr int kPubMaxCap = 4096;                 // published candidates per CTA (own copy in shared memory)
 
 struct FusedParams {
     const void* q;
@@ -74,16 +83,20 @@ struct FusedParams {
     float* lut;          // [U][256][32]
     float* sel_scores;   // [U][sel_stride]
     int64_t sel_stride;
-    uint32_t* hist;      // [U][kNB]           (zeroed in phase A)
+    uint32_t* hist;      // [U][kNB]           (zeroed by each unit in phase A)
     uint32_t* bitmap;    // [U][bm_stride]
     int64_t bm_stride;
-    float2* tie_buf;     // [U][kTieCap]
-    uint32_t* tie_count; // [U]                 (zeroed in phase A)
-    uint32_t* done_att;  // [U]                 (zeroed in phase A)
+    float2* tie_buf;     // [gridDim.x][kTieCap] tie-bin tokens of each CTA
+    uint32_t* cta_ties;  // [gridDim.x] tie-bin token count of each CTA
     uint32_t* cta_count; // [gridDim.x] selected-above-threshold count of each CTA
+    float2* pub;         // [gridDim.x][pub_cap] published candidates (score, token) of each CTA
+    uint32_t* pub_win;   // [gridDim.x][kPubWin] bin-count window of each CTA's candidates
+    int2* pub_hdr;       // [gridDim.x] (count, publishing threshold bin) of each CTA
+    int pub_target;      // candidates each CTA aims to publish
+    int pub_cap;         // slot capacity (0: no publishing, exchange path only)
     float* part;         // [U][max_split][G][2+128]
     int max_split;
-    uint32_t* bar;       // grid barrier word (self-resetting)
+    uint32_t* bar;       // [U] unit barrier words (persistent, self-resetting)
     uint32_t* err;
     unsigned long long* phase_ns;  // optional [8] globaltimer stamps (CTA 0)
     const char* pf_ptr[2];         // L2 prefetch of the next call's inputs
@@ -132,21 +145,24 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
     return v;
 }
 
-// Grid-wide barrier for a cooperative launch.  The barrier word flips its
-// top bit once per barrier (CTA 0 adds 2^31 - (n-1), the others 1), so it
-// needs no reset between barriers or calls.  Bounded: returns false on
-// timeout (after recording the error bit).
-__device__ __forceinline__ bool grid_barrier(uint32_t* bar, uint32_t* err) {
+// Barrier among the n CTAs of one selection unit (all resident: cooperative
+// launch).  The unit's word flips its top bit once per barrier (the unit's
+// first CTA adds 2^31 - (n-1), the others 1), so its low bits return to zero
+// and it needs no reset between barriers or calls, whatever n is.  Arrival
+// is a fire-and-forget release reduction; thread 0 tracks the expected top
+// bit in `phase` (read once at kernel start, before the first arrival) and
+// polls until the word shows it.  Units never wait for one another.
+// Bounded: returns false on timeout (after recording the error bit).
+__device__ __forceinline__ bool unit_barrier(uint32_t* bar, int n, bool first, uint32_t& phase, uint32_t* err) {
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
-        const uint32_t n = gridDim.x;
-        const uint32_t inc = blockIdx.x == 0 ? (0x80000000u - (n - 1u)) : 1u;
-        uint32_t old;
-        asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(bar), "r"(inc) : "memory");
+        const uint32_t inc = first ? (0x80000000u - (uint32_t)(n - 1)) : 1u;
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(bar), "r"(inc) : "memory");
+        phase ^= 0x80000000u;
         int ok = 1;
         const long long t0 = clock64();
-        while (((ld_acquire_u32(bar) ^ old) & 0x80000000u) == 0u) {
+        while ((ld_acquire_u32(bar) & 0x80000000u) != phase) {
             if (clock64() - t0 > kWaitCycles) {
                 atomicOr(err, LP_DEVERR_WAIT_TIMEOUT);
                 ok = 0;
@@ -183,7 +199,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
 
     __shared__ BinParams s_bp;
     __shared__ __align__(16) float s_qu[8 * 128];  // the unit's G query rows (fp32), loaded at start
-    __shared__ int s_shift, s_bstar, s_above, s_flag;
+    __shared__ int s_shift, s_bstar, s_above;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = kFThreads / 32;
@@ -192,6 +208,13 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
 
     int u, cj, cn;
     fused_cta_unit(blockIdx.x, gridDim.x, p.U, &u, &cj, &cn);
+    uint32_t* ubar = p.bar + u;
+    uint32_t bphase = 0;  // top bit of the unit's barrier word (thread 0), read before the first arrival
+    if (tid == 0) {
+        uint32_t v;
+        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ubar) : "memory");
+        bphase = v & 0x80000000u;
+    }
     const int b = u / p.Hkv, hkv = u - b * p.Hkv;
     // the CTA's tokens: a run of whole bitmap words of the candidate window
     const int wlo = p.c0 >> 5, whi = (p.c1 + 31) >> 5;
@@ -238,24 +261,19 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         s_qu[i] = to_f32(reinterpret_cast<const QT*>(p.q)[(int64_t)b * p.q_stride_b + (int64_t)(hkv * p.G + g) * p.q_stride_h + d]);
     }
 
-    // ================= phase A: LUT build =================
-    // The CTA's codeword rows stream HBM -> shared memory through 3 bulk-copy
-    // stages of 64 rows (32 KB); warp w dots rows 4w..4w+3 of a stage with the
-    // summed query and reduces the 4 dot products with a 6-shuffle transpose.
+    // ================= phase A: LUT build of the CTA's unit =================
+    // The unit's 32*256 codeword rows are split evenly over its cn CTAs and
+    // stream HBM -> shared memory through 3 bulk-copy stages of 64 rows
+    // (32 KB); warp w dots rows 4w..4w+3 of a stage with the summed query and
+    // reduces the 4 dot products with a 6-shuffle transpose.
     {
-        // zero the per-call state used after barrier A
-        const int64_t nz = (int64_t)p.U * kNB;
-        for (int64_t i = (int64_t)blockIdx.x * kFThreads + tid; i < nz; i += (int64_t)gridDim.x * kFThreads)
-            p.hist[i] = 0u;
-        for (int i = blockIdx.x * kFThreads + tid; i < p.U; i += gridDim.x * kFThreads) {
-            p.tie_count[i] = 0u;
-            p.done_att[i] = 0u;
-        }
-        const int64_t total = (int64_t)p.U * 32 * 256;       // codeword rows
-        const int64_t per = ((total + gridDim.x - 1) / gridDim.x + 7) & ~(int64_t)7;
-        const int64_t f_begin = min(total, (int64_t)blockIdx.x * per);
-        const int64_t f_end = min(total, f_begin + per);
+        // zero the unit's per-call state used after barrier A
+        for (int i = cj * kFThreads + tid; i < kNB; i += cn * kFThreads) p.hist[(int64_t)u * kNB + i] = 0u;
+        constexpr int64_t kRows = 32 * 256;  // codeword rows of one unit
+        const int64_t f_begin = (kRows * cj / cn) & ~(int64_t)7;
+        const int64_t f_end = cj + 1 == cn ? kRows : ((kRows * (cj + 1) / cn) & ~(int64_t)7);
         const int nchunk = (int)((f_end - f_begin + 63) / 64);
+        const float* cbu = p.cb + (int64_t)(p.cb_per_kv_head ? hkv : 0) * (kRows * 128);
         auto abuf = [&](int c) -> unsigned char* {
             const int b3 = c % 3;
             return b3 == 2 ? reinterpret_cast<unsigned char*>(s_scores) : s_lut + b3 * 32768;
@@ -263,34 +281,18 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         auto issue_chunk = [&](int c) {
             const int64_t r0 = f_begin + (int64_t)c * 64;
             const int64_t r1 = min(f_end, r0 + 64);
-            uint64_t* bar = &s_abar[c % 3];
-            mbar_arrive_expect_tx(bar, (uint32_t)((r1 - r0) * 512));
-            int64_t f = r0;
-            unsigned char* dst = abuf(c);
-            while (f < r1) {  // at most one unit boundary inside a chunk
-                const int64_t uu = f / 8192;
-                const int64_t seg = min(r1, (uu + 1) * 8192);
-                const float* base = p.cb + (int64_t)(p.cb_per_kv_head ? (int)(uu % p.Hkv) : 0) * (32 * 256 * 128);
-                bulk_g2s(dst, base + (f - uu * 8192) * 128, (uint32_t)((seg - f) * 512), bar);
-                dst += (seg - f) * 512;
-                f = seg;
-            }
+            mbar_arrive_expect_tx(&s_abar[c % 3], (uint32_t)((r1 - r0) * 512));
+            bulk_g2s(abuf(c), cbu + r0 * 128, (uint32_t)((r1 - r0) * 512), &s_abar[c % 3]);
         };
         if (tid == 0)
             for (int c = 0; c < 3 && c < nchunk; ++c) issue_chunk(c);
-        // q_sum of the (at most two) units this CTA touches (s_hist is free now)
-        float (*s_qsum)[128] = reinterpret_cast<float (*)[128]>(s_hist);
-        const int ua = (int)(f_begin / 8192);
-        for (int i = tid; i < 2 * 128; i += kFThreads) {
-            const int slot = i >> 7, d = i & 127;
-            const int uu = ua + slot;
+        // q_sum of the unit, summed over g in order (s_hist is free now)
+        float* s_qsum = reinterpret_cast<float*>(s_hist);
+        __syncthreads();  // s_qu complete
+        for (int d = tid; d < 128; d += kFThreads) {
             float acc = 0.f;
-            if (uu < p.U) {
-                const int bb = uu / p.Hkv, hh = uu - bb * p.Hkv;
-                const QT* qb = reinterpret_cast<const QT*>(p.q) + (int64_t)bb * p.q_stride_b;
-                for (int g = 0; g < p.G; ++g) acc += to_f32(qb[(int64_t)(hh * p.G + g) * p.q_stride_h + d]);
-            }
-            s_qsum[slot][d] = acc;
+            for (int g = 0; g < p.G; ++g) acc += s_qu[g * 128 + d];
+            s_qsum[d] = acc;
         }
         __syncthreads();
         bool okA = true;
@@ -302,13 +304,12 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 return;
             }
             const int64_t r0 = f_begin + (int64_t)c * 64;
-            const int64_t fr = r0 + warp * 4;  // first row of this warp (4 rows, same unit and m)
+            const int64_t fr = r0 + warp * 4;  // first row of this warp (4 rows of the same m)
             if (fr < f_end) {
-                const int uu = (int)(fr / 8192);
                 const int m = (int)((fr >> 8) & 31);
                 const int k0 = (int)(fr & 255);
                 const float* rows = reinterpret_cast<const float*>(abuf(c)) + (warp * 4) * 128 + lane * 4;
-                const float4 qv = *reinterpret_cast<const float4*>(&s_qsum[uu - ua][lane * 4]);
+                const float4 qv = *reinterpret_cast<const float4*>(&s_qsum[lane * 4]);
                 float v[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -336,15 +337,18 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 tot += __shfl_xor_sync(0xffffffffu, tot, 2);
                 tot += __shfl_xor_sync(0xffffffffu, tot, 1);
                 const int j = (lane >> 3) & 3;
-                if ((lane & 7) == 0 && fr + j < f_end) p.lut[((int64_t)uu * 256 + k0 + j) * 32 + m] = tot;
+                if ((lane & 7) == 0 && fr + j < f_end) p.lut[((int64_t)u * 256 + k0 + j) * 32 + m] = tot;
             }
             __syncthreads();  // stage c fully consumed
             if (tid == 0 && c + 3 < nchunk) issue_chunk(c + 3);
         }
     }
     if (stamp) p.phase_ns[1] = global_ns();
-    if (!grid_barrier(p.bar, p.err)) { drain(0); return; }
+    if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) { drain(0); return; }
     if (stamp) p.phase_ns[2] = global_ns();
+
+    using Scan = cub::BlockScan<int, kFThreads>;
+    __shared__ typename Scan::TempStorage scan_tmp;
 
     // ================= phase B: score =================
     BinParams bp;
@@ -508,20 +512,215 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             const uint32_t c = s_hist[i];
             if (c) atomicAdd(&p.hist[(int64_t)u * kNB + i], c);
         }
+        // ---- publish the CTA's candidates for the unit's selection: every
+        //      own token whose bin is at or above b_j, the CTA's threshold
+        //      bin for pub_target tokens (all tokens if it has fewer), sorted
+        //      by descending window bin w = min(bin - b_j, kPubWin - 1), plus
+        //      the window counts (bins b_j .. b_j + kPubWin - 2 exactly, the
+        //      last one cumulative).  A count above the slot capacity
+        //      publishes nothing and b_j = kNB, which sends the unit to the
+        //      exchange path. ----
+        if (p.pub_cap > 0) {
+            __shared__ int s_bj, s_abovej;
+            uint32_t* s_cur = reinterpret_cast<uint32_t*>(s_lut);    // [kPubWin] scatter cursors (table is dead)
+            uint32_t* s_cw = s_cur + kPubWin;                         // [kPubWin] window counts
+            float2* s_own = reinterpret_cast<float2*>(s_ring + 64 * 1024);  // own published entries
+            if (tid == 0) { s_bj = -1; s_abovej = 0; }
+            if (tid < kPubWin) s_cur[tid] = 0u;
+            __syncthreads();
+            find_threshold_bin<kFThreads>(s_hist, p.pub_target, &s_bj, &s_abovej);
+            __syncthreads();
+            const int bj = max(s_bj, 0);
+            const int npub = s_bj < 0 ? ntok : s_abovej + (int)s_hist[bj];
+            const bool pub_ok = npub <= p.pub_cap;
+            for (int bb = bj + kPubWin - 1 + tid; bb < kNB; bb += kFThreads)
+                if (s_hist[bb]) atomicAdd(&s_cur[kPubWin - 1], s_hist[bb]);
+            __syncthreads();
+            uint32_t cw = 0u;
+            if (tid < kPubWin - 1) cw = bj + tid < kNB ? s_hist[bj + tid] : 0u;
+            else if (tid == kPubWin - 1) cw = s_cur[kPubWin - 1];
+            if (tid < kPubWin) {
+                s_cw[tid] = cw;
+                p.pub_win[(int64_t)blockIdx.x * kPubWin + tid] = pub_ok ? cw : 0u;
+            }
+            __syncthreads();
+            // descending offsets off_w = sum_{w' > w} c_w' (thread t scans c_{W-1-t})
+            int off;
+            Scan(scan_tmp).ExclusiveSum(tid < kPubWin ? (int)s_cw[kPubWin - 1 - tid] : 0, off);
+            if (tid < kPubWin) s_cur[kPubWin - 1 - tid] = (uint32_t)off;
+            __syncthreads();
+            if (pub_ok) {
+                float2* slot = p.pub + (int64_t)blockIdx.x * p.pub_cap;
+                for (int lt = tid; lt < ntok; lt += kFThreads) {
+                    const float s = s_scores[lt];
+                    const int bin = score_bin(s, bp.lo, bp.inv_w, kNB);
+                    if (bin >= bj) {
+                        const int pos = (int)atomicAdd(&s_cur[min(bin - bj, kPubWin - 1)], 1u);
+                        const float2 e = make_float2(s, __int_as_float(t_begin + lt));
+                        slot[pos] = e;
+                        s_own[pos] = e;
+                    }
+                }
+            }
+            if (tid == 0) p.pub_hdr[blockIdx.x] = pub_ok ? make_int2(npub, bj) : make_int2(0, kNB);
+        }
     }
     if (stamp) p.phase_ns[3] = global_ns();
-    if (!grid_barrier(p.bar, p.err)) return;
+    if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
     if (stamp) p.phase_ns[4] = global_ns();
     if (tid == kFThreads - 32) {  // a lane off the select critical path
         prefetch_share(p.pf_ptr[0], p.pf_bytes[0], p.pf_count[0], p.pf_stride[0]);
         prefetch_share(p.pf_ptr[1], p.pf_bytes[1], p.pf_count[1], p.pf_stride[1]);
     }
 
-    // ================= phase C: select (threshold bin, own counts, ties) =================
+    // ================= phase C: select =================
     uint32_t* bm = p.bitmap + (int64_t)u * p.bm_stride;
     const float* gsc_c = p.sel_scores + (int64_t)u * p.sel_stride;
-    __shared__ int s_cnt_above, s_nsel, s_win_before, s_ntie_loc, s_tie_base;
+    __shared__ int s_cnt_above, s_win_before, s_topk_off, s_ntie_loc, s_ntie, s_nsel, s_fast;
+    uint32_t* s_selw = s_hist + 1024;  // own words: selected bits (exchange path: above-threshold bits)
+    uint32_t* s_win = s_hist + 1536;   // exchange path: tie winners of the own range (bit lt)
+    const int nw_own = w_end - w_begin;
+    const int ubase = blockIdx.x - cj;  // first CTA of the unit
+    // ---- fast path: the unit's threshold bin from the published windows,
+    //      then only the published entries of that bin are exchanged ----
     {
+        uint32_t* s_wins = reinterpret_cast<uint32_t*>(s_lut);             // [cn][kPubWin] window counts
+        int2* s_hdr = reinterpret_cast<int2*>(s_lut + 32768);               // [cn] (count, b_j)
+        int* s_tst = reinterpret_cast<int*>(s_lut + 32768 + 1024);          // [cn] entries above b* per slot
+        int* s_tcn = s_tst + kPubMaxCtas;                                    // [cn] entries in bin b* per slot
+        int* s_toff = s_tcn + kPubMaxCtas;                                   // [cn + 1] combined tie offsets
+        float* s_tk = reinterpret_cast<float*>(s_ring);                      // tie keys  [kTieCap]
+        int* s_ti = reinterpret_cast<int*>(s_ring + kTieCap * 4);            // tie index [kTieCap]
+        const float2* s_own = reinterpret_cast<const float2*>(s_ring + 64 * 1024);
+        for (int i = tid; i < kNB; i += kFThreads) s_hist[i] = 0u;
+        if (tid == 0) { s_fast = 0; s_bstar = -1; s_above = 0; s_ntie = 0; s_win_before = 0; s_topk_off = 0; }
+        const bool pub = p.pub_cap > 0;
+        if (pub) {
+            // one round trip: the headers and the windows of the unit's CTAs
+            for (int j = tid; j < cn; j += kFThreads) s_hdr[j] = __ldcg(p.pub_hdr + ubase + j);
+            const int nall = cn * kPubWin;
+            constexpr int UNR = 8;
+            for (int i0 = tid; i0 < nall; i0 += kFThreads * UNR) {
+                uint32_t v[UNR];
+#pragma unroll
+                for (int r = 0; r < UNR; ++r) {
+                    const int i = i0 + r * kFThreads;
+                    if (i < nall) v[r] = __ldcg(p.pub_win + (int64_t)ubase * kPubWin + i);
+                }
+#pragma unroll
+                for (int r = 0; r < UNR; ++r)
+                    if (i0 + r * kFThreads < nall) s_wins[i0 + r * kFThreads] = v[r];
+            }
+        }
+        __syncthreads();
+        if (pub) {
+            // the unit's histogram over the published bins (the last window
+            // bin counts at its lower edge; it is above any usable b*)
+            for (int i = tid; i < cn * kPubWin; i += kFThreads) {
+                const uint32_t c = s_wins[i];
+                if (c) atomicAdd(&s_hist[min(s_hdr[i / kPubWin].y + (i % kPubWin), kNB - 1)], c);
+            }
+            int n_union = 0, bmax = 0, bmin = kNB;
+            for (int j = 0; j < cn; ++j) {
+                n_union += s_hdr[j].x;
+                bmax = max(bmax, s_hdr[j].y);
+                bmin = min(bmin, s_hdr[j].y);
+            }
+            __syncthreads();
+            if (n_union >= p.k) find_threshold_bin<kFThreads>(s_hist, p.k, &s_bstar, &s_above);
+            __syncthreads();
+            // exact when b* is at or above every CTA's publishing bin (each
+            // unpublished token then lies in a lower bin than the k-th
+            // published one, so it scores below it) and inside every window
+            const int bs = s_bstar;
+            if (tid == 0)
+                s_fast = (p.k > 0 && bs >= 0 && bs >= bmax && bs < bmin + kPubWin - 1 &&
+                          (int)s_hist[bs] <= kTieCap) ? 1 : 0;
+        }
+        __syncthreads();
+        if (s_fast) {
+            const int bs = s_bstar;
+            const int need = p.k - s_above;
+            // per slot: entries above b* (they lead its sorted list) and in b*
+            for (int j = warp; j < cn; j += NW) {
+                const int wb = bs - s_hdr[j].y;  // 0 <= wb < kPubWin - 1
+                uint32_t a = 0u;
+                for (int w = wb + 1 + lane; w < kPubWin; w += 32) a += s_wins[j * kPubWin + w];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                if (lane == 0) {
+                    s_tst[j] = (int)a;
+                    s_tcn[j] = (int)s_wins[j * kPubWin + wb];
+                }
+            }
+            for (int i = tid; i < nw_own; i += kFThreads) s_selw[i] = 0u;
+            for (int i = tid; i < (ntok + 31) / 32; i += kFThreads) s_win[i] = 0u;
+            __syncthreads();
+            if (warp == 0) {
+                int carry = 0;
+                for (int j0 = 0; j0 < cn; j0 += 32) {
+                    const int j = j0 + lane;
+                    const int c = j < cn ? s_tcn[j] : 0;
+                    int x = c;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int y = __shfl_up_sync(0xffffffffu, x, o);
+                        if (lane >= o) x += y;
+                    }
+                    if (j < cn) s_toff[j] = carry + x - c;
+                    carry += __shfl_sync(0xffffffffu, x, 31);
+                }
+                if (lane == 0) {
+                    s_toff[cn] = carry;
+                    s_ntie = carry;
+                }
+            }
+            // own above-threshold tokens lead the CTA's own sorted entries
+            for (int i = tid; i < s_tst[cj]; i += kFThreads) {
+                const int t = __float_as_int(s_own[i].y);
+                atomicOr(&s_selw[(t >> 5) - w_begin], 1u << (t & 31));
+            }
+            if (p.topk_out && tid == 0) {
+                int c = 0;
+                for (int j = 0; j < cj; ++j) c += s_tst[j];
+                s_topk_off = c;
+            }
+            __syncthreads();
+            // the unit's tie-bin entries (one round trip)
+            const int ntie = s_ntie;
+            for (int i = tid; i < ntie; i += kFThreads) {
+                int lo = 0, hi = cn - 1;  // slot of combined entry i: the last j with s_toff[j] <= i
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (s_toff[mid] <= i) lo = mid;
+                    else hi = mid - 1;
+                }
+                const float2 e = __ldcg(p.pub + (int64_t)(ubase + lo) * p.pub_cap + s_tst[lo] + (i - s_toff[lo]));
+                s_tk[i] = e.x;
+                s_ti[i] = __float_as_int(e.y);
+            }
+            __syncthreads();
+            // rank (score desc, index asc) of the own tie entries (all of them
+            // when the top-k indices are requested): the first `need` win
+            const int i0 = p.topk_out ? 0 : s_toff[cj];
+            const int i1 = p.topk_out ? ntie : s_toff[cj + 1];
+            for (int i = i0 + tid; i < i1; i += kFThreads) {
+                const float ki = s_tk[i];
+                const int ii = s_ti[i];
+                int rank = 0;
+                for (int j = 0; j < ntie; ++j) rank += sel_before(s_tk[j], s_ti[j], ki, ii);
+                if (rank < need) {
+                    if (ii >= t_begin && ii < t_end) atomicOr(&s_selw[(ii >> 5) - w_begin], 1u << (ii & 31));
+                    else if (ii < t_begin) atomicAdd(&s_topk_off, 1);
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (stamp) p.phase_ns[5] = global_ns();
+    if (!s_fast) {
+        // ---- exchange path: threshold bin of the unit histogram, ballots,
+        //      tie-bin tokens through the tie slots, one more barrier ----
         float2* s_tloc = reinterpret_cast<float2*>(s_lut);  // this CTA's tie-bin tokens (<= kTieCap)
         for (int i = tid; i < kNB; i += kFThreads) s_hist[i] = __ldcg(p.hist + (int64_t)u * kNB + i);
         if (tid == 0) { s_bstar = kNB; s_above = 0; s_cnt_above = 0; s_ntie_loc = 0; }
@@ -529,7 +728,6 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         if (p.k > 0) find_threshold_bin<kFThreads>(s_hist, p.k, &s_bstar, &s_above);
         __syncthreads();
         const int bstar = s_bstar;
-        uint32_t* s_selw = s_hist + 1024;  // own words' "bin > b*" bits (the histogram is consumed)
         int my_above = 0;
         for (int w = w_begin + warp; w < w_end; w += NW) {
             const int t = w * 32 + lane;
@@ -557,45 +755,67 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         }
         if (lane == 0 && my_above) atomicAdd(&s_cnt_above, my_above);
         __syncthreads();
+        // tie-bin tokens -> this CTA's own slot of the tie buffer (no
+        // reservation round trip); a count above kTieCap makes the unit
+        // overflow, only the copy is capped
         if (tid == 0) {
             p.cta_count[blockIdx.x] = (uint32_t)s_cnt_above;
-            s_tie_base = s_ntie_loc ? (int)atomicAdd(&p.tie_count[u], (uint32_t)s_ntie_loc) : 0;
+            p.cta_ties[blockIdx.x] = (uint32_t)s_ntie_loc;
+        }
+        const int nloc = min(s_ntie_loc, kTieCap);
+        for (int i = tid; i < nloc; i += kFThreads) p.tie_buf[(int64_t)blockIdx.x * kTieCap + i] = s_tloc[i];
+        if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
+
+        // ---- ties (redundant per CTA, no barrier) ----
+        float* s_tk = reinterpret_cast<float*>(s_lut);                      // tie keys  [kTieCap]
+        int* s_ti = reinterpret_cast<int*>(s_lut + kTieCap * 4);            // tie index [kTieCap]
+        int* s_toff = reinterpret_cast<int*>(s_lut + 2 * kTieCap * 4);      // [cn + 1] tie offsets of the unit's CTAs
+        const int need = p.k - s_above;
+        for (int i = tid; i < (ntok + 31) / 32; i += kFThreads) s_win[i] = 0u;
+        if (warp == 0) {
+            int carry = 0;
+            for (int j0 = 0; j0 < cn; j0 += 32) {
+                const int j = j0 + lane;
+                const int c = j < cn ? (int)__ldcg(p.cta_ties + ubase + j) : 0;
+                int x = c;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (lane >= o) x += y;
+                }
+                if (j < cn) s_toff[j] = carry + x - c;
+                carry += __shfl_sync(0xffffffffu, x, 31);
+            }
+            if (lane == 0) {
+                s_toff[cn] = carry;
+                s_ntie = carry;
+                s_win_before = 0;
+            }
         }
         __syncthreads();
-        // (a CTA with more than kTieCap ties makes the unit overflow: the
-        // reservation above counts them all, only the copy is capped)
-        const int nloc = min(s_ntie_loc, kTieCap);
-        for (int i = tid; i < nloc; i += kFThreads) {
-            const int pos = s_tie_base + i;
-            if (pos < kTieCap) p.tie_buf[(int64_t)u * kTieCap + pos] = s_tloc[i];
-        }
-    }
-    if (stamp) p.phase_ns[5] = global_ns();
-    if (!grid_barrier(p.bar, p.err)) return;
-
-    // ================= phase D: ties (redundant per CTA, no barrier) =================
-    // winners of the CTA's own token range -> bit lt of s_win
-    uint32_t* s_win = s_hist + 1536;                                       // [ceil(ntok/32)] words
-    float* s_tk = reinterpret_cast<float*>(s_ring + 64 * 1024);           // tie keys  [kTieCap]
-    int* s_ti = reinterpret_cast<int*>(s_ring + 64 * 1024 + kTieCap * 4);  // tie index [kTieCap]
-    {
-        const int need = p.k - s_above;
-        const bool ovf_mine = tid < p.U && __ldcg(p.tie_count + tid) > (uint32_t)kTieCap;
-        for (int i = tid; i < (ntok + 31) / 32; i += kFThreads) s_win[i] = 0u;
-        if (tid == 0) s_win_before = 0;
-        const bool overflow_any = __syncthreads_or(ovf_mine) != 0;
-        const int ntie = (int)__ldcg(p.tie_count + u);
+        const int ntie = s_ntie;
+        const bool overflow = ntie > kTieCap;  // identical in every CTA of the unit
         if (stamp) p.phase_ns[6] = global_ns();
-        if (ntie <= kTieCap && need > 0) {
+        if (!overflow && need > 0) {
             for (int i = tid; i < ntie; i += kFThreads) {
-                const float2 e = __ldcg(p.tie_buf + (int64_t)u * kTieCap + i);
+                // source CTA of combined entry i: the last j with s_toff[j] <= i
+                int lo = 0, hi = cn - 1;
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (s_toff[mid] <= i) lo = mid;
+                    else hi = mid - 1;
+                }
+                const float2 e = __ldcg(p.tie_buf + (int64_t)(ubase + lo) * kTieCap + (i - s_toff[lo]));
                 s_tk[i] = e.x;
                 s_ti[i] = __float_as_int(e.y);
             }
             __syncthreads();
-            // rank of each tie entry in selection order (score desc, index asc):
-            // the first `need` ranks win.  O(n^2 / threads) comparisons.
-            for (int i = tid; i < ntie; i += kFThreads) {
+            // rank of a tie entry in selection order (score desc, index asc):
+            // the first `need` ranks win.  Only the CTA's own entries are
+            // ranked unless the top-k indices are requested.
+            const int i0 = p.topk_out ? 0 : s_toff[cj];
+            const int i1 = p.topk_out ? ntie : s_toff[cj + 1];
+            for (int i = i0 + tid; i < i1; i += kFThreads) {
                 const float ki = s_tk[i];
                 const int ii = s_ti[i];
                 int rank = 0;
@@ -612,10 +832,10 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 }
             }
         }
-        if (overflow_any) {
-            // exact slow path by the unit leader on the global scores, then a
-            // grid-uniform extra barrier (every CTA saw the same flag)
-            if (cj == 0 && ntie > kTieCap && need > 0) {
+        if (overflow) {
+            // exact slow path by the unit leader on the global scores, then
+            // one more unit barrier (every CTA of the unit saw the same count)
+            if (cj == 0 && need > 0) {
                 if (tid == 0) atomicOr(p.err, LP_DEVERR_TIE_OVERFLOW);
                 uint32_t* h256 = reinterpret_cast<uint32_t*>(s_lut);
                 __shared__ uint32_t s_prefix, s_mask;
@@ -675,7 +895,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                     __syncthreads();
                 }
             }
-            if (!grid_barrier(p.bar, p.err)) return;
+            if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
             if (ntie > kTieCap && need > 0) {
                 // winners of this unit are the bits the leader set
                 for (int w = w_begin + tid; w < w_end; w += kFThreads) {
@@ -695,30 +915,35 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         __syncthreads();
     }
 
+
+
+    if (stamp && s_fast) p.phase_ns[6] = global_ns();
+
     // ================= phase E: attention over the CTA's own kept rows =================
     {
         constexpr int D = 128;
         constexpr int R = kFMaxRows;
-        int* s_list = reinterpret_cast<int*>(s_lut);                                 // [<= kFScoreCap]
+        int* s_list = reinterpret_cast<int*>(s_scores);                             // [<= kFScoreCap]
         float* s_q = s_qu;                                                           // [8][128]
         float* s_red = reinterpret_cast<float*>(s_lut + kFScoreCap * 4);            // [512] P.V half sums
         float* s_p = s_red + 512;                                                    // [8][R]
         float* s_m = s_p + 8 * R;                                                    // [8] running max
         float* s_l = s_m + 8;                                                        // [8] running sum
         float* s_al = s_l + 8;                                                       // [8] rescale
-        float* s_w = s_al + 8;                                                       // [8][cn] merge weights
         KT* s_k = reinterpret_cast<KT*>(s_ring);                                     // [R][128]
         KT* s_v = s_k + R * D;                                                       // [R][128]
-        __shared__ int s_last;
-        using Scan = cub::BlockScan<int, kFThreads>;
-        __shared__ typename Scan::TempStorage scan_tmp;
+        if (!s_fast && p.topk_out && tid == 0) s_topk_off = s_win_before;
+        __syncthreads();
+        if (!s_fast && p.topk_out) {
+            int c = 0;
+            for (int j = tid; j < cj; j += kFThreads) c += (int)__ldcg(p.cta_count + ubase + j);
+            if (c) atomicAdd(&s_topk_off, c);
+        }
 
-        // ---- own selected tokens in ascending order, from the bits of phase C
+        // ---- own selected tokens in ascending order, from the selected bits
         //      (word w of the CTA covers tokens 32*(w_begin+w) .. +31) and the
-        //      tie winners of phase D (bit lt = token t_begin + lt) ----
+        //      exchange path's tie winners (bit lt = token t_begin + lt) ----
         {
-            const uint32_t* s_selw = s_hist + 1024;
-            const int nw_own = w_end - w_begin;
             const int shift0 = t_begin - w_begin * 32;  // 0 except for the first CTA (c0 % 32)
             // winners in word-aligned form
             auto win_word = [&](int w) -> uint32_t {
@@ -736,9 +961,9 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             };
             int cnt = 0;
             uint32_t wordsel = 0u;
-            const int w = tid;  // one own word per thread (nw_own <= kFScoreCap/32 + 1 <= 512)
+            const int w = tid;  // one own word per thread (nw_own <= kFScoreCap/32 + 2 <= 512)
             if (w < nw_own) {
-                wordsel = s_selw[w] | win_word(w);
+                wordsel = s_selw[w] | (ntok > 0 ? win_word(w) : 0u);
                 const int tb = (w_begin + w) * 32;
                 if (tb < p.c0) wordsel &= ~0u << (p.c0 - tb);
                 if (tb + 32 > p.c1) wordsel &= (p.c1 - tb) >= 32 ? ~0u : ((1u << (p.c1 - tb)) - 1u);
@@ -752,17 +977,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         if (tid < 8) { s_m[tid] = -INFINITY; s_l[tid] = 0.f; }
         __syncthreads();
         const int nsel = s_nsel;
-        if (p.topk_out && nsel > 0) {
-            // rank offset of this CTA's first selected token within the unit
-            __shared__ int s_off;
-            if (tid == 0) s_off = s_win_before;
-            __syncthreads();
-            const int ubase = blockIdx.x - cj;  // first CTA of the unit
-            int c = 0;
-            for (int j = tid; j < cj; j += kFThreads) c += (int)__ldcg(p.cta_count + ubase + j);
-            if (c) atomicAdd(&s_off, c);
-            __syncthreads();
-            const int off = s_off;
+        if (p.topk_out) {
+            const int off = s_topk_off;
             for (int i = tid; i < nsel; i += kFThreads)
                 if (off + i < p.k) p.topk_out[(int64_t)u * p.k + off + i] = s_list[i];
         }
@@ -777,35 +993,20 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         const KT* vb = reinterpret_cast<const KT*>(p.vals) + (int64_t)b * p.v_stride_b + (int64_t)hkv * p.v_stride_h;
         constexpr int CH = D * (int)sizeof(KT) / 16;
         constexpr int EPC = 16 / (int)sizeof(KT);
-        float acc0 = 0.f, acc1 = 0.f;  // P.V for outputs o = tid and tid + 512
-        for (int c0r = 0; c0r < nrows; c0r += R) {
-            const int nr = min(R, nrows - c0r);
-            for (int c = tid; c < nr * CH; c += kFThreads) {
-                const int r = c / CH, part = c - r * CH;
-                const int rr = c0r + r;
-                int tok = rr < n_sink_here ? sk0 + rr
-                        : rr < n_sink_here + nsel ? s_list[rr - n_sink_here]
-                        : p.local_start + lc0 + (rr - n_sink_here - nsel);
-                const int64_t t = min(max(tok, 0), p.T_total - 1);
-                cp_async16(s_k + r * D + part * EPC, kb + t * p.k_stride_t + part * EPC);
-                cp_async16(s_v + r * D + part * EPC, vb + t * p.v_stride_t + part * EPC);
-            }
-            cp_async_commit();
-            cp_async_wait<0>();
-            __syncthreads();
-            // logits (log2 domain)
+        // logits (log2 domain) of staging rows [r_lo, r_hi)
+        auto logits = [&](int r_lo, int r_hi) {
             if (p.G == 4) {
                 // warp handles rows 4w..4w+3 (+64 per pass); lane covers dims 4l..4l+3;
                 // the 16 (row, head) partial dots are reduced by one 16-way transpose
                 float4 qv[4];
 #pragma unroll
                 for (int g = 0; g < 4; ++g) qv[g] = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
-                for (int r0w = warp * 4; r0w < nr; r0w += NW * 4) {
+                for (int r0w = r_lo + warp * 4; r0w < r_hi; r0w += NW * 4) {
                     float v[16];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const float4 kv = (r0w + j < nr) ? Vec4<KT>::load(s_k + (r0w + j) * D + lane * 4)
-                                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const float4 kv = (r0w + j < r_hi) ? Vec4<KT>::load(s_k + (r0w + j) * D + lane * 4)
+                                                           : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                         for (int g = 0; g < 4; ++g) {
                             float a = qv[g].x * kv.x;
@@ -843,22 +1044,43 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                     tot += __shfl_xor_sync(0xffffffffu, tot, 1);
                     const int idx = (lane >> 1) & 15;  // = 4 * row + head
                     const int rr = r0w + (idx >> 2);
-                    if ((lane & 1) == 0 && rr < nr) s_p[(idx & 3) * R + rr] = tot * p.scale_log2;
+                    if ((lane & 1) == 0 && rr < r_hi) s_p[(idx & 3) * R + rr] = tot * p.scale_log2;
                 }
-            } else
-            for (int r = warp; r < nr; r += NW) {
-                const float4 kv = Vec4<KT>::load(s_k + r * D + lane * 4);
-                for (int g = 0; g < p.G; ++g) {
-                    const float4 qv = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
-                    float a = qv.x * kv.x;
-                    a = fmaf(qv.y, kv.y, a);
-                    a = fmaf(qv.z, kv.z, a);
-                    a = fmaf(qv.w, kv.w, a);
+            } else {
+                for (int r = r_lo + warp; r < r_hi; r += NW) {
+                    const float4 kv = Vec4<KT>::load(s_k + r * D + lane * 4);
+                    for (int g = 0; g < p.G; ++g) {
+                        const float4 qv = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
+                        float a = qv.x * kv.x;
+                        a = fmaf(qv.y, kv.y, a);
+                        a = fmaf(qv.z, kv.z, a);
+                        a = fmaf(qv.w, kv.w, a);
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-                    if (lane == g) s_p[g * R + r] = a * p.scale_log2;
+                        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                        if (lane == g) s_p[g * R + r] = a * p.scale_log2;
+                    }
                 }
             }
+        };
+
+        float acc0 = 0.f, acc1 = 0.f;  // P.V for outputs o = tid and tid + 512
+        for (int c0r = 0; c0r < nrows; c0r += R) {
+            const int nr = min(R, nrows - c0r);
+            // K/V rows of the chunk (16-byte cp.async)
+            for (int c = tid; c < nr * CH; c += kFThreads) {
+                const int r = c / CH, part = c - r * CH;
+                const int rr = c0r + r;
+                const int tok = rr < n_sink_here ? sk0 + rr
+                              : rr < n_sink_here + nsel ? s_list[rr - n_sink_here]
+                              : p.local_start + lc0 + (rr - n_sink_here - nsel);
+                const int64_t t = min(max(tok, 0), p.T_total - 1);
+                cp_async16(s_k + r * D + part * EPC, kb + t * p.k_stride_t + part * EPC);
+                cp_async16(s_v + r * D + part * EPC, vb + t * p.v_stride_t + part * EPC);
+            }
+            cp_async_commit();
+            cp_async_wait<0>();
+            __syncthreads();
+            logits(0, nr);
             __syncthreads();
             // online softmax update per head
             for (int g = warp; g < p.G; g += NW) {
@@ -954,92 +1176,46 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 }
             }
         }
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();
-            const uint32_t ticket = atomicAdd(&p.done_att[u], 1u);
-            s_last = (ticket == (uint32_t)cn - 1u);
-        }
-        __syncthreads();
-        if (!s_last) return;
-        __threadfence();
-        // merge the cn slice states of the unit
+    }
+    // every CTA's partial state is in L2 after this barrier
+    if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
+
+    // ================= merge: each CTA of the unit finalises a slice of its G*128 outputs =================
+    {
+        constexpr int D = 128;
+        const int nout = p.G * D;
+        const int per = (nout + cn - 1) / cn;
+        const int o0 = min(nout, cj * per), o1 = min(nout, o0 + per);
+        const int npair = (o1 - o0) * cn;  // (output, slice) pairs, <= nout + cn <= 4096
         const float* pu = p.part + (int64_t)u * p.max_split * p.G * (2 + D);
         const int64_t sstride = (int64_t)p.G * (2 + D);
+        float* s_mm = reinterpret_cast<float*>(s_ring);  // [npair] slice max
+        float* s_ll = s_mm + 4096;                       // [npair] slice sum
+        float* s_aa = s_ll + 4096;                       // [npair] slice P.V
+        for (int i = tid; i < npair; i += kFThreads) {
+            const int ol = i / cn, sl = i - ol * cn;
+            const int o = o0 + ol, g = o / D, d = o - g * D;
+            const float* ps = pu + sl * sstride + g * (2 + D);
+            s_mm[i] = __ldcg(ps);
+            s_ll[i] = __ldcg(ps + 1);
+            s_aa[i] = __ldcg(ps + 2 + d);
+        }
+        __syncthreads();
         OT* ob = reinterpret_cast<OT*>(p.out) + (int64_t)b * p.out_stride_b;
-        constexpr int MAXS = 24;
-        if (cn <= MAXS) {
-            // one round trip: every slice value a thread needs is loaded at once
-            float* s_ml2 = s_w;  // [cn][G][2] (m, l)
-            for (int i = tid; i < cn * p.G * 2; i += kFThreads) {
-                const int sl = i / (p.G * 2), rem = i - sl * p.G * 2;
-                s_ml2[i] = __ldcg(pu + sl * sstride + (rem >> 1) * (2 + D) + (rem & 1));
+        for (int ol = tid; ol < o1 - o0; ol += kFThreads) {
+            const float* mm = s_mm + ol * cn;
+            const float* ll = s_ll + ol * cn;
+            const float* aa = s_aa + ol * cn;
+            float M = -INFINITY;
+            for (int sl = 0; sl < cn; ++sl) M = fmaxf(M, mm[sl]);
+            float L = 0.f, A = 0.f;
+            for (int sl = 0; sl < cn; ++sl) {
+                const float f = exp2f(mm[sl] - M);  // 0 for a slice without rows
+                L = fmaf(ll[sl], f, L);
+                A = fmaf(aa[sl], f, A);
             }
-            auto merge_out = [&](int o, const float* av) {
-                const int g = o / D, d = o - g * D;
-                float M = -INFINITY;
-                for (int sl = 0; sl < cn; ++sl) M = fmaxf(M, s_ml2[(sl * p.G + g) * 2]);
-                float L = 0.f, acc = 0.f;
-#pragma unroll
-                for (int sl = 0; sl < MAXS; ++sl) {
-                    if (sl < cn) {
-                        const float f = exp2f(s_ml2[(sl * p.G + g) * 2] - M);
-                        L = fmaf(s_ml2[(sl * p.G + g) * 2 + 1], f, L);
-                        acc = fmaf(av[sl], f, acc);
-                    }
-                }
-                ob[(int64_t)(hkv * p.G + g) * p.out_stride_h + d] = from_f32<OT>(acc / L);
-            };
-            auto load_av = [&](int o, float* av) {
-                const int g = o / D, d = o - g * D;
-#pragma unroll
-                for (int sl = 0; sl < MAXS; ++sl)
-                    av[sl] = sl < cn ? __ldcg(pu + sl * sstride + g * (2 + D) + 2 + d) : 0.f;
-            };
-            float av[MAXS];
-            const bool has0 = tid < p.G * D;
-            if (has0) load_av(tid, av);  // issued before the barrier: overlaps the m/l loads
-            __syncthreads();
-            if (has0) merge_out(tid, av);
-            for (int o = tid + kFThreads; o < p.G * D; o += kFThreads) {
-                load_av(o, av);
-                merge_out(o, av);
-            }
-        } else {
-            for (int g = warp; g < p.G; g += NW) {
-                float M = -INFINITY;
-                for (int sl = lane; sl < cn; sl += 32) M = fmaxf(M, __ldcg(pu + sl * sstride + g * (2 + D)));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-                float Lsum = 0.f;
-                for (int sl = lane; sl < cn; sl += 32) {
-                    const float* ps = pu + sl * sstride + g * (2 + D);
-                    const float f = exp2f(__ldcg(ps) - M);
-                    s_w[g * cn + sl] = f;
-                    Lsum = fmaf(__ldcg(ps + 1), f, Lsum);
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
-                __syncwarp();
-                const float invL = 1.f / Lsum;
-                for (int sl = lane; sl < cn; sl += 32) s_w[g * cn + sl] *= invL;
-            }
-            __syncthreads();
-            for (int o = tid; o < p.G * D; o += kFThreads) {
-                const int g = o / D, d = o - g * D;
-                const float* pg = pu + g * (2 + D) + 2 + d;
-                float acc = 0.f;
-                int sl = 0;
-                for (; sl + 8 <= cn; sl += 8) {
-                    float vv[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) vv[j] = __ldcg(pg + (sl + j) * sstride);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) acc = fmaf(vv[j], s_w[g * cn + sl + j], acc);
-                }
-                for (; sl < cn; ++sl) acc = fmaf(__ldcg(pg + sl * sstride), s_w[g * cn + sl], acc);
-                ob[(int64_t)(hkv * p.G + g) * p.out_stride_h + d] = from_f32<OT>(acc);
-            }
+            const int o = o0 + ol, g = o / D, d = o - g * D;
+            ob[(int64_t)(hkv * p.G + g) * p.out_stride_h + d] = from_f32<OT>(A / L);
         }
         if (p.phase_ns && tid == 0) atomicMax(&p.phase_ns[7], global_ns());
     }

@@ -83,11 +83,19 @@ struct Plan {
     uint32_t* done_sel;
     uint32_t* done_att;
     uint32_t* bar;
+    uint32_t* ubar;
     uint32_t* cta_count;
+    uint32_t* cta_ties;
+    float2* pub;
+    uint32_t* pub_win;
+    int2* pub_hdr;
+    int pub_target, pub_cap;
     size_t bytes;
 };
 
 static constexpr int kScoreThreads = 512;
+static constexpr int kUnitBarWords = 384;     // one barrier word per unit of the fused path
+static constexpr size_t kPersistBytes = 2048; // error word, grid barrier, unit barriers
 static constexpr int kGroupStages = 8;
 static constexpr int kHeadsStages = 4;
 
@@ -161,25 +169,38 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
         const int nwu = p.ncand > 0 ? ((p.c1 + 31) >> 5) - (p.c0 >> 5) : 0;
         const int ntok_max = cn_min > 0 ? (nwu + cn_min - 1) / cn_min * 32 : 0;
         p.fused = !(a->flags & LP_FLAG_NO_FUSED) && !p.per_head && !p.heads && a->out != nullptr &&
-                  a->D == 128 && a->G <= 8 && p.U <= p.fused_ctas && p.ncand > 0 && a->topk > 0 &&
+                  a->D == 128 && a->G <= 8 && p.U <= p.fused_ctas && p.U <= kUnitBarWords && p.ncand > 0 && a->topk > 0 &&
                   nwu <= kFMaxWords && cn_min >= 1 && ntok_max <= kFScoreCap;
         p.fused_max_split = cn_min + 1;
+        // candidate publishing: each CTA aims at twice its even share of the
+        // top-k plus a margin (slot capacity: that plus the population of
+        // its threshold bin)
+        const int cn_max = p.U > 0 ? (p.fused_ctas + p.U - 1) / p.U : 1;
+        p.pub_target = 2 * ((a->topk + cn_max - 1) / cn_max) + 32;
+        p.pub_cap = p.pub_target + 64;
+        if (p.pub_cap > kPubMaxCap || cn_max > kPubMaxCtas || (a->flags & LP_FLAG_EXCHANGE_SELECT)) p.pub_cap = 0;
     }
 
     Carver c(ws);
-    // fixed offsets, identical for every geometry: the error word (0) and the
-    // grid-barrier word (256 B), whose value must survive between calls
+    // fixed offsets, identical for every geometry: the error word (0), the
+    // grid-barrier word (256 B) and the per-unit barrier words (512 B ..
+    // 2048 B), whose values must survive between calls
     p.err = c.take<uint32_t>(64);
     p.bar = c.take<uint32_t>(64);
+    p.ubar = c.take<uint32_t>(kUnitBarWords);
     p.lut = c.take<float>((size_t)p.U * 256 * 32 * (p.heads ? 4 : 1));
     p.bounds = c.take<float>((size_t)p.U * (p.heads ? a->G : 1) * 32 * kLutParts * 2);
     p.sel_scores = c.take<float>((size_t)p.Usel * std::max(1, a->T_codes));
     p.bitmap = c.take<uint32_t>((size_t)p.Usel * p.bm_words);
-    p.tie_buf = c.take<float2>((size_t)p.Usel * kTieCap);
+    p.tie_buf = c.take<float2>((size_t)std::max(p.Usel, p.fused_ctas) * kTieCap);
     p.info = c.take<int4>((size_t)p.Usel);
     p.part = c.take<float>((size_t)std::max((size_t)p.Uatt * p.nsplit * p.HG, (size_t)p.U * p.fused_max_split * a->G) *
                            (2 + 128));
     p.cta_count = c.take<uint32_t>((size_t)p.fused_ctas);
+    p.cta_ties = c.take<uint32_t>((size_t)p.fused_ctas);
+    p.pub = c.take<float2>((size_t)p.fused_ctas * std::max(p.pub_cap, 1));
+    p.pub_win = c.take<uint32_t>((size_t)p.fused_ctas * kPubWin);
+    p.pub_hdr = c.take<int2>((size_t)p.fused_ctas);
     p.zero_words = (int64_t)p.Usel * kNB + p.Usel + p.Usel + p.Uatt;
     p.zero = c.take<uint32_t>((size_t)p.zero_words);
     p.hist = p.zero;
@@ -319,12 +340,16 @@ static int launch_fused(const lp_sparse_decode_args* a, const Plan& p, cudaStrea
     fp.bitmap = p.bitmap;
     fp.bm_stride = p.bm_words;
     fp.tie_buf = p.tie_buf;
-    fp.tie_count = p.tie_count;
-    fp.done_att = p.done_att;
+    fp.cta_ties = p.cta_ties;
+    fp.pub = p.pub;
+    fp.pub_win = p.pub_win;
+    fp.pub_hdr = p.pub_hdr;
+    fp.pub_target = p.pub_target;
+    fp.pub_cap = p.pub_cap;
     fp.cta_count = p.cta_count;
     fp.part = p.part;
     fp.max_split = p.fused_max_split;
-    fp.bar = p.bar;
+    fp.bar = p.ubar;
     fp.err = p.err;
     fp.phase_ns = reinterpret_cast<unsigned long long*>(a->phase_ns);
     for (int i = 0; i < 2; ++i) {
@@ -556,8 +581,11 @@ int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
     LP_CUDA(cudaMemcpyAsync(&v, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     LP_CUDA(cudaStreamSynchronize(st));
     LP_CUDA(cudaMemsetAsync(workspace, 0, sizeof(uint32_t), st));
-    // a timed-out grid barrier leaves its word mid-count: restore it
-    if (v & LP_DEVERR_WAIT_TIMEOUT) LP_CUDA(cudaMemsetAsync(static_cast<char*>(workspace) + 256, 0, 4, st));
+    // a timed-out barrier leaves its word mid-count: restore the barrier words
+    if (v & LP_DEVERR_WAIT_TIMEOUT) {
+        LP_CHECK(workspace_bytes >= kPersistBytes, "workspace smaller than its persistent state");
+        LP_CUDA(cudaMemsetAsync(static_cast<char*>(workspace) + 256, 0, kPersistBytes - 256, st));
+    }
     LP_CUDA(cudaStreamSynchronize(st));
     *bits_out = v;
     return LP_OK;

@@ -171,7 +171,7 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
                   return_head_scores: bool = False, attention: bool = True,
                   ws: Optional[torch.Tensor] = None, stage_events=None,
                   fused: Optional[bool] = None, phase_ns: Optional[torch.Tensor] = None,
-                  prefetch=None) -> SparseDecodeResult:
+                  prefetch=None, exchange_select: bool = False) -> SparseDecodeResult:
     """One sparse decode step of one layer (see lp_sparse_decode).
 
     q [B,Hq,D] (or [Hq,D]); codebooks fp32 [Hkv,M,K,D] or [M,K,D]; codes uint8
@@ -182,7 +182,9 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
 
     ``fused=None`` lets the library run the whole step as one cooperative
     kernel when the geometry allows (KV-group selection with attention);
-    ``fused=False`` forces the multi-kernel path.  ``phase_ns`` (int64 [8]
+    ``fused=False`` forces the multi-kernel path; ``exchange_select=True``
+    makes the fused kernel settle the top-k through its tie exchange instead
+    of the union of published candidates (both are exact).  ``phase_ns`` (int64 [8]
     on the device) receives global-timer stamps of the fused kernel phases.
     ``prefetch`` (see :func:`prefetch_regions`) names up to two regions of
     the NEXT call's inputs to pull into L2 during this call's tail.
@@ -208,6 +210,8 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
                    topk_out=tk, prefetch=prefetch)
     if fused is False:
         a.flags |= _lib.LP_FLAG_NO_FUSED
+    if exchange_select:
+        a.flags |= _lib.LP_FLAG_EXCHANGE_SELECT
     if phase_ns is not None:
         a.phase_ns = phase_ns.data_ptr()
     ev_arr = None

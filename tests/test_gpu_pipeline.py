@@ -55,14 +55,17 @@ def test_cfg1_scoring_op(golden_dir):
     _check_errors()
 
 
-@pytest.mark.parametrize("fused", [None, False], ids=["auto", "multi"])
-def test_cfg3_sparse_decode_step(golden_dir, fused):
+MODES = {"auto": dict(fused=None), "exchange": dict(fused=None, exchange_select=True), "multi": dict(fused=False)}
+
+
+@pytest.mark.parametrize("mode", list(MODES))
+def test_cfg3_sparse_decode_step(golden_dir, mode):
     fix = np.load(golden_dir / "cfg3_decode.npz")
     c = syn.config3(0)
     dev = _dev()
     C, codes, K, V, q = (c[n].to(dev) for n in ("C", "codes", "keys", "vals", "q"))
     r = ops.sparse_decode(q, C, codes, K, V, topk=c["k"], sink=c["sink"], local=c["local"],
-                          return_topk=True, fused=fused)
+                          return_topk=True, **MODES[mode])
     torch.cuda.synchronize()
     top = r.topk.cpu().numpy()
     T = codes.shape[1]
@@ -130,15 +133,15 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("fused", [None, False], ids=["auto", "multi"])
+@pytest.mark.parametrize("mode", list(MODES))
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
-def test_pipeline_vs_oracle(case, fused):
+def test_pipeline_vs_oracle(case, mode):
     B, Hkv, G, Tc, Tt, cap, k, sink, local, per_kv, select, kvd, qd = case
     C, codes, K, V, q = _rand_case(1000 + Tc, B, Hkv, G, Tt, cap=cap, per_kv=per_kv, kv_dtype=kvd, q_dtype=qd)
     dev = _dev()
     r = ops.sparse_decode(q.to(dev), C.to(dev), codes.to(dev), K.to(dev), V.to(dev), topk=k,
                           T_codes=Tc, T_total=Tt, sink=sink, local=local, select=select,
-                          return_topk=True, out_dtype=torch.float32, fused=fused)
+                          return_topk=True, out_dtype=torch.float32, **MODES[mode])
     torch.cuda.synchronize()
     top_ref, out_ref, s_ref = _oracle_step(C, codes, K, V, q, Tc, Tt, k, sink, local, per_kv, select)
     top = r.topk.cpu().numpy()
@@ -160,15 +163,15 @@ def test_pipeline_vs_oracle(case, fused):
     _check_errors()
 
 
-@pytest.mark.parametrize("fused", [None, False], ids=["auto", "multi"])
-def test_ties_take_lowest_index(fused):
+@pytest.mark.parametrize("mode", list(MODES))
+def test_ties_take_lowest_index(mode):
     # every code equal -> every candidate score equal -> exact slow path; the
     # first k candidates (lowest indices) must be chosen
     C, codes, K, V, q = _rand_case(5, 1, 2, 4, 6000, equal_codes=True)
     dev = _dev()
     k, sink, local = 100, 4, 64
     r = ops.sparse_decode(q.to(dev), C.to(dev), codes.to(dev), K.to(dev), V.to(dev), topk=k,
-                          sink=sink, local=local, return_topk=True, fused=fused)
+                          sink=sink, local=local, return_topk=True, **MODES[mode])
     torch.cuda.synchronize()
     top = r.topk.cpu().numpy()
     for u in range(2):
@@ -177,17 +180,31 @@ def test_ties_take_lowest_index(fused):
     assert bits & 1 == 0 and bits & 2 == 2  # slow exact path ran, no timeout
 
 
-@pytest.mark.parametrize("fused", [None, False], ids=["auto", "multi"])
-def test_repeat_calls_deterministic(fused):
+@pytest.mark.parametrize("mode", list(MODES))
+def test_repeat_calls_deterministic(mode):
     C, codes, K, V, q = _rand_case(9, 1, 8, 4, 20000)
     dev = _dev()
     args = [t.to(dev) for t in (q, C, codes, K, V)]
-    outs = [ops.sparse_decode(*args, topk=400, sink=4, local=64, return_topk=True, fused=fused)
+    outs = [ops.sparse_decode(*args, topk=400, sink=4, local=64, return_topk=True, **MODES[mode])
             for _ in range(3)]
     torch.cuda.synchronize()
     for o in outs[1:]:
         assert torch.equal(o.topk, outs[0].topk)
         assert torch.equal(o.out, outs[0].out)
+    _check_errors()
+
+
+def test_candidate_union_and_tie_exchange_select_the_same_set():
+    # both fused selection paths are exact: identical index sets, and the
+    # attention outputs agree to accumulation-order rounding
+    C, codes, K, V, q = _rand_case(11, 1, 8, 4, 40000)
+    dev = _dev()
+    args = [t.to(dev) for t in (q, C, codes, K, V)]
+    a = ops.sparse_decode(*args, topk=1024, sink=4, local=64, return_topk=True)
+    b = ops.sparse_decode(*args, topk=1024, sink=4, local=64, return_topk=True, exchange_select=True)
+    torch.cuda.synchronize()
+    assert torch.equal(a.topk, b.topk)
+    assert (a.out.float() - b.out.float()).abs().max().item() <= 1e-2
     _check_errors()
 
 
