@@ -156,6 +156,40 @@ int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t wor
 int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
                           uint32_t* bits_out);
 
+/* ======================================================================
+ * Allocation-free variant (no counterpart in the reference)
+ * ====================================================================== */
+
+/* Size of the library's built-in per-device scratch (16 MiB): enough for one
+ * sequence (B = 1) with 8 KV heads up to about 300k tokens; the workspace
+ * size lp_sparse_decode_workspace_size() reports must not exceed it. */
+#define LP_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* lp_sparse_decode for callers that must not allocate device memory: a
+ * serving runtime that has handed all of HBM to its own pool (a cudaMalloc
+ * there fails or fragments the pool), or a latency-critical decode loop in
+ * which cudaMalloc/cudaFree would synchronise the device.  Instead of a
+ * caller-owned workspace it uses a scratch array that the library holds in
+ * device memory (LP_NOALLOC_SCRATCH_BYTES per GPU that loads the library,
+ * kept until the process exits); it calls no cudaMalloc, cudaFree or other
+ * allocating routine.  The caller still passes every input and output.
+ *   - The first call on a device looks up the scratch's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture starts on the device.
+ *   - Geometries whose workspace exceeds LP_NOALLOC_SCRATCH_BYTES are
+ *     rejected with LP_ERR_WORKSPACE (use lp_sparse_decode with a workspace
+ *     of your own for those).
+ *   - Every call on a device shares the one scratch, which keeps the last
+ *     call's contents.  Its first 2048 bytes (error bits, barrier words) must
+ *     start at zero: the array is zero when the library loads and the calls
+ *     leave those words consistent.  Calls whose kernels may overlap on the
+ *     GPU (different streams, threads or processes sharing the context) race
+ *     on it: order them on one stream.
+ *   - device_errors: NULL, or a host pointer that receives the device error
+ *     bits (LP_DEVERR_*) of the scratch after this call; the call then
+ *     synchronises `stream` and clears the bits, as lp_read_device_errors. */
+int lp_sparse_decode_noalloc(const lp_sparse_decode_args* a, void* stream, uint32_t* device_errors);
+
 #ifdef __cplusplus
 }
 #endif

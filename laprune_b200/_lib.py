@@ -51,7 +51,10 @@ SIGNATURES = {
     "lp_sparse_decode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SparseDecodeArgs)]),
     "lp_sparse_decode": (ctypes.c_int, [ctypes.POINTER(SparseDecodeArgs), _c_p, ctypes.c_size_t, _c_p]),
     "lp_read_device_errors": (ctypes.c_int, [_c_p, ctypes.c_size_t, _c_p, ctypes.POINTER(ctypes.c_uint32)]),
+    "lp_sparse_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(SparseDecodeArgs), _c_p,
+                                                ctypes.POINTER(ctypes.c_uint32)]),
 }
+LP_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 _lib = None
 

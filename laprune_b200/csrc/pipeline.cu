@@ -592,3 +592,54 @@ int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of lp_sparse_decode: the workspace is a file-scope
+// device array instead of caller-owned memory.
+// ---------------------------------------------------------------------------
+namespace lp {
+
+// One scratch per device, zero when the module loads.  Host code must not
+// pass `g_noalloc_scratch` itself to a kernel (on the host it names a
+// stand-in, not device memory): noalloc_scratch() looks up its device
+// address once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LP_NOALLOC_SCRATCH_BYTES];
+
+static int noalloc_scratch(void** out) {
+    static std::mutex mu;
+    static void* addr[64] = {nullptr};
+    int dev = 0;
+    LP_CUDA(cudaGetDevice(&dev));
+    LP_CHECK(dev >= 0 && dev < 64, "device ordinal out of range (at most 64 devices)");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* ptr = nullptr;
+        LP_CUDA(cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch));
+        LP_CHECK(ptr != nullptr && (reinterpret_cast<uintptr_t>(ptr) & 255u) == 0,
+                 "built-in scratch has no 256-byte aligned device address");
+        addr[dev] = ptr;
+    }
+    *out = addr[dev];
+    return LP_OK;
+}
+
+}  // namespace lp
+
+extern "C" int lp_sparse_decode_noalloc(const lp_sparse_decode_args* a, void* stream, uint32_t* device_errors) {
+    using namespace lp;
+    LP_CHECK(a != nullptr, "args must not be NULL");
+    const size_t need = lp_sparse_decode_workspace_size(a);
+    if (need == 0) return LP_ERR_INVALID;  // the plan's message is already set
+    if (need > (size_t)LP_NOALLOC_SCRATCH_BYTES)
+        return fail(LP_ERR_WORKSPACE,
+                    "lp_sparse_decode_noalloc: this geometry needs " + std::to_string(need) +
+                        " bytes of workspace, more than the built-in scratch of " +
+                        std::to_string((size_t)LP_NOALLOC_SCRATCH_BYTES) +
+                        " bytes; call lp_sparse_decode with a workspace of your own");
+    void* ws = nullptr;
+    int rc = noalloc_scratch(&ws);
+    if (rc != LP_OK) return rc;
+    rc = lp_sparse_decode(a, ws, (size_t)LP_NOALLOC_SCRATCH_BYTES, stream);
+    if (rc != LP_OK || device_errors == nullptr) return rc;
+    return lp_read_device_errors(ws, (size_t)LP_NOALLOC_SCRATCH_BYTES, stream, device_errors);
+}
