@@ -376,9 +376,9 @@ def run_ours(args):
                 "step_hbm_gbs": step_bytes / (elapsed_ms / args.steps / 1e3) / 1e9,
                 "launch_us_timed": launch_ms * 1e3,
                 "launch_us_isolated": kernel_ms * 1e3,
-                "fused_phase_us": {"A_lut": phase_us[0], "barrier_A": phase_us[1], "B_score": phase_us[2],
-                                   "barrier_B": phase_us[3], "C_select": phase_us[4],
-                                   "barrier_C+D_ties": phase_us[5], "E_attention": phase_us[6]},
+                "fused_phase_us": {"A_lut": phase_us[0], "wait_lut": phase_us[1], "B_score_publish": phase_us[2],
+                                   "wait_windows": phase_us[3], "C_select": phase_us[4],
+                                   "E_attention_wait_states": phase_us[5], "M_merge": phase_us[6]},
                 "outputs_finite": ok, "device_error_bits": errs,
             },
             "roofline": {"bound": "hbm",

@@ -60,6 +60,7 @@ constexpr int kFMaxRows = 192;                   // kept rows per attention chun
 constexpr int kPubWin = 128;                     // bins in a CTA's published count window
 constexpr int kPubMaxCtas = 64;                  // CTAs per unit of the published-candidate path
 constexpr int kPubMaxCap = 4096;                 // published candidates per CTA (own copy in shared memory)
+constexpr int kFastTieCap = 1024;                // tie-bin entries the fast selection path settles
 
 struct FusedParams {
     const void* q;
@@ -80,23 +81,23 @@ struct FusedParams {
     int64_t out_stride_b, out_stride_h;
     int32_t* topk_out;
     // workspace
-    float* lut;          // [U][256][32]
+    unsigned long long* lut;   // [U][256][32] tagged fp32 LUT_sum (value bits | epoch << 32)
     float* sel_scores;   // [U][sel_stride]
     int64_t sel_stride;
-    uint32_t* hist;      // [U][kNB]           (zeroed by each unit in phase A)
+    uint32_t* chist;     // [gridDim.x][kNB] local score histogram of each CTA (exchange path)
     uint32_t* bitmap;    // [U][bm_stride]
     int64_t bm_stride;
     float2* tie_buf;     // [gridDim.x][kTieCap] tie-bin tokens of each CTA
     uint32_t* cta_ties;  // [gridDim.x] tie-bin token count of each CTA
     uint32_t* cta_count; // [gridDim.x] selected-above-threshold count of each CTA
-    float2* pub;         // [gridDim.x][pub_cap] published candidates (score, token) of each CTA
-    uint32_t* pub_win;   // [gridDim.x][kPubWin] bin-count window of each CTA's candidates
-    int2* pub_hdr;       // [gridDim.x] (count, publishing threshold bin) of each CTA
+    unsigned long long* pub;   // [gridDim.x][pub_cap][2] tagged (score, token) candidates of each CTA
+    unsigned long long* pwin;  // [gridDim.x][kPubWin + 2] tagged bin-count window, count, threshold bin
     int pub_target;      // candidates each CTA aims to publish
     int pub_cap;         // slot capacity (0: no publishing, exchange path only)
-    float* part;         // [U][max_split][G][2+128]
+    unsigned long long* part;  // [U][max_split][G][2+128] tagged split-K states (max, sum, P.V)
     int max_split;
     uint32_t* bar;       // [U] unit barrier words (persistent, self-resetting)
+    unsigned long long* epoch_ctr;  // persistent launch counter: this call's epoch tags its exchanged words
     uint32_t* err;
     unsigned long long* phase_ns;  // optional [8] globaltimer stamps (CTA 0)
     const char* pf_ptr[2];         // L2 prefetch of the next call's inputs
@@ -176,6 +177,63 @@ __device__ __forceinline__ bool unit_barrier(uint32_t* bar, int n, bool first, u
     return s_ok != 0;
 }
 
+// Words exchanged between the CTAs of a unit carry the call's epoch in their
+// upper 32 bits; a reader polls a word until it shows the epoch.  A 64-bit
+// access is single-copy atomic, so value and tag arrive together and no
+// fence or barrier is needed between writer and reader.  Stale words (earlier
+// calls, or zero-filled memory) carry smaller epochs.
+__device__ __forceinline__ void st_tag(unsigned long long* p, uint32_t v, uint32_t epoch) {
+    const unsigned long long x = ((unsigned long long)epoch << 32) | v;
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(x) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tag(const unsigned long long* p) {
+    unsigned long long x;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(x) : "l"(p) : "memory");
+    return x;
+}
+__device__ __forceinline__ bool tag_ok(unsigned long long x, uint32_t epoch) {
+    return (uint32_t)(x >> 32) == epoch;
+}
+
+// dst[i] = value of src[i] for i in [0, n), each polled until it carries
+// `epoch`; the CTA's threads take i = tid + k * blockDim.x, 4 loads in flight
+// per thread.  Bounded: false (and the error bit) on timeout.
+__device__ __forceinline__ bool poll_copy(uint32_t* dst, const unsigned long long* src, int n, uint32_t epoch,
+                                          uint32_t* err) {
+    constexpr int UNR = 4;
+    const long long t0 = clock64();
+    for (int i0 = threadIdx.x; i0 < n; i0 += blockDim.x * UNR) {
+        unsigned long long w[UNR];
+        uint32_t pend = 0u;
+#pragma unroll
+        for (int r = 0; r < UNR; ++r) {
+            const int i = i0 + r * blockDim.x;
+            if (i < n) {
+                w[r] = ld_tag(src + i);
+                pend |= 1u << r;
+            }
+        }
+        while (true) {
+#pragma unroll
+            for (int r = 0; r < UNR; ++r) {
+                if ((pend >> r & 1u) && tag_ok(w[r], epoch)) {
+                    dst[i0 + r * blockDim.x] = (uint32_t)w[r];
+                    pend &= ~(1u << r);
+                }
+            }
+            if (!pend) break;
+            if (clock64() - t0 > kWaitCycles) {
+                atomicOr(err, LP_DEVERR_WAIT_TIMEOUT);
+                return false;
+            }
+#pragma unroll
+            for (int r = 0; r < UNR; ++r)
+                if (pend >> r & 1u) w[r] = ld_tag(src + i0 + r * blockDim.x);
+        }
+    }
+    return true;
+}
+
 // CTA -> (unit, index within unit, CTAs of the unit)
 __device__ __forceinline__ void fused_cta_unit(int cta, int nctas, int U, int* u, int* j, int* n) {
     const int base = nctas / U, extra = nctas % U;
@@ -210,10 +268,17 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     fused_cta_unit(blockIdx.x, gridDim.x, p.U, &u, &cj, &cn);
     uint32_t* ubar = p.bar + u;
     uint32_t bphase = 0;  // top bit of the unit's barrier word (thread 0), read before the first arrival
+    __shared__ uint32_t s_epoch;
     if (tid == 0) {
         uint32_t v;
         asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ubar) : "memory");
         bphase = v & 0x80000000u;
+        // every CTA of every call adds 1: in call n the old values lie in
+        // [G*(n-1), G*n) for G = gridDim.x, whatever the order and even if a
+        // CTA of an earlier call returned early
+        unsigned long long old;
+        asm volatile("atom.add.relaxed.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(p.epoch_ctr) : "memory");
+        s_epoch = (uint32_t)(old / gridDim.x) + 1u;
     }
     const int b = u / p.Hkv, hkv = u - b * p.Hkv;
     // the CTA's tokens: a run of whole bitmap words of the candidate window
@@ -239,6 +304,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         fence_barrier_init();
     }
     __syncthreads();
+    // (the epoch stays in shared memory, s_epoch: a register held across the
+    // scorer would spill)
     // ---- start streaming the phase-B code tiles right away ----
     uint64_t policy = 0;
     const int npre = ntiles < kFStages ? ntiles : kFStages;
@@ -267,8 +334,6 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     // (32 KB); warp w dots rows 4w..4w+3 of a stage with the summed query and
     // reduces the 4 dot products with a 6-shuffle transpose.
     {
-        // zero the unit's per-call state used after barrier A
-        for (int i = cj * kFThreads + tid; i < kNB; i += cn * kFThreads) p.hist[(int64_t)u * kNB + i] = 0u;
         constexpr int64_t kRows = 32 * 256;  // codeword rows of one unit
         const int64_t f_begin = (kRows * cj / cn) & ~(int64_t)7;
         const int64_t f_end = cj + 1 == cn ? kRows : ((kRows * (cj + 1) / cn) & ~(int64_t)7);
@@ -337,15 +402,14 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 tot += __shfl_xor_sync(0xffffffffu, tot, 2);
                 tot += __shfl_xor_sync(0xffffffffu, tot, 1);
                 const int j = (lane >> 3) & 3;
-                if ((lane & 7) == 0 && fr + j < f_end) p.lut[((int64_t)u * 256 + k0 + j) * 32 + m] = tot;
+                if ((lane & 7) == 0 && fr + j < f_end)
+                    st_tag(p.lut + ((int64_t)u * 256 + k0 + j) * 32 + m, __float_as_uint(tot), s_epoch);
             }
             __syncthreads();  // stage c fully consumed
             if (tid == 0 && c + 3 < nchunk) issue_chunk(c + 3);
         }
     }
     if (stamp) p.phase_ns[1] = global_ns();
-    if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) { drain(0); return; }
-    if (stamp) p.phase_ns[2] = global_ns();
 
     using Scan = cub::BlockScan<int, kFThreads>;
     __shared__ typename Scan::TempStorage scan_tmp;
@@ -354,11 +418,40 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     BinParams bp;
     float from_fx;
     {
-        // stage the unit table: fp32 -> per-m bounds -> int32 fixed point (dup layout)
-        const float4* g4 = reinterpret_cast<const float4*>(p.lut + (int64_t)u * 256 * 32);
+        // stage the unit table: fp32 -> per-m bounds -> int32 fixed point (dup
+        // layout).  Its rows come from all CTAs of the unit: each value is
+        // polled until it carries this call's epoch.
         float4 v[4];
+        {
+            const unsigned long long* gl = p.lut + (int64_t)u * 256 * 32;
+            bool ok = true;
+            const long long t0 = clock64();
+            // two rounds of 8 words (two float4 each) keep the register count down
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = __ldcg(g4 + tid + j * kFThreads);
+            for (int h = 0; h < 2; ++h) {
+                unsigned long long w[8];
+                uint32_t pend = 0xFFu;
+                while (ok) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        if (pend >> e & 1u) w[e] = ld_tag(gl + 4 * (tid + (2 * h + (e >> 2)) * kFThreads) + (e & 3));
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        if (tag_ok(w[e], s_epoch)) pend &= ~(1u << e);
+                    if (!pend) break;
+                    if (clock64() - t0 > kWaitCycles) {
+                        atomicOr(p.err, LP_DEVERR_WAIT_TIMEOUT);
+                        ok = false;
+                    }
+                }
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj)
+                    v[2 * h + jj] = make_float4(__uint_as_float((uint32_t)w[4 * jj]), __uint_as_float((uint32_t)w[4 * jj + 1]),
+                                                __uint_as_float((uint32_t)w[4 * jj + 2]), __uint_as_float((uint32_t)w[4 * jj + 3]));
+            }
+            if (__syncthreads_or(!ok)) { drain(0); return; }
+        }
+        if (stamp) p.phase_ns[2] = global_ns();
         // thread's m group is (tid & 7); reduce min/max per m over k
         // (scratch in the score buffer, which is not written yet)
         float (*s_mmin)[32] = reinterpret_cast<float (*)[32]>(s_scores);
@@ -508,10 +601,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             }
         }
         if (__syncthreads_or(s_abort)) { drain(0); return; }
-        for (int i = tid; i < kNB; i += kFThreads) {
-            const uint32_t c = s_hist[i];
-            if (c) atomicAdd(&p.hist[(int64_t)u * kNB + i], c);
-        }
+        // the local histogram, for the exchange path (read after a unit barrier)
+        for (int i = tid; i < kNB; i += kFThreads) p.chist[(int64_t)blockIdx.x * kNB + i] = s_hist[i];
         // ---- publish the CTA's candidates for the unit's selection: every
         //      own token whose bin is at or above b_j, the CTA's threshold
         //      bin for pub_target tokens (all tokens if it has fewer), sorted
@@ -539,9 +630,10 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             uint32_t cw = 0u;
             if (tid < kPubWin - 1) cw = bj + tid < kNB ? s_hist[bj + tid] : 0u;
             else if (tid == kPubWin - 1) cw = s_cur[kPubWin - 1];
+            unsigned long long* pw = p.pwin + (int64_t)blockIdx.x * (kPubWin + 2);
             if (tid < kPubWin) {
                 s_cw[tid] = cw;
-                p.pub_win[(int64_t)blockIdx.x * kPubWin + tid] = pub_ok ? cw : 0u;
+                st_tag(pw + tid, pub_ok ? cw : 0u, s_epoch);
             }
             __syncthreads();
             // descending offsets off_w = sum_{w' > w} c_w' (thread t scans c_{W-1-t})
@@ -550,33 +642,72 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             if (tid < kPubWin) s_cur[kPubWin - 1 - tid] = (uint32_t)off;
             __syncthreads();
             if (pub_ok) {
-                float2* slot = p.pub + (int64_t)blockIdx.x * p.pub_cap;
+                unsigned long long* slot = p.pub + (int64_t)blockIdx.x * p.pub_cap * 2;
                 for (int lt = tid; lt < ntok; lt += kFThreads) {
                     const float s = s_scores[lt];
                     const int bin = score_bin(s, bp.lo, bp.inv_w, kNB);
                     if (bin >= bj) {
                         const int pos = (int)atomicAdd(&s_cur[min(bin - bj, kPubWin - 1)], 1u);
-                        const float2 e = make_float2(s, __int_as_float(t_begin + lt));
-                        slot[pos] = e;
-                        s_own[pos] = e;
+                        st_tag(slot + 2 * pos, __float_as_uint(s), s_epoch);
+                        st_tag(slot + 2 * pos + 1, (uint32_t)(t_begin + lt), s_epoch);
+                        s_own[pos] = make_float2(s, __int_as_float(t_begin + lt));
                     }
                 }
             }
-            if (tid == 0) p.pub_hdr[blockIdx.x] = pub_ok ? make_int2(npub, bj) : make_int2(0, kNB);
+            if (tid == 0) {
+                st_tag(pw + kPubWin, pub_ok ? (uint32_t)npub : 0u, s_epoch);
+                st_tag(pw + kPubWin + 1, pub_ok ? (uint32_t)bj : (uint32_t)kNB, s_epoch);
+            }
         }
     }
     if (stamp) p.phase_ns[3] = global_ns();
-    if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
-    if (stamp) p.phase_ns[4] = global_ns();
     if (tid == kFThreads - 32) {  // a lane off the select critical path
         prefetch_share(p.pf_ptr[0], p.pf_bytes[0], p.pf_count[0], p.pf_stride[0]);
         prefetch_share(p.pf_ptr[1], p.pf_bytes[1], p.pf_count[1], p.pf_stride[1]);
     }
 
+    // ---- phase E staging and row order, shared with phase C's early gather:
+    //      rows = [above-threshold tokens][sink share][local share][tie winners];
+    //      s_list holds the above-threshold tokens followed by the tie winners ----
+    constexpr int D = 128;
+    constexpr int R = kFMaxRows;
+    int* s_list = reinterpret_cast<int*>(s_scores);  // [<= kFScoreCap] (scores consumed by then)
+    KT* s_k = reinterpret_cast<KT*>(s_ring);         // [R][128] (the ring is free after phase B)
+    KT* s_v = s_k + R * D;                           // [R][128]
+    const KT* kb = reinterpret_cast<const KT*>(p.keys) + (int64_t)b * p.k_stride_b + (int64_t)hkv * p.k_stride_h;
+    const KT* vb = reinterpret_cast<const KT*>(p.vals) + (int64_t)b * p.v_stride_b + (int64_t)hkv * p.v_stride_h;
+    constexpr int CH = D * (int)sizeof(KT) / 16;
+    constexpr int EPC = 16 / (int)sizeof(KT);
+    // the unit's sink and local-window rows are spread evenly over its CTAs
+    const int sk0 = (int)((int64_t)p.n_sink * cj / cn), sk1 = (int)((int64_t)p.n_sink * (cj + 1) / cn);
+    const int lc0 = (int)((int64_t)p.n_local * cj / cn), lc1 = (int)((int64_t)p.n_local * (cj + 1) / cn);
+    const int n_sink_here = sk1 - sk0;
+    const int n_loc_here = lc1 - lc0;
+    auto row_token = [&](int rr, int nabove) -> int {
+        if (rr < nabove) return s_list[rr];
+        rr -= nabove;
+        if (rr < n_sink_here) return sk0 + rr;
+        rr -= n_sink_here;
+        if (rr < n_loc_here) return p.local_start + lc0 + rr;
+        return s_list[nabove + rr - n_loc_here];
+    };
+    // rows c0r + [r_lo, r_hi) of the row list -> staging rows [r_lo, r_hi)
+    // (16-byte cp.async; every thread commits one group)
+    auto issue_rows = [&](int c0r, int r_lo, int r_hi, int nabove) {
+        for (int c = r_lo * CH + tid; c < r_hi * CH; c += kFThreads) {
+            const int r = c / CH, part = c - r * CH;
+            const int64_t t = min(max(row_token(c0r + r, nabove), 0), p.T_total - 1);
+            cp_async16(s_k + r * D + part * EPC, kb + t * p.k_stride_t + part * EPC);
+            cp_async16(s_v + r * D + part * EPC, vb + t * p.v_stride_t + part * EPC);
+        }
+        cp_async_commit();
+    };
+    __shared__ int s_nabove, s_nwin;
+
     // ================= phase C: select =================
     uint32_t* bm = p.bitmap + (int64_t)u * p.bm_stride;
     const float* gsc_c = p.sel_scores + (int64_t)u * p.sel_stride;
-    __shared__ int s_cnt_above, s_win_before, s_topk_off, s_ntie_loc, s_ntie, s_nsel, s_fast;
+    __shared__ int s_cnt_above, s_win_before, s_topk_off, s_ntie_loc, s_ntie, s_fast;
     uint32_t* s_selw = s_hist + 1024;  // own words: selected bits (exchange path: above-threshold bits)
     uint32_t* s_win = s_hist + 1536;   // exchange path: tie winners of the own range (bit lt)
     const int nw_own = w_end - w_begin;
@@ -584,47 +715,38 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     // ---- fast path: the unit's threshold bin from the published windows,
     //      then only the published entries of that bin are exchanged ----
     {
-        uint32_t* s_wins = reinterpret_cast<uint32_t*>(s_lut);             // [cn][kPubWin] window counts
-        int2* s_hdr = reinterpret_cast<int2*>(s_lut + 32768);               // [cn] (count, b_j)
-        int* s_tst = reinterpret_cast<int*>(s_lut + 32768 + 1024);          // [cn] entries above b* per slot
+        constexpr int PW = kPubWin + 2;                                      // window, count, b_j per CTA
+        uint32_t* s_pw = reinterpret_cast<uint32_t*>(s_lut);                 // [cn][PW]
+        int* s_tst = reinterpret_cast<int*>(s_lut + 33792);                  // [cn] entries above b* per slot
         int* s_tcn = s_tst + kPubMaxCtas;                                    // [cn] entries in bin b* per slot
         int* s_toff = s_tcn + kPubMaxCtas;                                   // [cn + 1] combined tie offsets
-        float* s_tk = reinterpret_cast<float*>(s_ring);                      // tie keys  [kTieCap]
-        int* s_ti = reinterpret_cast<int*>(s_ring + kTieCap * 4);            // tie index [kTieCap]
+        float* s_tk = reinterpret_cast<float*>(s_lut + 35840);               // tie keys  [kFastTieCap]
+        int* s_ti = reinterpret_cast<int*>(s_lut + 35840 + kFastTieCap * 4); // tie index [kFastTieCap]
         const float2* s_own = reinterpret_cast<const float2*>(s_ring + 64 * 1024);
         for (int i = tid; i < kNB; i += kFThreads) s_hist[i] = 0u;
         if (tid == 0) { s_fast = 0; s_bstar = -1; s_above = 0; s_ntie = 0; s_win_before = 0; s_topk_off = 0; }
         const bool pub = p.pub_cap > 0;
         if (pub) {
-            // one round trip: the headers and the windows of the unit's CTAs
-            for (int j = tid; j < cn; j += kFThreads) s_hdr[j] = __ldcg(p.pub_hdr + ubase + j);
-            const int nall = cn * kPubWin;
-            constexpr int UNR = 8;
-            for (int i0 = tid; i0 < nall; i0 += kFThreads * UNR) {
-                uint32_t v[UNR];
-#pragma unroll
-                for (int r = 0; r < UNR; ++r) {
-                    const int i = i0 + r * kFThreads;
-                    if (i < nall) v[r] = __ldcg(p.pub_win + (int64_t)ubase * kPubWin + i);
-                }
-#pragma unroll
-                for (int r = 0; r < UNR; ++r)
-                    if (i0 + r * kFThreads < nall) s_wins[i0 + r * kFThreads] = v[r];
-            }
+            // the unit's windows and headers, as their CTAs publish them
+            const bool ok = poll_copy(s_pw, p.pwin + (int64_t)ubase * PW, cn * PW, s_epoch, p.err);
+            if (__syncthreads_or(!ok)) return;
+        } else {
+            __syncthreads();
         }
-        __syncthreads();
+        if (stamp) p.phase_ns[4] = global_ns();
         if (pub) {
             // the unit's histogram over the published bins (the last window
             // bin counts at its lower edge; it is above any usable b*)
-            for (int i = tid; i < cn * kPubWin; i += kFThreads) {
-                const uint32_t c = s_wins[i];
-                if (c) atomicAdd(&s_hist[min(s_hdr[i / kPubWin].y + (i % kPubWin), kNB - 1)], c);
+            for (int i = tid; i < cn * PW; i += kFThreads) {
+                const int j = i / PW, w = i - j * PW;
+                const uint32_t c = s_pw[i];
+                if (w < kPubWin && c) atomicAdd(&s_hist[min((int)s_pw[j * PW + kPubWin + 1] + w, kNB - 1)], c);
             }
             int n_union = 0, bmax = 0, bmin = kNB;
             for (int j = 0; j < cn; ++j) {
-                n_union += s_hdr[j].x;
-                bmax = max(bmax, s_hdr[j].y);
-                bmin = min(bmin, s_hdr[j].y);
+                n_union += (int)s_pw[j * PW + kPubWin];
+                bmax = max(bmax, (int)s_pw[j * PW + kPubWin + 1]);
+                bmin = min(bmin, (int)s_pw[j * PW + kPubWin + 1]);
             }
             __syncthreads();
             if (n_union >= p.k) find_threshold_bin<kFThreads>(s_hist, p.k, &s_bstar, &s_above);
@@ -635,7 +757,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             const int bs = s_bstar;
             if (tid == 0)
                 s_fast = (p.k > 0 && bs >= 0 && bs >= bmax && bs < bmin + kPubWin - 1 &&
-                          (int)s_hist[bs] <= kTieCap) ? 1 : 0;
+                          (int)s_hist[bs] <= kFastTieCap) ? 1 : 0;
         }
         __syncthreads();
         if (s_fast) {
@@ -643,14 +765,14 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             const int need = p.k - s_above;
             // per slot: entries above b* (they lead its sorted list) and in b*
             for (int j = warp; j < cn; j += NW) {
-                const int wb = bs - s_hdr[j].y;  // 0 <= wb < kPubWin - 1
+                const int wb = bs - (int)s_pw[j * PW + kPubWin + 1];  // 0 <= wb < kPubWin - 1
                 uint32_t a = 0u;
-                for (int w = wb + 1 + lane; w < kPubWin; w += 32) a += s_wins[j * kPubWin + w];
+                for (int w = wb + 1 + lane; w < kPubWin; w += 32) a += s_pw[j * PW + w];
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
                 if (lane == 0) {
                     s_tst[j] = (int)a;
-                    s_tcn[j] = (int)s_wins[j * kPubWin + wb];
+                    s_tcn[j] = (int)s_pw[j * PW + wb];
                 }
             }
             for (int i = tid; i < nw_own; i += kFThreads) s_selw[i] = 0u;
@@ -686,20 +808,71 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 s_topk_off = c;
             }
             __syncthreads();
-            // the unit's tie-bin entries (one round trip)
+            // the unit's tie-bin entries: loads issued first (up to 2 per thread)
             const int ntie = s_ntie;
-            for (int i = tid; i < ntie; i += kFThreads) {
-                int lo = 0, hi = cn - 1;  // slot of combined entry i: the last j with s_toff[j] <= i
-                while (lo < hi) {
-                    const int mid = (lo + hi + 1) >> 1;
-                    if (s_toff[mid] <= i) lo = mid;
-                    else hi = mid - 1;
+            const unsigned long long* tsrc[2];
+            unsigned long long tw[2][2];
+            uint32_t tpend = 0u;
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int i = tid + r * kFThreads;
+                tsrc[r] = nullptr;
+                if (i < ntie) {
+                    int lo = 0, hi = cn - 1;  // slot of combined entry i: the last j with s_toff[j] <= i
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if (s_toff[mid] <= i) lo = mid;
+                        else hi = mid - 1;
+                    }
+                    tsrc[r] = p.pub + ((int64_t)(ubase + lo) * p.pub_cap + s_tst[lo] + (i - s_toff[lo])) * 2;
+                    tw[r][0] = ld_tag(tsrc[r]);
+                    tw[r][1] = ld_tag(tsrc[r] + 1);
+                    tpend |= 1u << r;
                 }
-                const float2 e = __ldcg(p.pub + (int64_t)(ubase + lo) * p.pub_cap + s_tst[lo] + (i - s_toff[lo]));
-                s_tk[i] = e.x;
-                s_ti[i] = __float_as_int(e.y);
+            }
+            // own above-threshold tokens in ascending order -> s_list; their
+            // K/V rows and the sink and local shares start loading now, while
+            // the tie bin is settled
+            {
+                const uint32_t bits = tid < nw_own ? s_selw[tid] : 0u;
+                int pos, total;
+                Scan(scan_tmp).ExclusiveSum(__popc(bits), pos, total);
+                for (uint32_t b2 = bits; b2; b2 &= b2 - 1) s_list[pos++] = (w_begin + tid) * 32 + __ffs(b2) - 1;
+                if (tid == 0) s_nabove = total;
             }
             __syncthreads();
+            issue_rows(0, 0, min(s_nabove + n_sink_here + n_loc_here, R), s_nabove);
+            {
+                bool ok = true;
+                const long long t0 = clock64();
+                while (tpend) {
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        if ((tpend >> r & 1u) && tag_ok(tw[r][0], s_epoch) && tag_ok(tw[r][1], s_epoch)) {
+                            const int i = tid + r * kFThreads;
+                            s_tk[i] = __uint_as_float((uint32_t)tw[r][0]);
+                            s_ti[i] = (int)(uint32_t)tw[r][1];
+                            tpend &= ~(1u << r);
+                        }
+                    }
+                    if (!tpend) break;
+                    if (clock64() - t0 > kWaitCycles) {
+                        atomicOr(p.err, LP_DEVERR_WAIT_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
+#pragma unroll
+                    for (int r = 0; r < 2; ++r)
+                        if (tpend >> r & 1u) {
+                            tw[r][0] = ld_tag(tsrc[r]);
+                            tw[r][1] = ld_tag(tsrc[r] + 1);
+                        }
+                }
+                if (__syncthreads_or(!ok)) {
+                    cp_async_wait<0>();
+                    return;
+                }
+            }
             // rank (score desc, index asc) of the own tie entries (all of them
             // when the top-k indices are requested): the first `need` win
             const int i0 = p.topk_out ? 0 : s_toff[cj];
@@ -710,7 +883,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 int rank = 0;
                 for (int j = 0; j < ntie; ++j) rank += sel_before(s_tk[j], s_ti[j], ki, ii);
                 if (rank < need) {
-                    if (ii >= t_begin && ii < t_end) atomicOr(&s_selw[(ii >> 5) - w_begin], 1u << (ii & 31));
+                    if (ii >= t_begin && ii < t_end) atomicOr(&s_win[(ii - t_begin) >> 5], 1u << ((ii - t_begin) & 31));
                     else if (ii < t_begin) atomicAdd(&s_topk_off, 1);
                 }
             }
@@ -722,7 +895,14 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         // ---- exchange path: threshold bin of the unit histogram, ballots,
         //      tie-bin tokens through the tie slots, one more barrier ----
         float2* s_tloc = reinterpret_cast<float2*>(s_lut);  // this CTA's tie-bin tokens (<= kTieCap)
-        for (int i = tid; i < kNB; i += kFThreads) s_hist[i] = __ldcg(p.hist + (int64_t)u * kNB + i);
+        // the unit histogram: sum of its CTAs' local histograms (published
+        // with plain stores in phase B, visible after this barrier)
+        if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
+        for (int i = tid; i < kNB; i += kFThreads) {
+            uint32_t c = 0u;
+            for (int j = 0; j < cn; ++j) c += __ldcg(p.chist + (int64_t)(ubase + j) * kNB + i);
+            s_hist[i] = c;
+        }
         if (tid == 0) { s_bstar = kNB; s_above = 0; s_cnt_above = 0; s_ntie_loc = 0; }
         __syncthreads();
         if (p.k > 0) find_threshold_bin<kFThreads>(s_hist, p.k, &s_bstar, &s_above);
@@ -795,7 +975,6 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         __syncthreads();
         const int ntie = s_ntie;
         const bool overflow = ntie > kTieCap;  // identical in every CTA of the unit
-        if (stamp) p.phase_ns[6] = global_ns();
         if (!overflow && need > 0) {
             for (int i = tid; i < ntie; i += kFThreads) {
                 // source CTA of combined entry i: the last j with s_toff[j] <= i
@@ -917,96 +1096,101 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
 
 
 
-    if (stamp && s_fast) p.phase_ns[6] = global_ns();
 
     // ================= phase E: attention over the CTA's own kept rows =================
     {
-        constexpr int D = 128;
-        constexpr int R = kFMaxRows;
-        int* s_list = reinterpret_cast<int*>(s_scores);                             // [<= kFScoreCap]
-        float* s_q = s_qu;                                                           // [8][128]
-        float* s_red = reinterpret_cast<float*>(s_lut + kFScoreCap * 4);            // [512] P.V half sums
-        float* s_p = s_red + 512;                                                    // [8][R]
-        float* s_m = s_p + 8 * R;                                                    // [8] running max
-        float* s_l = s_m + 8;                                                        // [8] running sum
-        float* s_al = s_l + 8;                                                       // [8] rescale
-        KT* s_k = reinterpret_cast<KT*>(s_ring);                                     // [R][128]
-        KT* s_v = s_k + R * D;                                                       // [R][128]
+        const float* s_q = s_qu;  // [G][128] fp32 query rows
+        // ---- row list: above-threshold tokens (built in phase C on the fast
+        //      path), then the tie winners (bit lt of s_win = token t_begin + lt),
+        //      each in ascending token order ----
+        if (!s_fast) {
+            const uint32_t bits = tid < nw_own ? s_selw[tid] : 0u;
+            int pos, total;
+            Scan(scan_tmp).ExclusiveSum(__popc(bits), pos, total);
+            for (uint32_t b2 = bits; b2; b2 &= b2 - 1) s_list[pos++] = (w_begin + tid) * 32 + __ffs(b2) - 1;
+            if (tid == 0) s_nabove = total;
+            __syncthreads();
+        }
+        {
+            const int nww = (ntok + 31) / 32;
+            const uint32_t bits = tid < nww ? s_win[tid] : 0u;
+            int pos, total;
+            Scan(scan_tmp).ExclusiveSum(__popc(bits), pos, total);
+            pos += s_nabove;
+            for (uint32_t b2 = bits; b2; b2 &= b2 - 1) s_list[pos++] = t_begin + tid * 32 + __ffs(b2) - 1;
+            if (tid == 0) s_nwin = total;
+        }
         if (!s_fast && p.topk_out && tid == 0) s_topk_off = s_win_before;
         __syncthreads();
-        if (!s_fast && p.topk_out) {
-            int c = 0;
-            for (int j = tid; j < cj; j += kFThreads) c += (int)__ldcg(p.cta_count + ubase + j);
-            if (c) atomicAdd(&s_topk_off, c);
-        }
-
-        // ---- own selected tokens in ascending order, from the selected bits
-        //      (word w of the CTA covers tokens 32*(w_begin+w) .. +31) and the
-        //      exchange path's tie winners (bit lt = token t_begin + lt) ----
-        {
+        if (p.topk_out) {
+            // the CTA's selected tokens (above-threshold | tie winners) in
+            // ascending order, at its rank offset within the unit
+            if (!s_fast) {
+                int c = 0;
+                for (int j = tid; j < cj; j += kFThreads) c += (int)__ldcg(p.cta_count + ubase + j);
+                if (c) atomicAdd(&s_topk_off, c);
+            }
             const int shift0 = t_begin - w_begin * 32;  // 0 except for the first CTA (c0 % 32)
-            // winners in word-aligned form
-            auto win_word = [&](int w) -> uint32_t {
-                // bits of tokens 32*(w_begin+w) + i  <->  lt = 32*w + i - shift0
-                const int lt0 = 32 * w - shift0;
-                uint32_t r = 0u;
-                const int wl = lt0 >> 5, sh = lt0 & 31;  // lt0 may be negative for w = 0
-                if (lt0 >= 0) {
-                    r = s_win[wl] >> sh;
-                    if (sh && wl + 1 < (ntok + 31) / 32) r |= s_win[wl + 1] << (32 - sh);
-                } else {
-                    r = s_win[0] << (-lt0);
-                }
-                return r;
-            };
-            int cnt = 0;
             uint32_t wordsel = 0u;
             const int w = tid;  // one own word per thread (nw_own <= kFScoreCap/32 + 2 <= 512)
             if (w < nw_own) {
-                wordsel = s_selw[w] | (ntok > 0 ? win_word(w) : 0u);
+                // winners of tokens 32*(w_begin+w) + i  <->  bit lt = 32*w + i - shift0
+                const int lt0 = 32 * w - shift0;
+                uint32_t r = 0u;
+                if (ntok > 0) {
+                    const int wl = lt0 >> 5, sh = lt0 & 31;  // lt0 may be negative for w = 0
+                    if (lt0 >= 0) {
+                        r = s_win[wl] >> sh;
+                        if (sh && wl + 1 < (ntok + 31) / 32) r |= s_win[wl + 1] << (32 - sh);
+                    } else {
+                        r = s_win[0] << (-lt0);
+                    }
+                }
+                wordsel = s_selw[w] | r;
                 const int tb = (w_begin + w) * 32;
                 if (tb < p.c0) wordsel &= ~0u << (p.c0 - tb);
                 if (tb + 32 > p.c1) wordsel &= (p.c1 - tb) >= 32 ? ~0u : ((1u << (p.c1 - tb)) - 1u);
-                cnt = __popc(wordsel);
             }
             int pos, total;
-            Scan(scan_tmp).ExclusiveSum(cnt, pos, total);
-            for (uint32_t b2 = wordsel; b2; b2 &= b2 - 1) s_list[pos++] = (w_begin + w) * 32 + __ffs(b2) - 1;
-            if (tid == 0) s_nsel = total;
-        }
-        if (tid < 8) { s_m[tid] = -INFINITY; s_l[tid] = 0.f; }
-        __syncthreads();
-        const int nsel = s_nsel;
-        if (p.topk_out) {
+            __syncthreads();  // s_topk_off complete; scan_tmp free
+            Scan(scan_tmp).ExclusiveSum(__popc(wordsel), pos, total);
             const int off = s_topk_off;
-            for (int i = tid; i < nsel; i += kFThreads)
-                if (off + i < p.k) p.topk_out[(int64_t)u * p.k + off + i] = s_list[i];
+            for (uint32_t b2 = wordsel; b2; b2 &= b2 - 1) {
+                if (off + pos < p.k) p.topk_out[(int64_t)u * p.k + off + pos] = (w_begin + w) * 32 + __ffs(b2) - 1;
+                ++pos;
+            }
         }
-        // the unit's sink and local-window rows are spread evenly over its CTAs
-        const int sk0 = (int)((int64_t)p.n_sink * cj / cn), sk1 = (int)((int64_t)p.n_sink * (cj + 1) / cn);
-        const int lc0 = (int)((int64_t)p.n_local * cj / cn), lc1 = (int)((int64_t)p.n_local * (cj + 1) / cn);
-        const int n_sink_here = sk1 - sk0;
-        const int n_loc_here = lc1 - lc0;
-        const int nrows = n_sink_here + nsel + n_loc_here;
+        const int nabove = s_nabove;
+        const int n_early = nabove + n_sink_here + n_loc_here;
+        const int nrows = n_early + s_nwin;
+        const int n_issued = s_fast ? min(n_early, R) : 0;  // rows already loading since phase C
 
-        const KT* kb = reinterpret_cast<const KT*>(p.keys) + (int64_t)b * p.k_stride_b + (int64_t)hkv * p.k_stride_h;
-        const KT* vb = reinterpret_cast<const KT*>(p.vals) + (int64_t)b * p.v_stride_b + (int64_t)hkv * p.v_stride_h;
-        constexpr int CH = D * (int)sizeof(KT) / 16;
-        constexpr int EPC = 16 / (int)sizeof(KT);
-        // logits (log2 domain) of staging rows [r_lo, r_hi)
-        auto logits = [&](int r_lo, int r_hi) {
+        // ---- per-warp flash-decode: warp w takes rows 4w..4w+3 (+64 per
+        //      pass) of every chunk; lane l owns dims 4l..4l+3 of every head
+        //      and keeps its own running max / sum / P.V (online softmax) ----
+        float wm[8], wl[8];
+        float4 wacc[8];
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            wm[g] = -INFINITY;
+            wl[g] = 0.f;
+            wacc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        auto attend = [&](int r_lo, int r_hi) {
             if (p.G == 4) {
-                // warp handles rows 4w..4w+3 (+64 per pass); lane covers dims 4l..4l+3;
-                // the 16 (row, head) partial dots are reduced by one 16-way transpose
                 float4 qv[4];
 #pragma unroll
                 for (int g = 0; g < 4; ++g) qv[g] = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
-                for (int r0w = r_lo + warp * 4; r0w < r_hi; r0w += NW * 4) {
+                for (int r0 = r_lo + warp * 4; r0 < r_hi; r0 += NW * 4) {
+                    // the 16 (row, head) dots, reduced by one 16-way transpose:
+                    // lanes 2i, 2i+1 end with the total of idx i = 4 * row + head
                     float v[16];
+                    float4 vv[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const float4 kv = (r0w + j < r_hi) ? Vec4<KT>::load(s_k + (r0w + j) * D + lane * 4)
-                                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const bool ok = r0 + j < r_hi;
+                        const float4 kv = ok ? Vec4<KT>::load(s_k + (r0 + j) * D + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        vv[j] = ok ? Vec4<KT>::load(s_v + (r0 + j) * D + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                         for (int g = 0; g < 4; ++g) {
                             float a = qv[g].x * kv.x;
@@ -1042,14 +1226,40 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                     const float send = b1 ? x2[0] : x2[1];
                     float tot = keep + __shfl_xor_sync(0xffffffffu, send, 2);
                     tot += __shfl_xor_sync(0xffffffffu, tot, 1);
-                    const int idx = (lane >> 1) & 15;  // = 4 * row + head
-                    const int rr = r0w + (idx >> 2);
-                    if ((lane & 1) == 0 && rr < r_hi) s_p[(idx & 3) * R + rr] = tot * p.scale_log2;
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        float s[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float x = __shfl_sync(0xffffffffu, tot, 2 * (4 * j + g)) * p.scale_log2;
+                            s[j] = r0 + j < r_hi ? x : -INFINITY;
+                        }
+                        const float mn = fmaxf(wm[g], fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3])));
+                        const float sc = exp2f(wm[g] - mn);  // 0 while the warp has no row yet
+                        float pr[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) pr[j] = exp2f(s[j] - mn);
+                        wl[g] = fmaf(wl[g], sc, (pr[0] + pr[1]) + (pr[2] + pr[3]));
+                        float4 a = wacc[g];
+                        a.x *= sc; a.y *= sc; a.z *= sc; a.w *= sc;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            a.x = fmaf(pr[j], vv[j].x, a.x);
+                            a.y = fmaf(pr[j], vv[j].y, a.y);
+                            a.z = fmaf(pr[j], vv[j].z, a.z);
+                            a.w = fmaf(pr[j], vv[j].w, a.w);
+                        }
+                        wacc[g] = a;
+                        wm[g] = mn;
+                    }
                 }
             } else {
                 for (int r = r_lo + warp; r < r_hi; r += NW) {
                     const float4 kv = Vec4<KT>::load(s_k + r * D + lane * 4);
-                    for (int g = 0; g < p.G; ++g) {
+                    const float4 vv = Vec4<KT>::load(s_v + r * D + lane * 4);
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        if (g >= p.G) break;
                         const float4 qv = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
                         float a = qv.x * kv.x;
                         a = fmaf(qv.y, kv.y, a);
@@ -1057,128 +1267,87 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                         a = fmaf(qv.w, kv.w, a);
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-                        if (lane == g) s_p[g * R + r] = a * p.scale_log2;
+                        const float s = a * p.scale_log2;
+                        const float mn = fmaxf(wm[g], s);
+                        const float sc = exp2f(wm[g] - mn);
+                        const float pr = exp2f(s - mn);
+                        wl[g] = fmaf(wl[g], sc, pr);
+                        float4 c = wacc[g];
+                        c.x = fmaf(c.x, sc, pr * vv.x);
+                        c.y = fmaf(c.y, sc, pr * vv.y);
+                        c.z = fmaf(c.z, sc, pr * vv.z);
+                        c.w = fmaf(c.w, sc, pr * vv.w);
+                        wacc[g] = c;
+                        wm[g] = mn;
                     }
                 }
             }
         };
-
-        float acc0 = 0.f, acc1 = 0.f;  // P.V for outputs o = tid and tid + 512
         for (int c0r = 0; c0r < nrows; c0r += R) {
             const int nr = min(R, nrows - c0r);
-            // K/V rows of the chunk (16-byte cp.async)
-            for (int c = tid; c < nr * CH; c += kFThreads) {
-                const int r = c / CH, part = c - r * CH;
-                const int rr = c0r + r;
-                const int tok = rr < n_sink_here ? sk0 + rr
-                              : rr < n_sink_here + nsel ? s_list[rr - n_sink_here]
-                              : p.local_start + lc0 + (rr - n_sink_here - nsel);
-                const int64_t t = min(max(tok, 0), p.T_total - 1);
-                cp_async16(s_k + r * D + part * EPC, kb + t * p.k_stride_t + part * EPC);
-                cp_async16(s_v + r * D + part * EPC, vb + t * p.v_stride_t + part * EPC);
+            int r_ready = 0;
+            if (c0r == 0 && n_issued > 0) {
+                // the chunk's first n_issued rows were issued in phase C; the
+                // rest (tie winners) loads while those are attended
+                issue_rows(0, n_issued, nr, nabove);
+                cp_async_wait<1>();
+                __syncthreads();
+                attend(0, n_issued);
+                r_ready = n_issued;
+            } else {
+                issue_rows(c0r, 0, nr, nabove);
             }
-            cp_async_commit();
             cp_async_wait<0>();
             __syncthreads();
-            logits(0, nr);
-            __syncthreads();
-            // online softmax update per head
-            for (int g = warp; g < p.G; g += NW) {
-                float mx = -INFINITY;
-                for (int r = lane; r < nr; r += 32) mx = fmaxf(mx, s_p[g * R + r]);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                const float m_old = s_m[g];
-                const float m_new = fmaxf(m_old, mx);
-                float sum = 0.f;
-                for (int r = lane; r < nr; r += 32) {
-                    const float e = exp2f(s_p[g * R + r] - m_new);
-                    s_p[g * R + r] = e;
-                    sum += e;
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-                __syncwarp();
-                if (lane == 0) {
-                    const float alpha = exp2f(m_old - m_new);  // 0 on the first chunk
-                    s_al[g] = alpha;
-                    s_l[g] = s_l[g] * alpha + sum;
-                    s_m[g] = m_new;
-                }
-            }
-            __syncthreads();
-            // P.V: thread -> (half, head g, dim pair dp); rows interleaved by half
-            {
-                const int npairs = p.G * (D / 2);
-                const int nhalf = npairs <= kFThreads / 2 ? 2 : 1;
-                const int pair = tid % (kFThreads / nhalf);
-                const int half = tid / (kFThreads / nhalf);
-                float x = 0.f, y = 0.f;
-                if (pair < npairs) {
-                    const int g = pair / (D / 2), dp = pair - g * (D / 2);
-                    const float* pg = s_p + g * R;
-                    float x1 = 0.f, y1 = 0.f;
-                    int r = half;
-                    for (; r + 3 * nhalf < nr; r += 4 * nhalf) {
-                        const float2 v0 = Vec4<KT>::load2(s_v + r * D + 2 * dp);
-                        const float2 v1 = Vec4<KT>::load2(s_v + (r + nhalf) * D + 2 * dp);
-                        const float2 v2 = Vec4<KT>::load2(s_v + (r + 2 * nhalf) * D + 2 * dp);
-                        const float2 v3 = Vec4<KT>::load2(s_v + (r + 3 * nhalf) * D + 2 * dp);
-                        const float p0 = pg[r], p1 = pg[r + nhalf], p2 = pg[r + 2 * nhalf], p3 = pg[r + 3 * nhalf];
-                        x = fmaf(p0, v0.x, x);
-                        y = fmaf(p0, v0.y, y);
-                        x1 = fmaf(p1, v1.x, x1);
-                        y1 = fmaf(p1, v1.y, y1);
-                        x = fmaf(p2, v2.x, x);
-                        y = fmaf(p2, v2.y, y);
-                        x1 = fmaf(p3, v3.x, x1);
-                        y1 = fmaf(p3, v3.y, y1);
-                    }
-                    for (; r < nr; r += nhalf) {
-                        const float2 vv = Vec4<KT>::load2(s_v + r * D + 2 * dp);
-                        x = fmaf(pg[r], vv.x, x);
-                        y = fmaf(pg[r], vv.y, y);
-                    }
-                    x += x1;
-                    y += y1;
-                }
-                if (nhalf == 2 && half == 1 && pair < npairs) {
-                    s_red[2 * pair] = x;
-                    s_red[2 * pair + 1] = y;
-                }
-                __syncthreads();
-                if (half == 0 && pair < npairs) {
-                    if (nhalf == 2) {
-                        x += s_red[2 * pair];
-                        y += s_red[2 * pair + 1];
-                    }
-                    const int g = pair / (D / 2);
-                    acc0 = fmaf(acc0, s_al[g], x);
-                    acc1 = fmaf(acc1, s_al[g], y);
-                }
-            }
-            __syncthreads();
+            attend(r_ready, nr);
+            __syncthreads();  // staging rows consumed before the next chunk lands
         }
-        // partial state of this CTA: (half 0, pair) threads own dims 2dp, 2dp+1
-        float* part = p.part + ((int64_t)u * p.max_split + cj) * p.G * (2 + D);
+        // ---- combine the warps' states into the CTA's slice state ----
         {
-            const int npairs = p.G * (D / 2);
-            const int nhalf = npairs <= kFThreads / 2 ? 2 : 1;
-            const int pair = tid % (kFThreads / nhalf);
-            const int half = tid / (kFThreads / nhalf);
-            if (half == 0 && pair < npairs) {
-                const int g = pair / (D / 2), dp = pair - g * (D / 2);
-                part[g * (2 + D) + 2 + 2 * dp] = acc0;
-                part[g * (2 + D) + 3 + 2 * dp] = acc1;
-                if (dp == 0) {
-                    part[g * (2 + D)] = s_m[g];
-                    part[g * (2 + D) + 1] = s_l[g];
+            float* s_wacc = reinterpret_cast<float*>(s_lut);  // [NW][G][128]
+            float* s_wm = reinterpret_cast<float*>(s_hist);   // [NW][8] (the histogram is consumed)
+            float* s_wl = s_wm + NW * 8;                       // [NW][8]
+            float* s_wf = s_wl + NW * 8;                       // [NW][8] rescale of each warp's state
+            float* s_cm = s_wf + NW * 8;                       // [8] slice max
+            float* s_cl = s_cm + 8;                            // [8] slice sum
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                if (g >= p.G) break;
+                *reinterpret_cast<float4*>(s_wacc + (warp * p.G + g) * D + lane * 4) = wacc[g];
+                if (lane == 0) {
+                    s_wm[warp * 8 + g] = wm[g];
+                    s_wl[warp * 8 + g] = wl[g];
+                }
+            }
+            __syncthreads();
+            if (tid < p.G) {
+                const int g = tid;
+                float mx = -INFINITY;
+                for (int w = 0; w < NW; ++w) mx = fmaxf(mx, s_wm[w * 8 + g]);
+                float l = 0.f;
+                for (int w = 0; w < NW; ++w) {
+                    const float f = s_wm[w * 8 + g] == -INFINITY ? 0.f : exp2f(s_wm[w * 8 + g] - mx);
+                    s_wf[w * 8 + g] = f;
+                    l = fmaf(s_wl[w * 8 + g], f, l);
+                }
+                s_cm[g] = mx;
+                s_cl[g] = l;
+            }
+            __syncthreads();
+            unsigned long long* part = p.part + ((int64_t)u * p.max_split + cj) * p.G * (2 + D);
+            for (int o = tid; o < p.G * D; o += kFThreads) {
+                const int g = o / D, d = o - g * D;
+                float a = 0.f;
+#pragma unroll 4
+                for (int w = 0; w < NW; ++w) a = fmaf(s_wacc[(w * p.G + g) * D + d], s_wf[w * 8 + g], a);
+                st_tag(part + g * (2 + D) + 2 + d, __float_as_uint(a), s_epoch);
+                if (d == 0) {
+                    st_tag(part + g * (2 + D), __float_as_uint(s_cm[g]), s_epoch);
+                    st_tag(part + g * (2 + D) + 1, __float_as_uint(s_cl[g]), s_epoch);
                 }
             }
         }
     }
-    // every CTA's partial state is in L2 after this barrier
-    if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
 
     // ================= merge: each CTA of the unit finalises a slice of its G*128 outputs =================
     {
@@ -1187,20 +1356,36 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         const int per = (nout + cn - 1) / cn;
         const int o0 = min(nout, cj * per), o1 = min(nout, o0 + per);
         const int npair = (o1 - o0) * cn;  // (output, slice) pairs, <= nout + cn <= 4096
-        const float* pu = p.part + (int64_t)u * p.max_split * p.G * (2 + D);
+        const unsigned long long* pu = p.part + (int64_t)u * p.max_split * p.G * (2 + D);
         const int64_t sstride = (int64_t)p.G * (2 + D);
         float* s_mm = reinterpret_cast<float*>(s_ring);  // [npair] slice max
         float* s_ll = s_mm + 4096;                       // [npair] slice sum
         float* s_aa = s_ll + 4096;                       // [npair] slice P.V
-        for (int i = tid; i < npair; i += kFThreads) {
+        // the slice states of the unit's CTAs, polled until this call's
+        // epoch shows (no barrier: each word carries its own tag)
+        bool ok = true;
+        const long long t0 = clock64();
+        for (int i = tid; i < npair && ok; i += kFThreads) {
             const int ol = i / cn, sl = i - ol * cn;
             const int o = o0 + ol, g = o / D, d = o - g * D;
-            const float* ps = pu + sl * sstride + g * (2 + D);
-            s_mm[i] = __ldcg(ps);
-            s_ll[i] = __ldcg(ps + 1);
-            s_aa[i] = __ldcg(ps + 2 + d);
+            const unsigned long long* ps = pu + sl * sstride + g * (2 + D);
+            unsigned long long a = ld_tag(ps), l = ld_tag(ps + 1), x = ld_tag(ps + 2 + d);
+            while (!(tag_ok(a, s_epoch) && tag_ok(l, s_epoch) && tag_ok(x, s_epoch))) {
+                if (clock64() - t0 > kWaitCycles) {
+                    atomicOr(p.err, LP_DEVERR_WAIT_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+                a = ld_tag(ps);
+                l = ld_tag(ps + 1);
+                x = ld_tag(ps + 2 + d);
+            }
+            s_mm[i] = __uint_as_float((uint32_t)a);
+            s_ll[i] = __uint_as_float((uint32_t)l);
+            s_aa[i] = __uint_as_float((uint32_t)x);
         }
-        __syncthreads();
+        if (__syncthreads_or(!ok)) return;
+        if (stamp) p.phase_ns[6] = global_ns();
         OT* ob = reinterpret_cast<OT*>(p.out) + (int64_t)b * p.out_stride_b;
         for (int ol = tid; ol < o1 - o0; ol += kFThreads) {
             const float* mm = s_mm + ol * cn;

@@ -86,9 +86,11 @@ struct Plan {
     uint32_t* ubar;
     uint32_t* cta_count;
     uint32_t* cta_ties;
-    float2* pub;
-    uint32_t* pub_win;
-    int2* pub_hdr;
+    unsigned long long* fpub;   // fused path: tagged candidates [ctas][pub_cap][2]
+    unsigned long long* fwin;   // fused path: tagged windows + headers [ctas][kPubWin + 2]
+    unsigned long long* flut;   // fused path: tagged LUT [U][256][32]
+    unsigned long long* fpart;  // fused path: tagged split-K states [U][max_split][G][130]
+    uint32_t* chist;            // fused path: local histograms [ctas][kNB]
     int pub_target, pub_cap;
     size_t bytes;
 };
@@ -183,8 +185,8 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
 
     Carver c(ws);
     // fixed offsets, identical for every geometry: the error word (0), the
-    // grid-barrier word (256 B) and the per-unit barrier words (512 B ..
-    // 2048 B), whose values must survive between calls
+    // fused kernel's 64-bit launch counter (256 B) and the per-unit barrier
+    // words (512 B .. 2048 B), whose values must survive between calls
     p.err = c.take<uint32_t>(64);
     p.bar = c.take<uint32_t>(64);
     p.ubar = c.take<uint32_t>(kUnitBarWords);
@@ -198,9 +200,13 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
                            (2 + 128));
     p.cta_count = c.take<uint32_t>((size_t)p.fused_ctas);
     p.cta_ties = c.take<uint32_t>((size_t)p.fused_ctas);
-    p.pub = c.take<float2>((size_t)p.fused_ctas * std::max(p.pub_cap, 1));
-    p.pub_win = c.take<uint32_t>((size_t)p.fused_ctas * kPubWin);
-    p.pub_hdr = c.take<int2>((size_t)p.fused_ctas);
+    if (p.fused) {
+        p.fpub = c.take<unsigned long long>((size_t)p.fused_ctas * std::max(p.pub_cap, 1) * 2);
+        p.fwin = c.take<unsigned long long>((size_t)p.fused_ctas * (kPubWin + 2));
+        p.flut = c.take<unsigned long long>((size_t)p.U * 256 * 32);
+        p.fpart = c.take<unsigned long long>((size_t)p.U * p.fused_max_split * a->G * (2 + 128));
+        p.chist = c.take<uint32_t>((size_t)p.fused_ctas * kNB);
+    }
     p.zero_words = (int64_t)p.Usel * kNB + p.Usel + p.Usel + p.Uatt;
     p.zero = c.take<uint32_t>((size_t)p.zero_words);
     p.hist = p.zero;
@@ -333,23 +339,23 @@ static int launch_fused(const lp_sparse_decode_args* a, const Plan& p, cudaStrea
     fp.out_stride_b = a->out_stride_b;
     fp.out_stride_h = a->out_stride_h;
     fp.topk_out = a->topk_out;
-    fp.lut = p.lut;
+    fp.lut = p.flut;
     fp.sel_scores = p.sel_scores;
     fp.sel_stride = std::max(1, a->T_codes);
-    fp.hist = p.hist;
+    fp.chist = p.chist;
     fp.bitmap = p.bitmap;
     fp.bm_stride = p.bm_words;
     fp.tie_buf = p.tie_buf;
     fp.cta_ties = p.cta_ties;
-    fp.pub = p.pub;
-    fp.pub_win = p.pub_win;
-    fp.pub_hdr = p.pub_hdr;
+    fp.pub = p.fpub;
+    fp.pwin = p.fwin;
     fp.pub_target = p.pub_target;
     fp.pub_cap = p.pub_cap;
     fp.cta_count = p.cta_count;
-    fp.part = p.part;
+    fp.part = p.fpart;
     fp.max_split = p.fused_max_split;
     fp.bar = p.ubar;
+    fp.epoch_ctr = reinterpret_cast<unsigned long long*>(p.bar);
     fp.err = p.err;
     fp.phase_ns = reinterpret_cast<unsigned long long*>(a->phase_ns);
     for (int i = 0; i < 2; ++i) {
@@ -581,10 +587,11 @@ int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
     LP_CUDA(cudaMemcpyAsync(&v, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     LP_CUDA(cudaStreamSynchronize(st));
     LP_CUDA(cudaMemsetAsync(workspace, 0, sizeof(uint32_t), st));
-    // a timed-out barrier leaves its word mid-count: restore the barrier words
+    // a timed-out barrier leaves its word mid-count: restore the barrier
+    // words (the launch counter at 256 B only ever grows and is kept)
     if (v & LP_DEVERR_WAIT_TIMEOUT) {
         LP_CHECK(workspace_bytes >= kPersistBytes, "workspace smaller than its persistent state");
-        LP_CUDA(cudaMemsetAsync(static_cast<char*>(workspace) + 256, 0, kPersistBytes - 256, st));
+        LP_CUDA(cudaMemsetAsync(static_cast<char*>(workspace) + 512, 0, kPersistBytes - 512, st));
     }
     LP_CUDA(cudaStreamSynchronize(st));
     *bits_out = v;
