@@ -16,9 +16,10 @@
  *   - The caller owns every buffer, including `workspace` (size from the
  *     matching *_workspace_size function, 256-byte aligned, device memory,
  *     ZERO-FILLED before its first use).  Its first 2048 bytes hold state
- *     that persists between calls (device error bits, barrier words), at
- *     the same offsets for every geometry; the rest is scratch.  A
- *     workspace must not be shared by calls that may run concurrently.
+ *     that persists between calls (device error bits, a launch counter,
+ *     barrier words), at the same offsets for every geometry; the rest is
+ *     scratch.  A workspace must not be shared by calls that may run
+ *     concurrently.
  */
 #ifndef LAPRUNE_B200_H
 #define LAPRUNE_B200_H
@@ -180,8 +181,8 @@ int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
  *     rejected with LP_ERR_WORKSPACE (use lp_sparse_decode with a workspace
  *     of your own for those).
  *   - Every call on a device shares the one scratch, which keeps the last
- *     call's contents.  Its first 2048 bytes (error bits, barrier words) must
- *     start at zero: the array is zero when the library loads and the calls
+ *     call's contents.  Its first 2048 bytes (error bits, launch counter,
+ *     barrier words) must start at zero: the array is zero when the library loads and the calls
  *     leave those words consistent.  Calls whose kernels may overlap on the
  *     GPU (different streams, threads or processes sharing the context) race
  *     on it: order them on one stream.
