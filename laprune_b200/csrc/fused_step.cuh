@@ -258,6 +258,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     __shared__ BinParams s_bp;
     __shared__ __align__(16) float s_qu[8 * 128];  // the unit's G query rows (fp32), loaded at start
     __shared__ int s_shift, s_bstar, s_above;
+    __shared__ __align__(16) float s_lg[kFThreads / 32][kFMaxRows / 64 * 16];  // per-warp logits / weights (phase E)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = kFThreads / 32;
@@ -1178,19 +1179,21 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         }
         auto attend = [&](int r_lo, int r_hi) {
             if (p.G == 4) {
+                // pass 1: logits of the warp's rows (groups of 4 rows, +64 per
+                // group) into its buffer s_lgw[group][4 * row + head]
+                float* s_lgw = s_lg[warp];
                 float4 qv[4];
 #pragma unroll
                 for (int g = 0; g < 4; ++g) qv[g] = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
-                for (int r0 = r_lo + warp * 4; r0 < r_hi; r0 += NW * 4) {
+                int ngrp = 0;
+                for (int r0 = r_lo + warp * 4; r0 < r_hi; r0 += NW * 4, ++ngrp) {
                     // the 16 (row, head) dots, reduced by one 16-way transpose:
                     // lanes 2i, 2i+1 end with the total of idx i = 4 * row + head
                     float v[16];
-                    float4 vv[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const bool ok = r0 + j < r_hi;
-                        const float4 kv = ok ? Vec4<KT>::load(s_k + (r0 + j) * D + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-                        vv[j] = ok ? Vec4<KT>::load(s_v + (r0 + j) * D + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const float4 kv = r0 + j < r_hi ? Vec4<KT>::load(s_k + (r0 + j) * D + lane * 4)
+                                                        : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                         for (int g = 0; g < 4; ++g) {
                             float a = qv[g].x * kv.x;
@@ -1226,33 +1229,63 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                     const float send = b1 ? x2[0] : x2[1];
                     float tot = keep + __shfl_xor_sync(0xffffffffu, send, 2);
                     tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+                    const int idx = (lane >> 1) & 15;
+                    if ((lane & 1) == 0)
+                        s_lgw[ngrp * 16 + idx] = r0 + (idx >> 2) < r_hi ? tot * p.scale_log2 : -INFINITY;
+                }
+                if (ngrp == 0) return;
+                __syncwarp();
+                // pass 2: one softmax step for all of them.  Lane l takes the
+                // values l and l + 32 (head l & 3); heads reduce over lanes
+                // with equal l & 3.
+                const int nval = ngrp * 16;  // <= 48 (kFMaxRows / 64 groups)
+                const float a0 = lane < nval ? s_lgw[lane] : -INFINITY;
+                const float a1 = lane + 32 < nval ? s_lgw[lane + 32] : -INFINITY;
+                const int hg = lane & 3;
+                const float wmh = hg == 0 ? wm[0] : hg == 1 ? wm[1] : hg == 2 ? wm[2] : wm[3];
+                float mx = fmaxf(a0, a1);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float mn = fmaxf(wmh, mx);  // finite: the warp has a row
+                const float p0 = exp2f(a0 - mn), p1 = exp2f(a1 - mn);
+                float sm = p0 + p1;
+                sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+                sm += __shfl_xor_sync(0xffffffffu, sm, 8);
+                sm += __shfl_xor_sync(0xffffffffu, sm, 16);
+                const float sc = exp2f(wmh - mn);  // 0 while the warp had no row
+                if (lane < nval) s_lgw[lane] = p0;
+                if (lane + 32 < nval) s_lgw[lane + 32] = p1;
 #pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        float s[4];
+                for (int g = 0; g < 4; ++g) {
+                    const float scg = __shfl_sync(0xffffffffu, sc, g);
+                    wm[g] = __shfl_sync(0xffffffffu, mn, g);
+                    wl[g] = fmaf(wl[g], scg, __shfl_sync(0xffffffffu, sm, g));
+                    wacc[g].x *= scg;
+                    wacc[g].y *= scg;
+                    wacc[g].z *= scg;
+                    wacc[g].w *= scg;
+                }
+                __syncwarp();
+                // pass 3: P.V over the warp's rows
+                int grp = 0;
+                for (int r0 = r_lo + warp * 4; r0 < r_hi; r0 += NW * 4, ++grp) {
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const float x = __shfl_sync(0xffffffffu, tot, 2 * (4 * j + g)) * p.scale_log2;
-                            s[j] = r0 + j < r_hi ? x : -INFINITY;
+                    for (int j = 0; j < 4; ++j) {
+                        if (r0 + j >= r_hi) break;
+                        const float4 vv = Vec4<KT>::load(s_v + (r0 + j) * D + lane * 4);
+                        const float4 pj = *reinterpret_cast<const float4*>(s_lgw + grp * 16 + 4 * j);
+#pragma unroll
+                        for (int g = 0; g < 4; ++g) {
+                            const float pg = g == 0 ? pj.x : g == 1 ? pj.y : g == 2 ? pj.z : pj.w;
+                            wacc[g].x = fmaf(pg, vv.x, wacc[g].x);
+                            wacc[g].y = fmaf(pg, vv.y, wacc[g].y);
+                            wacc[g].z = fmaf(pg, vv.z, wacc[g].z);
+                            wacc[g].w = fmaf(pg, vv.w, wacc[g].w);
                         }
-                        const float mn = fmaxf(wm[g], fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3])));
-                        const float sc = exp2f(wm[g] - mn);  // 0 while the warp has no row yet
-                        float pr[4];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) pr[j] = exp2f(s[j] - mn);
-                        wl[g] = fmaf(wl[g], sc, (pr[0] + pr[1]) + (pr[2] + pr[3]));
-                        float4 a = wacc[g];
-                        a.x *= sc; a.y *= sc; a.z *= sc; a.w *= sc;
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            a.x = fmaf(pr[j], vv[j].x, a.x);
-                            a.y = fmaf(pr[j], vv[j].y, a.y);
-                            a.z = fmaf(pr[j], vv[j].z, a.z);
-                            a.w = fmaf(pr[j], vv[j].w, a.w);
-                        }
-                        wacc[g] = a;
-                        wm[g] = mn;
                     }
                 }
+                __syncwarp();
             } else {
                 for (int r = r_lo + warp; r < r_hi; r += NW) {
                     const float4 kv = Vec4<KT>::load(s_k + r * D + lane * 4);
@@ -1320,18 +1353,27 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 }
             }
             __syncthreads();
-            if (tid < p.G) {
-                const int g = tid;
-                float mx = -INFINITY;
-                for (int w = 0; w < NW; ++w) mx = fmaxf(mx, s_wm[w * 8 + g]);
-                float l = 0.f;
-                for (int w = 0; w < NW; ++w) {
-                    const float f = s_wm[w * 8 + g] == -INFINITY ? 0.f : exp2f(s_wm[w * 8 + g] - mx);
+            // 16 lanes per head (one per warp): max, rescale factors, sum.
+            // Whole warps take part in the shuffles (lanes of heads >= G
+            // carry neutral values and write nothing).
+            if (tid < ((NW * p.G + 31) & ~31)) {
+                const int g = tid / NW, w = tid - g * NW;
+                const bool live = g < p.G;
+                const float m = live ? s_wm[w * 8 + g] : -INFINITY;
+                float mx = m;
+#pragma unroll
+                for (int o = 1; o < NW; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                const float f = m == -INFINITY ? 0.f : exp2f(m - mx);
+                float l = live ? s_wl[w * 8 + g] * f : 0.f;
+#pragma unroll
+                for (int o = 1; o < NW; o <<= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+                if (live) {
                     s_wf[w * 8 + g] = f;
-                    l = fmaf(s_wl[w * 8 + g], f, l);
+                    if (w == 0) {
+                        s_cm[g] = mx;
+                        s_cl[g] = l;
+                    }
                 }
-                s_cm[g] = mx;
-                s_cl[g] = l;
             }
             __syncthreads();
             unsigned long long* part = p.part + ((int64_t)u * p.max_split + cj) * p.G * (2 + D);
