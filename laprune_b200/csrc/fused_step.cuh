@@ -427,29 +427,26 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             const unsigned long long* gl = p.lut + (int64_t)u * 256 * 32;
             bool ok = true;
             const long long t0 = clock64();
-            // two rounds of 8 words (two float4 each) keep the register count down
+            unsigned long long w[16];
+            uint32_t pend = 0xFFFFu;
+            while (true) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                unsigned long long w[8];
-                uint32_t pend = 0xFFu;
-                while (ok) {
+                for (int e = 0; e < 16; ++e)
+                    if (pend >> e & 1u) w[e] = ld_tag(gl + 4 * (tid + (e >> 2) * kFThreads) + (e & 3));
 #pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        if (pend >> e & 1u) w[e] = ld_tag(gl + 4 * (tid + (2 * h + (e >> 2)) * kFThreads) + (e & 3));
-#pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        if (tag_ok(w[e], s_epoch)) pend &= ~(1u << e);
-                    if (!pend) break;
-                    if (clock64() - t0 > kWaitCycles) {
-                        atomicOr(p.err, LP_DEVERR_WAIT_TIMEOUT);
-                        ok = false;
-                    }
+                for (int e = 0; e < 16; ++e)
+                    if (tag_ok(w[e], s_epoch)) pend &= ~(1u << e);
+                if (!pend) break;
+                if (clock64() - t0 > kWaitCycles) {
+                    atomicOr(p.err, LP_DEVERR_WAIT_TIMEOUT);
+                    ok = false;
+                    break;
                 }
-#pragma unroll
-                for (int jj = 0; jj < 2; ++jj)
-                    v[2 * h + jj] = make_float4(__uint_as_float((uint32_t)w[4 * jj]), __uint_as_float((uint32_t)w[4 * jj + 1]),
-                                                __uint_as_float((uint32_t)w[4 * jj + 2]), __uint_as_float((uint32_t)w[4 * jj + 3]));
             }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                v[j] = make_float4(__uint_as_float((uint32_t)w[4 * j]), __uint_as_float((uint32_t)w[4 * j + 1]),
+                                   __uint_as_float((uint32_t)w[4 * j + 2]), __uint_as_float((uint32_t)w[4 * j + 3]));
             if (__syncthreads_or(!ok)) { drain(0); return; }
         }
         if (stamp) p.phase_ns[2] = global_ns();
@@ -613,51 +610,74 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         //      publishes nothing and b_j = kNB, which sends the unit to the
         //      exchange path. ----
         if (p.pub_cap > 0) {
-            __shared__ int s_bj, s_abovej;
-            uint32_t* s_cur = reinterpret_cast<uint32_t*>(s_lut);    // [kPubWin] scatter cursors (table is dead)
-            uint32_t* s_cw = s_cur + kPubWin;                         // [kPubWin] window counts
+            __shared__ int s_bj;
+            uint32_t* s_suf = reinterpret_cast<uint32_t*>(s_lut);    // [kNB + 1] suffix counts (table is dead)
+            uint32_t* s_cur = s_suf + kNB + 1;                        // [kPubWin] scatter cursors
             float2* s_own = reinterpret_cast<float2*>(s_ring + 64 * 1024);  // own published entries
-            if (tid == 0) { s_bj = -1; s_abovej = 0; }
-            if (tid < kPubWin) s_cur[tid] = 0u;
-            __syncthreads();
-            find_threshold_bin<kFThreads>(s_hist, p.pub_target, &s_bj, &s_abovej);
-            __syncthreads();
-            const int bj = max(s_bj, 0);
-            const int npub = s_bj < 0 ? ntok : s_abovej + (int)s_hist[bj];
-            const bool pub_ok = npub <= p.pub_cap;
-            for (int bb = bj + kPubWin - 1 + tid; bb < kNB; bb += kFThreads)
-                if (s_hist[bb]) atomicAdd(&s_cur[kPubWin - 1], s_hist[bb]);
-            __syncthreads();
-            uint32_t cw = 0u;
-            if (tid < kPubWin - 1) cw = bj + tid < kNB ? s_hist[bj + tid] : 0u;
-            else if (tid == kPubWin - 1) cw = s_cur[kPubWin - 1];
-            unsigned long long* pw = p.pwin + (int64_t)blockIdx.x * (kPubWin + 2);
-            if (tid < kPubWin) {
-                s_cw[tid] = cw;
-                st_tag(pw + tid, pub_ok ? cw : 0u, s_epoch);
+            // suffix counts s_suf[b] = tokens in bins >= b: thread t owns bins
+            // [kNB - 4(t+1), kNB - 4t), the top bins first
+            {
+                constexpr int PER = kNB / kFThreads;
+                const int hi = kNB - PER * tid;
+                uint32_t c[PER];
+                int loc = 0;
+#pragma unroll
+                for (int j = 0; j < PER; ++j) {
+                    c[j] = s_hist[hi - 1 - j];
+                    loc += (int)c[j];
+                }
+                int before;
+                Scan(scan_tmp).ExclusiveSum(loc, before);
+                int run = before;
+#pragma unroll
+                for (int j = 0; j < PER; ++j) {
+                    run += (int)c[j];
+                    s_suf[hi - 1 - j] = (uint32_t)run;
+                }
+                if (tid == 0) {
+                    s_suf[kNB] = 0u;
+                    s_bj = 0;  // fewer tokens than pub_target: publish them all
+                }
             }
             __syncthreads();
-            // descending offsets off_w = sum_{w' > w} c_w' (thread t scans c_{W-1-t})
-            int off;
-            Scan(scan_tmp).ExclusiveSum(tid < kPubWin ? (int)s_cw[kPubWin - 1 - tid] : 0, off);
-            if (tid < kPubWin) s_cur[kPubWin - 1 - tid] = (uint32_t)off;
+            // b_j: the highest bin whose suffix reaches pub_target
+            for (int bb = tid; bb < kNB; bb += kFThreads)
+                if ((int)s_suf[bb] >= p.pub_target && (int)s_suf[bb + 1] < p.pub_target) s_bj = bb;
             __syncthreads();
-            if (pub_ok) {
-                unsigned long long* slot = p.pub + (int64_t)blockIdx.x * p.pub_cap * 2;
-                for (int lt = tid; lt < ntok; lt += kFThreads) {
-                    const float s = s_scores[lt];
-                    const int bin = score_bin(s, bp.lo, bp.inv_w, kNB);
-                    if (bin >= bj) {
-                        const int pos = (int)atomicAdd(&s_cur[min(bin - bj, kPubWin - 1)], 1u);
-                        st_tag(slot + 2 * pos, __float_as_uint(s), s_epoch);
-                        st_tag(slot + 2 * pos + 1, (uint32_t)(t_begin + lt), s_epoch);
-                        s_own[pos] = make_float2(s, __int_as_float(t_begin + lt));
-                    }
+            const int bj = s_bj;
+            const int npub = (int)s_suf[bj];
+            const bool pub_ok = npub <= p.pub_cap;
+            // window w counts bin bj + w (the last one: all bins >= bj + kPubWin - 1);
+            // entries go in descending window order, so window w starts at
+            // the count of bins >= bj + w + 1
+            unsigned long long* pw = p.pwin + (int64_t)blockIdx.x * (kPubWin + 2);
+            if (tid < kPubWin) {
+                const int b0 = bj + tid;
+                uint32_t cw = 0u, start = 0u;
+                if (b0 < kNB) {
+                    cw = tid < kPubWin - 1 ? s_hist[b0] : s_suf[b0];
+                    start = tid < kPubWin - 1 ? s_suf[b0 + 1] : 0u;
                 }
+                s_cur[tid] = start;
+                st_tag(pw + tid, pub_ok ? cw : 0u, s_epoch);
             }
             if (tid == 0) {
                 st_tag(pw + kPubWin, pub_ok ? (uint32_t)npub : 0u, s_epoch);
                 st_tag(pw + kPubWin + 1, pub_ok ? (uint32_t)bj : (uint32_t)kNB, s_epoch);
+            }
+            __syncthreads();
+            if (pub_ok) {
+                unsigned long long* slot = p.pub + (int64_t)blockIdx.x * p.pub_cap * 2;
+                for (int lt = tid; lt < ntok; lt += kFThreads) {
+                    const float sc = s_scores[lt];
+                    const int bin = score_bin(sc, bp.lo, bp.inv_w, kNB);
+                    if (bin >= bj) {
+                        const int pos = (int)atomicAdd(&s_cur[min(bin - bj, kPubWin - 1)], 1u);
+                        st_tag(slot + 2 * pos, __float_as_uint(sc), s_epoch);
+                        st_tag(slot + 2 * pos + 1, (uint32_t)(t_begin + lt), s_epoch);
+                        s_own[pos] = make_float2(sc, __int_as_float(t_begin + lt));
+                    }
+                }
             }
         }
     }
@@ -724,7 +744,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         float* s_tk = reinterpret_cast<float*>(s_lut + 35840);               // tie keys  [kFastTieCap]
         int* s_ti = reinterpret_cast<int*>(s_lut + 35840 + kFastTieCap * 4); // tie index [kFastTieCap]
         const float2* s_own = reinterpret_cast<const float2*>(s_ring + 64 * 1024);
-        for (int i = tid; i < kNB; i += kFThreads) s_hist[i] = 0u;
+        if (tid <= kPubWin) s_hist[tid] = 0u;  // the fast path's 128-bin histogram + "above"
         if (tid == 0) { s_fast = 0; s_bstar = -1; s_above = 0; s_ntie = 0; s_win_before = 0; s_topk_off = 0; }
         const bool pub = p.pub_cap > 0;
         if (pub) {
@@ -735,50 +755,114 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             __syncthreads();
         }
         if (stamp) p.phase_ns[4] = global_ns();
+        for (int i = tid; i < nw_own; i += kFThreads) s_selw[i] = 0u;
+        for (int i = tid; i < (ntok + 31) / 32; i += kFThreads) s_win[i] = 0u;
         if (pub) {
-            // the unit's histogram over the published bins (the last window
-            // bin counts at its lower edge; it is above any usable b*)
+            // b* can only be usable in [bmax, bmin + kPubWin - 2]: every CTA's
+            // window covers those bins exactly.  The unit histogram is built
+            // on the 128 bins from bmax; anything above goes to one counter.
+            __shared__ int s_bmax, s_bmin, s_nun;
+            uint32_t* s_uh = s_hist;  // [kPubWin + 1]: bins bmax .. bmax + 127, then "above"
+            if (warp == 0) {
+                int n = 0, mx = 0, mn = kNB;
+                for (int j = lane; j < cn; j += 32) {
+                    n += (int)s_pw[j * PW + kPubWin];
+                    mx = max(mx, (int)s_pw[j * PW + kPubWin + 1]);
+                    mn = min(mn, (int)s_pw[j * PW + kPubWin + 1]);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    n += __shfl_xor_sync(0xffffffffu, n, o);
+                    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+                }
+                if (lane == 0) { s_nun = n; s_bmax = mx; s_bmin = mn; }
+            }
+            __syncthreads();
+            const int bmax = s_bmax, bmin = s_bmin;
             for (int i = tid; i < cn * PW; i += kFThreads) {
                 const int j = i / PW, w = i - j * PW;
                 const uint32_t c = s_pw[i];
-                if (w < kPubWin && c) atomicAdd(&s_hist[min((int)s_pw[j * PW + kPubWin + 1] + w, kNB - 1)], c);
-            }
-            int n_union = 0, bmax = 0, bmin = kNB;
-            for (int j = 0; j < cn; ++j) {
-                n_union += (int)s_pw[j * PW + kPubWin];
-                bmax = max(bmax, (int)s_pw[j * PW + kPubWin + 1]);
-                bmin = min(bmin, (int)s_pw[j * PW + kPubWin + 1]);
+                if (w < kPubWin && c) {
+                    const int rb = (int)s_pw[j * PW + kPubWin + 1] + w - bmax;  // bin relative to bmax
+                    if (rb >= 0) atomicAdd(&s_uh[min(rb, kPubWin)], c);
+                }
             }
             __syncthreads();
-            if (n_union >= p.k) find_threshold_bin<kFThreads>(s_hist, p.k, &s_bstar, &s_above);
-            __syncthreads();
-            // exact when b* is at or above every CTA's publishing bin (each
-            // unpublished token then lies in a lower bin than the k-th
-            // published one, so it scores below it) and inside every window
-            const int bs = s_bstar;
-            if (tid == 0)
-                s_fast = (p.k > 0 && bs >= 0 && bs >= bmax && bs < bmin + kPubWin - 1 &&
-                          (int)s_hist[bs] <= kFastTieCap) ? 1 : 0;
+            if (warp == 0) {
+                // suffix counts over the 128 bins (lane holds bins 4l .. 4l+3)
+                uint32_t c[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) c[e] = s_uh[4 * lane + e];
+                const uint32_t above_all = s_uh[kPubWin];
+                uint32_t loc = c[0] + c[1] + c[2] + c[3];
+                uint32_t suf = loc;  // inclusive suffix over lanes >= lane
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_down_sync(0xffffffffu, suf, o);
+                    if (lane + o < 32) suf += y;
+                }
+                uint32_t run = suf - loc + above_all;  // tokens in bins above this lane's 4
+                int bs = -1, above = 0;
+#pragma unroll
+                for (int e = 3; e >= 0; --e) {
+                    if (bs < 0 && (int)(run + c[e]) >= p.k && (int)run < p.k) {
+                        bs = bmax + 4 * lane + e;
+                        above = (int)run;
+                    }
+                    run += c[e];
+                }
+                const unsigned found = __ballot_sync(0xffffffffu, bs >= 0);
+                if (found) {
+                    const int src = __ffs(found) - 1;
+                    bs = __shfl_sync(0xffffffffu, bs, src);
+                    above = __shfl_sync(0xffffffffu, above, src);
+                }
+                if (lane == 0) {
+                    // exact when b* is at or above every CTA's publishing bin
+                    // (each unpublished token then lies in a lower bin than the
+                    // k-th published one, so it scores below it) and inside
+                    // every window
+                    const bool fast = found && p.k > 0 && s_nun >= p.k && bs < bmin + kPubWin - 1 &&
+                                      (int)s_uh[bs - bmax] <= kFastTieCap;
+                    s_fast = fast ? 1 : 0;
+                    s_bstar = bs;
+                    s_above = above;
+                }
+            }
         }
         __syncthreads();
         if (s_fast) {
             const int bs = s_bstar;
             const int need = p.k - s_above;
-            // per slot: entries above b* (they lead its sorted list) and in b*
-            for (int j = warp; j < cn; j += NW) {
-                const int wb = bs - (int)s_pw[j * PW + kPubWin + 1];  // 0 <= wb < kPubWin - 1
+            // per slot (16 threads each): entries above b* (they lead its
+            // sorted list) and in b*; the own above-threshold tokens, by bin
+            for (int j0 = 0; j0 < cn; j0 += kFThreads / 16) {
+                const int j = j0 + tid / 16, q = tid & 15;
                 uint32_t a = 0u;
-                for (int w = wb + 1 + lane; w < kPubWin; w += 32) a += s_pw[j * PW + w];
+                int wb = 0;
+                if (j < cn) {
+                    wb = bs - (int)s_pw[j * PW + kPubWin + 1];  // 0 <= wb < kPubWin - 1
+                    for (int w = wb + 1 + q; w < kPubWin; w += 16) a += s_pw[j * PW + w];
+                }
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-                if (lane == 0) {
+                for (int o = 8; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                if (q == 0 && j < cn) {
                     s_tst[j] = (int)a;
                     s_tcn[j] = (int)s_pw[j * PW + wb];
                 }
             }
-            for (int i = tid; i < nw_own; i += kFThreads) s_selw[i] = 0u;
-            for (int i = tid; i < (ntok + 31) / 32; i += kFThreads) s_win[i] = 0u;
+            const int nown = (int)s_pw[cj * PW + kPubWin];
+            for (int i = tid; i < nown; i += kFThreads) {
+                const float2 e = s_own[i];
+                if (score_bin(e.x, bp.lo, bp.inv_w, kNB) > bs) {
+                    const int t = __float_as_int(e.y);
+                    atomicOr(&s_selw[(t >> 5) - w_begin], 1u << (t & 31));
+                }
+            }
             __syncthreads();
+            // offsets of the slots' tie entries (warp 0); the own
+            // above-threshold tokens in ascending order -> s_list (all)
             if (warp == 0) {
                 int carry = 0;
                 for (int j0 = 0; j0 < cn; j0 += 32) {
@@ -798,18 +882,22 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                     s_ntie = carry;
                 }
             }
-            // own above-threshold tokens lead the CTA's own sorted entries
-            for (int i = tid; i < s_tst[cj]; i += kFThreads) {
-                const int t = __float_as_int(s_own[i].y);
-                atomicOr(&s_selw[(t >> 5) - w_begin], 1u << (t & 31));
-            }
-            if (p.topk_out && tid == 0) {
+            if (p.topk_out && tid == 32) {
                 int c = 0;
                 for (int j = 0; j < cj; ++j) c += s_tst[j];
                 s_topk_off = c;
             }
+            {
+                const uint32_t bits = tid < nw_own ? s_selw[tid] : 0u;
+                int pos, total;
+                Scan(scan_tmp).ExclusiveSum(__popc(bits), pos, total);
+                for (uint32_t b2 = bits; b2; b2 &= b2 - 1) s_list[pos++] = (w_begin + tid) * 32 + __ffs(b2) - 1;
+                if (tid == 0) s_nabove = total;
+            }
             __syncthreads();
-            // the unit's tie-bin entries: loads issued first (up to 2 per thread)
+            // the unit's tie-bin entries: loads issued first (up to 2 per
+            // thread), then the K/V rows known now (own above-threshold
+            // tokens, sink and local shares), while the tie bin is settled
             const int ntie = s_ntie;
             const unsigned long long* tsrc[2];
             unsigned long long tw[2][2];
@@ -831,17 +919,6 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                     tpend |= 1u << r;
                 }
             }
-            // own above-threshold tokens in ascending order -> s_list; their
-            // K/V rows and the sink and local shares start loading now, while
-            // the tie bin is settled
-            {
-                const uint32_t bits = tid < nw_own ? s_selw[tid] : 0u;
-                int pos, total;
-                Scan(scan_tmp).ExclusiveSum(__popc(bits), pos, total);
-                for (uint32_t b2 = bits; b2; b2 &= b2 - 1) s_list[pos++] = (w_begin + tid) * 32 + __ffs(b2) - 1;
-                if (tid == 0) s_nabove = total;
-            }
-            __syncthreads();
             issue_rows(0, 0, min(s_nabove + n_sink_here + n_loc_here, R), s_nabove);
             {
                 bool ok = true;
