@@ -158,6 +158,46 @@ int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
                           uint32_t* bits_out);
 
 /* ======================================================================
+ * Key encode: greedy residual additive quantization of new keys
+ * ====================================================================== */
+
+/* Arguments of lp_encode_keys.  Vectors x[b][h][t][0..D) (post-RoPE keys of
+ * the code cache's encode buffer); codes[b][h][t][0..M) may point straight
+ * into a code cache [B][Hkv][cap][M] at the buffer's first position. */
+typedef struct lp_encode_args {
+    const void* x;              /* at x + b*x_stride_b + h*x_stride_h + t*x_stride_t (elements) */
+    int32_t x_dtype;            /* LP_BF16 | LP_F16 | LP_F32 */
+    int32_t cb_per_kv_head;     /* 1: codebooks [H][M][K][D], vector (b,h,t) uses set h;
+                                   0: one set [M][K][D] for every vector */
+    int64_t x_stride_b, x_stride_h, x_stride_t;
+    const float* codebooks;     /* fp32, contiguous, 16-byte aligned */
+    uint8_t* codes;             /* at codes + b*sb + h*sh + t*st + m (bytes) */
+    int64_t codes_stride_b, codes_stride_h, codes_stride_t;
+    int32_t B, H, T, D, M, K;   /* D = 128, M = 32, K = 256 */
+    int32_t flags;              /* LP_ENCODE_FLAG_* bits */
+    int32_t _pad0;
+} lp_encode_args;
+
+#define LP_ENCODE_FLAG_EXACT 1 /* compute every distance on CUDA cores (testing) */
+
+/* sizeof(lp_encode_args), for bindings to verify their struct layout */
+size_t lp_sizeof_encode_args(void);
+/* Workspace bytes needed by lp_encode_keys (first 2048 bytes: error word
+ * and reserved state, as for lp_sparse_decode). */
+size_t lp_encode_workspace_size(const lp_encode_args* a);
+
+/* Greedy residual encode: for m = 0..M-1, code_m = the first k minimising
+ * ||r||^2 + ||C_m[k]||^2 - 2 r.C_m[k] (fp32, every sum a sequential chain of
+ * fused multiply-adds in index order), then r -= C_m[code_m].  The
+ * contraction runs on tcgen05 tensor cores (tf32) as a filter under an error
+ * bound; near-ties are settled exactly on CUDA cores.  Reference path this
+ * replaces: aq_kernels/fused_linear_encode.cu:168-234
+ * (fused_linear_encode_forward), laprune/llm/aq_kv.py:44-75
+ * (_fast_greedy_encode) and laprune/quantizer.py:346-374
+ * (AdditiveQuantizer._batch_icm_lut with 0 ICM iterations). */
+int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ======================================================================
  * Allocation-free variant (no counterpart in the reference)
  * ====================================================================== */
 

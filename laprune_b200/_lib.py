@@ -43,6 +43,20 @@ class SparseDecodeArgs(ctypes.Structure):
     ]
 
 
+class EncodeArgs(ctypes.Structure):
+    """Mirror of lp_encode_args."""
+    _fields_ = [
+        ("x", _c_p), ("x_dtype", _c_i32), ("cb_per_kv_head", _c_i32),
+        ("x_stride_b", _c_i64), ("x_stride_h", _c_i64), ("x_stride_t", _c_i64),
+        ("codebooks", _c_p), ("codes", _c_p),
+        ("codes_stride_b", _c_i64), ("codes_stride_h", _c_i64), ("codes_stride_t", _c_i64),
+        ("B", _c_i32), ("H", _c_i32), ("T", _c_i32), ("D", _c_i32), ("M", _c_i32), ("K", _c_i32),
+        ("flags", _c_i32), ("_pad0", _c_i32),
+    ]
+
+
+LP_ENCODE_FLAG_EXACT = 1
+
 # name -> (restype, argtypes) of every exported entry point
 SIGNATURES = {
     "lp_last_error": (ctypes.c_char_p, []),
@@ -53,6 +67,9 @@ SIGNATURES = {
     "lp_read_device_errors": (ctypes.c_int, [_c_p, ctypes.c_size_t, _c_p, ctypes.POINTER(ctypes.c_uint32)]),
     "lp_sparse_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(SparseDecodeArgs), _c_p,
                                                 ctypes.POINTER(ctypes.c_uint32)]),
+    "lp_sizeof_encode_args": (ctypes.c_size_t, []),
+    "lp_encode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(EncodeArgs)]),
+    "lp_encode_keys": (ctypes.c_int, [ctypes.POINTER(EncodeArgs), _c_p, ctypes.c_size_t, _c_p]),
 }
 LP_NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -78,6 +95,8 @@ def load() -> ctypes.CDLL:
             fn.argtypes = args
         if lib.lp_sizeof_sparse_decode_args() != ctypes.sizeof(SparseDecodeArgs):
             raise ImportError("lp_sparse_decode_args layout mismatch between the binding and the library")
+        if lib.lp_sizeof_encode_args() != ctypes.sizeof(EncodeArgs):
+            raise ImportError("lp_encode_args layout mismatch between the binding and the library")
         _lib = lib
     return _lib
 

@@ -4,6 +4,7 @@
 #include <string>
 
 #include "attention.cuh"
+#include "encode.cuh"
 #include "fused_step.cuh"
 #include "lut_build.cuh"
 #include "score.cuh"
@@ -578,6 +579,95 @@ int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t wor
     }
     if ((rc = mark(4)) != LP_OK) return rc;
     return LP_OK;
+}
+
+size_t lp_sizeof_encode_args(void) { return sizeof(lp_encode_args); }
+
+static int encode_plan(const lp_encode_args* a, size_t* bytes, int64_t* nsets, int64_t* nvec_set) {
+    LP_CHECK(a != nullptr, "args must not be NULL");
+    LP_CHECK(a->D == 128 && a->M == 32 && a->K == 256, "the encoder supports D=128, M=32 codebooks of K=256 entries");
+    LP_CHECK(a->B >= 0 && a->H > 0 && a->T >= 0, "need B >= 0, H > 0, T >= 0");
+    *nsets = a->cb_per_kv_head ? a->H : 1;
+    *nvec_set = a->cb_per_kv_head ? (int64_t)a->B * a->T : (int64_t)a->B * a->H * a->T;
+    LP_CHECK(*nvec_set <= (int64_t)1 << 30, "too many vectors");
+    Carver c(nullptr);
+    c.take<unsigned char>(kPersistBytes);
+    c.take<float>((size_t)*nsets * 32 * 256);
+    c.take<float>((size_t)*nsets * 32 * 256);
+    *bytes = c.used();
+    return LP_OK;
+}
+
+size_t lp_encode_workspace_size(const lp_encode_args* a) {
+    size_t bytes = 0;
+    int64_t ns = 0, nv = 0;
+    if (encode_plan(a, &bytes, &ns, &nv) != LP_OK) return 0;
+    return bytes;
+}
+
+int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+    size_t need = 0;
+    int64_t nsets = 0, nvec_set = 0;
+    int rc = encode_plan(a, &need, &nsets, &nvec_set);
+    if (rc != LP_OK) return rc;
+    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return fail(LP_ERR_WORKSPACE, "workspace missing, misaligned (256 B) or smaller than lp_encode_workspace_size()");
+    LP_CHECK(a->x_dtype == LP_BF16 || a->x_dtype == LP_F16 || a->x_dtype == LP_F32,
+             "x_dtype must be LP_BF16, LP_F16 or LP_F32");
+    if (nvec_set == 0) return LP_OK;
+    LP_CHECK(a->x && a->codebooks && a->codes, "x, codebooks and codes must not be NULL");
+    LP_CHECK(aligned16(a->codebooks), "codebooks must be 16-byte aligned");
+    int dev = 0;
+    LP_CUDA(cudaGetDevice(&dev));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    Carver c(workspace);
+    uint32_t* err = c.take<uint32_t>(kPersistBytes / 4);
+    float* nrm = c.take<float>((size_t)nsets * 32 * 256);
+    float* cnorm = c.take<float>((size_t)nsets * 32 * 256);
+    const int64_t ncw = nsets * 32 * 256;
+    encode_norms_kernel<<<(unsigned)((ncw + 255) / 256), 256, 0, st>>>(a->codebooks, ncw, nrm, cnorm);
+    rc = check_launch("encode_norms_kernel");
+    if (rc != LP_OK) return rc;
+
+    EncodeParams ep{};
+    ep.x = a->x;
+    ep.xs_b = a->x_stride_b;
+    ep.xs_h = a->x_stride_h;
+    ep.xs_t = a->x_stride_t;
+    ep.B = a->B;
+    ep.H = a->H;
+    ep.T = a->T;
+    ep.per_head = a->cb_per_kv_head ? 1 : 0;
+    ep.cb = a->codebooks;
+    ep.nrm = nrm;
+    ep.cnorm = cnorm;
+    ep.codes = a->codes;
+    ep.cs_b = a->codes_stride_b;
+    ep.cs_h = a->codes_stride_h;
+    ep.cs_t = a->codes_stride_t;
+    ep.ctas_per_set = (int)((nvec_set + kEncRows - 1) / kEncRows);
+    ep.force_exact = (a->flags & LP_ENCODE_FLAG_EXACT) ? 1 : 0;
+    ep.err = err;
+    const dim3 grid((unsigned)(nsets * ep.ctas_per_set));
+    static bool opt_enc[3][64] = {{false}};
+    switch (a->x_dtype) {
+        case LP_BF16:
+            rc = smem_opt_in(encode_keys_kernel<__nv_bfloat16>, EncSmem::kTotal, dev, opt_enc[0]);
+            if (rc != LP_OK) return rc;
+            encode_keys_kernel<__nv_bfloat16><<<grid, kEncThreads, EncSmem::kTotal, st>>>(ep);
+            break;
+        case LP_F16:
+            rc = smem_opt_in(encode_keys_kernel<__half>, EncSmem::kTotal, dev, opt_enc[1]);
+            if (rc != LP_OK) return rc;
+            encode_keys_kernel<__half><<<grid, kEncThreads, EncSmem::kTotal, st>>>(ep);
+            break;
+        default:
+            rc = smem_opt_in(encode_keys_kernel<float>, EncSmem::kTotal, dev, opt_enc[2]);
+            if (rc != LP_OK) return rc;
+            encode_keys_kernel<float><<<grid, kEncThreads, EncSmem::kTotal, st>>>(ep);
+            break;
+    }
+    return check_launch("encode_keys_kernel");
 }
 
 int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream, uint32_t* bits_out) {

@@ -231,6 +231,61 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
     return SparseDecodeResult(out=o, topk=tk[:, :topk] if tk is not None else None, head_scores=hs)
 
 
+def encode_keys(x: torch.Tensor, codebooks: torch.Tensor, codes: Optional[torch.Tensor] = None, *,
+                exact: bool = False, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Greedy residual additive-quantization codes of vectors (lp_encode_keys).
+
+    x: [B,H,T,128] (bf16/fp16/fp32, any strides) or [N,128]; codebooks fp32
+    [H,32,256,128] (vector (b,h,t) uses set h) or [32,256,128] (one set).
+    ``codes``: optional uint8 [B,H,T,32] destination (e.g. a slice of a code
+    cache, rows of 32 contiguous bytes); allocated when omitted.  Returns it.
+    Every distance follows the CPU arithmetic exactly (first minimum on
+    ties); ``exact=True`` computes all of them on CUDA cores (testing).
+    """
+    flat = x.dim() == 2
+    x4 = x.view(1, 1, *x.shape) if flat else x
+    if x4.dim() != 4:
+        raise RuntimeError("x must be [B,H,T,128] or [N,128]")
+    if not x4.is_cuda or not codebooks.is_cuda:
+        raise RuntimeError("x and codebooks must be CUDA tensors")
+    B, H, T, D = x4.shape
+    per_head = codebooks.dim() == 4
+    if codebooks.dtype != torch.float32 or not codebooks.is_contiguous():
+        raise RuntimeError("codebooks must be contiguous fp32")
+    if per_head and codebooks.shape[0] != H:
+        raise RuntimeError("per-KV-head codebooks need one set per head of x")
+    M, K = codebooks.shape[-3], codebooks.shape[-2]
+    if codes is None:
+        codes = torch.empty((T, M) if flat else (B, H, T, M), dtype=torch.uint8, device=x.device)
+    c4 = codes.view(1, 1, *codes.shape) if codes.dim() == 2 else codes
+    if c4.dtype != torch.uint8 or tuple(c4.shape) != (B, H, T, M) or c4.stride(3) != 1:
+        raise RuntimeError("codes must be uint8 [B,H,T,M] with contiguous rows")
+    dt = {torch.bfloat16: _lib.LP_BF16, torch.float16: _lib.LP_F16, torch.float32: _lib.LP_F32}.get(x4.dtype)
+    if dt is None:
+        raise RuntimeError("x must be bf16, fp16 or fp32")
+    if x4.stride(3) != 1:
+        raise RuntimeError("x rows must be contiguous")
+    a = _lib.EncodeArgs()
+    a.x = x4.data_ptr()
+    a.x_dtype = dt
+    a.cb_per_kv_head = 1 if per_head else 0
+    a.x_stride_b, a.x_stride_h, a.x_stride_t = x4.stride(0), x4.stride(1), x4.stride(2)
+    a.codebooks = codebooks.data_ptr()
+    a.codes = c4.data_ptr()
+    a.codes_stride_b, a.codes_stride_h, a.codes_stride_t = c4.stride(0), c4.stride(1), c4.stride(2)
+    a.B, a.H, a.T, a.D, a.M, a.K = B, H, T, D, M, K
+    a.flags = _lib.LP_ENCODE_FLAG_EXACT if exact else 0
+    lib = _lib.load()
+    need = lib.lp_encode_workspace_size(ctypes.byref(a))
+    if need == 0:
+        _lib.check(_lib.LP_ERR_INVALID)
+    if ws is None:
+        ws = workspace(need, x.device, tag="encode")
+    with torch.cuda.device(x.device):
+        _lib.check(lib.lp_encode_keys(ctypes.byref(a), ws.data_ptr(), ws.numel(), _stream_handle(x.device)))
+    return codes
+
+
 def event_array(events) -> ctypes.Array:
     """ctypes array of raw cudaEvent_t handles of torch.cuda.Event objects
     (each event is created on the current device if it was not yet)."""

@@ -157,7 +157,7 @@ void orc_encode_greedy(const float* x, const float* cb, const int32_t* cb_index,
         for (int mk = 0; mk < M * K; ++mk) {
             const float* c = cb + ((int64_t)s * M * K + mk) * d;
             float acc = 0.f;
-            for (int j = 0; j < d; ++j) acc += c[j] * c[j];
+            for (int j = 0; j < d; ++j) acc = fmaf(c[j], c[j], acc);
             norms[(int64_t)s * M * K + mk] = acc;
         }
     }
@@ -171,15 +171,18 @@ void orc_encode_greedy(const float* x, const float* cb, const int32_t* cb_index,
             const float* nrm = norms + (int64_t)s * M * K;
             memcpy(r, x + (int64_t)n * d, sizeof(float) * (size_t)d);
             for (int m = 0; m < M; ++m) {
+                /* every sum is a sequential chain of fused multiply-adds in
+                 * index order, written out explicitly so that the rounding
+                 * does not depend on the compiler's contraction choices */
                 float rn = 0.f;
-                for (int j = 0; j < d; ++j) rn += r[j] * r[j];
+                for (int j = 0; j < d; ++j) rn = fmaf(r[j], r[j], rn);
                 float best = INFINITY;
                 int best_k = 0;
                 for (int k = 0; k < K; ++k) {
                     const float* c = cbs + ((int64_t)m * K + k) * d;
                     float dot = 0.f;
-                    for (int j = 0; j < d; ++j) dot += r[j] * c[j];
-                    float dist = (rn + nrm[(int64_t)m * K + k]) - 2.f * dot;
+                    for (int j = 0; j < d; ++j) dot = fmaf(r[j], c[j], dot);
+                    const float dist = fmaf(-2.f, dot, rn + nrm[(int64_t)m * K + k]);
                     if (dist < best) { best = dist; best_k = k; }
                 }
                 codes[(int64_t)n * M + m] = (uint8_t)best_k;
