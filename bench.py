@@ -209,6 +209,43 @@ def run_reference(args):
     return 0
 
 
+def encode_measurement(dev, reps: int = 20):
+    """Key encoder (lp_encode_keys) timing, outside the decode timed region:
+    BASELINE config 2 (4 x 8 x 64 post-RoPE bf16 keys, per-KV-head codebooks)
+    and a prefill-scale batch (8 x 4096 keys).  Tensor throughput counts the
+    tf32 contraction 2*128*256*128 flop per vector and stage; the tf32 peak is
+    taken as half the measured dense bf16 peak."""
+    import torch
+    from laprune_b200 import ops, synthetic as syn
+    out = {}
+    p = ROOT / "MEASURED_PEAKS.json"
+    bf16 = float(json.loads(p.read_text())["bf16_tflops"]) if p.exists() else 1590.0
+    tf32_peak = bf16 / 2
+    c = syn.config2(0)
+    C = c["C"].to(dev)
+    cases = {"cfg2_4x8x64": c["keys"].to(dev),
+             "prefill_1x8x4096": torch.randn((1, 8, 4096, 128), device=dev).to(torch.bfloat16)}
+    for name, keys in cases.items():
+        codes = ops.encode_keys(keys, C)
+        for _ in range(3):
+            ops.encode_keys(keys, C, codes=codes)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            ops.encode_keys(keys, C, codes=codes)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        nvec = keys.numel() // 128
+        tflops = nvec * 32 * 2 * 128 * 256 * 128 / (us * 1e-6) / 1e12
+        out[name] = {"us": us, "vectors": nvec, "tensor_tflops": tflops,
+                     "frac_of_tf32_peak": tflops / tf32_peak}
+    out["tf32_peak_tflops"] = tf32_peak
+    out["tf32_peak_kind"] = "half of measured bf16" if p.exists() else "half of fallback bf16"
+    return out
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -396,6 +433,8 @@ def run_ours(args):
                     "api": "laprune_b200.ops.sparse_decode per layer, q from pinned host, out to pinned host"},
             "gpu_launches": args.steps * N_LAYERS,
         }
+        if world == 1:
+            line["encode"] = encode_measurement(dev)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         print(json.dumps(line), flush=True)

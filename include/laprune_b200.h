@@ -198,6 +198,64 @@ size_t lp_encode_workspace_size(const lp_encode_args* a);
 int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ======================================================================
+ * Building blocks behind the aq_kernels-named Python surface
+ * ====================================================================== */
+
+/* out[q][n] = sum_{m in [m0,m1)} lut[q][m][codes[q/G][t][m]] (fp32
+ * accumulation in m order, then out_dtype), t = indices ? indices[q][n] : n;
+ * tokens outside [0,T) give 0.  Replaces aq_kernels/aq_lut_gqa.cu:350-534
+ * (aq_lut_gather, aq_lut_gather_grouped) and aq_kernels/aq_lut.cu:581-738
+ * (aq_lut_gather_forward). */
+typedef struct lp_lut_gather_args {
+    const void* lut;          /* LP_F16 | LP_F32, row q: [M_stride][K] contiguous */
+    int32_t lut_dtype;
+    int32_t code_mode;        /* 0: clamp codes to K-1; 1: codes >= K add nothing */
+    int64_t lut_stride_q;     /* elements between rows */
+    int32_t M_stride, K, m0, m1;
+    const uint8_t* codes;     /* codes[h][t][m] at codes + h*sh + t*st + m (bytes) */
+    int64_t codes_stride_h, codes_stride_t;
+    int32_t Q, G, T, N;
+    const int64_t* indices;   /* optional [Q][N] token indices; NULL: n = t, N = T */
+    int64_t indices_stride_q;
+    void* out;                /* [Q][N] of out_dtype (LP_F16 | LP_F32) */
+    int32_t out_dtype;
+    int32_t _pad0;
+    int64_t out_stride_q;
+} lp_lut_gather_args;
+int lp_lut_gather(const lp_lut_gather_args* a, void* stream);
+
+/* lut[q][m][k] = q_q . C[m][k] (fp32, sequential fma over d).  The LUT step
+ * of aq_kernels/aq_lut.cu:445-574 (aq_lut_forward). */
+typedef struct lp_lut_build_args {
+    const void* q;            /* [Q][D] at q + i*q_stride (elements) */
+    int32_t q_dtype;          /* LP_BF16 | LP_F16 | LP_F32 */
+    int32_t _pad0;
+    int64_t q_stride;
+    const float* codebooks;   /* fp32 [M][K][D] contiguous */
+    int32_t Q, M, K, D;
+    float* lut;               /* fp32 [Q][M][K] contiguous */
+} lp_lut_build_args;
+int lp_lut_build(const lp_lut_build_args* a, void* stream);
+
+/* out_k/out_v[b][hq][n] = K/V[b][hq/G][token] for token = indices[b][hq][n]
+ * (n < N_explicit) or tail_start + n - N_explicit (implicit local tail);
+ * tokens outside [0,T) give zero rows.  Replaces aq_kernels/aq_lut_gqa.cu:
+ * 536-664 (gqa_gather_kv, gqa_gather_kv_with_tail). */
+typedef struct lp_gqa_gather_args {
+    const void* keys;
+    const void* vals;
+    int32_t kv_dtype;         /* LP_F16 | LP_BF16 */
+    int32_t _pad0;
+    int64_t k_stride_b, k_stride_h, k_stride_t, v_stride_b, v_stride_h, v_stride_t;
+    const int64_t* indices;   /* [B][Hq][N_explicit] */
+    int64_t indices_stride_b, indices_stride_h;
+    int32_t B, Hkv, G, T, D, N_explicit, tail_start, tail_count;
+    void* out_k;              /* [B][Hq][N_explicit + tail_count][D] contiguous */
+    void* out_v;
+} lp_gqa_gather_args;
+int lp_gqa_gather_kv(const lp_gqa_gather_args* a, void* stream);
+
+/* ======================================================================
  * Allocation-free variant (no counterpart in the reference)
  * ====================================================================== */
 

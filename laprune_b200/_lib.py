@@ -57,6 +57,42 @@ class EncodeArgs(ctypes.Structure):
 
 LP_ENCODE_FLAG_EXACT = 1
 
+
+class LutGatherArgs(ctypes.Structure):
+    """Mirror of lp_lut_gather_args."""
+    _fields_ = [
+        ("lut", _c_p), ("lut_dtype", _c_i32), ("code_mode", _c_i32),
+        ("lut_stride_q", _c_i64),
+        ("M_stride", _c_i32), ("K", _c_i32), ("m0", _c_i32), ("m1", _c_i32),
+        ("codes", _c_p), ("codes_stride_h", _c_i64), ("codes_stride_t", _c_i64),
+        ("Q", _c_i32), ("G", _c_i32), ("T", _c_i32), ("N", _c_i32),
+        ("indices", _c_p), ("indices_stride_q", _c_i64),
+        ("out", _c_p), ("out_dtype", _c_i32), ("_pad0", _c_i32),
+        ("out_stride_q", _c_i64),
+    ]
+
+
+class LutBuildArgs(ctypes.Structure):
+    """Mirror of lp_lut_build_args."""
+    _fields_ = [
+        ("q", _c_p), ("q_dtype", _c_i32), ("_pad0", _c_i32), ("q_stride", _c_i64),
+        ("codebooks", _c_p), ("Q", _c_i32), ("M", _c_i32), ("K", _c_i32),
+        ("D", _c_i32), ("lut", _c_p),
+    ]
+
+
+class GqaGatherArgs(ctypes.Structure):
+    """Mirror of lp_gqa_gather_args."""
+    _fields_ = [
+        ("keys", _c_p), ("vals", _c_p), ("kv_dtype", _c_i32), ("_pad0", _c_i32),
+        ("k_stride_b", _c_i64), ("k_stride_h", _c_i64), ("k_stride_t", _c_i64),
+        ("v_stride_b", _c_i64), ("v_stride_h", _c_i64), ("v_stride_t", _c_i64),
+        ("indices", _c_p), ("indices_stride_b", _c_i64), ("indices_stride_h", _c_i64),
+        ("B", _c_i32), ("Hkv", _c_i32), ("G", _c_i32), ("T", _c_i32),
+        ("D", _c_i32), ("N_explicit", _c_i32), ("tail_start", _c_i32),
+        ("tail_count", _c_i32), ("out_k", _c_p), ("out_v", _c_p),
+    ]
+
 # name -> (restype, argtypes) of every exported entry point
 SIGNATURES = {
     "lp_last_error": (ctypes.c_char_p, []),
@@ -70,6 +106,9 @@ SIGNATURES = {
     "lp_sizeof_encode_args": (ctypes.c_size_t, []),
     "lp_encode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(EncodeArgs)]),
     "lp_encode_keys": (ctypes.c_int, [ctypes.POINTER(EncodeArgs), _c_p, ctypes.c_size_t, _c_p]),
+    "lp_lut_gather": (ctypes.c_int, [ctypes.POINTER(LutGatherArgs), _c_p]),
+    "lp_lut_build": (ctypes.c_int, [ctypes.POINTER(LutBuildArgs), _c_p]),
+    "lp_gqa_gather_kv": (ctypes.c_int, [ctypes.POINTER(GqaGatherArgs), _c_p]),
 }
 LP_NOALLOC_SCRATCH_BYTES = 16 << 20
 

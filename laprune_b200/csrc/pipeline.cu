@@ -4,6 +4,7 @@
 #include <string>
 
 #include "attention.cuh"
+#include "compat.cuh"
 #include "encode.cuh"
 #include "fused_step.cuh"
 #include "lut_build.cuh"
@@ -668,6 +669,106 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
             break;
     }
     return check_launch("encode_keys_kernel");
+}
+
+int lp_lut_gather(const lp_lut_gather_args* a, void* stream) {
+    LP_CHECK(a != nullptr, "args must not be NULL");
+    LP_CHECK(a->lut_dtype == LP_F16 || a->lut_dtype == LP_F32, "lut must be fp16 or fp32");
+    LP_CHECK(a->out_dtype == LP_F16 || a->out_dtype == LP_F32, "out must be fp16 or fp32");
+    LP_CHECK(a->Q >= 0 && a->G > 0 && a->T >= 0 && a->N >= 0 && a->K > 0, "invalid sizes");
+    LP_CHECK(a->m0 >= 0 && a->m1 > a->m0 && a->m1 <= a->M_stride, "M range must satisfy 0 <= M_start < M_end <= M");
+    LP_CHECK((int64_t)(a->m1 - a->m0) * a->K <= 12288, "LUT slice too large (at most 12288 entries per row)");
+    if (a->Q == 0 || a->N == 0) return LP_OK;
+    LP_CHECK(a->lut && a->codes && a->out, "lut, codes and out must not be NULL");
+    LutGatherParams p{};
+    p.lut = a->lut;
+    p.lut_f16 = a->lut_dtype == LP_F16;
+    p.lut_stride_q = a->lut_stride_q;
+    p.M_stride = a->M_stride;
+    p.K = a->K;
+    p.m0 = a->m0;
+    p.m1 = a->m1;
+    p.codes = a->codes;
+    p.cs_h = a->codes_stride_h;
+    p.cs_t = a->codes_stride_t;
+    p.Q = a->Q;
+    p.G = a->G;
+    p.T = a->T;
+    p.N = a->N;
+    p.indices = a->indices;
+    p.is_q = a->indices_stride_q;
+    p.code_mode = a->code_mode;
+    p.out = a->out;
+    p.out_f16 = a->out_dtype == LP_F16;
+    p.os_q = a->out_stride_q;
+    const int smem = (a->m1 - a->m0) * a->K * 4;
+    lut_gather_kernel<<<dim3((a->N + 255) / 256, a->Q), 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+    return check_launch("lut_gather_kernel");
+}
+
+int lp_lut_build(const lp_lut_build_args* a, void* stream) {
+    LP_CHECK(a != nullptr, "args must not be NULL");
+    LP_CHECK(a->Q >= 0 && a->M > 0 && a->K > 0 && a->D > 0 && a->D <= 12288, "invalid sizes");
+    if (a->Q == 0) return LP_OK;
+    LP_CHECK(a->q && a->codebooks && a->lut, "q, codebooks and lut must not be NULL");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const dim3 grid(a->M, a->Q);
+    const int smem = a->D * 4;
+    switch (a->q_dtype) {
+        case LP_BF16:
+            lut_build_rows_kernel<__nv_bfloat16><<<grid, 256, smem, st>>>(
+                reinterpret_cast<const __nv_bfloat16*>(a->q), a->q_stride, a->codebooks, a->M, a->K, a->D, a->lut);
+            break;
+        case LP_F16:
+            lut_build_rows_kernel<__half><<<grid, 256, smem, st>>>(
+                reinterpret_cast<const __half*>(a->q), a->q_stride, a->codebooks, a->M, a->K, a->D, a->lut);
+            break;
+        case LP_F32:
+            lut_build_rows_kernel<float><<<grid, 256, smem, st>>>(
+                reinterpret_cast<const float*>(a->q), a->q_stride, a->codebooks, a->M, a->K, a->D, a->lut);
+            break;
+        default:
+            return fail(LP_ERR_INVALID, "q_dtype must be LP_BF16, LP_F16 or LP_F32");
+    }
+    return check_launch("lut_build_rows_kernel");
+}
+
+int lp_gqa_gather_kv(const lp_gqa_gather_args* a, void* stream) {
+    LP_CHECK(a != nullptr, "args must not be NULL");
+    LP_CHECK(a->kv_dtype == LP_F16 || a->kv_dtype == LP_BF16, "K/V must be fp16 or bf16");
+    LP_CHECK(a->B >= 0 && a->Hkv > 0 && a->G > 0 && a->T >= 0 && a->D > 0 && a->N_explicit >= 0,
+             "invalid sizes");
+    LP_CHECK(a->tail_count >= 0 && a->tail_start >= 0 && (int64_t)a->tail_start + a->tail_count <= a->T,
+             "invalid implicit tail range");
+    const int64_t N = (int64_t)a->N_explicit + a->tail_count;
+    const int64_t rows = (int64_t)a->B * a->Hkv * a->G * N;
+    if (rows == 0) return LP_OK;
+    LP_CHECK(a->keys && a->vals && a->out_k && a->out_v && (a->indices || a->N_explicit == 0),
+             "keys, vals, indices and outputs must not be NULL");
+    GqaGatherParams p{};
+    p.keys = static_cast<const uint16_t*>(a->keys);
+    p.vals = static_cast<const uint16_t*>(a->vals);
+    p.ks_b = a->k_stride_b;
+    p.ks_h = a->k_stride_h;
+    p.ks_t = a->k_stride_t;
+    p.vs_b = a->v_stride_b;
+    p.vs_h = a->v_stride_h;
+    p.vs_t = a->v_stride_t;
+    p.indices = a->indices;
+    p.is_b = a->indices_stride_b;
+    p.is_h = a->indices_stride_h;
+    p.B = a->B;
+    p.Hkv = a->Hkv;
+    p.G = a->G;
+    p.T = a->T;
+    p.D = a->D;
+    p.N_explicit = a->N_explicit;
+    p.tail_start = a->tail_start;
+    p.N = (int)N;
+    p.out_k = static_cast<uint16_t*>(a->out_k);
+    p.out_v = static_cast<uint16_t*>(a->out_v);
+    gqa_gather_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+    return check_launch("gqa_gather_kernel");
 }
 
 int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream, uint32_t* bits_out) {
