@@ -213,7 +213,7 @@ def encode_measurement(dev, reps: int = 20):
     """Key encoder (lp_encode_keys) timing, outside the decode timed region:
     BASELINE config 2 (4 x 8 x 64 post-RoPE bf16 keys, per-KV-head codebooks)
     and a prefill-scale batch (8 x 4096 keys).  Tensor throughput counts the
-    tf32 contraction 2*128*256*128 flop per vector and stage; the tf32 peak is
+    tf32 contraction 2*256*128 flop per vector and stage; the tf32 peak is
     taken as half the measured dense bf16 peak."""
     import torch
     from laprune_b200 import ops, synthetic as syn
@@ -238,7 +238,7 @@ def encode_measurement(dev, reps: int = 20):
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / reps
         nvec = keys.numel() // 128
-        tflops = nvec * 32 * 2 * 128 * 256 * 128 / (us * 1e-6) / 1e12
+        tflops = nvec * 32 * 2 * 256 * 128 / (us * 1e-6) / 1e12
         out[name] = {"us": us, "vectors": nvec, "tensor_tflops": tflops,
                      "frac_of_tf32_peak": tflops / tf32_peak}
     out["tf32_peak_tflops"] = tf32_peak

@@ -21,11 +21,14 @@
 //
 // Shared memory holds the residuals (A operand, 64 KB) and the stage's
 // codewords in two halves of 128 (B operands, 64 KB each), both in the UMMA
-// canonical K-major layout without swizzle: 8-row x 16-byte core matrices,
-// K-adjacent ones 128 B apart (LBO), 8-row groups 4096 B apart (SBO).  The
-// next stage's codewords load (cp.async) while the current stage's
-// distances are searched.
+// K-major SWIZZLE_128B layout: per 32-dim K chunk (16 KB), 8-row atoms of
+// 1024 B, rows 128 B apart, 16-byte units XOR-swizzled with the row.  The
+// codewords arrive by 2-D TMA tensor copies (box 32 dims x 128 rows, the
+// same swizzle); the next stage's copies start as soon as the current
+// stage's MMAs complete, so they overlap the distance search, which reads
+// the winning codeword rows from L2.
 #pragma once
+#include <cuda.h>
 #include "common.cuh"
 
 namespace lp {
@@ -42,6 +45,7 @@ struct EncodeParams {
     const float* cb;           // [S][32][256][128] fp32
     const float* nrm;          // [S][32][256]  ||C||^2 (sequential fma)
     const float* cnorm;        // [S][32][256]  ||C|| rounded up
+    const float* smax;         // [S][32][4]    per stage: max ||C||^2, max ||C||, 0, 0
     uint8_t* codes;
     int64_t cs_b, cs_h, cs_t;  // bytes
     int ctas_per_set;          // ceil(vectors of a set / 128)
@@ -52,22 +56,38 @@ struct EncodeParams {
 struct EncSmem {
     static constexpr int kA = kEncRows * kEncD * 4;          // 64 KB
     static constexpr int kBHalf = 128 * kEncD * 4;           // 64 KB
-    static constexpr int kNorm = 2 * 2 * kEncK * 4;          // nrm + cnorm, double buffered (4 KB)
-    static constexpr int kTotal = kA + 2 * kBHalf + kNorm + 64;
+    static constexpr int kNormStride = 2 * kEncK + 4;       // nrm[256] cnorm[256] nmax cmax . .
+    static constexpr int kNorm = 2 * kNormStride * 4;        // double buffered
+    static constexpr int kTotal = kA + 2 * kBHalf + kNorm + 64 + 1024;  // + alignment slack
 };
 
-// byte offset of element (row n, dim d) in the canonical K-major layout
+// byte offset of (row n, dim d) of a [128][128] fp32 operand in the K-major
+// SWIZZLE_128B layout: K chunk d/32 at 16 KB steps, 8-row atoms of 1024 B,
+// row r of an atom at 128 r with its 16-byte units XOR-ed with r
 __device__ __forceinline__ uint32_t enc_off(int n, int d) {
-    return (uint32_t)((((n >> 3) * (kEncD / 4) + (d >> 2)) << 7) + ((n & 7) << 4) + ((d & 3) << 2));
+    const int b = (d & 31) << 2;
+    const int u = (b >> 4) ^ (n & 7);
+    return (uint32_t)(((d >> 5) << 14) + ((n >> 3) << 10) + ((n & 7) << 7) + (u << 4) + (b & 15));
 }
 
-// UMMA shared-memory descriptor: K-major, no swizzle, LBO 128 B, SBO 4096 B
+// UMMA shared-memory descriptor: K-major SWIZZLE_128B, SBO 1024 B (8-row
+// atoms), LBO unused (1); the start address may step inside an atom by the
+// 32 bytes of one K step (the swizzle works on absolute address bits)
 __device__ __forceinline__ uint64_t enc_desc(uint32_t saddr) {
     uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
-    d |= (uint64_t)(128u >> 4) << 16;
-    d |= (uint64_t)(4096u >> 4) << 32;
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
     d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;  // SWIZZLE_128B
     return d;
+}
+
+__device__ __forceinline__ void enc_tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // instruction descriptor: D fp32, A/B tf32, both K-major, N = 128, M = 128
@@ -111,6 +131,27 @@ __device__ __forceinline__ void enc_tmem_ld64(uint32_t taddr, float* v) {
     for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// per stage (set, m): the largest ||C||^2 and ||C|| of its 256 codewords
+__global__ void __launch_bounds__(256) encode_stage_max_kernel(const float* nrm, const float* cnorm, float* smax) {
+    __shared__ float s_a[8], s_b[8];
+    const int st = blockIdx.x, k = threadIdx.x;
+    float a = nrm[(int64_t)st * kEncK + k], b = cnorm[(int64_t)st * kEncK + k];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
+    }
+    if ((k & 31) == 0) { s_a[k >> 5] = a; s_b[k >> 5] = b; }
+    __syncthreads();
+    if (k == 0) {
+        for (int w = 1; w < 8; ++w) { a = fmaxf(a, s_a[w]); b = fmaxf(b, s_b[w]); }
+        smax[st * 4 + 0] = a;
+        smax[st * 4 + 1] = b;
+        smax[st * 4 + 2] = 0.f;
+        smax[st * 4 + 3] = 0.f;
+    }
+}
+
 // ||C||^2 of every codeword (sequential fma over d) and ||C|| rounded up.
 __global__ void __launch_bounds__(256) encode_norms_kernel(const float* cb, int64_t n, float* nrm, float* cnorm) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -130,12 +171,16 @@ __global__ void __launch_bounds__(256) encode_norms_kernel(const float* cb, int6
 }
 
 template <typename XT>
-__global__ void __launch_bounds__(kEncThreads, 1) encode_keys_kernel(EncodeParams p) {
-    extern __shared__ __align__(1024) unsigned char smem[];
+__global__ void __launch_bounds__(kEncThreads, 1)
+    encode_keys_kernel(const __grid_constant__ CUtensorMap cmap, EncodeParams p) {
+    extern __shared__ unsigned char smem_raw[];
+    // operands need 1024-byte alignment (SWIZZLE_128B atoms)
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     unsigned char* sA = smem;
-    unsigned char* sB = smem + EncSmem::kA;  // two halves
+    unsigned char* sB = smem + EncSmem::kA;  // half hf, K chunk c at hf * 64 KB + c * 16 KB
     float* sNorm = reinterpret_cast<float*>(sB + 2 * EncSmem::kBHalf);  // [2][nrm 256 | cnorm 256]
     uint64_t* s_mbar = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(sNorm) + EncSmem::kNorm);
+    uint64_t* s_tbar = s_mbar + 1;
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
 
@@ -147,6 +192,7 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_keys_kernel(EncodeParam
     const float* cbs = p.cb + (int64_t)set * kEncM * kEncK * kEncD;
     const float* nrms = p.nrm + (int64_t)set * kEncM * kEncK;
     const float* cns = p.cnorm + (int64_t)set * kEncM * kEncK;
+    const float* smx = p.smax + (int64_t)set * kEncM * 4;
 
     // vector i of the set -> (b, h, t)
     auto vec_bht = [&](int i, int* b, int* h, int* t) {
@@ -162,18 +208,21 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_keys_kernel(EncodeParam
             *t = r - *h * p.T;
         }
     };
-
-    // stage m's codewords (both halves) and norms -> buffers (cp.async, one group)
-    auto load_stage = [&](int m) {
-        const float* cm = cbs + (int64_t)m * kEncK * kEncD;
-        for (int c = tid; c < kEncK * (kEncD / 4); c += kEncThreads) {
-            const int n = c >> 5, d4 = c & 31;  // codeword, 4-float chunk
-            unsigned char* dst = sB + (n >> 7) * EncSmem::kBHalf + enc_off(n & 127, d4 * 4);
-            cp_async16(dst, cm + (int64_t)n * kEncD + d4 * 4);
-        }
-        float* nb = sNorm + (m & 1) * 2 * kEncK;
+    // stage m's 256 codewords: 8 tensor copies (2 halves x 4 K chunks), one thread
+    auto issue_stage = [&](int m) {
+        mbar_arrive_expect_tx(s_tbar, (uint32_t)(2 * EncSmem::kBHalf));
+        const int row0 = (set * kEncM + m) * kEncK;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) enc_tma_2d(sB + hf * EncSmem::kBHalf + c * 16384, &cmap, 32 * c, row0 + 128 * hf, s_tbar);
+    };
+    // stage m's norms (cp.async, one group per thread)
+    auto load_norms = [&](int m) {
+        float* nb = sNorm + (m & 1) * EncSmem::kNormStride;
         if (tid < 64) cp_async16(nb + tid * 4, nrms + (int64_t)m * kEncK + tid * 4);
         else if (tid < 128) cp_async16(nb + kEncK + (tid - 64) * 4, cns + (int64_t)m * kEncK + (tid - 64) * 4);
+        else if (tid == 128) cp_async16(nb + 2 * kEncK, smx + m * 4);
         cp_async_commit();
     };
 
@@ -184,11 +233,13 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_keys_kernel(EncodeParam
     }
     if (tid == 0) {
         mbar_init(s_mbar, 1);
+        mbar_init(s_tbar, 1);
         fence_barrier_init();
         s_abort = 0;
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&cmap)) : "memory");
+        issue_stage(0);
     }
-    // the CTA's vectors -> residuals (fp32, canonical layout); rows past the
-    // set's end are zero
+    // the CTA's vectors -> residuals (fp32); rows past the set's end are zero
     for (int e = tid; e < kEncRows * (kEncD / 4); e += kEncThreads) {
         const int n = e >> 5, d = (e & 31) * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -200,36 +251,48 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_keys_kernel(EncodeParam
         }
         *reinterpret_cast<float4*>(sA + enc_off(n, d)) = v;
     }
-    load_stage(0);
+    load_norms(0);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = s_tmem;
 
-    // epilogue threads: warps 0-3, thread = vector row (TMEM lane)
-    const bool epi = warp < 4;
-    const int row = tid;  // valid for epi
-    bool row_valid = false;
+    // epilogue: warp w reads TMEM lane quarter q = w & 3 (vector rows
+    // 32q .. 32q+31) and the 64 columns of group cg = w >> 2
+    const int q4 = warp & 3, cg = warp >> 2;
+    const int row = q4 * 32 + lane;
+    const bool row_valid = v0 + row < nvec_set;
     uint8_t* code_out = nullptr;
-    if (epi && v0 + row < nvec_set) {
+    if (row_valid && cg == 0) {
         int b, h, t;
         vec_bht(v0 + row, &b, &h, &t);
-        row_valid = true;
         code_out = p.codes + (int64_t)b * p.cs_b + (int64_t)h * p.cs_h + (int64_t)t * p.cs_t;
     }
     // |exact dist - (approx dist + ||r||^2)| <= kEps ||r|| ||c_k|| + kAbs (||r||^2 + ||c_k||^2 + |approx|):
     // the tf32 operands (10 mantissa bits) and fp32 accumulation give about
-    // 2^-8 ||r|| ||c||, the fp32 roundings of the exact formula about 2^-23
-    // of the magnitudes; both are taken with a margin of 4 or more
-    constexpr float kEps = 1.0f / 64.0f;
+    // 2^-8 ||r|| ||c|| (Cauchy-Schwarz), the fp32 roundings of the exact
+    // formula about 2^-23 of the magnitudes; both are taken with a margin of 2
+    // or more
+    constexpr float kEps = 1.0f / 128.0f;
     constexpr float kAbs = 1.0f / 1048576.0f;
+    __shared__ float s_rn[kEncRows];
+    __shared__ float s_u[4][kEncRows];
+    __shared__ int s_cnt[4][kEncRows];
+    __shared__ float s_bd[4][kEncRows];
+    __shared__ int s_bk[4][kEncRows];
+    __shared__ int s_code[kEncRows];
 
-    uint32_t phase = 0;
     for (int m = 0; m < kEncM; ++m) {
+        const uint32_t par = (uint32_t)(m & 1);
+        // this stage's codewords (tensor copies) and norms have landed
+        const bool landed = mbar_wait(s_tbar, par, p.err);
         cp_async_wait<0>();
-        fence_proxy_async();  // generic / cp.async shared writes -> async proxy (MMA)
-        __syncthreads();
-        if (s_abort) break;
+        fence_proxy_async();  // residual writes (generic) -> async proxy (MMA)
+        if (__syncthreads_or(!landed)) {
+            if (tid == 0) s_abort = 1;
+            mbar_wait(s_tbar, par, nullptr);  // copies may still run: bounded second wait
+            break;
+        }
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t a0 = smem_u32(sA);
@@ -237,14 +300,16 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_keys_kernel(EncodeParam
             for (int hf = 0; hf < 2; ++hf) {
                 const uint32_t b0 = smem_u32(sB + hf * EncSmem::kBHalf);
 #pragma unroll
-                for (int s = 0; s < kEncD / 8; ++s)
-                    enc_mma(tmem + hf * 128, enc_desc(a0 + s * 256), enc_desc(b0 + s * 256), s > 0 ? 1u : 0u);
+                for (int s = 0; s < kEncD / 8; ++s) {
+                    const uint32_t ko = (uint32_t)((s >> 2) * 16384 + (s & 3) * 32);
+                    enc_mma(tmem + hf * 128, enc_desc(a0 + ko), enc_desc(b0 + ko), s > 0 ? 1u : 0u);
+                }
             }
             enc_commit(s_mbar);
         }
-        // meanwhile: ||r||^2 of the row, exactly (sequential fma in d order)
-        float rn = 0.f;
-        if (epi) {
+        // meanwhile: ||r||^2 of each row, exactly (sequential fma in d order)
+        if (cg == 0) {
+            float rn = 0.f;
 #pragma unroll 4
             for (int d4 = 0; d4 < kEncD / 4; ++d4) {
                 const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(row, d4 * 4));
@@ -253,67 +318,63 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_keys_kernel(EncodeParam
                 rn = __fmaf_rn(r4.z, r4.z, rn);
                 rn = __fmaf_rn(r4.w, r4.w, rn);
             }
+            s_rn[row] = rn;
         }
-        const bool done = mbar_wait(s_mbar, phase, p.err);
-        phase ^= 1u;
+        const bool done = mbar_wait(s_mbar, par, p.err);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (__syncthreads_or(!done)) {
             if (tid == 0) s_abort = 1;
-            mbar_wait(s_mbar, phase ^ 1u, nullptr);  // the MMA may still run: bounded second wait
+            mbar_wait(s_mbar, par, nullptr);  // the MMAs may still run: bounded second wait
             break;
         }
-        // the next stage's codewords load while this stage's distances are searched
-        if (m + 1 < kEncM) load_stage(m + 1);
-        if (epi) {
-            const float* nb = sNorm + (m & 1) * 2 * kEncK;
-            const float rnorm = __fmul_ru(__fsqrt_ru(rn), 1.0000001f);
-            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-            // pass 1: U = min_k (approx_k + bound_k)
-            float U = INFINITY;
-            for (int c0 = 0; c0 < kEncK; c0 += 64) {
-                float v[64];
-                enc_tmem_ld64(taddr + c0, v);
+        const float* nb = sNorm + (m & 1) * EncSmem::kNormStride;
+        const float rn = s_rn[row];
+        const float rnorm = __fmul_ru(__fsqrt_ru(rn), 1.0000001f);
+        // the bound's absolute part, one upper bound per row: |approx| <=
+        // ||c||^2 + 2 ||r|| ||c|| <= nmax + 2 rnorm cmax
+        const float slack = kAbs * (rn + 2.f * (nb[2 * kEncK] + rnorm * nb[2 * kEncK + 1]));
+        const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + 64 * cg;
+        float v[64];
+        enc_tmem_ld64(taddr, v);
+        // pass 1: the row's best upper bound U = min_k (approx_k + bound_k)
+        float u = INFINITY;
+        const float er = kEps * rnorm;
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const float ap = fmaf(-2.f, v[i], nb[c0 + i]);
-                    const float bd = fmaf(kEps * rnorm, nb[kEncK + c0 + i], kAbs * (rn + nb[c0 + i] + fabsf(ap)));
-                    U = fminf(U, ap + bd);
-                }
-            }
-            // pass 2: candidates approx_k - bound_k <= U
-            int ncand = 0, first = -1;
-            int cand[8];
-            for (int c0 = 0; c0 < kEncK; c0 += 64) {
-                float v[64];
-                enc_tmem_ld64(taddr + c0, v);
+        for (int i = 0; i < 64; ++i) {
+            const int k = 64 * cg + i;
+            const float ap = fmaf(-2.f, v[i], nb[k]);
+            v[i] = ap;
+            u = fminf(u, ap + fmaf(er, nb[kEncK + k], slack));
+        }
+        s_u[cg][row] = u;
+        __syncthreads();
+        const float U = fminf(fminf(s_u[0][row], s_u[1][row]), fminf(s_u[2][row], s_u[3][row]));
+        // pass 2: candidates approx_k - bound_k <= U (bit i of the mask = column 64cg + i)
+        uint32_t cm0 = 0u, cm1 = 0u;
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const float ap = fmaf(-2.f, v[i], nb[c0 + i]);
-                    const float bd = fmaf(kEps * rnorm, nb[kEncK + c0 + i], kAbs * (rn + nb[c0 + i] + fabsf(ap)));
-                    if (ap - bd <= U) {
-                        if (ncand < 8) cand[ncand] = c0 + i;
-                        if (first < 0) first = c0 + i;
-                        ++ncand;
-                    }
-                }
-            }
-            int code = first < 0 ? 0 : first;
-            if (p.force_exact || ncand > 1) {
-                // exact distances of the candidates (all codewords if more
-                // than 8 or in the exact test mode), first minimum wins
-                const float* cm = cbs + (int64_t)m * kEncK * kEncD;
-                const bool all = p.force_exact || ncand > 8;
-                const int nk = all ? kEncK : ncand;
-                float best = INFINITY;
-                int best_k = 0;
-                for (int i = 0; i < nk; ++i) {
-                    const int k = all ? i : cand[i];
-                    const float4* c4 = reinterpret_cast<const float4*>(cm + (int64_t)k * kEncD);
+        for (int i = 0; i < 64; ++i) {
+            const int k = 64 * cg + i;
+            const bool c = p.force_exact || v[i] - fmaf(er, nb[kEncK + k], slack) <= U;
+            if (i < 32) cm0 |= (uint32_t)c << i;
+            else cm1 |= (uint32_t)c << (i - 32);
+        }
+        s_cnt[cg][row] = __popc(cm0) + __popc(cm1);
+        s_bk[cg][row] = cm0 ? __ffs(cm0) - 1 + 64 * cg : (cm1 ? __ffs(cm1) + 31 + 64 * cg : -1);
+        __syncthreads();
+        const int total = s_cnt[0][row] + s_cnt[1][row] + s_cnt[2][row] + s_cnt[3][row];
+        if (total > 1) {
+            // several candidates: exact distances of this group's ones, first minimum
+            float best = INFINITY;
+            int best_k = -1;
+            for (int w2 = 0; w2 < 2; ++w2) {
+                for (uint32_t bits = w2 ? cm1 : cm0; bits; bits &= bits - 1) {
+                    const int k = (__ffs(bits) - 1) + 32 * w2 + 64 * cg;
+                    const unsigned char* bh = sB + (k >> 7) * EncSmem::kBHalf;
                     float dot = 0.f;
-#pragma unroll 4
+#pragma unroll 8
                     for (int d4 = 0; d4 < kEncD / 4; ++d4) {
                         const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(row, d4 * 4));
-                        const float4 cv = __ldg(c4 + d4);
+                        const float4 cv = *reinterpret_cast<const float4*>(bh + enc_off(k & 127, d4 * 4));
                         dot = __fmaf_rn(r4.x, cv.x, dot);
                         dot = __fmaf_rn(r4.y, cv.y, dot);
                         dot = __fmaf_rn(r4.z, cv.z, dot);
@@ -325,16 +386,39 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_keys_kernel(EncodeParam
                         best_k = k;
                     }
                 }
-                code = best_k;
             }
+            s_bd[cg][row] = best;
+            s_bk[cg][row] = best_k;
+        }
+        __syncthreads();
+        if (cg == 0) {
+            int code = 0;
+            if (total > 1) {
+                // groups in column order: a later group wins only if strictly better
+                float best = INFINITY;
+                for (int g = 0; g < 4; ++g)
+                    if (s_bk[g][row] >= 0 && s_bd[g][row] < best) {
+                        best = s_bd[g][row];
+                        code = s_bk[g][row];
+                    }
+            } else {
+                for (int g = 3; g >= 0; --g)
+                    if (s_bk[g][row] >= 0) code = s_bk[g][row];
+            }
+            s_code[row] = code;
             if (row_valid) code_out[m] = (uint8_t)code;
-            // r -= C_m[code]
-            const float4* c4 = reinterpret_cast<const float4*>(cbs + ((int64_t)m * kEncK + code) * kEncD);
-#pragma unroll 4
-            for (int d4 = 0; d4 < kEncD / 4; ++d4) {
-                float4* r4p = reinterpret_cast<float4*>(sA + enc_off(row, d4 * 4));
+        }
+        __syncthreads();
+        // r -= C_m[code]: the row's 4 column groups take 32 dims each
+        {
+            const int code = s_code[row];
+            const unsigned char* bh = sB + (code >> 7) * EncSmem::kBHalf;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int d = (8 * cg + j) * 4;
+                const float4 cv = *reinterpret_cast<const float4*>(bh + enc_off(code & 127, d));
+                float4* r4p = reinterpret_cast<float4*>(sA + enc_off(row, d));
                 float4 r4 = *r4p;
-                const float4 cv = __ldg(c4 + d4);
                 r4.x = __fsub_rn(r4.x, cv.x);
                 r4.y = __fsub_rn(r4.y, cv.y);
                 r4.z = __fsub_rn(r4.z, cv.z);
@@ -343,6 +427,11 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_keys_kernel(EncodeParam
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();  // the stage's codewords are no longer read: the next stage's copies start
+        if (m + 1 < kEncM) {
+            if (tid == 0) issue_stage(m + 1);
+            load_norms(m + 1);
+        }
     }
     cp_async_wait<0>();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

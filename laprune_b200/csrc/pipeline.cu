@@ -595,6 +595,7 @@ static int encode_plan(const lp_encode_args* a, size_t* bytes, int64_t* nsets, i
     c.take<unsigned char>(kPersistBytes);
     c.take<float>((size_t)*nsets * 32 * 256);
     c.take<float>((size_t)*nsets * 32 * 256);
+    c.take<float>((size_t)*nsets * 32 * 4);
     *bytes = c.used();
     return LP_OK;
 }
@@ -625,9 +626,13 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
     uint32_t* err = c.take<uint32_t>(kPersistBytes / 4);
     float* nrm = c.take<float>((size_t)nsets * 32 * 256);
     float* cnorm = c.take<float>((size_t)nsets * 32 * 256);
+    float* smax = c.take<float>((size_t)nsets * 32 * 4);
     const int64_t ncw = nsets * 32 * 256;
     encode_norms_kernel<<<(unsigned)((ncw + 255) / 256), 256, 0, st>>>(a->codebooks, ncw, nrm, cnorm);
     rc = check_launch("encode_norms_kernel");
+    if (rc != LP_OK) return rc;
+    encode_stage_max_kernel<<<(unsigned)(nsets * 32), 256, 0, st>>>(nrm, cnorm, smax);
+    rc = check_launch("encode_stage_max_kernel");
     if (rc != LP_OK) return rc;
 
     EncodeParams ep{};
@@ -642,6 +647,7 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
     ep.cb = a->codebooks;
     ep.nrm = nrm;
     ep.cnorm = cnorm;
+    ep.smax = smax;
     ep.codes = a->codes;
     ep.cs_b = a->codes_stride_b;
     ep.cs_h = a->codes_stride_h;
@@ -649,23 +655,54 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
     ep.ctas_per_set = (int)((nvec_set + kEncRows - 1) / kEncRows);
     ep.force_exact = (a->flags & LP_ENCODE_FLAG_EXACT) ? 1 : 0;
     ep.err = err;
+    // the codebooks as a 2-D tensor [S*32*256 rows][128 fp32], copied in boxes
+    // of 32 dims x 128 rows with the 128-byte swizzle the UMMA layout expects
+    CUtensorMap cmap;
+    {
+        const cuuint64_t gdim[2] = {128, (cuuint64_t)nsets * 32 * 256};
+        const cuuint64_t gstride[1] = {128 * sizeof(float)};
+        const cuuint32_t box[2] = {32, 128};
+        const cuuint32_t estride[2] = {1, 1};
+        // resolved through the runtime, so the library has no link-time
+        // dependency on the driver library (it loads on hosts without one)
+        using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                           const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                           CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                           CUtensorMapFloatOOBfill);
+        static EncodeTiledFn encode_tiled = nullptr;
+        static std::once_flag once;
+        std::call_once(once, [] {
+            void* fn = nullptr;
+            cudaDriverEntryPointQueryResult q;
+            if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+                q == cudaDriverEntryPointSuccess)
+                encode_tiled = reinterpret_cast<EncodeTiledFn>(fn);
+        });
+        if (!encode_tiled) return fail(LP_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+        const CUresult cr = encode_tiled(&cmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                                                   const_cast<float*>(a->codebooks), gdim, gstride, box, estride,
+                                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (cr != CUDA_SUCCESS) return fail(LP_ERR_CUDA, "cuTensorMapEncodeTiled failed for the codebooks");
+    }
     const dim3 grid((unsigned)(nsets * ep.ctas_per_set));
     static bool opt_enc[3][64] = {{false}};
     switch (a->x_dtype) {
         case LP_BF16:
             rc = smem_opt_in(encode_keys_kernel<__nv_bfloat16>, EncSmem::kTotal, dev, opt_enc[0]);
             if (rc != LP_OK) return rc;
-            encode_keys_kernel<__nv_bfloat16><<<grid, kEncThreads, EncSmem::kTotal, st>>>(ep);
+            encode_keys_kernel<__nv_bfloat16><<<grid, kEncThreads, EncSmem::kTotal, st>>>(cmap, ep);
             break;
         case LP_F16:
             rc = smem_opt_in(encode_keys_kernel<__half>, EncSmem::kTotal, dev, opt_enc[1]);
             if (rc != LP_OK) return rc;
-            encode_keys_kernel<__half><<<grid, kEncThreads, EncSmem::kTotal, st>>>(ep);
+            encode_keys_kernel<__half><<<grid, kEncThreads, EncSmem::kTotal, st>>>(cmap, ep);
             break;
         default:
             rc = smem_opt_in(encode_keys_kernel<float>, EncSmem::kTotal, dev, opt_enc[2]);
             if (rc != LP_OK) return rc;
-            encode_keys_kernel<float><<<grid, kEncThreads, EncSmem::kTotal, st>>>(ep);
+            encode_keys_kernel<float><<<grid, kEncThreads, EncSmem::kTotal, st>>>(cmap, ep);
             break;
     }
     return check_launch("encode_keys_kernel");
