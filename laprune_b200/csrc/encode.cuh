@@ -24,9 +24,12 @@
 // K-major SWIZZLE_128B layout: per 32-dim K chunk (16 KB), 8-row atoms of
 // 1024 B, rows 128 B apart, 16-byte units XOR-swizzled with the row.  The
 // codewords arrive by 2-D TMA tensor copies (box 32 dims x 128 rows, the
-// same swizzle); the next stage's copies start as soon as the current
-// stage's MMAs complete, so they overlap the distance search, which reads
-// the winning codeword rows from L2.
+// same swizzle).  The exact recomputation and the residual update read the
+// codeword rows from there, so the next stage's copies start once the
+// residual update is done.  Rows with several candidates put their (row,
+// codeword) pairs on a CTA-wide list, one pair per thread, so that the
+// sequential 128-term chains run side by side; the codes collect in shared
+// memory and leave once, 32 bytes per vector.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
@@ -36,6 +39,7 @@ namespace lp {
 constexpr int kEncRows = 128;  // vectors per CTA (UMMA M)
 constexpr int kEncThreads = 512;
 constexpr int kEncD = 128, kEncK = 256, kEncM = 32;
+constexpr int kEncListCap = 2048;  // (row, codeword) pairs refined per round
 
 struct EncodeParams {
     const void* x;
@@ -262,11 +266,16 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     const int q4 = warp & 3, cg = warp >> 2;
     const int row = q4 * 32 + lane;
     const bool row_valid = v0 + row < nvec_set;
-    uint8_t* code_out = nullptr;
-    if (row_valid && cg == 0) {
-        int b, h, t;
-        vec_bht(v0 + row, &b, &h, &t);
-        code_out = p.codes + (int64_t)b * p.cs_b + (int64_t)h * p.cs_h + (int64_t)t * p.cs_t;
+    __shared__ uint8_t* s_cptr[kEncRows];         // the row's 32 codes in the output (null: no vector)
+    __shared__ __align__(16) uint8_t s_codes[kEncRows][kEncM];
+    if (cg == 0) {
+        uint8_t* co = nullptr;
+        if (row_valid) {
+            int b, h, t;
+            vec_bht(v0 + row, &b, &h, &t);
+            co = p.codes + (int64_t)b * p.cs_b + (int64_t)h * p.cs_h + (int64_t)t * p.cs_t;
+        }
+        s_cptr[row] = co;
     }
     // |exact dist - (approx dist + ||r||^2)| <= kEps ||r|| ||c_k|| + kAbs (||r||^2 + ||c_k||^2 + |approx|):
     // the tf32 operands (10 mantissa bits) and fp32 accumulation give about
@@ -278,9 +287,10 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     __shared__ float s_rn[kEncRows];
     __shared__ float s_u[4][kEncRows];
     __shared__ int s_cnt[4][kEncRows];
-    __shared__ float s_bd[4][kEncRows];
-    __shared__ int s_bk[4][kEncRows];
-    __shared__ int s_code[kEncRows];
+    __shared__ int s_bk[4][kEncRows];               // the group's first candidate (-1: none)
+    __shared__ unsigned long long s_best[kEncRows];  // (ordered exact distance, codeword), minimum
+    __shared__ uint32_t s_list[kEncListCap];         // (row << 8) | codeword
+    __shared__ int s_nlist[2];
 
     for (int m = 0; m < kEncM; ++m) {
         const uint32_t par = (uint32_t)(m & 1);
@@ -360,58 +370,58 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         }
         s_cnt[cg][row] = __popc(cm0) + __popc(cm1);
         s_bk[cg][row] = cm0 ? __ffs(cm0) - 1 + 64 * cg : (cm1 ? __ffs(cm1) + 31 + 64 * cg : -1);
+        if (cg == 0) s_best[row] = ~0ull;
+        if (tid == 0) {
+            s_nlist[0] = 0;
+            s_nlist[1] = 0;
+        }
         __syncthreads();
         const int total = s_cnt[0][row] + s_cnt[1][row] + s_cnt[2][row] + s_cnt[3][row];
-        if (total > 1) {
-            // several candidates: exact distances of this group's ones, first minimum
-            float best = INFINITY;
-            int best_k = -1;
-            for (int w2 = 0; w2 < 2; ++w2) {
-                for (uint32_t bits = w2 ? cm1 : cm0; bits; bits &= bits - 1) {
-                    const int k = (__ffs(bits) - 1) + 32 * w2 + 64 * cg;
-                    const unsigned char* bh = sB + (k >> 7) * EncSmem::kBHalf;
-                    float dot = 0.f;
+        // a row with several candidates: their exact distances, one (row,
+        // codeword) pair per thread through a CTA-wide list (rounds of at most
+        // kEncListCap pairs); the smallest (distance, codeword) key is the
+        // first minimum of the CPU scan
+        uint64_t pend = total > 1 ? ((uint64_t)cm1 << 32) | cm0 : 0ull;
+        for (int round = 0;; ++round) {
+            int* nl = &s_nlist[round & 1];
+            const bool had = pend != 0ull;
+            while (pend) {
+                const int i = atomicAdd(nl, 1);
+                if (i >= kEncListCap) break;
+                s_list[i] = ((uint32_t)row << 8) | (uint32_t)(__ffsll((long long)pend) - 1 + 64 * cg);
+                pend &= pend - 1;
+            }
+            if (!__syncthreads_or(had)) break;
+            if (tid == 0) s_nlist[(round + 1) & 1] = 0;  // the next round's counter (last read a round ago)
+            const int n = min(*nl, kEncListCap);
+            for (int e = tid; e < n; e += kEncThreads) {
+                const uint32_t it = s_list[e];
+                const int r = (int)(it >> 8), k = (int)(it & 255u);
+                const unsigned char* bh = sB + (k >> 7) * EncSmem::kBHalf;
+                float dot = 0.f;
 #pragma unroll 8
-                    for (int d4 = 0; d4 < kEncD / 4; ++d4) {
-                        const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(row, d4 * 4));
-                        const float4 cv = *reinterpret_cast<const float4*>(bh + enc_off(k & 127, d4 * 4));
-                        dot = __fmaf_rn(r4.x, cv.x, dot);
-                        dot = __fmaf_rn(r4.y, cv.y, dot);
-                        dot = __fmaf_rn(r4.z, cv.z, dot);
-                        dot = __fmaf_rn(r4.w, cv.w, dot);
-                    }
-                    const float dist = __fmaf_rn(-2.f, dot, __fadd_rn(rn, nb[k]));
-                    if (dist < best) {
-                        best = dist;
-                        best_k = k;
-                    }
+                for (int d4 = 0; d4 < kEncD / 4; ++d4) {
+                    const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(r, d4 * 4));
+                    const float4 cv = *reinterpret_cast<const float4*>(bh + enc_off(k & 127, d4 * 4));
+                    dot = __fmaf_rn(r4.x, cv.x, dot);
+                    dot = __fmaf_rn(r4.y, cv.y, dot);
+                    dot = __fmaf_rn(r4.z, cv.z, dot);
+                    dot = __fmaf_rn(r4.w, cv.w, dot);
                 }
+                // +0 folds a -0 into +0, so that equal distances have equal keys
+                const float dist = __fadd_rn(__fmaf_rn(-2.f, dot, __fadd_rn(s_rn[r], nb[k])), 0.f);
+                uint32_t key = __float_as_uint(dist);
+                key = (key & 0x80000000u) ? ~key : (key | 0x80000000u);  // float order as unsigned order
+                atomicMin(&s_best[r], ((unsigned long long)key << 32) | (unsigned)k);
             }
-            s_bd[cg][row] = best;
-            s_bk[cg][row] = best_k;
+            if (!__syncthreads_or(pend != 0ull)) break;
         }
-        __syncthreads();
-        if (cg == 0) {
-            int code = 0;
-            if (total > 1) {
-                // groups in column order: a later group wins only if strictly better
-                float best = INFINITY;
-                for (int g = 0; g < 4; ++g)
-                    if (s_bk[g][row] >= 0 && s_bd[g][row] < best) {
-                        best = s_bd[g][row];
-                        code = s_bk[g][row];
-                    }
-            } else {
-                for (int g = 3; g >= 0; --g)
-                    if (s_bk[g][row] >= 0) code = s_bk[g][row];
-            }
-            s_code[row] = code;
-            if (row_valid) code_out[m] = (uint8_t)code;
-        }
-        __syncthreads();
+        // the code: the refined minimum, else the one candidate (one group has it)
+        const int code = total > 1 ? (int)(s_best[row] & 0xffu)
+                                   : max(max(max(s_bk[0][row], s_bk[1][row]), max(s_bk[2][row], s_bk[3][row])), 0);
+        if (cg == 0) s_codes[row][m] = (uint8_t)code;
         // r -= C_m[code]: the row's 4 column groups take 32 dims each
         {
-            const int code = s_code[row];
             const unsigned char* bh = sB + (code >> 7) * EncSmem::kBHalf;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -436,6 +446,13 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     cp_async_wait<0>();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
+    // the codes, 32 bytes per vector
+    if (!s_abort) {
+        for (int e = tid; e < kEncRows * kEncM; e += kEncThreads) {
+            uint8_t* co = s_cptr[e >> 5];
+            if (co) co[e & 31] = s_codes[e >> 5][e & 31];
+        }
+    }
     if (warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
