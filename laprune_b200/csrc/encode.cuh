@@ -6,9 +6,12 @@
 // counterpart laprune/quantizer.py:346-374 (_batch_icm_lut with 0 ICM
 // iterations: code_m = first argmin_k ||r||^2 + ||C_m[k]||^2 - 2 r . C_m[k]).
 //
-// Result: the codes of the CPU arithmetic, exactly -- every sum a sequential
-// chain of fp32 fused multiply-adds in index order (the oracle states the
-// same), the first minimum on ties.
+// Result: the codes of the CPU arithmetic, exactly: ||r||^2 and ||c||^2
+// sequential chains of fp32 fused multiply-adds in index order, r . c in a
+// fixed 32-lane order (lane l a 4-term fma chain over dims 4l..4l+3, then a
+// shuffle-xor butterfly at strides 16, 8, 4, 2, 1, whose lanes all end with
+// the same bits because fp32 addition is commutative), the first minimum on
+// ties.  The oracle states the same order.
 //
 // Work: per stage the residuals of the CTA's 128 vectors meet the stage's
 // 256 codewords, R[128 x 128] . C_m^T[128 x 256], on the 5th-generation
@@ -378,41 +381,68 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         __syncthreads();
         const int total = s_cnt[0][row] + s_cnt[1][row] + s_cnt[2][row] + s_cnt[3][row];
         // a row with several candidates: their exact distances, one (row,
-        // codeword) pair per thread through a CTA-wide list (rounds of at most
+        // codeword) pair per 8 lanes through a CTA-wide list (rounds of at most
         // kEncListCap pairs); the smallest (distance, codeword) key is the
         // first minimum of the CPU scan
         uint64_t pend = total > 1 ? ((uint64_t)cm1 << 32) | cm0 : 0ull;
         for (int round = 0;; ++round) {
             int* nl = &s_nlist[round & 1];
             const bool had = pend != 0ull;
-            while (pend) {
-                const int i = atomicAdd(nl, 1);
-                if (i >= kEncListCap) break;
+            // the warp's pairs take one range of the list (one atomic per warp)
+            const int mine = __popcll((long long)pend);
+            int incl = mine;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += t;
+            }
+            int base = 0;
+            if (lane == 31 && incl > 0) base = atomicAdd(nl, incl);
+            base = __shfl_sync(0xffffffffu, base, 31);
+            for (int i = base + incl - mine; pend && i < kEncListCap; ++i) {
                 s_list[i] = ((uint32_t)row << 8) | (uint32_t)(__ffsll((long long)pend) - 1 + 64 * cg);
                 pend &= pend - 1;
             }
             if (!__syncthreads_or(had)) break;
             if (tid == 0) s_nlist[(round + 1) & 1] = 0;  // the next round's counter (last read a round ago)
             const int n = min(*nl, kEncListCap);
-            for (int e = tid; e < n; e += kEncThreads) {
-                const uint32_t it = s_list[e];
-                const int r = (int)(it >> 8), k = (int)(it & 255u);
-                const unsigned char* bh = sB + (k >> 7) * EncSmem::kBHalf;
+            // 8 lanes per pair, 4 pairs per warp: lane l8 of a group holds
+            // the order's lanes 8j + l8 (dims 32j + 4 l8 .. +3, j = 0..3), so
+            // the strides 16 and 8 of the butterfly are its own additions and
+            // 4, 2, 1 are shuffles; each 16-byte load of a group covers one
+            // 128-byte row segment.  The loop is warp-uniform: every lane
+            // takes part in the shuffles.
+            for (int e0 = warp * 4; e0 < n; e0 += kEncThreads / 8) {
+                const int e = e0 + (lane >> 3), l8 = lane & 7;
+                const bool live = e < n;
                 float dot = 0.f;
-#pragma unroll 8
-                for (int d4 = 0; d4 < kEncD / 4; ++d4) {
-                    const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(r, d4 * 4));
-                    const float4 cv = *reinterpret_cast<const float4*>(bh + enc_off(k & 127, d4 * 4));
-                    dot = __fmaf_rn(r4.x, cv.x, dot);
-                    dot = __fmaf_rn(r4.y, cv.y, dot);
-                    dot = __fmaf_rn(r4.z, cv.z, dot);
-                    dot = __fmaf_rn(r4.w, cv.w, dot);
+                int r = 0, k = 0;
+                if (live) {
+                    const uint32_t it = s_list[e];
+                    r = (int)(it >> 8);
+                    k = (int)(it & 255u);
+                    const unsigned char* bh = sB + (k >> 7) * EncSmem::kBHalf;
+                    float pj[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(r, 32 * j + 4 * l8));
+                        const float4 cv = *reinterpret_cast<const float4*>(bh + enc_off(k & 127, 32 * j + 4 * l8));
+                        float a = __fmaf_rn(r4.x, cv.x, 0.f);
+                        a = __fmaf_rn(r4.y, cv.y, a);
+                        a = __fmaf_rn(r4.z, cv.z, a);
+                        pj[j] = __fmaf_rn(r4.w, cv.w, a);
+                    }
+                    dot = __fadd_rn(__fadd_rn(pj[0], pj[2]), __fadd_rn(pj[1], pj[3]));
                 }
-                // +0 folds a -0 into +0, so that equal distances have equal keys
-                const float dist = __fadd_rn(__fmaf_rn(-2.f, dot, __fadd_rn(s_rn[r], nb[k])), 0.f);
-                uint32_t key = __float_as_uint(dist);
-                key = (key & 0x80000000u) ? ~key : (key | 0x80000000u);  // float order as unsigned order
-                atomicMin(&s_best[r], ((unsigned long long)key << 32) | (unsigned)k);
+#pragma unroll
+                for (int o = 4; o > 0; o >>= 1) dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, o));
+                if (live && l8 == 0) {
+                    // +0 folds a -0 into +0, so that equal distances have equal keys
+                    const float dist = __fadd_rn(__fmaf_rn(-2.f, dot, __fadd_rn(s_rn[r], nb[k])), 0.f);
+                    uint32_t key = __float_as_uint(dist);
+                    key = (key & 0x80000000u) ? ~key : (key | 0x80000000u);  // float order as unsigned order
+                    atomicMin(&s_best[r], ((unsigned long long)key << 32) | (unsigned)k);
+                }
             }
             if (!__syncthreads_or(pend != 0ull)) break;
         }

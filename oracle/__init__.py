@@ -183,6 +183,7 @@ def keep_positions(topk_idx, T_total: int, sink: int, local: int) -> np.ndarray:
 
 def encode_greedy(x, codebooks, cb_index=None) -> np.ndarray:
     """Greedy AQ codes (uint8 [N,M]) of fp32 vectors.  quantizer.py:346-355.
+    ``d`` must be a multiple of 32 (the fixed 32-lane order of r . c).
 
     ``codebooks`` is ``[M,K,d]`` or a stack ``[S,M,K,d]`` addressed per vector
     by ``cb_index`` (int32 ``[N]``).
@@ -194,6 +195,8 @@ def encode_greedy(x, codebooks, cb_index=None) -> np.ndarray:
     out = np.empty((N, M), dtype=np.uint8)
     if N == 0:
         return out
+    if d % 32:
+        raise ValueError(f"encode_greedy: d={d} is not a multiple of 32")
     idxp = None
     if cb_index is not None:
         cbi = np.ascontiguousarray(np.asarray(cb_index, dtype=np.int32))

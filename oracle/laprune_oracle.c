@@ -137,10 +137,31 @@ void orc_topk_rows(const float* scores, int R, int n, int lo, int hi, int k,
 }
 
 /* ---- greedy additive-quantization encode -------------------------------- */
+/* r . c in the encoder's fixed order: 32 lanes, lane l a sequential fma chain
+ * over its d/32 consecutive dims, then the lanes folded pairwise at strides
+ * 16, 8, 4, 2, 1 (p[l] += p[l + s]) -- the order of a warp with a
+ * shuffle-xor butterfly, whose every lane ends with the same bits because
+ * fp32 addition is commutative.  d must be a multiple of 32. */
+static float enc_dot(const float* a, const float* b, int d) {
+    float p[32];
+    const int per = d / 32;
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.f;
+        for (int j = l * per; j < (l + 1) * per; ++j) acc = fmaf(a[j], b[j], acc);
+        p[l] = acc;
+    }
+    for (int st = 16; st >= 1; st >>= 1)
+        for (int l = 0; l < st; ++l) p[l] = p[l] + p[l + st];
+    return p[0];
+}
+
 /* Greedy residual encode (icm iters = 0):
  *   for m: dists[k] = (||r||^2 + ||C_m[k]||^2) - 2 * (r . C_m[k]);
  *          code_m = first argmin; r -= C_m[code_m]
  * Follows laprune/quantizer.py:346-355 (with the norms of :315-316).
+ * The norms are sequential fma chains in index order, r . C_m[k] is
+ * enc_dot's order (the reference's own sums come from BLAS in an
+ * implementation-defined order; these are this build's fixed choices).
  * x [N][d] fp32, cb [M][K][d] fp32; codes written as uint8 [N][M].
  * cb_index[n] selects, per vector, which [M,K,d] codebook set of cb to use
  * (NULL = set 0), so per-KV-head codebooks can be encoded in one call. */
@@ -171,17 +192,16 @@ void orc_encode_greedy(const float* x, const float* cb, const int32_t* cb_index,
             const float* nrm = norms + (int64_t)s * M * K;
             memcpy(r, x + (int64_t)n * d, sizeof(float) * (size_t)d);
             for (int m = 0; m < M; ++m) {
-                /* every sum is a sequential chain of fused multiply-adds in
-                 * index order, written out explicitly so that the rounding
-                 * does not depend on the compiler's contraction choices */
+                /* every sum is written out explicitly (fmaf), so that the
+                 * rounding does not depend on the compiler's contraction
+                 * choices */
                 float rn = 0.f;
                 for (int j = 0; j < d; ++j) rn = fmaf(r[j], r[j], rn);
                 float best = INFINITY;
                 int best_k = 0;
                 for (int k = 0; k < K; ++k) {
                     const float* c = cbs + ((int64_t)m * K + k) * d;
-                    float dot = 0.f;
-                    for (int j = 0; j < d; ++j) dot = fmaf(r[j], c[j], dot);
+                    const float dot = enc_dot(r, c, d);
                     const float dist = fmaf(-2.f, dot, rn + nrm[(int64_t)m * K + k]);
                     if (dist < best) { best = dist; best_k = k; }
                 }
