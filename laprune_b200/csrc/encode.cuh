@@ -51,7 +51,6 @@ struct EncodeParams {
     int per_head;              // codebook set of vector (b, h, t) is h (else 0)
     const float* cb;           // [S][32][256][128] fp32
     const float* nrm;          // [S][32][256]  ||C||^2 (sequential fma)
-    const float* cnorm;        // [S][32][256]  ||C|| rounded up
     const float* smax;         // [S][32][4]    per stage: max ||C||^2, max ||C||, 0, 0
     uint8_t* codes;
     int64_t cs_b, cs_h, cs_t;  // bytes
@@ -63,7 +62,7 @@ struct EncodeParams {
 struct EncSmem {
     static constexpr int kA = kEncRows * kEncD * 4;          // 64 KB
     static constexpr int kBHalf = 128 * kEncD * 4;           // 64 KB
-    static constexpr int kNormStride = 2 * kEncK + 4;       // nrm[256] cnorm[256] nmax cmax . .
+    static constexpr int kNormStride = kEncK + 4;           // nrm[256] nmax cmax . .
     static constexpr int kNorm = 2 * kNormStride * 4;        // double buffered
     static constexpr int kTotal = kA + 2 * kBHalf + kNorm + 64 + 1024;  // + alignment slack
 };
@@ -182,10 +181,12 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     encode_keys_kernel(const __grid_constant__ CUtensorMap cmap, EncodeParams p) {
     extern __shared__ unsigned char smem_raw[];
     // operands need 1024-byte alignment (SWIZZLE_128B atoms)
-    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // (offset from the shared array itself, so that the compiler keeps every
+    // access below a shared-memory access rather than a generic one)
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* sA = smem;
     unsigned char* sB = smem + EncSmem::kA;  // half hf, K chunk c at hf * 64 KB + c * 16 KB
-    float* sNorm = reinterpret_cast<float*>(sB + 2 * EncSmem::kBHalf);  // [2][nrm 256 | cnorm 256]
+    float* sNorm = reinterpret_cast<float*>(sB + 2 * EncSmem::kBHalf);  // [2][nrm 256 | nmax cmax . .]
     uint64_t* s_mbar = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(sNorm) + EncSmem::kNorm);
     uint64_t* s_tbar = s_mbar + 1;
     __shared__ uint32_t s_tmem;
@@ -198,7 +199,6 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     const int v0 = tile * kEncRows;
     const float* cbs = p.cb + (int64_t)set * kEncM * kEncK * kEncD;
     const float* nrms = p.nrm + (int64_t)set * kEncM * kEncK;
-    const float* cns = p.cnorm + (int64_t)set * kEncM * kEncK;
     const float* smx = p.smax + (int64_t)set * kEncM * 4;
 
     // vector i of the set -> (b, h, t)
@@ -228,8 +228,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     auto load_norms = [&](int m) {
         float* nb = sNorm + (m & 1) * EncSmem::kNormStride;
         if (tid < 64) cp_async16(nb + tid * 4, nrms + (int64_t)m * kEncK + tid * 4);
-        else if (tid < 128) cp_async16(nb + kEncK + (tid - 64) * 4, cns + (int64_t)m * kEncK + (tid - 64) * 4);
-        else if (tid == 128) cp_async16(nb + 2 * kEncK, smx + m * 4);
+        else if (tid == 64) cp_async16(nb + kEncK, smx + m * 4);
         cp_async_commit();
     };
 
@@ -345,29 +344,30 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         const float rnorm = __fmul_ru(__fsqrt_ru(rn), 1.0000001f);
         // the bound's absolute part, one upper bound per row: |approx| <=
         // ||c||^2 + 2 ||r|| ||c|| <= nmax + 2 rnorm cmax
-        const float slack = kAbs * (rn + 2.f * (nb[2 * kEncK] + rnorm * nb[2 * kEncK + 1]));
+        const float slack = kAbs * (rn + 2.f * (nb[kEncK] + rnorm * nb[kEncK + 1]));
+        // the row's bound for every codeword of the stage: kEps ||r|| max ||c|| + slack
+        const float bnd = __fmaf_ru(kEps * rnorm, nb[kEncK + 1], slack);
         const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + 64 * cg;
         float v[64];
         enc_tmem_ld64(taddr, v);
-        // pass 1: the row's best upper bound U = min_k (approx_k + bound_k)
+        // pass 1: the row's smallest approximate distance A (less ||r||^2)
         float u = INFINITY;
-        const float er = kEps * rnorm;
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
-            const int k = 64 * cg + i;
-            const float ap = fmaf(-2.f, v[i], nb[k]);
+            const float ap = fmaf(-2.f, v[i], nb[64 * cg + i]);
             v[i] = ap;
-            u = fminf(u, ap + fmaf(er, nb[kEncK + k], slack));
+            u = fminf(u, ap);
         }
         s_u[cg][row] = u;
         __syncthreads();
-        const float U = fminf(fminf(s_u[0][row], s_u[1][row]), fminf(s_u[2][row], s_u[3][row]));
-        // pass 2: candidates approx_k - bound_k <= U (bit i of the mask = column 64cg + i)
+        // pass 2: candidates approx_k <= A + 2 bnd -- the winner's exact
+        // distance is at most A + bnd and its approximation at most bnd below
+        // that (bit i of the mask = column 64cg + i)
+        const float thr = __fmaf_ru(2.f, bnd, fminf(fminf(s_u[0][row], s_u[1][row]), fminf(s_u[2][row], s_u[3][row])));
         uint32_t cm0 = 0u, cm1 = 0u;
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
-            const int k = 64 * cg + i;
-            const bool c = p.force_exact || v[i] - fmaf(er, nb[kEncK + k], slack) <= U;
+            const bool c = p.force_exact || v[i] <= thr;
             if (i < 32) cm0 |= (uint32_t)c << i;
             else cm1 |= (uint32_t)c << (i - 32);
         }

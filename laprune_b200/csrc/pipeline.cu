@@ -646,7 +646,6 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
     ep.per_head = a->cb_per_kv_head ? 1 : 0;
     ep.cb = a->codebooks;
     ep.nrm = nrm;
-    ep.cnorm = cnorm;
     ep.smax = smax;
     ep.codes = a->codes;
     ep.cs_b = a->codes_stride_b;
