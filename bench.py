@@ -12,9 +12,12 @@ one decode token through the 30 sparse layers (layers 2..31), each layer with
 its own resident caches (≈18 GB, far above the 126 MB L2), inputs seeded
 synthetic.  Dense layers 0-1, projections and MLP are not part of this path.
 
-Prints ONE JSON line (rank 0).  Under torchrun (N>1) every rank runs its own
-independent copy of the workload (weak scaling, no collective on the data
-path); timings are max-reduced over ranks.
+Prints ONE JSON line (rank 0).  Under torchrun (N>1) the KV heads are
+sharded tensor-parallel (laprune_b200.tp): rank r owns KV heads
+[r*8/N, (r+1)*8/N) and their query heads, for a global batch of N sequences,
+so every GPU holds 8 (sequence, KV head) units per layer, as at N=1 (weak
+scaling).  The decode path itself has no collective (the heads are
+independent); timings are max-reduced over ranks.
 """
 from __future__ import annotations
 
@@ -256,24 +259,27 @@ def run_ours(args):
     import torch.distributed as dist
     from laprune_b200 import _lib, ops
 
-    world, rank, local = _dist_env()
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", init_method="env://",
-                                timeout=__import__("datetime").timedelta(seconds=300))
+    from laprune_b200 import tp
+
+    world, rank, local = tp.init_process_group("nccl", timeout_s=300)
     dev = torch.device("cuda", torch.cuda.current_device())
     lib = _lib.load()
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
+    # this rank's shard of a global batch of `world` sequences: its KV heads
+    # (and their query heads) for every sequence, generated in place
+    h0, h1 = tp.kv_head_range(HKV, world, rank)
+    q0, q1 = tp.query_head_range(HQ, HKV, world, rank)
+    B_loc, hkv_loc, hq_loc = world, h1 - h0, q1 - q0
 
     layers = []
     for li in range(args.layers):
-        C = torch.randn((HKV, M, K, D), generator=g, device=dev) * 0.05
-        codes = torch.randint(0, 256, (HKV, T_CTX, M), generator=g, device=dev, dtype=torch.uint8)
-        keys = torch.randn((HKV, T_CTX, D), generator=g, device=dev).to(torch.bfloat16)
-        vals = torch.randn((HKV, T_CTX, D), generator=g, device=dev).to(torch.bfloat16)
-        q = torch.randn((HQ, D), generator=g, device=dev).to(torch.bfloat16)
-        out = torch.empty((1, HQ, D), dtype=torch.bfloat16, device=dev)
+        C = torch.randn((hkv_loc, M, K, D), generator=g, device=dev) * 0.05
+        codes = torch.randint(0, 256, (B_loc, hkv_loc, T_CTX, M), generator=g, device=dev, dtype=torch.uint8)
+        keys = torch.randn((B_loc, hkv_loc, T_CTX, D), generator=g, device=dev).to(torch.bfloat16)
+        vals = torch.randn((B_loc, hkv_loc, T_CTX, D), generator=g, device=dev).to(torch.bfloat16)
+        q = torch.randn((B_loc, hq_loc, D), generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty((B_loc, hq_loc, D), dtype=torch.bfloat16, device=dev)
         layers.append({"C": C, "codes": codes, "keys": keys, "vals": vals, "q": q, "out": out})
     for L in layers:
         L["args"] = ops.build_args(L["q"], L["C"], L["codes"], L["keys"], L["vals"], topk=TOPK,
@@ -352,18 +358,18 @@ def run_ours(args):
     errs = ops.device_errors(ws, dev)
 
     # ---- end to end through the public API: host q in, host out back ----
-    q_host = torch.empty((N_LAYERS, HQ, D), dtype=torch.bfloat16).pin_memory()
+    q_host = torch.empty((N_LAYERS, B_loc, hq_loc, D), dtype=torch.bfloat16).pin_memory()
     q_host.copy_(torch.stack([layers[li % len(layers)]["q"].cpu() for li in range(N_LAYERS)]))
-    out_host = torch.empty((N_LAYERS, HQ, D), dtype=torch.bfloat16).pin_memory()
-    q_dev = torch.empty((N_LAYERS, HQ, D), dtype=torch.bfloat16, device=dev)
-    out_dev = torch.empty((N_LAYERS, HQ, D), dtype=torch.bfloat16, device=dev)
+    out_host = torch.empty((N_LAYERS, B_loc, hq_loc, D), dtype=torch.bfloat16).pin_memory()
+    q_dev = torch.empty((N_LAYERS, B_loc, hq_loc, D), dtype=torch.bfloat16, device=dev)
+    out_dev = torch.empty((N_LAYERS, B_loc, hq_loc, D), dtype=torch.bfloat16, device=dev)
 
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
         for li in range(N_LAYERS):
             L = layers[li % len(layers)]
             ops.sparse_decode(q_dev[li], L["C"], L["codes"], L["keys"], L["vals"], topk=TOPK,
-                              sink=SINK, local=LOCAL, out=out_dev[li:li + 1], ws=ws)
+                              sink=SINK, local=LOCAL, out=out_dev[li], ws=ws)
         out_host.copy_(out_dev, non_blocking=True)
 
     for _ in range(max(1, min(args.warmup, 3))):
@@ -392,9 +398,10 @@ def run_ours(args):
         e2e_tok_s = world * args.steps / (e2e_ms / 1e3)
         peak, peak_kind = _peaks()
         ncand = T_CTX - SINK - LOCAL
-        score_bytes = HKV * ncand * M                  # uint8 codes streamed per launch
-        lut_bytes = HKV * M * K * D * 4                 # fp32 codebooks read per launch
-        gather_bytes = HKV * (TOPK + SINK + LOCAL) * D * 2 * 2
+        units = B_loc * hkv_loc                         # (sequence, KV head) pairs per launch
+        score_bytes = units * ncand * M                 # uint8 codes streamed per launch
+        lut_bytes = hkv_loc * M * K * D * 4             # fp32 codebooks of the owned heads
+        gather_bytes = units * (TOPK + SINK + LOCAL) * D * 2 * 2
         launch_bytes = score_bytes + lut_bytes + gather_bytes
         achieved = launch_bytes / (launch_ms / 1e3) / 1e9
         step_bytes = N_LAYERS * launch_bytes
@@ -405,7 +412,8 @@ def run_ours(args):
             "data": "synthetic (seeded, generated on device)",
             "config": {
                 "workload": WORKLOAD, "global_batch": world, "seq_len": T_CTX,
-                "parallelism": f"replicas x{world} (independent sequences per GPU)",
+                "parallelism": (f"tp{world}: KV heads sharded, {hkv_loc} KV / {hq_loc} query heads "
+                                f"x {B_loc} sequences per GPU" if world > 1 else "single GPU"),
                 "l2": f"inputs larger than L2: {len(layers)} resident layer instance(s) "
                       f"({len(layers) * 0.6:.1f} GB) cycled over the {N_LAYERS} layer calls of a step",
                 "layer_steps_per_s": tok_s * N_LAYERS,
