@@ -20,6 +20,11 @@
  *     barrier words), at the same offsets for every geometry; the rest is
  *     scratch.  A workspace must not be shared by calls that may run
  *     concurrently.
+ *   - A lp_sparse_decode workspace also holds, after those 2048 bytes, the
+ *     fused kernel's exchange arena: words tagged with the call's launch
+ *     number, at a fixed offset and of a fixed size for the device, so that
+ *     calls of any geometry can share the workspace.  Give lp_encode_keys a
+ *     workspace of its own (its scratch would land in that arena).
  */
 #ifndef LAPRUNE_B200_H
 #define LAPRUNE_B200_H
@@ -187,8 +192,10 @@ size_t lp_sizeof_encode_args(void);
 size_t lp_encode_workspace_size(const lp_encode_args* a);
 
 /* Greedy residual encode: for m = 0..M-1, code_m = the first k minimising
- * ||r||^2 + ||C_m[k]||^2 - 2 r.C_m[k] (fp32, every sum a sequential chain of
- * fused multiply-adds in index order), then r -= C_m[code_m].  The
+ * ||r||^2 + ||C_m[k]||^2 - 2 r.C_m[k] (fp32: the norms sequential chains of
+ * fused multiply-adds in index order, r.C_m[k] 32 four-term chains over
+ * dims 4l..4l+3 folded pairwise at strides 16, 8, 4, 2, 1), then
+ * r -= C_m[code_m].  The
  * contraction runs on tcgen05 tensor cores (tf32) as a filter under an error
  * bound; near-ties are settled exactly on CUDA cores.  Reference path this
  * replaces: aq_kernels/fused_linear_encode.cu:168-234
@@ -259,10 +266,10 @@ int lp_gqa_gather_kv(const lp_gqa_gather_args* a, void* stream);
  * Allocation-free variant (no counterpart in the reference)
  * ====================================================================== */
 
-/* Size of the library's built-in per-device scratch (16 MiB): enough for one
- * sequence (B = 1) with 8 KV heads up to about 300k tokens; the workspace
+/* Size of the library's built-in per-device scratch (32 MiB): enough for one
+ * sequence (B = 1) with 8 KV heads up to about 380k tokens; the workspace
  * size lp_sparse_decode_workspace_size() reports must not exceed it. */
-#define LP_NOALLOC_SCRATCH_BYTES (16u << 20)
+#define LP_NOALLOC_SCRATCH_BYTES (32u << 20)
 
 /* lp_sparse_decode for callers that must not allocate device memory: a
  * serving runtime that has handed all of HBM to its own pool (a cudaMalloc

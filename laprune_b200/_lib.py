@@ -110,7 +110,7 @@ SIGNATURES = {
     "lp_lut_build": (ctypes.c_int, [ctypes.POINTER(LutBuildArgs), _c_p]),
     "lp_gqa_gather_kv": (ctypes.c_int, [ctypes.POINTER(GqaGatherArgs), _c_p]),
 }
-LP_NOALLOC_SCRATCH_BYTES = 16 << 20
+LP_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 _lib = None
 

@@ -59,7 +59,7 @@ constexpr int kFMaxWords = 8192;                 // bitmap words per unit in sme
 constexpr int kFMaxRows = 192;                   // kept rows per attention chunk in phase E
 constexpr int kPubWin = 128;                     // bins in a CTA's published count window
 constexpr int kPubMaxCtas = 64;                  // CTAs per unit of the published-candidate path
-constexpr int kPubMaxCap = 4096;                 // published candidates per CTA (own copy in shared memory)
+constexpr int kPubMaxCap = 1024;                 // published candidates per CTA (own copy in shared memory)
 constexpr int kFastTieCap = 1024;                // tie-bin entries the fast selection path settles
 
 struct FusedParams {

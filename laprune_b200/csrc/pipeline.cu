@@ -102,6 +102,7 @@ static constexpr int kUnitBarWords = 384;     // one barrier word per unit of th
 static constexpr size_t kPersistBytes = 2048; // error word, grid barrier, unit barriers
 static constexpr int kGroupStages = 8;
 static constexpr int kHeadsStages = 4;
+static constexpr int kFusedMaxG = 8;  // query heads per KV head on the fused path
 
 static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int device) {
     LP_CHECK(a != nullptr, "args must not be NULL");
@@ -173,7 +174,7 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
         const int nwu = p.ncand > 0 ? ((p.c1 + 31) >> 5) - (p.c0 >> 5) : 0;
         const int ntok_max = cn_min > 0 ? (nwu + cn_min - 1) / cn_min * 32 : 0;
         p.fused = !(a->flags & LP_FLAG_NO_FUSED) && !p.per_head && !p.heads && a->out != nullptr &&
-                  a->D == 128 && a->G <= 8 && p.U <= p.fused_ctas && p.U <= kUnitBarWords && p.ncand > 0 && a->topk > 0 &&
+                  a->D == 128 && a->G <= kFusedMaxG && p.U <= p.fused_ctas && p.U <= kUnitBarWords && p.ncand > 0 && a->topk > 0 &&
                   nwu <= kFMaxWords && cn_min >= 1 && ntok_max <= kFScoreCap;
         p.fused_max_split = cn_min + 1;
         // candidate publishing: each CTA aims at twice its even share of the
@@ -192,6 +193,16 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     p.err = c.take<uint32_t>(64);
     p.bar = c.take<uint32_t>(64);
     p.ubar = c.take<uint32_t>(kUnitBarWords);
+    // the fused kernel's epoch-tagged exchange arena: a fixed offset and a
+    // fixed size (its worst case for this device), written only with tagged
+    // stores.  A reader accepts a word once its tag shows the call's epoch,
+    // so no plain data of any call (another geometry, the multi-kernel
+    // path) may ever land here: a stale plain word whose upper half equals
+    // a later epoch would be taken for that call's data.
+    p.fwin = c.take<unsigned long long>((size_t)sms * (kPubWin + 2));
+    p.fpub = c.take<unsigned long long>((size_t)sms * kPubMaxCap * 2);
+    p.flut = c.take<unsigned long long>((size_t)sms * 256 * 32);                 // U <= sms units
+    p.fpart = c.take<unsigned long long>((size_t)2 * sms * kFusedMaxG * (2 + 128));  // U * (sms/U + 1) * G
     p.lut = c.take<float>((size_t)p.U * 256 * 32 * (p.heads ? 4 : 1));
     p.bounds = c.take<float>((size_t)p.U * (p.heads ? a->G : 1) * 32 * kLutParts * 2);
     p.sel_scores = c.take<float>((size_t)p.Usel * std::max(1, a->T_codes));
@@ -202,13 +213,7 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
                            (2 + 128));
     p.cta_count = c.take<uint32_t>((size_t)p.fused_ctas);
     p.cta_ties = c.take<uint32_t>((size_t)p.fused_ctas);
-    if (p.fused) {
-        p.fpub = c.take<unsigned long long>((size_t)p.fused_ctas * std::max(p.pub_cap, 1) * 2);
-        p.fwin = c.take<unsigned long long>((size_t)p.fused_ctas * (kPubWin + 2));
-        p.flut = c.take<unsigned long long>((size_t)p.U * 256 * 32);
-        p.fpart = c.take<unsigned long long>((size_t)p.U * p.fused_max_split * a->G * (2 + 128));
-        p.chist = c.take<uint32_t>((size_t)p.fused_ctas * kNB);
-    }
+    if (p.fused) p.chist = c.take<uint32_t>((size_t)p.fused_ctas * kNB);
     p.zero_words = (int64_t)p.Usel * kNB + p.Usel + p.Usel + p.Uatt;
     p.zero = c.take<uint32_t>((size_t)p.zero_words);
     p.hist = p.zero;

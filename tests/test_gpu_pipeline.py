@@ -5,12 +5,14 @@ Bars (from the north-star definition of correctness):
   * top-k index sets >= 99.9% overlap (ties at the k-th value count);
   * attention outputs within bf16 tolerance: max abs err <= 2e-2.
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
 
 import oracle
-from laprune_b200 import ops
+from laprune_b200 import _lib, ops
 from laprune_b200 import synthetic as syn
 
 pytestmark = pytest.mark.gpu
@@ -253,3 +255,37 @@ def test_prefetch_of_next_inputs_does_not_change_results():
     torch.cuda.synchronize()
     assert torch.equal(r0.topk, r1.topk) and torch.equal(r0.out, r1.out)
     assert ops.device_errors(device=dev) & 1 == 0
+
+
+def test_fused_calls_after_other_paths_on_a_fresh_shared_workspace():
+    # a fresh workspace gives the fused kernel small launch numbers (1, 2, 3
+    # ...) as exchange tags; the calls before them -- the multi-kernel path,
+    # per-query-head selection, other geometries -- write small integers
+    # (histogram counts, bitmap words) into their scratch.  None of that may
+    # reach the fused kernel's exchange arena: every result must equal the
+    # one computed on a workspace of its own.
+    dev = _dev()
+    cases = [dict(T=20000, Hkv=2, B=1, fused=False, select="kv_group"),
+             dict(T=3000, Hkv=2, B=2, fused=None, select="query_head"),
+             dict(T=8192, Hkv=2, B=2, fused=None, select="kv_group"),
+             dict(T=20000, Hkv=8, B=1, fused=None, select="kv_group"),
+             dict(T=4096, Hkv=1, B=4, fused=False, select="kv_group"),
+             dict(T=8192, Hkv=4, B=1, fused=None, select="kv_group")]
+    inputs, refs = [], []
+    for i, c in enumerate(cases):
+        C, codes, K, V, q = [t.to(dev) for t in _rand_case(300 + i, c["B"], c["Hkv"], 4, c["T"])]
+        kw = dict(topk=64, sink=4, local=64, return_topk=True, fused=c["fused"], select=c["select"])
+        a = ops.build_args(q, C, codes, K, V, topk=64, sink=4, local=64, select=c["select"],
+                           out=torch.empty((c["B"], c["Hkv"] * 4, 128), dtype=K.dtype, device=dev))
+        own = torch.zeros(_lib.load().lp_sparse_decode_workspace_size(ctypes.byref(a)), dtype=torch.uint8,
+                          device=dev)
+        refs.append(ops.sparse_decode(q, C, codes, K, V, ws=own, **kw))
+        inputs.append((q, C, codes, K, V, kw))
+    torch.cuda.synchronize()
+    shared = torch.zeros(256 << 20, dtype=torch.uint8, device=dev)
+    for rep in range(3):
+        for (q, C, codes, K, V, kw), ref in zip(inputs, refs):
+            r = ops.sparse_decode(q, C, codes, K, V, ws=shared, **kw)
+            torch.cuda.synchronize()
+            assert torch.equal(r.topk, ref.topk) and torch.equal(r.out, ref.out)
+    assert ops.device_errors(shared, dev) & 1 == 0
