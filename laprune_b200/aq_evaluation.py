@@ -1,0 +1,210 @@
+"""Drop-in for the reference's decode hook (laprune/llm/modifiers/aq_evaluation.py).
+
+``_decode_attention`` (aq_evaluation.py:146-253), ``_prepare_aq_cache``
+(:324-494) and ``_kv_cache_append`` (:65-112) with the reference's
+signatures, config keys and cache dictionaries, the compute on this
+package's kernels:
+
+* one decode token (Tq == 1): per-query-head LUT scores over the candidate
+  window, top-k of the reference's size (``mask_out`` / ``min_remain``), the
+  union with the sink and local-window tokens, the GQA K/V gather and the
+  attention -- all in one ``ops.sparse_decode(select="query_head")`` call;
+  then ``self_attn.o_proj``.  With ``aq_use_pruned_attn`` off the reference
+  attends the same token set through a mask (:255-278), so both settings run
+  the same kernel;
+* new keys are encoded greedily straight into the code cache slice
+  (``ops.encode_keys(..., codes=cache[:, :, t0:t1])``), every
+  ``aq_decode_group_size`` tokens as the reference does.
+
+fp16 / bf16 K/V caches only (the reference's CUDA kernels take fp16; its
+fp32 path is its torch fallback).  Multi-token decode (Tq > 1), ICM
+refinement and key reconstruction are outside the decode path and raise.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import ops
+from .aq_kv import AQLayerCodebookManager
+
+__all__ = ["_decode_attention", "_prepare_aq_cache", "_kv_cache_append", "decode_keep_size"]
+
+
+def decode_keep_size(num_candidate: int, mask_out: float = 0.98, min_remain: int = 20) -> int:
+    """Top-k size of the decode hook (aq_evaluation.py:193-197)."""
+    if num_candidate <= 0:
+        return 0
+    k = num_candidate - int(num_candidate * mask_out)
+    k = max(min(num_candidate, min_remain), k)
+    return max(1, min(k, num_candidate))
+
+
+def _scoring_codebooks(manager: AQLayerCodebookManager, layer_idx: int, Hq: int, Hkv: int) -> torch.Tensor:
+    """The decode hook's codebooks: one for every head when heads_per_group
+    covers the Hq query heads (aq_evaluation.py:161-167), else query head h
+    uses group h // heads_per_group (:169-176) -- stacked per KV head, which
+    needs the G query heads of a KV head in one group."""
+    cfg = manager.layer_cfgs.get(layer_idx)
+    if cfg is None or cfg.heads_per_group <= 0 or cfg.heads_per_group >= Hq:
+        return manager.codebooks(layer_idx, 0)
+    G, hpg = Hq // Hkv, cfg.heads_per_group
+    groups = [(kv * G) // hpg for kv in range(Hkv)]
+    if any((kv * G + G - 1) // hpg != groups[kv] for kv in range(Hkv)):
+        raise NotImplementedError(f"heads_per_group={hpg} splits the {G} query heads of a KV head over codebooks")
+    return manager.group_codebooks(layer_idx, groups)
+
+
+def _encoding_codebooks(manager: AQLayerCodebookManager, layer_idx: int, Hkv: int) -> torch.Tensor:
+    """The code cache's codebooks: one for all when heads_per_group covers
+    the Hkv cached heads, else KV head h uses group h // heads_per_group
+    (aq_evaluation.py:384-401)."""
+    cfg = manager.layer_cfgs.get(layer_idx)
+    if cfg is None or cfg.heads_per_group <= 0 or cfg.heads_per_group >= Hkv:
+        return manager.codebooks(layer_idx, 0)
+    return manager.group_codebooks(layer_idx, [h // cfg.heads_per_group for h in range(Hkv)])
+
+
+def _decode_attention(self_attn, manager: AQLayerCodebookManager, layer_idx: int, Q_rope: torch.Tensor,
+                      K_rope: torch.Tensor, vals_full: torch.Tensor, aq_cache: dict, conf: dict) -> torch.Tensor:
+    """Sparse attention of the last query token over the AQ-selected keys,
+    then ``self_attn.o_proj`` (aq_evaluation.py:146-253).
+
+    Q_rope ``[B, H, 1, D]``; K_rope / vals_full ``[B, Hkv, Tk_total, D]``;
+    ``aq_cache["codes"]`` ``[B, Hkv, cap, M]`` uint8 with ``seq_len`` valid.
+    """
+    B, H, Tq, D = Q_rope.shape
+    scoring_m = int(conf.get("aq_scoring_m", 32))
+    if scoring_m != 32:
+        raise ValueError(f"aq_scoring_m must be 32, got {scoring_m}")
+    if Tq != 1:
+        raise NotImplementedError(f"decode of {Tq} query tokens at once is outside the single-token decode path")
+    codes = aq_cache["codes"]
+    seq_len_codes = int(aq_cache.get("seq_len", codes.shape[2]))
+    seq_len_codes = max(0, min(seq_len_codes, codes.shape[2]))
+    Hkv = int(codes.shape[1])
+    if H % Hkv != 0 or K_rope.shape[1] != Hkv:
+        raise ValueError(f"Invalid GQA code heads: Hq={H}, Hkv={Hkv}, K heads={K_rope.shape[1]}")
+    Tk_total = int(getattr(self_attn, "total_seq_len", seq_len_codes))
+    if K_rope.dtype not in (torch.float16, torch.bfloat16) or vals_full.dtype != K_rope.dtype:
+        raise RuntimeError(f"K/V caches must be fp16 or bf16 (got {K_rope.dtype}, {vals_full.dtype})")
+
+    sink = int(conf.get("sink_size", 4))
+    local = int(conf.get("local_window", 64))
+    n_cand = ops.num_candidates(seq_len_codes, Tk_total, sink, local)
+    k = decode_keep_size(n_cand, float(conf.get("mask_out", 0.98)), int(conf.get("min_remain", 20)))
+    cb = _scoring_codebooks(manager, layer_idx, H, Hkv)
+    r = ops.sparse_decode(Q_rope[:, :, -1, :], cb, codes, K_rope, vals_full, topk=k, T_codes=seq_len_codes,
+                          T_total=Tk_total, sink=sink, local=local, select="query_head")
+    attn_output = r.out.reshape(B, 1, H * D)
+    return self_attn.o_proj(attn_output)
+
+
+def _kv_cache_append(self_attn, k_new: torch.Tensor, v_new: torch.Tensor, total_len: int, input_kv_cache=None):
+    """Append ``k_new`` / ``v_new`` ``[B, H, Tn, D]`` to the growable K/V
+    buffers on ``self_attn`` (capacity doubling, ``aq_kv_extra_capacity``
+    spare slots; aq_evaluation.py:65-112).  Returns the ``[B, H, total, D]``
+    views and ``(K_view.data, V_view.data)``."""
+    k_buf = getattr(self_attn, "k_cache", None)
+    v_buf = getattr(self_attn, "v_cache", None)
+    k_len = int(getattr(self_attn, "k_cache_len", 0))
+    k_cap = int(getattr(self_attn, "k_cache_capacity", 0))
+    B, H, Tn, D = k_new.shape
+    conf = getattr(self_attn, "draft_kwargs", {}) or {}
+    extra = max(0, int(conf.get("aq_kv_extra_capacity", 0)))
+    if k_buf is None or v_buf is None or k_cap <= 0:
+        if input_kv_cache is not None:
+            k_prefix, v_prefix = input_kv_cache
+            k_len = int(k_prefix.shape[-2])
+            k_cap = max(total_len, max(16, k_len) * 2)
+            k_buf = k_prefix.new_empty((B, H, k_cap, D))
+            v_buf = v_prefix.new_empty((B, H, k_cap, D))
+            if k_len > 0:
+                k_buf[:, :, :k_len] = k_prefix
+                v_buf[:, :, :k_len] = v_prefix
+        else:
+            k_len = 0
+            k_cap = max(total_len + extra, 16)
+            k_buf = k_new.new_empty((B, H, k_cap, D))
+            v_buf = v_new.new_empty((B, H, k_cap, D))
+    if total_len > k_cap:
+        new_cap = max(total_len, k_cap * 2)
+        k2 = k_buf.new_empty((B, H, new_cap, D))
+        v2 = v_buf.new_empty((B, H, new_cap, D))
+        if k_len > 0:
+            k2[:, :, :k_len] = k_buf[:, :, :k_len]
+            v2[:, :, :k_len] = v_buf[:, :, :k_len]
+        k_buf, v_buf, k_cap = k2, v2, new_cap
+    end = k_len + Tn
+    k_buf[:, :, k_len:end] = k_new
+    v_buf[:, :, k_len:end] = v_new
+    self_attn.k_cache, self_attn.v_cache = k_buf, v_buf
+    self_attn.k_cache_len, self_attn.k_cache_capacity = end, k_cap
+    k_view, v_view = k_buf[:, :, :end], v_buf[:, :, :end]
+    return k_view, v_view, (k_view.data, v_view.data)
+
+
+def _encode_into(manager: AQLayerCodebookManager, layer_idx: int, keys: torch.Tensor, codes_dst: torch.Tensor) -> None:
+    # keys [B, H, t, d] -> codes_dst [B, H, t, M] (a slice of the cache)
+    if keys.shape[2] == 0:
+        return
+    ops.encode_keys(keys, _encoding_codebooks(manager, layer_idx, keys.shape[1]), codes=codes_dst)
+
+
+def _prepare_aq_cache(self, manager: AQLayerCodebookManager, layer_idx: int, keys: torch.Tensor, need_recon: bool,
+                      decode_group_size: int = 1, is_prefill: bool = False) -> dict:
+    """The layer's code cache ``self._aq_cache`` = ``{"seq_len",
+    "encoded_len", "batch_size", "codes" [B, H, cap, M] uint8, "approx"}``
+    kept in step with ``keys [B, H, T, d]`` (aq_evaluation.py:324-494):
+    capacity doubling, new keys encoded once ``decode_group_size`` of them
+    are pending (prefill: at once), ``aq_code_extra_capacity`` spare slots
+    after prefill."""
+    if need_recon:
+        raise NotImplementedError("key reconstruction (aq_use_exact_true_score=False) is not on the decode path")
+    conf = getattr(self, "draft_kwargs", {}) or {}
+    B, H, T, d = keys.shape
+    cfg = manager.layer_cfgs.get(layer_idx)
+    M = cfg.M if cfg is not None else manager.codebooks(layer_idx, 0).shape[0]
+    cache: Optional[dict] = getattr(self, "_aq_cache", None)
+    if cache is not None and cache.get("batch_size") == B:
+        cached_seq = int(cache.get("seq_len", 0))
+        encoded = int(cache.get("encoded_len", cached_seq))
+        if cached_seq == T:
+            return cache
+        if T > cached_seq:
+            codes = cache["codes"]
+            cap = codes.shape[2]
+            if T > cap:
+                new_cap = max(cap * 2 if cap > 0 else T, T)
+                grown = codes.new_empty((B, H, new_cap, codes.shape[3]))
+                if encoded > 0:
+                    grown[:, :, :encoded] = codes[:, :, :encoded]
+                codes = grown
+                cache["codes"] = codes
+            pending = T - encoded
+            if not is_prefill and decode_group_size > 1 and pending < decode_group_size:
+                cache["seq_len"], cache["encoded_len"] = T, encoded
+                self._aq_cache = cache
+                return cache
+            if pending > 0:
+                icm = int(conf.get("aq_encode_icm_iters_decode", 0))
+                if icm != 0:
+                    raise NotImplementedError(f"aq_encode_icm_iters_decode={icm}: ICM refinement is not on the decode path")
+                _encode_into(manager, layer_idx, keys[:, :, encoded:T], codes[:, :, encoded:T])
+            cache["seq_len"], cache["encoded_len"], cache["codes"] = T, T, codes
+            self._aq_cache = cache
+            return cache
+    icm = int(conf.get("aq_encode_icm_iters_prefill", 0 if is_prefill else 2))
+    if icm != 0:
+        raise NotImplementedError(f"aq_encode_icm_iters_prefill={icm}: ICM refinement is not on the decode path")
+    extra = max(0, int(conf.get("aq_code_extra_capacity", 0))) if is_prefill else 0
+    codes = torch.empty((B, H, T + extra, M), dtype=torch.uint8, device=keys.device)
+    group = int(conf.get("aq_prefill_group_size", 0))
+    group = T if group <= 0 else group
+    for t0 in range(0, T, group):
+        t1 = min(T, t0 + group)
+        _encode_into(manager, layer_idx, keys[:, :, t0:t1], codes[:, :, t0:t1])
+    cache = {"seq_len": T, "encoded_len": T, "batch_size": B, "codes": codes, "approx": None}
+    self._aq_cache = cache
+    return cache

@@ -107,8 +107,10 @@ def init_process_group(backend: str = "nccl", timeout_s: float = 60.0) -> tuple[
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1 and not dist.is_initialized():
+        kw = {}
         if backend == "nccl":
             torch.cuda.set_device(local)
+            kw["device_id"] = torch.device("cuda", local)
         dist.init_process_group(backend, init_method="env://",
-                                timeout=datetime.timedelta(seconds=timeout_s))
+                                timeout=datetime.timedelta(seconds=timeout_s), **kw)
     return world, rank, local

@@ -1,0 +1,95 @@
+"""Host logic of the reference-facing manager and decode-hook mirror (no GPU):
+the codebook file format, the top-k size rule, the K/V buffer growth and the
+refusal of work outside the decode path."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from laprune_b200 import aq_evaluation as aqe
+from laprune_b200.aq_kv import AQLayerCodebookManager, AQLayerConfig
+
+
+def _mgr(layers=(0, 3), hpg=4, num_heads=8):
+    return AQLayerCodebookManager({L: AQLayerConfig(M=32, K=256, d=128, heads_per_group=hpg, num_heads=num_heads)
+                                   for L in layers}, device="cpu")
+
+
+def test_codebook_files_round_trip(tmp_path):
+    g = torch.Generator().manual_seed(0)
+    a = _mgr()
+    cbs = {(L, G): torch.randn((32, 256, 128), generator=g) for L in (0, 3) for G in (0, 1)}
+    for (L, G), cb in cbs.items():
+        a.set_codebooks(L, G, cb)
+    a.save(str(tmp_path))
+    names = sorted(p.name for p in tmp_path.iterdir())
+    assert names == ["layer_0_group_0.pt", "layer_0_group_1.pt", "layer_3_group_0.pt", "layer_3_group_1.pt"]
+    b = _mgr()
+    b.load(str(tmp_path))
+    for (L, G), cb in cbs.items():
+        assert torch.equal(b.codebooks(L, G), cb)
+
+
+def test_load_skips_stale_groups_and_unknown_layers_and_adopts_file_shapes(tmp_path):
+    torch.save({"M": 16, "K": 256, "d": 128, "codebooks": torch.zeros(16, 256, 128)}, tmp_path / "layer_0_group_0.pt")
+    torch.save({"M": 16, "K": 256, "d": 128, "codebooks": torch.zeros(16, 256, 128)}, tmp_path / "layer_0_group_5.pt")
+    torch.save({"M": 16, "K": 256, "d": 128, "codebooks": torch.zeros(16, 256, 128)}, tmp_path / "layer_9_group_0.pt")
+    (tmp_path / "notes.txt").write_text("not a codebook")
+    m = _mgr(layers=(0,), hpg=4, num_heads=8)  # 2 groups expected: group 5 is stale
+    m.load(str(tmp_path))
+    assert m.layer_cfgs[0].M == 16 and m.layer_cfgs[0].heads_per_group == 4
+    assert m.codebooks(0, 0).shape == (16, 256, 128)
+    with pytest.raises(KeyError):
+        m.codebooks(0, 5)
+    with pytest.raises(KeyError):
+        m.codebooks(9, 0)
+    with pytest.raises(FileNotFoundError):
+        m.load(str(tmp_path / "missing"))
+
+
+def test_icm_refinement_is_refused_before_any_compute():
+    m = _mgr()
+    m.set_codebooks(0, 0, torch.zeros(32, 256, 128))
+    with pytest.raises(NotImplementedError):
+        m.encode_keys(0, 0, torch.zeros(4, 128), icm_iters=2)
+    with pytest.raises(NotImplementedError):
+        m.encode_keys_batch(0, 0, torch.zeros(4, 128), icm_iters=1)
+
+
+def test_group_stacks_follow_heads_per_group():
+    m = _mgr(layers=(0,), hpg=2, num_heads=8)
+    for G in range(4):
+        m.set_codebooks(0, G, torch.full((32, 256, 128), float(G)))
+    st = m.group_codebooks(0, [h // 2 for h in range(8)])
+    assert [int(st[h, 0, 0, 0]) for h in range(8)] == [0, 0, 1, 1, 2, 2, 3, 3]
+    # the decode hook's grouping: query heads (G=4 per KV head) over hpg=2 split a KV head
+    with pytest.raises(NotImplementedError):
+        aqe._scoring_codebooks(m, 0, 8, 2)
+    m.layer_cfgs[0].heads_per_group = 4
+    m._stacks.clear()
+    st = aqe._scoring_codebooks(m, 0, 8, 2)
+    assert st.shape[0] == 2 and int(st[1, 0, 0, 0]) == 1
+
+
+@pytest.mark.parametrize("n", [0, 1, 5, 19, 20, 21, 999, 1000, 1001, 131004])
+def test_decode_keep_size_matches_the_oracle(n):
+    assert aqe.decode_keep_size(n) == oracle.num_keep(n)
+
+
+def test_kv_cache_append_grows_and_keeps_the_prefix():
+    class Attn:
+        pass
+    a = Attn()
+    g = torch.Generator().manual_seed(1)
+    ks, vs = [], []
+    total = 0
+    for step, tn in enumerate([20, 1, 1, 30, 1]):
+        k = torch.randn((2, 2, tn, 8), generator=g)
+        v = torch.randn((2, 2, tn, 8), generator=g)
+        ks.append(k)
+        vs.append(v)
+        total += tn
+        kv, vv, (kd, vd) = aqe._kv_cache_append(a, k, v, total)
+        assert kv.shape == (2, 2, total, 8) and a.k_cache_len == total and a.k_cache_capacity >= total
+        assert torch.equal(kv, torch.cat(ks, 2)) and torch.equal(vv, torch.cat(vs, 2))
+    assert a.k_cache_capacity == 80  # 20 -> 20 (first: max(total, 16)), 21 -> 40, 52 -> 80
