@@ -17,8 +17,9 @@
 //
 // Phases (CTA c belongs to one selection unit u = (b, kv head)):
 //   A  LUT build: the unit's CTAs split its 32*256 codeword rows evenly and
-//      write LUT_sum[u][k][m] = q_sum . C_m[k] (fp32) to L2.  The code tiles
-//      of phase B are already streaming into the CTA's TMA ring.    | barrier
+//      write LUT_sum[u][k][m] = q_sum . C_m[k] (fp32) to L2.  The first
+//      code tiles of phase B are already streaming into the CTA's TMA ring;
+//      the rest follow once the codebook stream is done.           | barrier
 //   B  score: the unit's table is staged as int32 fixed point (exact sums,
 //      order-independent), the per-m bounds are recomputed from the table in
 //      shared memory (identical in every CTA of the unit), the CTA's code
@@ -53,6 +54,7 @@ namespace lp {
 
 constexpr int kFThreads = 512;
 constexpr int kFStages = 6;
+constexpr int kFPre0 = 2;                        // code tiles issued before phase A
 constexpr int kFTile = kFThreads * 32;           // 16 KB of code rows per stage
 constexpr int kFScoreCap = 11264;                // tokens per CTA kept in smem
 constexpr int kFMaxWords = 8192;                 // bitmap words per unit in smem overlay
@@ -310,16 +312,17 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     // ---- start streaming the phase-B code tiles right away ----
     uint64_t policy = 0;
     const int npre = ntiles < kFStages ? ntiles : kFStages;
+    const int npre0 = npre < kFPre0 ? npre : kFPre0;  // the rest after phase A
     if (tid == 0) {
         policy = policy_evict_first();
-        for (int i = 0; i < npre; ++i) {
+        for (int i = 0; i < npre0; ++i) {
             const int t0 = t_begin + i * kFThreads;
             const int nn = min(kFThreads, t_end - t0);
             mbar_arrive_expect_tx(&s_bar[i], (uint32_t)nn * 32u);
             bulk_g2s_stream(s_ring + i * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[i], policy);
         }
     }
-    int issued = npre;
+    int issued = npre0;
     auto drain = [&](int from) {
         for (int j = from; j < issued; ++j) mbar_wait(&s_bar[j % kFStages], (uint32_t)(j / kFStages) & 1u, nullptr);
     };
@@ -411,6 +414,17 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         }
     }
     if (stamp) p.phase_ns[1] = global_ns();
+    // the ring's other slots: issued once phase A's codebook stream is done,
+    // so that the two streams do not share HBM while the LUT is built
+    if (tid == 0) {
+        for (int i = npre0; i < npre; ++i) {
+            const int t0 = t_begin + i * kFThreads;
+            const int nn = min(kFThreads, t_end - t0);
+            mbar_arrive_expect_tx(&s_bar[i], (uint32_t)nn * 32u);
+            bulk_g2s_stream(s_ring + i * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[i], policy);
+        }
+    }
+    issued = npre;
 
     using Scan = cub::BlockScan<int, kFThreads>;
     __shared__ typename Scan::TempStorage scan_tmp;
