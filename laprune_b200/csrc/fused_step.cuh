@@ -794,13 +794,20 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             }
             __syncthreads();
             const int bmax = s_bmax, bmin = s_bmin;
-            for (int i = tid; i < cn * PW; i += kFThreads) {
-                const int j = i / PW, w = i - j * PW;
-                const uint32_t c = s_pw[i];
-                if (w < kPubWin && c) {
-                    const int rb = (int)s_pw[j * PW + kPubWin + 1] + w - bmax;  // bin relative to bmax
-                    if (rb >= 0) atomicAdd(&s_uh[min(rb, kPubWin)], c);
+            // bin bmax + rb gathers window rb + bmax - b_j of every slot j
+            // (4 threads per bin, no atomics); b_j <= bmax, so no window maps
+            // above bin bmax + 127 and s_uh[kPubWin] stays 0
+            {
+                static_assert(kFThreads == 4 * kPubWin, "4 threads per bin");
+                const int rb = tid >> 2;
+                uint32_t c = 0u;
+                for (int j = tid & 3; j < cn; j += 4) {
+                    const int w = rb + bmax - (int)s_pw[j * PW + kPubWin + 1];
+                    if (w < kPubWin) c += s_pw[j * PW + w];
                 }
+                c += __shfl_xor_sync(0xffffffffu, c, 1);
+                c += __shfl_xor_sync(0xffffffffu, c, 2);
+                if ((tid & 3) == 0) s_uh[rb] = c;
             }
             __syncthreads();
             if (warp == 0) {
@@ -969,12 +976,15 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             // when the top-k indices are requested): the first `need` win
             const int i0 = p.topk_out ? 0 : s_toff[cj];
             const int i1 = p.topk_out ? ntie : s_toff[cj + 1];
-            for (int i = i0 + tid; i < i1; i += kFThreads) {
+            // one warp per entry, its lanes over the unit's entries (the
+            // loop is warp-uniform: every lane takes part in the reduction)
+            for (int i = i0 + warp; i < i1; i += NW) {
                 const float ki = s_tk[i];
                 const int ii = s_ti[i];
                 int rank = 0;
-                for (int j = 0; j < ntie; ++j) rank += sel_before(s_tk[j], s_ti[j], ki, ii);
-                if (rank < need) {
+                for (int j = lane; j < ntie; j += 32) rank += sel_before(s_tk[j], s_ti[j], ki, ii);
+                rank = __reduce_add_sync(0xffffffffu, rank);
+                if (lane == 0 && rank < need) {
                     if (ii >= t_begin && ii < t_end) atomicOr(&s_win[(ii - t_begin) >> 5], 1u << ((ii - t_begin) & 31));
                     else if (ii < t_begin) atomicAdd(&s_topk_off, 1);
                 }
@@ -1086,12 +1096,13 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             // ranked unless the top-k indices are requested.
             const int i0 = p.topk_out ? 0 : s_toff[cj];
             const int i1 = p.topk_out ? ntie : s_toff[cj + 1];
-            for (int i = i0 + tid; i < i1; i += kFThreads) {
+            for (int i = i0 + warp; i < i1; i += NW) {  // one warp per entry (warp-uniform)
                 const float ki = s_tk[i];
                 const int ii = s_ti[i];
                 int rank = 0;
-                for (int j = 0; j < ntie; ++j) rank += sel_before(s_tk[j], s_ti[j], ki, ii);
-                if (rank < need) {
+                for (int j = lane; j < ntie; j += 32) rank += sel_before(s_tk[j], s_ti[j], ki, ii);
+                rank = __reduce_add_sync(0xffffffffu, rank);
+                if (lane == 0 && rank < need) {
                     const int lt = ii - t_begin;
                     if (ii >= t_begin && ii < t_end) atomicOr(&s_win[lt >> 5], 1u << (lt & 31));
                     if (p.topk_out && ii >= p.c0 && ii < p.c1) {
