@@ -44,6 +44,7 @@
 // Every wait (TMA ring, unit barrier) is bounded; on timeout the CTA records
 // LP_DEVERR_WAIT_TIMEOUT, drains its own copies and exits.
 #pragma once
+#include <type_traits>
 #include <cub/block/block_scan.cuh>
 #include "attention.cuh"
 #include "lut_build.cuh"
@@ -247,6 +248,47 @@ __device__ __forceinline__ void fused_cta_unit(int cta, int nctas, int U, int* u
     }
 }
 
+// ---- warp-level tensor-core tiles for phase E (mma.sync m16n8k16, fp32
+//      accumulators; A row-major, B column-major; A and B of one type) ----
+template <typename KT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    if constexpr (std::is_same<KT, __nv_bfloat16>::value) {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<const uint32_t*>(&v);
+    } else {
+        const __half2 v = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<const uint32_t*>(&v);
+    }
+}
+template <typename KT>
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, const uint32_t* b) {
+    if constexpr (std::is_same<KT, __nv_bfloat16>::value) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+    }
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t* r, uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t* r, uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+
 template <typename QT, typename KT, typename OT>
 __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(FusedParams p) {
     using S = FusedSmem;
@@ -260,7 +302,6 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     __shared__ BinParams s_bp;
     __shared__ __align__(16) float s_qu[8 * 128];  // the unit's G query rows (fp32), loaded at start
     __shared__ int s_shift, s_bstar, s_above;
-    __shared__ __align__(16) float s_lg[kFThreads / 32][kFMaxRows / 64 * 16];  // per-warp logits / weights (phase E)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = kFThreads / 32;
@@ -727,13 +768,17 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         return s_list[nabove + rr - n_loc_here];
     };
     // rows c0r + [r_lo, r_hi) of the row list -> staging rows [r_lo, r_hi)
-    // (16-byte cp.async; every thread commits one group)
+    // (16-byte cp.async; every thread commits one group).  16-byte unit u of
+    // staging row r sits at unit u ^ (r & 7), so that the 8 rows an
+    // ldmatrix reads at one dim offset fall in 8 different bank groups.
+    static_assert(CH == 16, "16 units of 16 bytes per staged row");
     auto issue_rows = [&](int c0r, int r_lo, int r_hi, int nabove) {
         for (int c = r_lo * CH + tid; c < r_hi * CH; c += kFThreads) {
             const int r = c / CH, part = c - r * CH;
             const int64_t t = min(max(row_token(c0r + r, nabove), 0), p.T_total - 1);
-            cp_async16(s_k + r * D + part * EPC, kb + t * p.k_stride_t + part * EPC);
-            cp_async16(s_v + r * D + part * EPC, vb + t * p.v_stride_t + part * EPC);
+            const int sw = (part ^ (r & 7)) * EPC;
+            cp_async16(s_k + r * D + sw, kb + t * p.k_stride_t + part * EPC);
+            cp_async16(s_v + r * D + sw, vb + t * p.v_stride_t + part * EPC);
         }
         cp_async_commit();
     };
@@ -1268,153 +1313,95 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         const int nrows = n_early + s_nwin;
         const int n_issued = s_fast ? min(n_early, R) : 0;  // rows already loading since phase C
 
-        // ---- per-warp flash-decode: warp w takes rows 4w..4w+3 (+64 per
-        //      pass) of every chunk; lane l owns dims 4l..4l+3 of every head
-        //      and keeps its own running max / sum / P.V (online softmax) ----
-        float wm[8], wl[8];
-        float4 wacc[8];
+        // ---- per-warp flash-decode on the tensor cores (mma.sync m16n8k16):
+        //      warp w takes the 16-row tiles w, w + NW, ... of every chunk.
+        //      Per tile: S^T[16 rows x 8 heads] = K_tile . Q^T (8 steps over
+        //      the 128 dims), online softmax per head, then
+        //      O^T[128 dims x 8 heads] += V_tile^T . P^T (8 blocks of 16 dims).
+        //      Lane (gq = lane / 4, tq = lane % 4) keeps heads 2tq, 2tq + 1:
+        //      their running max / sum and O^T rows 16mb + gq (+8).  Heads at
+        //      or above G have a zero query (finite, never written out). ----
+        const int gq = lane >> 2, tq = lane & 3;
+        float wm[2] = {-INFINITY, -INFINITY}, wl[2] = {0.f, 0.f};
+        float oacc[8][4];
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            wm[g] = -INFINITY;
-            wl[g] = 0.f;
-            wacc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        auto attend = [&](int r_lo, int r_hi) {
-            if (p.G == 4) {
-                // pass 1: logits of the warp's rows (groups of 4 rows, +64 per
-                // group) into its buffer s_lgw[group][4 * row + head]
-                float* s_lgw = s_lg[warp];
-                float4 qv[4];
+        for (int mb = 0; mb < 8; ++mb)
 #pragma unroll
-                for (int g = 0; g < 4; ++g) qv[g] = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
-                int ngrp = 0;
-                for (int r0 = r_lo + warp * 4; r0 < r_hi; r0 += NW * 4, ++ngrp) {
-                    // the 16 (row, head) dots, reduced by one 16-way transpose:
-                    // lanes 2i, 2i+1 end with the total of idx i = 4 * row + head
-                    float v[16];
+            for (int e = 0; e < 4; ++e) oacc[mb][e] = 0.f;
+        // Q^T (B operand): b0b1 = Q[head gq][16ks + 2tq, +1], b2b3 = dims +8
+        uint32_t qb[8][2];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float4 kv = r0 + j < r_hi ? Vec4<KT>::load(s_k + (r0 + j) * D + lane * 4)
-                                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                        for (int g = 0; g < 4; ++g) {
-                            float a = qv[g].x * kv.x;
-                            a = fmaf(qv[g].y, kv.y, a);
-                            a = fmaf(qv[g].z, kv.z, a);
-                            a = fmaf(qv[g].w, kv.w, a);
-                            v[j * 4 + g] = a;
-                        }
-                    }
-                    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
-                    float x8[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float keep = b4 ? v[8 + j] : v[j];
-                        const float send = b4 ? v[j] : v[8 + j];
-                        x8[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-                    }
-                    float x4[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float keep = b3 ? x8[4 + j] : x8[j];
-                        const float send = b3 ? x8[j] : x8[4 + j];
-                        x4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-                    }
-                    float x2[2];
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const float keep = b2 ? x4[2 + j] : x4[j];
-                        const float send = b2 ? x4[j] : x4[2 + j];
-                        x2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-                    }
-                    const float keep = b1 ? x2[1] : x2[0];
-                    const float send = b1 ? x2[0] : x2[1];
-                    float tot = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-                    tot += __shfl_xor_sync(0xffffffffu, tot, 1);
-                    const int idx = (lane >> 1) & 15;
-                    if ((lane & 1) == 0)
-                        s_lgw[ngrp * 16 + idx] = r0 + (idx >> 2) < r_hi ? tot * p.scale_log2 : -INFINITY;
-                }
-                if (ngrp == 0) return;
-                __syncwarp();
-                // pass 2: one softmax step for all of them.  Lane l takes the
-                // values l and l + 32 (head l & 3); heads reduce over lanes
-                // with equal l & 3.
-                const int nval = ngrp * 16;  // <= 48 (kFMaxRows / 64 groups)
-                const float a0 = lane < nval ? s_lgw[lane] : -INFINITY;
-                const float a1 = lane + 32 < nval ? s_lgw[lane + 32] : -INFINITY;
-                const int hg = lane & 3;
-                const float wmh = hg == 0 ? wm[0] : hg == 1 ? wm[1] : hg == 2 ? wm[2] : wm[3];
-                float mx = fmaxf(a0, a1);
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                const float mn = fmaxf(wmh, mx);  // finite: the warp has a row
-                const float p0 = exp2f(a0 - mn), p1 = exp2f(a1 - mn);
-                float sm = p0 + p1;
-                sm += __shfl_xor_sync(0xffffffffu, sm, 4);
-                sm += __shfl_xor_sync(0xffffffffu, sm, 8);
-                sm += __shfl_xor_sync(0xffffffffu, sm, 16);
-                const float sc = exp2f(wmh - mn);  // 0 while the warp had no row
-                if (lane < nval) s_lgw[lane] = p0;
-                if (lane + 32 < nval) s_lgw[lane + 32] = p1;
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    const float scg = __shfl_sync(0xffffffffu, sc, g);
-                    wm[g] = __shfl_sync(0xffffffffu, mn, g);
-                    wl[g] = fmaf(wl[g], scg, __shfl_sync(0xffffffffu, sm, g));
-                    wacc[g].x *= scg;
-                    wacc[g].y *= scg;
-                    wacc[g].z *= scg;
-                    wacc[g].w *= scg;
-                }
-                __syncwarp();
-                // pass 3: P.V over the warp's rows
-                int grp = 0;
-                for (int r0 = r_lo + warp * 4; r0 < r_hi; r0 += NW * 4, ++grp) {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        if (r0 + j >= r_hi) break;
-                        const float4 vv = Vec4<KT>::load(s_v + (r0 + j) * D + lane * 4);
-                        const float4 pj = *reinterpret_cast<const float4*>(s_lgw + grp * 16 + 4 * j);
-#pragma unroll
-                        for (int g = 0; g < 4; ++g) {
-                            const float pg = g == 0 ? pj.x : g == 1 ? pj.y : g == 2 ? pj.z : pj.w;
-                            wacc[g].x = fmaf(pg, vv.x, wacc[g].x);
-                            wacc[g].y = fmaf(pg, vv.y, wacc[g].y);
-                            wacc[g].z = fmaf(pg, vv.z, wacc[g].z);
-                            wacc[g].w = fmaf(pg, vv.w, wacc[g].w);
-                        }
-                    }
-                }
-                __syncwarp();
+        for (int ks = 0; ks < 8; ++ks) {
+            if (gq < p.G) {
+                const float* qr = s_q + gq * D + 16 * ks + 2 * tq;
+                qb[ks][0] = pack2<KT>(qr[0], qr[1]);
+                qb[ks][1] = pack2<KT>(qr[8], qr[9]);
             } else {
-                for (int r = r_lo + warp; r < r_hi; r += NW) {
-                    const float4 kv = Vec4<KT>::load(s_k + r * D + lane * 4);
-                    const float4 vv = Vec4<KT>::load(s_v + r * D + lane * 4);
+                qb[ks][0] = 0u;
+                qb[ks][1] = 0u;
+            }
+        }
+        const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: this lane addresses row rr of matrix mi
+        auto attend = [&](int r_lo, int r_hi) {
+            // warp-uniform loop: every lane takes part in the mma and shuffles
+            for (int r0 = r_lo + warp * 16; r0 < r_hi; r0 += NW * 16) {
+                // rows past r_hi read row r_lo instead (finite data, masked below)
+                int krow = r0 + (mi & 1) * 8 + rr;
+                if (krow >= r_hi) krow = r_lo;
+                const uint32_t kbase = smem_u32(s_k + krow * D);
+                float sv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                    for (int g = 0; g < 8; ++g) {
-                        if (g >= p.G) break;
-                        const float4 qv = *reinterpret_cast<const float4*>(s_q + g * D + lane * 4);
-                        float a = qv.x * kv.x;
-                        a = fmaf(qv.y, kv.y, a);
-                        a = fmaf(qv.z, kv.z, a);
-                        a = fmaf(qv.w, kv.w, a);
+                for (int ks = 0; ks < 8; ++ks) {
+                    uint32_t af[4];
+                    ldsm_x4(af, kbase + (uint32_t)((((2 * ks + (mi >> 1)) ^ (krow & 7)) * 16)));
+                    mma16816<KT>(sv, af, qb[ks]);
+                }
+                // sv: S[row r0+gq][head 2tq + e] (e = 0, 1), rows +8 in sv[2 + e]
+                const bool v0 = r0 + gq < r_hi, v1 = r0 + gq + 8 < r_hi;
+                float pv[4];
 #pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-                        const float s = a * p.scale_log2;
-                        const float mn = fmaxf(wm[g], s);
-                        const float sc = exp2f(wm[g] - mn);
-                        const float pr = exp2f(s - mn);
-                        wl[g] = fmaf(wl[g], sc, pr);
-                        float4 c = wacc[g];
-                        c.x = fmaf(c.x, sc, pr * vv.x);
-                        c.y = fmaf(c.y, sc, pr * vv.y);
-                        c.z = fmaf(c.z, sc, pr * vv.z);
-                        c.w = fmaf(c.w, sc, pr * vv.w);
-                        wacc[g] = c;
-                        wm[g] = mn;
+                for (int e = 0; e < 2; ++e) {
+                    const float s0 = v0 ? sv[e] * p.scale_log2 : -INFINITY;
+                    const float s1 = v1 ? sv[2 + e] * p.scale_log2 : -INFINITY;
+                    float mx = fmaxf(s0, s1);
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    const float mn = fmaxf(wm[e], mx);  // finite: row r0 is valid
+                    const float sc = exp2f(wm[e] - mn);
+                    pv[e] = exp2f(s0 - mn);
+                    pv[2 + e] = exp2f(s1 - mn);
+                    float sm = pv[e] + pv[2 + e];
+                    sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+                    sm += __shfl_xor_sync(0xffffffffu, sm, 8);
+                    sm += __shfl_xor_sync(0xffffffffu, sm, 16);
+                    wl[e] = fmaf(wl[e], sc, sm);
+                    wm[e] = mn;
+#pragma unroll
+                    for (int mb = 0; mb < 8; ++mb) {
+                        oacc[mb][e] *= sc;
+                        oacc[mb][2 + e] *= sc;
                     }
+                }
+                // P^T (B operand): b0b1 = P[rows 2tq, 2tq+1][head gq], b2b3 =
+                // rows +8; P[row r][head h] sits in lane 4 (r % 8) + h / 2,
+                // half h % 2 of its (row < 8 ? pv01 : pv23) pair
+                const uint32_t m01 = pack2<KT>(pv[0], pv[1]), m23 = pack2<KT>(pv[2], pv[3]);
+                const int srcA = 8 * tq + (gq >> 1), srcB = srcA + 4;
+                const uint32_t xa01 = __shfl_sync(0xffffffffu, m01, srcA), xb01 = __shfl_sync(0xffffffffu, m01, srcB);
+                const uint32_t xa23 = __shfl_sync(0xffffffffu, m23, srcA), xb23 = __shfl_sync(0xffffffffu, m23, srcB);
+                const uint32_t selp = (gq & 1) ? 0x7632u : 0x5410u;
+                uint32_t pb[2];
+                pb[0] = __byte_perm(xa01, xb01, selp);
+                pb[1] = __byte_perm(xa23, xb23, selp);
+                int vrow = r0 + (mi >> 1) * 8 + rr;
+                if (vrow >= r_hi) vrow = r_lo;
+                const uint32_t vbase = smem_u32(s_v + vrow * D);
+#pragma unroll
+                for (int mb = 0; mb < 8; ++mb) {
+                    uint32_t af[4];
+                    ldsm_x4_trans(af, vbase + (uint32_t)((((2 * mb + (mi & 1)) ^ (vrow & 7)) * 16)));
+                    mma16816<KT>(oacc[mb], af, pb);
                 }
             }
         };
@@ -1446,12 +1433,19 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             float* s_cm = s_wf + NW * 8;                       // [8] slice max
             float* s_cl = s_cm + 8;                            // [8] slice sum
 #pragma unroll
-            for (int g = 0; g < 8; ++g) {
-                if (g >= p.G) break;
-                *reinterpret_cast<float4*>(s_wacc + (warp * p.G + g) * D + lane * 4) = wacc[g];
-                if (lane == 0) {
-                    s_wm[warp * 8 + g] = wm[g];
-                    s_wl[warp * 8 + g] = wl[g];
+            for (int e = 0; e < 2; ++e) {
+                const int h = 2 * tq + e;
+                if (h < p.G) {
+                    float* dst = s_wacc + (warp * p.G + h) * D + gq;
+#pragma unroll
+                    for (int mb = 0; mb < 8; ++mb) {
+                        dst[16 * mb] = oacc[mb][e];
+                        dst[16 * mb + 8] = oacc[mb][2 + e];
+                    }
+                    if (gq == 0) {
+                        s_wm[warp * 8 + h] = wm[e];
+                        s_wl[warp * 8 + h] = wl[e];
+                    }
                 }
             }
             __syncthreads();
