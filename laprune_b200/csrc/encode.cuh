@@ -197,7 +197,6 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     const int tile = blockIdx.x - set * p.ctas_per_set;
     const int nvec_set = p.per_head ? p.B * p.T : p.B * p.H * p.T;  // vectors of this set
     const int v0 = tile * kEncRows;
-    const float* cbs = p.cb + (int64_t)set * kEncM * kEncK * kEncD;
     const float* nrms = p.nrm + (int64_t)set * kEncM * kEncK;
     const float* smx = p.smax + (int64_t)set * kEncM * 4;
 

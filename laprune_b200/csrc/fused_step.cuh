@@ -16,10 +16,11 @@
 // still building theirs.
 //
 // Phases (CTA c belongs to one selection unit u = (b, kv head)):
-//   A  LUT build: the unit's CTAs split its 32*256 codeword rows evenly and
-//      write LUT_sum[u][k][m] = q_sum . C_m[k] (fp32) to L2.  The first
-//      code tiles of phase B are already streaming into the CTA's TMA ring;
-//      the rest follow once the codebook stream is done.           | barrier
+//   A  LUT build: the unit's CTAs split its 32*256 codeword rows evenly,
+//      write LUT_sum[u][k][m] = q_sum . C_m[k] (fp32) to L2 and raise an
+//      epoch-tagged flag each.  The first code tiles of phase B are already
+//      streaming into the CTA's TMA ring; the rest follow once the codebook
+//      stream is done.                                     | the unit's flags
 //   B  score: the unit's table is staged as int32 fixed point (exact sums,
 //      order-independent), the per-m bounds are recomputed from the table in
 //      shared memory (identical in every CTA of the unit), the CTA's code
@@ -84,7 +85,8 @@ struct FusedParams {
     int64_t out_stride_b, out_stride_h;
     int32_t* topk_out;
     // workspace
-    unsigned long long* lut;   // [U][256][32] tagged fp32 LUT_sum (value bits | epoch << 32)
+    float* lut;                // [U][256][32] fp32 LUT_sum, plain stores
+    unsigned long long* lut_flag;  // [gridDim.x] tagged: CTA j's share of its unit's LUT is written
     float* sel_scores;   // [U][sel_stride]
     int64_t sel_stride;
     uint32_t* chist;     // [gridDim.x][kNB] local score histogram of each CTA (exchange path)
@@ -192,6 +194,11 @@ __device__ __forceinline__ void st_tag(unsigned long long* p, uint32_t v, uint32
 __device__ __forceinline__ unsigned long long ld_tag(const unsigned long long* p) {
     unsigned long long x;
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(x) : "l"(p) : "memory");
+    return x;
+}
+__device__ __forceinline__ unsigned long long ld_tag_acquire(const unsigned long long* p) {
+    unsigned long long x;
+    asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(x) : "l"(p) : "memory");
     return x;
 }
 __device__ __forceinline__ bool tag_ok(unsigned long long x, uint32_t epoch) {
@@ -447,12 +454,18 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 tot += __shfl_xor_sync(0xffffffffu, tot, 2);
                 tot += __shfl_xor_sync(0xffffffffu, tot, 1);
                 const int j = (lane >> 3) & 3;
-                if ((lane & 7) == 0 && fr + j < f_end)
-                    st_tag(p.lut + ((int64_t)u * 256 + k0 + j) * 32 + m, __float_as_uint(tot), s_epoch);
+                if ((lane & 7) == 0 && fr + j < f_end) p.lut[((int64_t)u * 256 + k0 + j) * 32 + m] = tot;
             }
             __syncthreads();  // stage c fully consumed
             if (tid == 0 && c + 3 < nchunk) issue_chunk(c + 3);
         }
+    }
+    // the CTA's LUT share is out: every thread's stores precede the barrier
+    // that ended the last chunk; the fence makes them visible GPU-wide
+    // before the flag
+    if (tid == 0) {
+        __threadfence();
+        st_tag(p.lut_flag + blockIdx.x, 1u, s_epoch);
     }
     if (stamp) p.phase_ns[1] = global_ns();
     // the ring's other slots: issued once phase A's codebook stream is done,
@@ -475,34 +488,27 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     float from_fx;
     {
         // stage the unit table: fp32 -> per-m bounds -> int32 fixed point (dup
-        // layout).  Its rows come from all CTAs of the unit: each value is
-        // polled until it carries this call's epoch.
+        // layout).  Its rows come from all CTAs of the unit: thread j < cn
+        // polls CTA j's flag (acquire) until it carries this call's epoch;
+        // after the barrier the table is read from L2.
         float4 v[4];
         {
-            const unsigned long long* gl = p.lut + (int64_t)u * 256 * 32;
             bool ok = true;
-            const long long t0 = clock64();
-            unsigned long long w[16];
-            uint32_t pend = 0xFFFFu;
-            while (true) {
-#pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    if (pend >> e & 1u) w[e] = ld_tag(gl + 4 * (tid + (e >> 2) * kFThreads) + (e & 3));
-#pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    if (tag_ok(w[e], s_epoch)) pend &= ~(1u << e);
-                if (!pend) break;
-                if (clock64() - t0 > kWaitCycles) {
-                    atomicOr(p.err, LP_DEVERR_WAIT_TIMEOUT);
-                    ok = false;
-                    break;
+            if (tid < cn) {
+                const unsigned long long* fl = p.lut_flag + (blockIdx.x - cj) + tid;  // the unit's CTAs
+                const long long t0 = clock64();
+                while (!tag_ok(ld_tag_acquire(fl), s_epoch)) {
+                    if (clock64() - t0 > kWaitCycles) {
+                        atomicOr(p.err, LP_DEVERR_WAIT_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
                 }
             }
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                v[j] = make_float4(__uint_as_float((uint32_t)w[4 * j]), __uint_as_float((uint32_t)w[4 * j + 1]),
-                                   __uint_as_float((uint32_t)w[4 * j + 2]), __uint_as_float((uint32_t)w[4 * j + 3]));
             if (__syncthreads_or(!ok)) { drain(0); return; }
+            const float4* gl = reinterpret_cast<const float4*>(p.lut + (int64_t)u * 256 * 32);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = __ldcg(gl + tid + j * kFThreads);
         }
         if (stamp) p.phase_ns[2] = global_ns();
         // thread's m group is (tid & 7); reduce min/max per m over k

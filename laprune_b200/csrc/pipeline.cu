@@ -90,7 +90,8 @@ struct Plan {
     uint32_t* cta_ties;
     unsigned long long* fpub;   // fused path: tagged candidates [ctas][pub_cap][2]
     unsigned long long* fwin;   // fused path: tagged windows + headers [ctas][kPubWin + 2]
-    unsigned long long* flut;   // fused path: tagged LUT [U][256][32]
+    float* flut;                // fused path: LUT [U][256][32] (plain, behind per-CTA flags)
+    unsigned long long* flutflag;  // fused path: tagged per-CTA "LUT share written" flags
     unsigned long long* fpart;  // fused path: tagged split-K states [U][max_split][G][130]
     uint32_t* chist;            // fused path: local histograms [ctas][kNB]
     int pub_target, pub_cap;
@@ -193,15 +194,17 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     p.err = c.take<uint32_t>(64);
     p.bar = c.take<uint32_t>(64);
     p.ubar = c.take<uint32_t>(kUnitBarWords);
-    // the fused kernel's epoch-tagged exchange arena: a fixed offset and a
-    // fixed size (its worst case for this device), written only with tagged
-    // stores.  A reader accepts a word once its tag shows the call's epoch,
-    // so no plain data of any call (another geometry, the multi-kernel
-    // path) may ever land here: a stale plain word whose upper half equals
-    // a later epoch would be taken for that call's data.
+    // the fused kernel's exchange arena: a fixed offset and a fixed size (its
+    // worst case for this device).  Its tagged words are accepted once their
+    // tag shows the call's epoch, so no plain data of any call (another
+    // geometry, the multi-kernel path) may ever land on them: a stale plain
+    // word whose upper half equals a later epoch would be taken for that
+    // call's data.  The one plain region, the LUT, is read only after the
+    // flags of its writers show the call's epoch.
     p.fwin = c.take<unsigned long long>((size_t)sms * (kPubWin + 2));
     p.fpub = c.take<unsigned long long>((size_t)sms * kPubMaxCap * 2);
-    p.flut = c.take<unsigned long long>((size_t)sms * 256 * 32);                 // U <= sms units
+    p.flutflag = c.take<unsigned long long>((size_t)sms);
+    p.flut = c.take<float>((size_t)sms * 256 * 32);  // U <= sms units; plain, read only behind the flags
     p.fpart = c.take<unsigned long long>((size_t)2 * sms * kFusedMaxG * (2 + 128));  // U * (sms/U + 1) * G
     p.lut = c.take<float>((size_t)p.U * 256 * 32 * (p.heads ? 4 : 1));
     p.bounds = c.take<float>((size_t)p.U * (p.heads ? a->G : 1) * 32 * kLutParts * 2);
@@ -347,6 +350,7 @@ static int launch_fused(const lp_sparse_decode_args* a, const Plan& p, cudaStrea
     fp.out_stride_h = a->out_stride_h;
     fp.topk_out = a->topk_out;
     fp.lut = p.flut;
+    fp.lut_flag = p.flutflag;
     fp.sel_scores = p.sel_scores;
     fp.sel_stride = std::max(1, a->T_codes);
     fp.chist = p.chist;
