@@ -310,6 +310,9 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     __shared__ __align__(16) float s_qu[8 * 128];  // the unit's G query rows (fp32), loaded at start
     __shared__ int s_shift, s_bstar, s_above;
 
+    // launched with programmatic stream serialisation: nothing of this call
+    // touches memory before the previous kernel on the stream has completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = kFThreads / 32;
     const bool stamp = p.phase_ns != nullptr && blockIdx.x == 0 && tid == 0;

@@ -380,15 +380,20 @@ static int launch_fused(const lp_sparse_decode_args* a, const Plan& p, cudaStrea
     int rc = smem_opt_in(kernel, FusedSmem::kTotal, dev, opt);
     if (rc != LP_OK) return rc;
     cudaLaunchConfig_t cfg{};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    // programmatic dependent launch: the grid may be scheduled while the
+    // previous kernel on the stream finishes; every CTA's first instruction
+    // waits for that kernel to complete (griddepcontrol.wait)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(p.fused_ctas);
     cfg.blockDim = dim3(kFThreads);
     cfg.dynamicSmemBytes = FusedSmem::kTotal;
     cfg.stream = st;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, fp);
     if (e != cudaSuccess) return fail(LP_ERR_CUDA, std::string("sparse_decode_fused_kernel launch: ") + cudaGetErrorString(e));
     return LP_OK;
