@@ -617,9 +617,11 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             }
             return __fmul_rn(__int2float_rn(iacc), from_fx);
         };
+        // scores stay in shared memory (the plan keeps every CTA's share
+        // there); global memory gets them only on the exact slow path
         auto commit_score = [&](int lt, float sc) {
             if (keep_smem) s_scores[lt] = sc;
-            gsc[t_begin + lt] = sc;
+            else gsc[t_begin + lt] = sc;
             atomicAdd(&s_hist[score_bin(sc, bp.lo, bp.inv_w, kNB)], 1u);
         };
         for (int i = 0; i < ntiles; i += 2) {
@@ -1170,7 +1172,13 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         }
         if (overflow) {
             // exact slow path by the unit leader on the global scores, then
-            // one more unit barrier (every CTA of the unit saw the same count)
+            // one more unit barrier (every CTA of the unit saw the same
+            // count).  First every CTA stores its scores, one barrier.
+            if (keep_smem) {
+                float* gsc_w = p.sel_scores + (int64_t)u * p.sel_stride;
+                for (int lt = tid; lt < ntok; lt += kFThreads) gsc_w[t_begin + lt] = s_scores[lt];
+            }
+            if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
             if (cj == 0 && need > 0) {
                 if (tid == 0) atomicOr(p.err, LP_DEVERR_TIE_OVERFLOW);
                 uint32_t* h256 = reinterpret_cast<uint32_t*>(s_lut);
