@@ -1449,10 +1449,13 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             float* s_wf = s_wl + NW * 8;                       // [NW][8] rescale of each warp's state
             float* s_cm = s_wf + NW * 8;                       // [8] slice max
             float* s_cl = s_cm + 8;                            // [8] slice sum
+            // warps past nwu never had a tile (16 rows per tile, at most
+            // min(nrows, R) rows per chunk): they hold no state
+            const int nwu = min(NW, (min(nrows, R) + 15) / 16);
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int h = 2 * tq + e;
-                if (h < p.G) {
+                if (h < p.G && warp < nwu) {
                     float* dst = s_wacc + (warp * p.G + h) * D + gq;
 #pragma unroll
                     for (int mb = 0; mb < 8; ++mb) {
@@ -1471,7 +1474,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             // carry neutral values and write nothing).
             if (tid < ((NW * p.G + 31) & ~31)) {
                 const int g = tid / NW, w = tid - g * NW;
-                const bool live = g < p.G;
+                const bool live = g < p.G && w < nwu;
                 const float m = live ? s_wm[w * 8 + g] : -INFINITY;
                 float mx = m;
 #pragma unroll
@@ -1480,12 +1483,10 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 float l = live ? s_wl[w * 8 + g] * f : 0.f;
 #pragma unroll
                 for (int o = 1; o < NW; o <<= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-                if (live) {
-                    s_wf[w * 8 + g] = f;
-                    if (w == 0) {
-                        s_cm[g] = mx;
-                        s_cl[g] = l;
-                    }
+                if (live) s_wf[w * 8 + g] = f;
+                if (g < p.G && w == 0) {
+                    s_cm[g] = mx;
+                    s_cl[g] = l;
                 }
             }
             __syncthreads();
@@ -1493,8 +1494,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             for (int o = tid; o < p.G * D; o += kFThreads) {
                 const int g = o / D, d = o - g * D;
                 float a = 0.f;
-#pragma unroll 4
-                for (int w = 0; w < NW; ++w) a = fmaf(s_wacc[(w * p.G + g) * D + d], s_wf[w * 8 + g], a);
+                for (int w = 0; w < nwu; ++w) a = fmaf(s_wacc[(w * p.G + g) * D + d], s_wf[w * 8 + g], a);
                 st_tag(part + g * (2 + D) + 2 + d, __float_as_uint(a), s_epoch);
                 if (d == 0) {
                     st_tag(part + g * (2 + D), __float_as_uint(s_cm[g]), s_epoch);
