@@ -101,7 +101,7 @@ struct FusedParams {
     int pub_cap;         // slot capacity (0: no publishing, exchange path only)
     unsigned long long* part;  // [U][max_split][G][2+128] tagged split-K states (max, sum, P.V)
     int max_split;
-    uint32_t* bar;       // [U] unit barrier words (persistent, self-resetting)
+    unsigned long long* bar;  // [U] unit barrier words (persistent; epoch-tagged arrival counts)
     unsigned long long* epoch_ctr;  // persistent launch counter: this call's epoch tags its exchanged words
     uint32_t* err;
     unsigned long long* phase_ns;  // optional [8] globaltimer stamps (CTA 0)
@@ -145,42 +145,6 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Barrier among the n CTAs of one selection unit (all resident: cooperative
-// launch).  The unit's word flips its top bit once per barrier (the unit's
-// first CTA adds 2^31 - (n-1), the others 1), so its low bits return to zero
-// and it needs no reset between barriers or calls, whatever n is.  Arrival
-// is a fire-and-forget release reduction; thread 0 tracks the expected top
-// bit in `phase` (read once at kernel start, before the first arrival) and
-// polls until the word shows it.  Units never wait for one another.
-// Bounded: returns false on timeout (after recording the error bit).
-__device__ __forceinline__ bool unit_barrier(uint32_t* bar, int n, bool first, uint32_t& phase, uint32_t* err) {
-    __shared__ int s_ok;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const uint32_t inc = first ? (0x80000000u - (uint32_t)(n - 1)) : 1u;
-        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(bar), "r"(inc) : "memory");
-        phase ^= 0x80000000u;
-        int ok = 1;
-        const long long t0 = clock64();
-        while ((ld_acquire_u32(bar) & 0x80000000u) != phase) {
-            if (clock64() - t0 > kWaitCycles) {
-                atomicOr(err, LP_DEVERR_WAIT_TIMEOUT);
-                ok = 0;
-                break;
-            }
-        }
-        __threadfence();
-        s_ok = ok;
-    }
-    __syncthreads();
-    return s_ok != 0;
-}
 
 // Words exchanged between the CTAs of a unit carry the call's epoch in their
 // upper 32 bits; a reader polls a word until it shows the epoch.  A 64-bit
@@ -203,6 +167,48 @@ __device__ __forceinline__ unsigned long long ld_tag_acquire(const unsigned long
 }
 __device__ __forceinline__ bool tag_ok(unsigned long long x, uint32_t epoch) {
     return (uint32_t)(x >> 32) == epoch;
+}
+
+// Barrier among the n CTAs of one selection unit (all resident: cooperative
+// launch).  The unit's 64-bit word holds (epoch << 32 | arrivals of this
+// call): the first arrival of a call replaces a word that still shows an
+// older epoch, later ones add 1 (compare-and-swap, lock-free: a failed swap
+// means another CTA's arrival succeeded).  Barrier number nb of the call is
+// complete once the word shows this epoch and nb*n arrivals.  Nothing is
+// read before the first arrival and nothing needs a reset between calls,
+// also after a call that timed out.  Units never wait for one another.
+// Bounded: returns false on timeout (after recording the error bit).
+__device__ __forceinline__ bool unit_barrier(unsigned long long* bar, int n, int& nb, uint32_t epoch, uint32_t* err) {
+    __shared__ int s_ok;
+    ++nb;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();  // the CTA's writes before its arrival
+        unsigned long long old = ld_tag(bar);
+        while (true) {
+            const unsigned long long nv =
+                tag_ok(old, epoch) ? old + 1ull : (((unsigned long long)epoch << 32) | 1ull);
+            const unsigned long long prev = atomicCAS(bar, old, nv);
+            if (prev == old) break;
+            old = prev;
+        }
+        const uint32_t target = (uint32_t)(nb * n);
+        int ok = 1;
+        const long long t0 = clock64();
+        while (true) {
+            const unsigned long long v = ld_tag_acquire(bar);
+            if (tag_ok(v, epoch) && (uint32_t)v >= target) break;
+            if (clock64() - t0 > kWaitCycles) {
+                atomicOr(err, LP_DEVERR_WAIT_TIMEOUT);
+                ok = 0;
+                break;
+            }
+        }
+        __threadfence();
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
 }
 
 // dst[i] = value of src[i] for i in [0, n), each polled until it carries
@@ -320,13 +326,10 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
 
     int u, cj, cn;
     fused_cta_unit(blockIdx.x, gridDim.x, p.U, &u, &cj, &cn);
-    uint32_t* ubar = p.bar + u;
-    uint32_t bphase = 0;  // top bit of the unit's barrier word (thread 0), read before the first arrival
+    unsigned long long* ubar = p.bar + u;
+    int nbar = 0;  // unit barriers passed in this call (uniform over the unit's CTAs)
     __shared__ uint32_t s_epoch;
     if (tid == 0) {
-        uint32_t v;
-        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ubar) : "memory");
-        bphase = v & 0x80000000u;
         // every CTA of every call adds 1: in call n the old values lie in
         // [G*(n-1), G*n) for G = gridDim.x, whatever the order and even if a
         // CTA of an earlier call returned early
@@ -1055,7 +1058,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         float2* s_tloc = reinterpret_cast<float2*>(s_lut);  // this CTA's tie-bin tokens (<= kTieCap)
         // the unit histogram: sum of its CTAs' local histograms (published
         // with plain stores in phase B, visible after this barrier)
-        if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
+        if (!unit_barrier(ubar, cn, nbar, s_epoch, p.err)) return;
         for (int i = tid; i < kNB; i += kFThreads) {
             uint32_t c = 0u;
             for (int j = 0; j < cn; ++j) c += __ldcg(p.chist + (int64_t)(ubase + j) * kNB + i);
@@ -1102,7 +1105,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         }
         const int nloc = min(s_ntie_loc, kTieCap);
         for (int i = tid; i < nloc; i += kFThreads) p.tie_buf[(int64_t)blockIdx.x * kTieCap + i] = s_tloc[i];
-        if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
+        if (!unit_barrier(ubar, cn, nbar, s_epoch, p.err)) return;
 
         // ---- ties (redundant per CTA, no barrier) ----
         float* s_tk = reinterpret_cast<float*>(s_lut);                      // tie keys  [kTieCap]
@@ -1178,7 +1181,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 float* gsc_w = p.sel_scores + (int64_t)u * p.sel_stride;
                 for (int lt = tid; lt < ntok; lt += kFThreads) gsc_w[t_begin + lt] = s_scores[lt];
             }
-            if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
+            if (!unit_barrier(ubar, cn, nbar, s_epoch, p.err)) return;
             if (cj == 0 && need > 0) {
                 if (tid == 0) atomicOr(p.err, LP_DEVERR_TIE_OVERFLOW);
                 uint32_t* h256 = reinterpret_cast<uint32_t*>(s_lut);
@@ -1239,7 +1242,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                     __syncthreads();
                 }
             }
-            if (!unit_barrier(ubar, cn, cj == 0, bphase, p.err)) return;
+            if (!unit_barrier(ubar, cn, nbar, s_epoch, p.err)) return;
             if (ntie > kTieCap && need > 0) {
                 // winners of this unit are the bits the leader set
                 for (int w = w_begin + tid; w < w_end; w += kFThreads) {

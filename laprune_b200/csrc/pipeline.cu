@@ -85,7 +85,7 @@ struct Plan {
     uint32_t* done_sel;
     uint32_t* done_att;
     uint32_t* bar;
-    uint32_t* ubar;
+    unsigned long long* ubar;
     uint32_t* cta_count;
     uint32_t* cta_ties;
     unsigned long long* fpub;   // fused path: tagged candidates [ctas][pub_cap][2]
@@ -99,7 +99,7 @@ struct Plan {
 };
 
 static constexpr int kScoreThreads = 512;
-static constexpr int kUnitBarWords = 384;     // one barrier word per unit of the fused path
+static constexpr int kUnitBarWords = 192;     // one 64-bit barrier word per unit of the fused path
 static constexpr size_t kPersistBytes = 2048; // error word, grid barrier, unit barriers
 static constexpr int kGroupStages = 8;
 static constexpr int kHeadsStages = 4;
@@ -193,7 +193,7 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     // words (512 B .. 2048 B), whose values must survive between calls
     p.err = c.take<uint32_t>(64);
     p.bar = c.take<uint32_t>(64);
-    p.ubar = c.take<uint32_t>(kUnitBarWords);
+    p.ubar = c.take<unsigned long long>(kUnitBarWords);
     // the fused kernel's exchange arena: a fixed offset and a fixed size (its
     // worst case for this device).  Its tagged words are accepted once their
     // tag shows the call's epoch, so no plain data of any call (another
