@@ -13,8 +13,9 @@
 // (all G heads of the KV group in KV_GROUP mode).  Partial softmax states
 // (max, sum, P.V) of the slices are merged by the unit's last CTA.
 //
-// The row list of a slice is recovered from the selection bitmap with a
-// block-wide prefix popcount, so no compacted index list is materialised.
+// The row list of a slice comes from the units' compacted selections (made
+// in parallel before this kernel), or, without them, from the selection
+// bitmap with a block-wide prefix popcount.
 #pragma once
 #include <cub/block/block_scan.cuh>
 #include "common.cuh"
@@ -32,6 +33,7 @@ struct AttnParams {
     int64_t v_stride_b, v_stride_h, v_stride_t;
     const uint32_t* bitmap;
     int64_t bm_stride;
+    const int32_t* toplist;  // [U][k] selected tokens in ascending order (NULL: recover them from the bitmap)
     int Hkv, G, HG;     // HG = query heads attended per unit (G or 1)
     int c0, c1;         // candidate window (bitmap range)
     int n_sink, k, local_start, n_local;
@@ -113,7 +115,10 @@ __global__ void __launch_bounds__(THREADS) sparse_attn_kernel(AttnParams p) {
     // selected part: ranks [n_sink, n_sink + k) are the set bits in order
     const int j0 = max(r0, p.n_sink) - p.n_sink;
     const int j1 = min(r1, p.n_sink + p.k) - p.n_sink;
-    if (j0 < j1) {
+    if (j0 < j1 && p.toplist) {
+        const int32_t* tl = p.toplist + (int64_t)u * p.k;
+        for (int j = j0 + tid; j < j1; j += THREADS) s_rows[p.n_sink + j - r0] = tl[j];
+    } else if (j0 < j1) {
         const uint32_t* bm = p.bitmap + (int64_t)u * p.bm_stride;
         const int wlo = p.c0 >> 5, whi = (p.c1 + 31) >> 5;
         const int nwords = whi - wlo;

@@ -75,6 +75,10 @@ struct Plan {
     float* bounds;
     float* sel_scores;
     uint32_t* bitmap;
+    int nchunk;        // multi-kernel path: 256-word chunks of the candidate window
+    int* chunk_cnt;    // [Usel][nchunk] selected tokens per chunk
+    int32_t* toplist;  // [Usel][k] selected tokens, ascending
+    bool compact;      // the multi-kernel path compacts the selection (top-k output, per-head attention)
     float2* tie_buf;
     int4* info;
     float* part;
@@ -210,6 +214,10 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     p.bounds = c.take<float>((size_t)p.U * (p.heads ? a->G : 1) * 32 * kLutParts * 2);
     p.sel_scores = c.take<float>((size_t)p.Usel * std::max(1, a->T_codes));
     p.bitmap = c.take<uint32_t>((size_t)p.Usel * p.bm_words);
+    p.nchunk = std::max(1, (nwords_cand + kCompactWords - 1) / kCompactWords);
+    p.chunk_cnt = c.take<int>((size_t)p.Usel * p.nchunk);
+    p.toplist = c.take<int32_t>((size_t)p.Usel * std::max(a->topk, 1));
+    p.compact = a->topk > 0 && p.ncand > 0 && (a->topk_out != nullptr || (a->out != nullptr && p.per_head));
     p.tie_buf = c.take<float2>((size_t)std::max(p.Usel, p.fused_ctas) * kTieCap);
     p.info = c.take<int4>((size_t)p.Usel);
     p.part = c.take<float>((size_t)std::max((size_t)p.Uatt * p.nsplit * p.HG, (size_t)p.U * p.fused_max_split * a->G) *
@@ -268,6 +276,7 @@ static int launch_attn(const lp_sparse_decode_args* a, const Plan& p, cudaStream
     ap.v_stride_t = a->v_stride_t;
     ap.bitmap = p.bitmap;
     ap.bm_stride = p.bm_words;
+    ap.toplist = p.compact ? (a->topk_out ? a->topk_out : p.toplist) : nullptr;
     ap.Hkv = a->Hkv;
     ap.G = a->G;
     ap.HG = p.HG;
@@ -573,9 +582,19 @@ int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t wor
         select_kernel<256><<<dim3(p.sel_ctas_per_unit, p.Usel), 256, sel_smem, st>>>(sel);
         rc = check_launch("select_kernel");
         if (rc != LP_OK) return rc;
-        if (a->topk_out && a->topk > 0) {
-            compact_kernel<256><<<p.Usel, 256, 0, st>>>(p.bitmap, p.bm_words, p.c0, p.c1, a->topk, a->topk_out);
-            rc = check_launch("compact_kernel");
+        // the selected tokens in ascending order: the caller's top-k output,
+        // and the attention's row lists when there are many selection units
+        // (per query head: the attention CTAs would each scan a whole bitmap)
+        if (p.compact) {
+            int32_t* list = a->topk_out ? a->topk_out : p.toplist;
+            const dim3 cg(p.nchunk, p.Usel);
+            bitmap_chunk_count_kernel<<<cg, kCompactWords, 0, st>>>(p.bitmap, p.bm_words, p.c0, p.c1, p.nchunk,
+                                                                   p.chunk_cnt);
+            rc = check_launch("bitmap_chunk_count_kernel");
+            if (rc != LP_OK) return rc;
+            bitmap_compact_kernel<<<cg, kCompactWords, 0, st>>>(p.bitmap, p.bm_words, p.c0, p.c1, a->topk, p.nchunk,
+                                                               p.chunk_cnt, list);
+            rc = check_launch("bitmap_compact_kernel");
             if (rc != LP_OK) return rc;
         }
     } else {

@@ -18,6 +18,7 @@
 //      exact 4 x 8-bit radix select on the float keys of bin b* instead.
 #pragma once
 #include <cub/block/block_scan.cuh>
+#include <cub/block/block_reduce.cuh>
 #include "score.cuh"
 
 namespace lp {
@@ -265,41 +266,59 @@ __global__ void __launch_bounds__(THREADS) select_kernel(SelectParams p) {
     }
 }
 
-// Writes the selected indices of every unit in ascending order (int32).
-template <int THREADS>
-__global__ void __launch_bounds__(THREADS) compact_kernel(const uint32_t* bitmap, int64_t bm_stride,
-                                                          int c0, int c1, int k, int32_t* out) {
-    using Scan = cub::BlockScan<int, THREADS>;
+// The same compaction in parallel, two launches of (chunks, units) CTAs:
+// selected-token counts per 256-word chunk of the candidate window, then
+// every chunk writes its tokens at the count of the chunks before it.
+constexpr int kCompactWords = 256;  // bitmap words per chunk (one per thread)
+
+__device__ __forceinline__ uint32_t window_bits(const uint32_t* bm, int w, int c0, int c1) {
+    uint32_t bits = bm[w];
+    const int lo = w * 32, hi = lo + 32;
+    if (lo < c0) bits &= ~0u << (c0 - lo);
+    if (hi > c1) bits &= (c1 - lo) >= 32 ? ~0u : ((1u << (c1 - lo)) - 1u);
+    return bits;
+}
+
+__global__ void __launch_bounds__(kCompactWords) bitmap_chunk_count_kernel(const uint32_t* bitmap, int64_t bm_stride,
+                                                                           int c0, int c1, int nchunk, int* cnt) {
+    using Reduce = cub::BlockReduce<int, kCompactWords>;
+    __shared__ typename Reduce::TempStorage tmp;
+    const int usel = blockIdx.y, ch = blockIdx.x;
+    const int wlo = c0 >> 5, whi = (c1 + 31) >> 5;
+    const int w = wlo + ch * kCompactWords + threadIdx.x;
+    const uint32_t bits = w < whi ? window_bits(bitmap + (int64_t)usel * bm_stride, w, c0, c1) : 0u;
+    const int total = Reduce(tmp).Sum(__popc(bits));
+    if (threadIdx.x == 0) cnt[(int64_t)usel * nchunk + ch] = total;
+}
+
+__global__ void __launch_bounds__(kCompactWords) bitmap_compact_kernel(const uint32_t* bitmap, int64_t bm_stride,
+                                                                       int c0, int c1, int k, int nchunk,
+                                                                       const int* cnt, int32_t* out) {
+    using Scan = cub::BlockScan<int, kCompactWords>;
     __shared__ typename Scan::TempStorage tmp;
     __shared__ int s_base;
-    const int usel = blockIdx.x;
-    const uint32_t* bm = bitmap + (int64_t)usel * bm_stride;
-    int32_t* o = out + (int64_t)usel * k;
+    const int usel = blockIdx.y, ch = blockIdx.x;
+    if (threadIdx.x < 32) {
+        int b = 0;
+        for (int j = threadIdx.x; j < ch; j += 32) b += cnt[(int64_t)usel * nchunk + j];
+        b = __reduce_add_sync(0xffffffffu, b);
+        if (threadIdx.x == 0) s_base = b;
+    }
     const int wlo = c0 >> 5, whi = (c1 + 31) >> 5;
-    if (threadIdx.x == 0) s_base = 0;
-    __syncthreads();
-    for (int wb = wlo; wb < whi; wb += THREADS) {
-        const int w = wb + threadIdx.x;
-        uint32_t bits = 0;
-        if (w < whi) {
-            bits = bm[w];
-            const int lo = w * 32, hi = lo + 32;
-            if (lo < c0) bits &= ~0u << (c0 - lo);
-            if (hi > c1) bits &= (c1 - lo) >= 32 ? ~0u : ((1u << (c1 - lo)) - 1u);
-        }
-        int rank, total;
-        Scan(tmp).ExclusiveSum(__popc(bits), rank, total);
-        int r = s_base + rank;
-        while (bits) {
-            const int bit = __ffs(bits) - 1;
-            bits &= bits - 1;
-            if (r < k) o[r] = w * 32 + bit;
-            ++r;
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) s_base += total;
-        __syncthreads();
+    const int w = wlo + ch * kCompactWords + threadIdx.x;
+    uint32_t bits = w < whi ? window_bits(bitmap + (int64_t)usel * bm_stride, w, c0, c1) : 0u;
+    int rank, total;
+    Scan(tmp).ExclusiveSum(__popc(bits), rank, total);
+    __syncthreads();  // s_base
+    int r = s_base + rank;
+    int32_t* o = out + (int64_t)usel * k;
+    while (bits) {
+        const int bit = __ffs(bits) - 1;
+        bits &= bits - 1;
+        if (r < k) o[r] = w * 32 + bit;
+        ++r;
     }
 }
+
 
 }  // namespace lp
