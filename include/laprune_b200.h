@@ -140,6 +140,11 @@ typedef struct lp_sparse_decode_args {
 #define LP_FLAG_NO_FUSED 1 /* use the multi-kernel path even when the fused kernel applies */
 #define LP_FLAG_EXCHANGE_SELECT 2 /* fused kernel: settle the top-k through the tie exchange,
                                     not the published-candidate union */
+#define LP_FLAG_TEST_WAIT_TIMEOUT 4 /* for testing the error path (fused kernel only): CTA 0
+                                      withholds its share of its unit's table, so the unit's
+                                      waits for it give up after about 2^20 cycles and the
+                                      call reports LP_DEVERR_WAIT_TIMEOUT (its outputs are
+                                      then undefined); no fault, no hang */
 
 /* Workspace bytes needed by lp_sparse_decode for this geometry. */
 size_t lp_sparse_decode_workspace_size(const lp_sparse_decode_args* a);

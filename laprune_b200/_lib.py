@@ -17,6 +17,7 @@ LP_SELECT_KV_GROUP, LP_SELECT_QUERY_HEAD = 0, 1
 LP_DEVERR_WAIT_TIMEOUT, LP_DEVERR_TIE_OVERFLOW = 1, 2
 LP_FLAG_NO_FUSED = 1
 LP_FLAG_EXCHANGE_SELECT = 2
+LP_FLAG_TEST_WAIT_TIMEOUT = 4
 
 _c_i32, _c_i64, _c_p, _c_f = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float
 

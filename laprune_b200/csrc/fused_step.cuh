@@ -101,6 +101,7 @@ struct FusedParams {
     int pub_cap;         // slot capacity (0: no publishing, exchange path only)
     unsigned long long* part;  // [U][max_split][G][2+128] tagged split-K states (max, sum, P.V)
     int max_split;
+    int test_timeout;          // LP_FLAG_TEST_WAIT_TIMEOUT: CTA 0 withholds its LUT flag; short LUT waits
     unsigned long long* bar;  // [U] unit barrier words (persistent; epoch-tagged arrival counts)
     unsigned long long* epoch_ctr;  // persistent launch counter: this call's epoch tags its exchanged words
     uint32_t* err;
@@ -469,7 +470,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     // the CTA's LUT share is out: every thread's stores precede the barrier
     // that ended the last chunk; the fence makes them visible GPU-wide
     // before the flag
-    if (tid == 0) {
+    if (tid == 0 && !(p.test_timeout && blockIdx.x == 0)) {
         __threadfence();
         st_tag(p.lut_flag + blockIdx.x, 1u, s_epoch);
     }
@@ -502,9 +503,10 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             bool ok = true;
             if (tid < cn) {
                 const unsigned long long* fl = p.lut_flag + (blockIdx.x - cj) + tid;  // the unit's CTAs
+                const long long lim = p.test_timeout ? (1ll << 20) : kWaitCycles;
                 const long long t0 = clock64();
                 while (!tag_ok(ld_tag_acquire(fl), s_epoch)) {
-                    if (clock64() - t0 > kWaitCycles) {
+                    if (clock64() - t0 > lim) {
                         atomicOr(p.err, LP_DEVERR_WAIT_TIMEOUT);
                         ok = false;
                         break;

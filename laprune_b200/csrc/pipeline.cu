@@ -374,6 +374,7 @@ static int launch_fused(const lp_sparse_decode_args* a, const Plan& p, cudaStrea
     fp.cta_count = p.cta_count;
     fp.part = p.fpart;
     fp.max_split = p.fused_max_split;
+    fp.test_timeout = (a->flags & LP_FLAG_TEST_WAIT_TIMEOUT) ? 1 : 0;
     fp.bar = p.ubar;
     fp.epoch_ctr = reinterpret_cast<unsigned long long*>(p.bar);
     fp.err = p.err;

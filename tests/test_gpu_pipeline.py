@@ -289,3 +289,26 @@ def test_fused_calls_after_other_paths_on_a_fresh_shared_workspace():
             torch.cuda.synchronize()
             assert torch.equal(r.topk, ref.topk) and torch.equal(r.out, ref.out)
     assert ops.device_errors(shared, dev) & 1 == 0
+
+
+def test_wait_timeout_is_reported_and_the_next_call_recovers():
+    # failure detection without a fault: with LP_FLAG_TEST_WAIT_TIMEOUT one
+    # CTA withholds its share of its unit's table, the unit's bounded waits
+    # give up, the error bit is read back on the host, and the next call on
+    # the same workspace gives the result of a clean workspace
+    dev = _dev()
+    C, codes, K, V, q = [t.to(dev) for t in _rand_case(77, 1, 8, 4, 8192)]
+    kw = dict(topk=256, sink=4, local=64)
+    ref = ops.sparse_decode(q, C, codes, K, V, return_topk=True, **kw)
+    out = torch.empty_like(ref.out)
+    a = ops.build_args(q, C, codes, K, V, out=out, **kw)
+    lib = _lib.load()
+    ws = torch.zeros(lib.lp_sparse_decode_workspace_size(ctypes.byref(a)), dtype=torch.uint8, device=dev)
+    a.flags |= _lib.LP_FLAG_TEST_WAIT_TIMEOUT
+    with torch.cuda.device(dev):
+        _lib.check(lib.lp_sparse_decode(ctypes.byref(a), ws.data_ptr(), ws.numel(), ops._stream_handle(dev)))
+    assert ops.device_errors(ws, dev) & _lib.LP_DEVERR_WAIT_TIMEOUT
+    again = ops.sparse_decode(q, C, codes, K, V, return_topk=True, ws=ws, **kw)
+    torch.cuda.synchronize()
+    assert ops.device_errors(ws, dev) == 0
+    assert torch.equal(again.topk, ref.topk) and torch.equal(again.out, ref.out)
