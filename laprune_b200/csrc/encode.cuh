@@ -54,7 +54,9 @@ struct EncodeParams {
     const float* smax;         // [S][32][4]    per stage: max ||C||^2, max ||C||, 0, 0
     uint8_t* codes;
     int64_t cs_b, cs_h, cs_t;  // bytes
-    int ctas_per_set;          // ceil(vectors of a set / 128)
+    int ctas_per_set;          // ceil(vectors of a set / rows_per_cta)
+    int rows_per_cta;          // 128, or 64 / 32 when the sets have too few vectors to fill the GPU
+                               // (the MMA still runs 128 rows; the others are zero)
     int force_exact;           // recompute every codeword exactly (testing)
     uint32_t* err;
 };
@@ -196,7 +198,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     const int set = blockIdx.x / p.ctas_per_set;
     const int tile = blockIdx.x - set * p.ctas_per_set;
     const int nvec_set = p.per_head ? p.B * p.T : p.B * p.H * p.T;  // vectors of this set
-    const int v0 = tile * kEncRows;
+    const int v0 = tile * p.rows_per_cta;
     const float* nrms = p.nrm + (int64_t)set * kEncM * kEncK;
     const float* smx = p.smax + (int64_t)set * kEncM * 4;
 
@@ -248,7 +250,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     for (int e = tid; e < kEncRows * (kEncD / 4); e += kEncThreads) {
         const int n = e >> 5, d = (e & 31) * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (v0 + n < nvec_set) {
+        if (n < p.rows_per_cta && v0 + n < nvec_set) {
             int b, h, t;
             vec_bht(v0 + n, &b, &h, &t);
             const XT* xr = reinterpret_cast<const XT*>(p.x) + (int64_t)b * p.xs_b + (int64_t)h * p.xs_h + (int64_t)t * p.xs_t;
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     // 32q .. 32q+31) and the 64 columns of group cg = w >> 2
     const int q4 = warp & 3, cg = warp >> 2;
     const int row = q4 * 32 + lane;
-    const bool row_valid = v0 + row < nvec_set;
+    const bool row_valid = row < p.rows_per_cta && v0 + row < nvec_set;
     __shared__ uint8_t* s_cptr[kEncRows];         // the row's 32 codes in the output (null: no vector)
     __shared__ __align__(16) uint8_t s_codes[kEncRows][kEncM];
     if (cg == 0) {

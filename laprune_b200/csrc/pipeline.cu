@@ -685,7 +685,12 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
     ep.cs_b = a->codes_stride_b;
     ep.cs_h = a->codes_stride_h;
     ep.cs_t = a->codes_stride_t;
-    ep.ctas_per_set = (int)((nvec_set + kEncRows - 1) / kEncRows);
+    // fewer rows per CTA while that still leaves SMs idle: the stages are a
+    // serial chain per CTA, so more, smaller CTAs finish sooner
+    int rows = kEncRows;
+    while (rows > 32 && nsets * ((nvec_set + rows / 2 - 1) / (rows / 2)) <= sm_count(dev)) rows /= 2;
+    ep.rows_per_cta = rows;
+    ep.ctas_per_set = (int)((nvec_set + rows - 1) / rows);
     ep.force_exact = (a->flags & LP_ENCODE_FLAG_EXACT) ? 1 : 0;
     ep.err = err;
     // the codebooks as a 2-D tensor [S*32*256 rows][128 fp32], copied in boxes
