@@ -66,6 +66,12 @@ def _encoding_codebooks(manager: AQLayerCodebookManager, layer_idx: int, Hkv: in
     return manager.group_codebooks(layer_idx, [h // cfg.heads_per_group for h in range(Hkv)])
 
 
+def _on_device(manager, device) -> AQLayerCodebookManager:
+    # a per-device manager (ShardedAQLayerCodebookManager) resolves to the
+    # one holding the codebooks on the tensors' device
+    return manager.for_device(device) if hasattr(manager, "for_device") else manager
+
+
 def _decode_attention(self_attn, manager: AQLayerCodebookManager, layer_idx: int, Q_rope: torch.Tensor,
                       K_rope: torch.Tensor, vals_full: torch.Tensor, aq_cache: dict, conf: dict) -> torch.Tensor:
     """Sparse attention of the last query token over the AQ-selected keys,
@@ -75,6 +81,7 @@ def _decode_attention(self_attn, manager: AQLayerCodebookManager, layer_idx: int
     ``aq_cache["codes"]`` ``[B, Hkv, cap, M]`` uint8 with ``seq_len`` valid.
     """
     B, H, Tq, D = Q_rope.shape
+    manager = _on_device(manager, Q_rope.device)
     scoring_m = int(conf.get("aq_scoring_m", 32))
     if scoring_m != 32:
         raise ValueError(f"aq_scoring_m must be 32, got {scoring_m}")
@@ -162,6 +169,7 @@ def _prepare_aq_cache(self, manager: AQLayerCodebookManager, layer_idx: int, key
     after prefill."""
     if need_recon:
         raise NotImplementedError("key reconstruction (aq_use_exact_true_score=False) is not on the decode path")
+    manager = _on_device(manager, keys.device)
     conf = getattr(self, "draft_kwargs", {}) or {}
     B, H, T, d = keys.shape
     cfg = manager.layer_cfgs.get(layer_idx)

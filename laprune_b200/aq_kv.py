@@ -29,7 +29,7 @@ import torch
 
 from . import ops
 
-__all__ = ["AQLayerConfig", "AQLayerCodebookManager"]
+__all__ = ["AQLayerConfig", "AQLayerCodebookManager", "ShardedAQLayerCodebookManager"]
 
 
 @dataclass
@@ -213,3 +213,59 @@ class AQLayerCodebookManager:
             raise ValueError(f"AQ shape mismatch: codebook={tuple(cb.shape)}, q={tuple(q.shape)}, codes={tuple(codes.shape)}")
         s = self._scores(q.reshape(kv_heads, group, -1), codes.reshape(kv_heads, 1, n_tokens, m_codes), cb)
         return s.reshape(q_heads, n_tokens).to(self.dtype)
+
+
+class ShardedAQLayerCodebookManager:
+    """One ``AQLayerCodebookManager`` per device, each loading the same
+    codebook directory (aq_kv.py:702-803).  For a model spread over several
+    GPUs layer by layer: every call runs on the device of its input tensor,
+    so no codebook crosses devices.  The first device's manager is created
+    at once, the others on first use."""
+
+    def __init__(self, layer_cfgs: Dict[int, AQLayerConfig], aq_codebook_dir: str, devices=None,
+                 dtype: torch.dtype = torch.float16) -> None:
+        self.layer_cfgs = layer_cfgs
+        self.aq_codebook_dir = aq_codebook_dir
+        self.dtype = dtype
+        if not devices:
+            devices = [torch.device("cuda", torch.cuda.current_device())]
+        self.devices = sorted({torch.device(d) for d in devices}, key=str)
+        self._mgr_by_device: Dict[str, AQLayerCodebookManager] = {}
+        self._default_device = self.devices[0]
+        self._default_mgr = self.for_device(self._default_device)
+
+    def for_device(self, device) -> AQLayerCodebookManager:
+        """The manager holding the codebooks on ``device`` (loaded on first use)."""
+        key = str(torch.device(device))
+        mgr = self._mgr_by_device.get(key)
+        if mgr is None:
+            mgr = AQLayerCodebookManager(self.layer_cfgs, device=torch.device(device), dtype=self.dtype)
+            mgr.load(self.aq_codebook_dir)
+            self._mgr_by_device[key] = mgr
+        return mgr
+
+    def _on(self, t) -> AQLayerCodebookManager:
+        return self.for_device(t.device if isinstance(t, torch.Tensor) else self._default_device)
+
+    def codebooks(self, layer_idx: int, group_idx: int = 0) -> torch.Tensor:
+        return self._default_mgr.codebooks(layer_idx, group_idx)
+
+    def encode_keys(self, layer_idx: int, head_idx: int, keys: torch.Tensor, **kwargs) -> torch.Tensor:
+        return self._on(keys).encode_keys(layer_idx, head_idx, keys, **kwargs)
+
+    def encode_keys_batch(self, layer_idx: int, group_idx: int, keys: torch.Tensor, **kwargs) -> torch.Tensor:
+        return self._on(keys).encode_keys_batch(layer_idx, group_idx, keys, **kwargs)
+
+    def reconstruct(self, layer_idx: int, head_idx: int, codes: torch.Tensor) -> torch.Tensor:
+        return self._on(codes).reconstruct(layer_idx, head_idx, codes)
+
+    def approx_inner_product(self, layer_idx: int, head_idx: int, q: torch.Tensor, codes: torch.Tensor) -> torch.Tensor:
+        return self._on(q).approx_inner_product(layer_idx, head_idx, q, codes)
+
+    def approx_inner_product_multihead(self, layer_idx: int, q: torch.Tensor, codes: torch.Tensor) -> torch.Tensor:
+        return self._on(q).approx_inner_product_multihead(layer_idx, q, codes)
+
+    def approx_inner_product_multihead_gqa(self, layer_idx: int, q: torch.Tensor, codes: torch.Tensor,
+                                           num_kv_group: int, scoring_m: int = 32) -> torch.Tensor:
+        return self._on(q).approx_inner_product_multihead_gqa(layer_idx, q, codes, num_kv_group,
+                                                               scoring_m=scoring_m)

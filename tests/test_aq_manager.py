@@ -93,3 +93,19 @@ def test_kv_cache_append_grows_and_keeps_the_prefix():
         assert kv.shape == (2, 2, total, 8) and a.k_cache_len == total and a.k_cache_capacity >= total
         assert torch.equal(kv, torch.cat(ks, 2)) and torch.equal(vv, torch.cat(vs, 2))
     assert a.k_cache_capacity == 80  # 20 -> 20 (first: max(total, 16)), 21 -> 40, 52 -> 80
+
+
+def test_sharded_manager_loads_one_copy_per_device_on_first_use(tmp_path):
+    from laprune_b200.aq_kv import ShardedAQLayerCodebookManager
+    src = _mgr(layers=(0,), hpg=8, num_heads=8)
+    cb = torch.randn((32, 256, 128), generator=torch.Generator().manual_seed(5))
+    src.set_codebooks(0, 0, cb)
+    src.save(str(tmp_path))
+    sh = ShardedAQLayerCodebookManager({0: AQLayerConfig(M=32, K=256, d=128, heads_per_group=8, num_heads=8)},
+                                       str(tmp_path), devices=["cpu"])
+    assert list(sh._mgr_by_device) == ["cpu"]
+    assert sh.for_device("cpu") is sh.for_device(torch.device("cpu"))
+    assert torch.equal(sh.codebooks(0, 0), cb)
+    assert sh._on(torch.zeros(1)) is sh.for_device("cpu")
+    with pytest.raises(NotImplementedError):
+        sh.encode_keys(0, 0, torch.zeros(4, 128), icm_iters=2)

@@ -115,3 +115,19 @@ def test_code_cache_follows_prefill_and_grouped_decode():
     for h in range(Hkv):
         want = oracle.encode_greedy(keys[0, h, :n].float().numpy(), cb[h].numpy())
         assert np.array_equal(got[h], want)
+
+
+def test_sharded_manager_drives_the_decode_hook(golden_dir, tmp_path):
+    from laprune_b200.aq_kv import ShardedAQLayerCodebookManager
+    fix = np.load(golden_dir / "decode_hook.npz")
+    dh = syn.decode_hook_case(11)
+    _mgr(dh["cb"], dh["Hq"]).save(str(tmp_path))
+    sh = ShardedAQLayerCodebookManager({0: AQLayerConfig(M=32, K=256, d=128, heads_per_group=dh["Hq"],
+                                                         num_heads=dh["Hq"])}, str(tmp_path), devices=[_dev()])
+    dev = _dev()
+    conf = {"mask_out": 0.98, "min_remain": 20, "sink_size": 4, "local_window": 64, "aq_scoring_m": 32}
+    self_attn = types.SimpleNamespace(total_seq_len=dh["T"], o_proj=torch.nn.Identity())
+    out = aqe._decode_attention(self_attn, sh, 0, dh["q"].to(dev).half(), dh["keys"].to(dev).half(),
+                                dh["vals"].to(dev).half(), {"codes": dh["codes"].to(dev), "seq_len": dh["T"]}, conf)
+    torch.cuda.synchronize()
+    assert np.abs(out.float().cpu().numpy() - fix["out_sink4"]).max() <= 2e-2
