@@ -1,9 +1,10 @@
 """Drop-in for the reference's decode hook (laprune/llm/modifiers/aq_evaluation.py).
 
-``_decode_attention`` (aq_evaluation.py:146-253), ``_prepare_aq_cache``
-(:324-494) and ``_kv_cache_append`` (:65-112) with the reference's
-signatures, config keys and cache dictionaries, the compute on this
-package's kernels:
+``self_attn_forward`` (aq_evaluation.py:279-322), ``_decode_attention``
+(:146-253), ``_prepare_aq_cache`` (:324-494), ``_kv_cache_append``
+(:65-112), ``_cached_position_ids`` (:56-63) and ``do_sdpa_attn``
+(laprune/attention.py:21-73) with the reference's signatures, config keys
+and cache dictionaries, the sparse path on this package's kernels:
 
 * one decode token (Tq == 1): per-query-head LUT scores over the candidate
   window, top-k of the reference's size (``mask_out`` / ``min_remain``), the
@@ -16,7 +17,8 @@ package's kernels:
   (``ops.encode_keys(..., codes=cache[:, :, t0:t1])``), every
   ``aq_decode_group_size`` tokens as the reference does.
 
-fp16 / bf16 K/V caches only (the reference's CUDA kernels take fp16; its
+Dense attention (prefill, dense layers) stays the reference's torch SDPA
+call.  fp16 / bf16 K/V caches only (the reference's CUDA kernels take fp16; its
 fp32 path is its torch fallback).  Multi-token decode (Tq > 1), ICM
 refinement and key reconstruction are outside the decode path and raise.
 """
@@ -29,7 +31,8 @@ import torch
 from . import ops
 from .aq_kv import AQLayerCodebookManager
 
-__all__ = ["_decode_attention", "_prepare_aq_cache", "_kv_cache_append", "decode_keep_size"]
+__all__ = ["self_attn_forward", "_decode_attention", "_prepare_aq_cache", "_kv_cache_append", "_cached_position_ids",
+           "do_sdpa_attn", "decode_keep_size"]
 
 
 def decode_keep_size(num_candidate: int, mask_out: float = 0.98, min_remain: int = 20) -> int:
@@ -216,3 +219,93 @@ def _prepare_aq_cache(self, manager: AQLayerCodebookManager, layer_idx: int, key
     cache = {"seq_len": T, "encoded_len": T, "batch_size": B, "codes": codes, "approx": None}
     self._aq_cache = cache
     return cache
+
+
+def _cached_position_ids(owner, device: torch.device, end: int) -> torch.Tensor:
+    """A shared ``arange`` on ``device``, grown only when needed (aq_evaluation.py:56-63)."""
+    cache = getattr(owner, "_laprune_position_ids", None)
+    if cache is None or cache.device != device or int(cache.numel()) < int(end):
+        cache = torch.arange(max(int(end), 1024), device=device, dtype=torch.long)
+        owner._laprune_position_ids = cache
+    return cache
+
+
+def do_sdpa_attn(query, key, value, cos=None, sin=None, out_proj=None, query_down_proj=None, key_down_proj=None,
+                 mask=None, already_rope: bool = False):
+    """Dense attention of post-RoPE q over a native GQA cache (laprune/attention.py:21-73): the
+    reference's path for dense layers and prefill, kept as its torch SDPA call (not part of the
+    sparse decode path)."""
+    if not already_rope:
+        raise ValueError("LAPrune attention expects post-RoPE query and key tensors")
+    q, k, v = query, key, value
+    hq, nq = int(q.shape[1]), int(q.shape[-2])
+    if query_down_proj is not None:
+        q = (q.transpose(1, 2).flatten(2) @ query_down_proj).unflatten(-1, (hq, -1)).transpose(1, 2)
+    if key_down_proj is not None:
+        k = (k.transpose(1, 2).flatten(2) @ key_down_proj).unflatten(-1, (hq, -1)).transpose(1, 2)
+    gqa = hq != int(k.shape[1])
+    if gqa and hq % int(k.shape[1]):
+        raise ValueError(f"invalid GQA head counts: Hq={hq}, Hkv={k.shape[1]}")
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+    nk = int(k.shape[-2])
+    if mask is not None:
+        o = sdpa(q, k, v, attn_mask=mask, is_causal=False, enable_gqa=gqa)
+    elif nk == nq:
+        o = sdpa(q, k, v, is_causal=True, enable_gqa=gqa)
+    elif nq == 1:
+        o = sdpa(q, k, v, is_causal=False, enable_gqa=gqa)
+    else:  # queries at the end of the cache
+        m = torch.full((1, 1, nq, nk), torch.finfo(q.dtype).min, dtype=torch.float32, device=q.device)
+        m[..., -nq:].triu_(diagonal=1)
+        m[..., :nk - nq].fill_(0)
+        o = sdpa(q, k, v, attn_mask=m.to(q.dtype), is_causal=False, enable_gqa=gqa)
+    o = o.transpose(1, 2).flatten(2)
+    return out_proj(o) if out_proj is not None else o
+
+
+def self_attn_forward(self, hidden_states: torch.Tensor, kv_cache=None):
+    """The reference's replacement Llama attention forward (aq_evaluation.py:279-322), bound to a
+    ``LlamaAttention`` that carries ``aq_manager``, ``layer_idx``, ``draft_kwargs``,
+    ``is_fix_layer``, ``rotary_emb`` and ``config``: projections, RoPE (cos/sin computed once per
+    step and shared by the layers), K/V append, code cache; prefill and dense layers attend
+    densely, a sparse layer's decode token goes through ``_decode_attention``.  Returns
+    ``(attn_output, kv_cache_out, None, None)``."""
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+    manager = self.aq_manager
+    layer_idx = self.layer_idx
+    conf = self.draft_kwargs
+    H = self.config.num_attention_heads
+    Hkv = self.config.num_key_value_heads
+    D = self.config.hidden_size // H
+    B, T_new = hidden_states.shape[0], hidden_states.shape[-2]
+    is_prefill = T_new > 1 and kv_cache is None
+    q = self.q_proj(hidden_states).unflatten(-1, (H, D)).transpose(1, 2)
+    k = self.k_proj(hidden_states).unflatten(-1, (Hkv, D)).transpose(1, 2)
+    v = self.v_proj(hidden_states).unflatten(-1, (Hkv, D)).transpose(1, 2)
+    past = int(getattr(self, "total_seq_len", 0))
+    total = past + T_new
+    pos = _cached_position_ids(manager, q.device, total)[past:total][None, :].expand(B, -1)
+    key = (str(q.device), past, int(T_new), int(B), q.dtype)
+    cached = getattr(manager, "_laprune_rope_step", None)
+    if layer_idx == 0 or cached is None or cached[0] != key:
+        cos, sin = self.rotary_emb(q, pos)
+        manager._laprune_rope_step = (key, cos, sin)
+    else:
+        cos, sin = cached[1], cached[2]
+    Q_rope, K_new = apply_rotary_pos_emb(q, k, cos, sin)
+    if layer_idx + 1 == int(self.config.num_hidden_layers):
+        manager._laprune_rope_step = None
+    K_rope, vals_full, kv_out = _kv_cache_append(self, K_new, v, total, kv_cache)
+    self.total_seq_len = total
+    sparse = (conf.get("enable", True) and not conf.get("aq_disable_encode", False) and not self.is_fix_layer
+              and not getattr(self, "full_kv_layer", False) and layer_idx in manager.layer_cfgs)
+    if is_prefill and conf.get("aq_disable_prefill", False):
+        sparse = False
+    if not sparse:
+        return do_sdpa_attn(Q_rope, K_rope, vals_full, out_proj=self.o_proj, already_rope=True), kv_out, None, None
+    aq_cache = _prepare_aq_cache(self, manager, layer_idx, K_rope,
+                                 need_recon=not conf.get("aq_use_exact_true_score", True),
+                                 decode_group_size=int(conf.get("aq_decode_group_size", 1)), is_prefill=is_prefill)
+    if is_prefill:
+        return do_sdpa_attn(Q_rope, K_rope, vals_full, out_proj=self.o_proj, already_rope=True), kv_out, None, None
+    return _decode_attention(self, manager, layer_idx, Q_rope, K_rope, vals_full, aq_cache, conf), kv_out, None, None

@@ -131,3 +131,47 @@ def test_sharded_manager_drives_the_decode_hook(golden_dir, tmp_path):
                                 dh["vals"].to(dev).half(), {"codes": dh["codes"].to(dev), "seq_len": dh["T"]}, conf)
     torch.cuda.synchronize()
     assert np.abs(out.float().cpu().numpy() - fix["out_sink4"]).max() <= 2e-2
+
+
+@torch.no_grad()
+def test_attention_forward_prefill_then_sparse_decode():
+    # the reference's attention forward on a small Llama layer (head_dim 128,
+    # GQA 4): a dense prefill that fills the code cache, then decode tokens
+    # through the sparse path, each checked against the oracle's decode hook
+    # on the same cache
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaAttention, LlamaRotaryEmbedding, apply_rotary_pos_emb
+    dev = _dev()
+    cfg = LlamaConfig(hidden_size=512, num_attention_heads=4, num_key_value_heads=1, num_hidden_layers=4,
+                      intermediate_size=1024, rope_theta=500000.0, max_position_embeddings=4096)
+    g = torch.Generator().manual_seed(12)
+    attn = LlamaAttention(cfg, layer_idx=2)
+    for prm in attn.parameters():
+        prm.copy_(torch.randn(prm.shape, generator=g) * 0.02)
+    attn = attn.to(dev, torch.float16)
+    attn.rotary_emb = LlamaRotaryEmbedding(cfg, device=dev)
+    cb = torch.randn((32, 256, 128), generator=g) * 0.05
+    attn.aq_manager = _mgr(cb, 4, layer=2)
+    attn.draft_kwargs = {"sink_size": 0, "local_window": 64, "mask_out": 0.98, "min_remain": 20,
+                         "aq_decode_group_size": 16, "aq_use_pruned_attn": True,
+                         "aq_encode_icm_iters_prefill": 0, "aq_encode_icm_iters_decode": 0}
+    attn.is_fix_layer = False
+    fwd = types.MethodType(aqe.self_attn_forward, attn)
+    T0 = 700
+    _, kv, _, _ = fwd((torch.randn((1, T0, 512), generator=g) * 0.5).to(dev, torch.float16))
+    for step in range(3):
+        h1 = (torch.randn((1, 1, 512), generator=g) * 0.5).to(dev, torch.float16)
+        out, kv, _, _ = fwd(h1, kv_cache=kv)
+        torch.cuda.synchronize()
+        total = T0 + step + 1
+        q = attn.q_proj(h1).unflatten(-1, (4, 128)).transpose(1, 2)
+        cos, sin = attn.rotary_emb(q, torch.tensor([[total - 1]], device=dev))
+        q_rope, _ = apply_rotary_pos_emb(q, q[:, :1], cos, sin)
+        c = attn._aq_cache
+        ref = oracle.decode_hook_reference(cb.numpy(), q_rope.float().cpu().numpy(), c["codes"].cpu().numpy(),
+                                           attn.k_cache[:, :, :total].float().cpu().numpy(),
+                                           attn.v_cache[:, :, :total].float().cpu().numpy(), total, 0, 64)
+        ref = ref @ attn.o_proj.weight.float().cpu().numpy().T
+        got = out.float().cpu().numpy()
+        assert got.shape == ref.shape
+        assert np.abs(got - ref).max() <= 2e-2 * np.abs(ref).max()
