@@ -109,3 +109,16 @@ def test_sharded_manager_loads_one_copy_per_device_on_first_use(tmp_path):
     assert sh._on(torch.zeros(1)) is sh.for_device("cpu")
     with pytest.raises(NotImplementedError):
         sh.encode_keys(0, 0, torch.zeros(4, 128), icm_iters=2)
+
+
+def test_quantizer_encode_surface_refuses_training_and_icm():
+    from laprune_b200.quantizer import AdditiveQuantizer
+    with pytest.raises(NotImplementedError):
+        AdditiveQuantizer(M=32, K=256, d=128, init="random", device="cpu")
+    with pytest.raises(ValueError):
+        AdditiveQuantizer(M=32, K=256, d=128, device="cpu", codebooks=torch.zeros(16, 256, 128))
+    aq = AdditiveQuantizer(M=32, K=256, d=128, device="cpu", codebooks=torch.zeros(32, 256, 128))
+    with pytest.raises(NotImplementedError):
+        aq.encode(torch.zeros(4, 128), icm_iters=2)
+    with pytest.raises(NotImplementedError):
+        aq.encode(torch.zeros(4, 128), method="beam", icm_iters=0)

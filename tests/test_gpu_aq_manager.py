@@ -175,3 +175,20 @@ def test_attention_forward_prefill_then_sparse_decode():
         got = out.float().cpu().numpy()
         assert got.shape == ref.shape
         assert np.abs(got - ref).max() <= 2e-2 * np.abs(ref).max()
+
+
+def test_quantizer_encode_matches_the_oracle_and_its_loss():
+    from laprune_b200.quantizer import AdditiveQuantizer
+    g = torch.Generator().manual_seed(13)
+    cb = torch.randn((32, 256, 128), generator=g) * 0.05
+    x = torch.randn((333, 128), generator=g) * 0.5
+    aq = AdditiveQuantizer(M=32, K=256, d=128, device=_dev(), codebooks=cb)
+    codes, loss, extra = aq.encode(x.to(_dev()), icm_iters=0)
+    want = oracle.encode_greedy(x.numpy(), cb.numpy()).astype(np.int64)
+    assert codes.dtype == torch.int64 and extra is None
+    assert np.array_equal(codes.cpu().numpy(), want)
+    recon = cb.numpy()[np.arange(32)[None, :], want].sum(1)
+    ref = np.sqrt(((x.numpy() - recon) ** 2).sum(1)).mean()
+    assert abs(loss - ref) <= 1e-4 * ref
+    codes2, loss2, _ = aq.encode(x.to(_dev()), icm_iters=0, return_loss=False)
+    assert torch.equal(codes2, codes) and loss2 == 0.0
