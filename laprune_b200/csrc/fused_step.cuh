@@ -317,27 +317,14 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     __shared__ __align__(16) float s_qu[8 * 128];  // the unit's G query rows (fp32), loaded at start
     __shared__ int s_shift, s_bstar, s_above;
 
-    // launched with programmatic stream serialisation: nothing of this call
-    // touches memory before the previous kernel on the stream has completed
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = kFThreads / 32;
-    const bool stamp = p.phase_ns != nullptr && blockIdx.x == 0 && tid == 0;
-    if (stamp) p.phase_ns[0] = global_ns();
 
     int u, cj, cn;
     fused_cta_unit(blockIdx.x, gridDim.x, p.U, &u, &cj, &cn);
     unsigned long long* ubar = p.bar + u;
     int nbar = 0;  // unit barriers passed in this call (uniform over the unit's CTAs)
     __shared__ uint32_t s_epoch;
-    if (tid == 0) {
-        // every CTA of every call adds 1: in call n the old values lie in
-        // [G*(n-1), G*n) for G = gridDim.x, whatever the order and even if a
-        // CTA of an earlier call returned early
-        unsigned long long old;
-        asm volatile("atom.add.relaxed.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(p.epoch_ctr) : "memory");
-        s_epoch = (uint32_t)(old / gridDim.x) + 1u;
-    }
     const int b = u / p.Hkv, hkv = u - b * p.Hkv;
     // the CTA's tokens: a run of whole bitmap words of the candidate window
     const int wlo = p.c0 >> 5, whi = (p.c1 + 31) >> 5;
@@ -353,6 +340,38 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
 
     uint64_t* s_empty = s_bar + kFStages;      // per-slot "all warps done" barriers
     uint64_t* s_abar = s_bar + 2 * kFStages;   // phase-A codebook stages
+    // phase A's share of the unit's 32*256 codeword rows, split evenly over
+    // its cn CTAs, streamed HBM -> shared memory in 64-row (32 KB) chunks
+    // through 3 stages
+    constexpr int64_t kRows = 32 * 256;
+    const int64_t f_begin = (kRows * cj / cn) & ~(int64_t)7;
+    const int64_t f_end = cj + 1 == cn ? kRows : ((kRows * (cj + 1) / cn) & ~(int64_t)7);
+    const int nchunk = (int)((f_end - f_begin + 63) / 64);
+    const float* cbu = p.cb + (int64_t)(p.cb_per_kv_head ? hkv : 0) * (kRows * 128);
+    auto abuf = [&](int c) -> unsigned char* {
+        const int b3 = c % 3;
+        return b3 == 2 ? reinterpret_cast<unsigned char*>(s_scores) : s_lut + b3 * 32768;
+    };
+    auto issue_chunk = [&](int c) {
+        const int64_t r0 = f_begin + (int64_t)c * 64;
+        const int64_t r1 = min(f_end, r0 + 64);
+        mbar_arrive_expect_tx(&s_abar[c % 3], (uint32_t)((r1 - r0) * 512));
+        bulk_g2s(abuf(c), cbu + r0 * 128, (uint32_t)((r1 - r0) * 512), &s_abar[c % 3]);
+    };
+    uint64_t policy = 0;
+    const int npre = ntiles < kFStages ? ntiles : kFStages;
+    const int npre0 = npre < kFPre0 ? npre : kFPre0;  // the rest after phase A
+    // the first 3 codebook chunks, then the first phase-B code tiles
+    auto issue_inputs = [&]() {
+        for (int c = 0; c < 3 && c < nchunk; ++c) issue_chunk(c);
+        policy = policy_evict_first();
+        for (int i = 0; i < npre0; ++i) {
+            const int t0 = t_begin + i * kFThreads;
+            const int nn = min(kFThreads, t_end - t0);
+            mbar_arrive_expect_tx(&s_bar[i], (uint32_t)nn * 32u);
+            bulk_g2s_stream(s_ring + i * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[i], policy);
+        }
+    };
     if (tid == 0) {
         for (int s = 0; s < kFStages; ++s) {
             mbar_init(&s_bar[s], 1);
@@ -361,22 +380,29 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         for (int s = 0; s < 3; ++s) mbar_init(&s_abar[s], 1);
         fence_barrier_init();
     }
-    __syncthreads();
-    // (the epoch stays in shared memory, s_epoch: a register held across the
-    // scorer would spill)
-    // ---- start streaming the phase-B code tiles right away ----
-    uint64_t policy = 0;
-    const int npre = ntiles < kFStages ? ntiles : kFStages;
-    const int npre0 = npre < kFPre0 ? npre : kFPre0;  // the rest after phase A
+    // launched with programmatic stream serialisation: nothing of this call
+    // touches global memory before the previous kernel on the stream has
+    // completed.  The next launch on the stream may be scheduled as soon as
+    // every CTA of this grid is past this point: its CTAs take the SMs this
+    // grid frees and wait here in turn, so the launch gap hides behind this
+    // grid's tail.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const bool stamp = p.phase_ns != nullptr && blockIdx.x == 0 && tid == 0;
+    if (stamp) p.phase_ns[0] = global_ns();
     if (tid == 0) {
-        policy = policy_evict_first();
-        for (int i = 0; i < npre0; ++i) {
-            const int t0 = t_begin + i * kFThreads;
-            const int nn = min(kFThreads, t_end - t0);
-            mbar_arrive_expect_tx(&s_bar[i], (uint32_t)nn * 32u);
-            bulk_g2s_stream(s_ring + i * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[i], policy);
-        }
+        // the input streams first: the epoch's round trip below overlaps them
+        issue_inputs();
+        // every CTA of every call adds 1: in call n the old values lie in
+        // [G*(n-1), G*n) for G = gridDim.x, whatever the order and even if a
+        // CTA of an earlier call returned early
+        unsigned long long old;
+        asm volatile("atom.add.relaxed.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(p.epoch_ctr) : "memory");
+        s_epoch = (uint32_t)(old / gridDim.x) + 1u;
     }
+    // (the epoch stays in shared memory, s_epoch: a register held across the
+    // scorer would spill; the mbarrier inits and s_epoch are visible to all
+    // threads after the barrier that completes s_qu below)
     int issued = npre0;
     auto drain = [&](int from) {
         for (int j = from; j < issued; ++j) mbar_wait(&s_bar[j % kFStages], (uint32_t)(j / kFStages) & 1u, nullptr);
@@ -388,28 +414,10 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     }
 
     // ================= phase A: LUT build of the CTA's unit =================
-    // The unit's 32*256 codeword rows are split evenly over its cn CTAs and
-    // stream HBM -> shared memory through 3 bulk-copy stages of 64 rows
-    // (32 KB); warp w dots rows 4w..4w+3 of a stage with the summed query and
-    // reduces the 4 dot products with a 6-shuffle transpose.
+    // The CTA's codeword rows arrive in the 3 chunk stages issued above;
+    // warp w dots rows 4w..4w+3 of a chunk with the summed query and reduces
+    // the 4 dot products with a 6-shuffle transpose.
     {
-        constexpr int64_t kRows = 32 * 256;  // codeword rows of one unit
-        const int64_t f_begin = (kRows * cj / cn) & ~(int64_t)7;
-        const int64_t f_end = cj + 1 == cn ? kRows : ((kRows * (cj + 1) / cn) & ~(int64_t)7);
-        const int nchunk = (int)((f_end - f_begin + 63) / 64);
-        const float* cbu = p.cb + (int64_t)(p.cb_per_kv_head ? hkv : 0) * (kRows * 128);
-        auto abuf = [&](int c) -> unsigned char* {
-            const int b3 = c % 3;
-            return b3 == 2 ? reinterpret_cast<unsigned char*>(s_scores) : s_lut + b3 * 32768;
-        };
-        auto issue_chunk = [&](int c) {
-            const int64_t r0 = f_begin + (int64_t)c * 64;
-            const int64_t r1 = min(f_end, r0 + 64);
-            mbar_arrive_expect_tx(&s_abar[c % 3], (uint32_t)((r1 - r0) * 512));
-            bulk_g2s(abuf(c), cbu + r0 * 128, (uint32_t)((r1 - r0) * 512), &s_abar[c % 3]);
-        };
-        if (tid == 0)
-            for (int c = 0; c < 3 && c < nchunk; ++c) issue_chunk(c);
         // q_sum of the unit, summed over g in order (s_hist is free now)
         float* s_qsum = reinterpret_cast<float*>(s_hist);
         __syncthreads();  // s_qu complete
