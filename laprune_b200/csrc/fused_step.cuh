@@ -659,9 +659,9 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 if (two) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_empty[s1])) : "memory");
             }
             if (tid == 0) {
-                // refill the slots of the two tiles consumed in the previous iteration
-                for (int pi = i - 2; pi < i; ++pi) {
-                    if (pi < 0 || pi + kFStages >= ntiles) continue;
+                // refill the slots of the two tiles just consumed
+                for (int pi = i; pi < i + 2; ++pi) {
+                    if (pi + kFStages >= ntiles) continue;
                     const int ps = pi % kFStages;
                     if (!mbar_wait(&s_empty[ps], (uint32_t)(pi / kFStages) & 1u, p.err)) {
                         s_abort = 1;
