@@ -289,13 +289,14 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
 
-    def step(events=None, phases=None):
+    def step(events=None, phases=None, on=None):
+        st = sh if on is None else on
         for li in range(N_LAYERS):
             L = layers[li % len(layers)]
             a = L["args"]
             a.stage_events = ctypes.cast(events[li], ctypes.c_void_p) if events is not None else None
             a.phase_ns = phases[li].data_ptr() if phases is not None else None
-            rc = lib.lp_sparse_decode(ctypes.byref(a), ws.data_ptr(), ws.numel(), sh)
+            rc = lib.lp_sparse_decode(ctypes.byref(a), ws.data_ptr(), ws.numel(), st)
             if rc != 0:
                 _lib.check(rc)
 
@@ -307,6 +308,15 @@ def run_ours(args):
     for _ in range(max(args.warmup, 1)):
         step()
     torch.cuda.synchronize()
+    # the timed step: the 30 layer launches captured once in a CUDA graph
+    # (the captured calls are the same lp_sparse_decode calls on the same
+    # arguments and workspace), replayed once per token
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph, capture_error_mode="thread_local"):
+        step(on=torch.cuda.current_stream(dev).cuda_stream)
+    for _ in range(max(args.warmup, 1)):
+        step_graph.replay()
+    torch.cuda.synchronize()
 
     sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
     sampler.start()
@@ -317,12 +327,23 @@ def run_ours(args):
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
     for _ in range(args.steps):
-        step()
+        step_graph.replay()
     t_end.record(stream)
     torch.cuda.synchronize()
     barrier()
+    # the same launches issued eagerly, one host call per layer (reported beside)
+    x_start = torch.cuda.Event(enable_timing=True)
+    x_end = torch.cuda.Event(enable_timing=True)
+    x_start.record(stream)
+    for _ in range(args.steps):
+        step()
+    x_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
     clocks = sampler.stop()
+    del step_graph
     elapsed_ms = t_start.elapsed_time(t_end)
+    eager_ms = x_start.elapsed_time(x_end)
     # the timed loop launches only the fused kernel, back to back on `stream`:
     # its average launch duration is the timed region over the launches
     launch_ms = elapsed_ms / (args.steps * N_LAYERS)
@@ -386,35 +407,34 @@ def run_ours(args):
     barrier()
     e2e_ms = e_start.elapsed_time(e_end)
 
-    # ---- one GPU only: the same end-to-end step captured once in a CUDA
-    # graph (host q in, 30 layer calls, host out back) and replayed, which
-    # takes the per-call host cost out; no capture runs beside a process group
-    graph = None
-    if world == 1:
-        cg = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(cg):
-            e2e_step()
-        for _ in range(max(1, min(args.warmup, 3))):
-            cg.replay()
-        torch.cuda.synchronize()
-        g_start = torch.cuda.Event(enable_timing=True)
-        g_end = torch.cuda.Event(enable_timing=True)
-        g_start.record(stream)
-        for _ in range(args.steps):
-            cg.replay()
-        g_end.record(stream)
-        torch.cuda.synchronize()
-        del cg
-        graph = {"value": args.steps / (g_start.elapsed_time(g_end) / 1e3), "unit": UNIT,
-                 "api": "the e2e step captured once in a CUDA graph and replayed (one GPU only)",
-                 "device_error_bits": ops.device_errors(ws, dev)}
+    # ---- the same end-to-end step captured once in a CUDA graph (host q in,
+    # 30 layer calls, host out back) and replayed: no per-call host cost ----
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        e2e_step()
+    for _ in range(max(1, min(args.warmup, 3))):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier()
+    g_start = torch.cuda.Event(enable_timing=True)
+    g_end = torch.cuda.Event(enable_timing=True)
+    g_start.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    g_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    graph_ms = g_start.elapsed_time(g_end)
+    del graph
+    graph_errs = ops.device_errors(ws, dev)
 
     # max over ranks
-    t = torch.tensor([elapsed_ms, e2e_ms, kernel_ms, launch_ms] + stage_ms, device=dev, dtype=torch.float64)
+    t = torch.tensor([elapsed_ms, e2e_ms, kernel_ms, launch_ms, graph_ms, eager_ms] + stage_ms, device=dev,
+                     dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_ms, kernel_ms, launch_ms = float(t[0]), float(t[1]), float(t[2]), float(t[3])
-    stage_ms = [float(x) for x in t[4:]]
+    elapsed_ms, e2e_ms, kernel_ms, launch_ms, graph_ms, eager_ms = (float(x) for x in t[:6])
+    stage_ms = [float(x) for x in t[6:]]
 
     if rank == 0:
         tok_s = world * args.steps / (elapsed_ms / 1e3)
@@ -442,7 +462,10 @@ def run_ours(args):
                 "layer_steps_per_s": tok_s * N_LAYERS,
                 "step_algorithmic_bytes": step_bytes,
                 "step_hbm_gbs": step_bytes / (elapsed_ms / args.steps / 1e3) / 1e9,
+                "timed_as": "one CUDA graph of the 30 layer launches, replayed once per token",
                 "launch_us_timed": launch_ms * 1e3,
+                "eager_tok_s": world * args.steps / (eager_ms / 1e3),
+                "launch_us_eager": eager_ms * 1e3 / (args.steps * N_LAYERS),
                 "launch_us_isolated": kernel_ms * 1e3,
                 "fused_phase_us": {"A_lut": phase_us[0], "wait_lut": phase_us[1], "B_score_publish": phase_us[2],
                                    "wait_windows": phase_us[3], "C_select": phase_us[4],
@@ -462,7 +485,9 @@ def run_ours(args):
                     "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
                     "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
                     "api": "laprune_b200.ops.sparse_decode per layer, q from pinned host, out to pinned host",
-                    **({"graph_replay": graph} if graph is not None else {})},
+                    "graph_replay": {"value": world * args.steps / (graph_ms / 1e3), "unit": UNIT,
+                                     "api": "the same step captured once in a CUDA graph and replayed",
+                                     "device_error_bits": graph_errs}},
             "gpu_launches": args.steps * N_LAYERS,
         }
         if world == 1:
