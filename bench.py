@@ -51,20 +51,17 @@ def _peaks():
     return 6650.0, "fallback"
 
 
-def _profile_traffic():
-    """Per-launch DRAM traffic of the scorer from the committed ncu summary
-    (a line 'traffic_bytes_per_launch: <int>'), scaled by the summary's own
-    note when it was captured on a smaller case; None if absent."""
-    p = ROOT / "profiles" / "fused_kernel_cfg3.md"
+def _profile_traffic(name: str = "fused_kernel_cfg3"):
+    """Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum)
+    of a kernel from the machine-readable record of its committed ncu
+    capture, ``profiles/<name>.json``; None if there is none."""
+    p = ROOT / "profiles" / f"{name}.json"
     if not p.exists():
         return None
-    for line in p.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return int(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+    try:
+        return int(json.loads(p.read_text())["traffic_bytes_per_launch"])
+    except (ValueError, KeyError, TypeError):
+        return None
 
 
 class ClockSampler:
@@ -180,6 +177,151 @@ def cpu_baseline(seconds: float = 10.0):
             "kind": "port", "sample": f"{n} samples in {el:.1f} s; " + SAMPLE_DESC}
 
 
+# The side measurements below use N_SIDE resident layer instances (each
+# about 0.6 GB, together far above the 126 MB L2) cycled over 30 calls, and
+# fp16 K/V: the reference's K/V gather kernel takes fp16 only (in bf16 it
+# falls back to torch.take_along_dim, aq_evaluation.py:243-250).
+N_SIDE = 8
+HOOK_K = 2621  # the decode hook's keep size at T=131072 (mask_out 0.98, sink 0, local 64)
+
+
+def _side_layers(dev, seed: int, shared_codebook: bool):
+    import torch
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    layers = []
+    for _ in range(N_SIDE):
+        shape = (M, K, D) if shared_codebook else (HKV, M, K, D)
+        layers.append({
+            "C": torch.randn(shape, generator=g, device=dev) * 0.05,
+            "codes": torch.randint(0, 256, (1, HKV, T_CTX, M), generator=g, device=dev, dtype=torch.uint8),
+            "keys": torch.randn((1, HKV, T_CTX, D), generator=g, device=dev).to(torch.float16),
+            "vals": torch.randn((1, HKV, T_CTX, D), generator=g, device=dev).to(torch.float16),
+            "q": torch.randn((1, HQ, D), generator=g, device=dev).to(torch.float16)})
+    return layers
+
+
+def _time_calls(fn, n_calls: int, warmup: int = 3):
+    """Mean µs per call of fn(i) over n_calls calls (CUDA events)."""
+    import torch
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(n_calls):
+        fn(i)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / n_calls
+
+
+def ref_cuda_measurement(reps: int = 3):
+    """The reference's own CUDA kernels, built unchanged from its sources for
+    sm_100a (oracle/_ref), timed on this GPU in the call chains of its decode
+    hook with torch doing the rest (cuBLAS LUT, torch.topk, SDPA), fp16 as the
+    reference runs (aq_manager_dtype fp16):
+      cfg3_layer: per-KV-head fp16 codebooks, LUT = q.C^T (torch.bmm),
+        aq_lut_gather_grouped, GQA sum, torch.topk 2048 per KV head on
+        [4, T-64), keep = top-k + 4 sink + 64 local, gqa_gather_kv, SDPA
+        (laprune/llm/aq_kv.py:681-687, modifiers/aq_evaluation.py:185-253);
+      hook_layer: the shipped decode configuration -- one fp16 codebook for
+        every head, torch.matmul LUT, aq_lut_gather_grouped, torch.topk 2621
+        per query head on [0, T-64), gqa_gather_kv_with_tail over the
+        64-token local tail, SDPA (aq_evaluation.py:160-253);
+      encoders: fused_linear_encode_forward (fused_linear_encode.cu:168-234)
+        at the decode batch (B=1: 8 heads x 64 keys = 512), config 2 (4 x 8 x
+        64 keys; per-KV-head codebooks: one call per head of 256 keys, and
+        one shared codebook: one call of 2048), and a prefill chunk (8 x 4096
+        keys, shared codebook).
+    The o_proj of the reference's chain is left out (not on this path)."""
+    import torch
+    import torch.nn.functional as F
+    from oracle import build_ref
+    gqa = build_ref.load("aq_lut_gqa")
+    enc = build_ref.load("fused_linear_encode").fused_linear_encode_forward
+    dev = torch.device("cuda", 0)
+    n_calls = reps * N_LAYERS
+    out = {"source": "reference aq_kernels/*.cu built for sm_100a by oracle/build_ref.py; fp16",
+           "resident_layers": N_SIDE}
+    sink_idx = torch.arange(SINK, device=dev).view(1, SINK).expand(HKV, SINK)
+    local_idx = torch.arange(T_CTX - LOCAL, T_CTX, device=dev).view(1, LOCAL).expand(HKV, LOCAL)
+
+    layers = _side_layers(dev, 77, shared_codebook=False)
+    for L in layers:  # the manager's per-process fp16 copy (aq_kv.py:61-72)
+        L["C16"] = L["C"].to(torch.float16)
+        L["C"] = None
+
+    def cfg3_layer(i):
+        L = layers[i % N_SIDE]
+        q = L["q"][0]
+        lut = torch.bmm(q.view(HKV, 4, D), L["C16"].view(HKV, M * K, D).transpose(1, 2))
+        sc = gqa.aq_lut_gather_grouped(lut.view(HQ, M, K), L["codes"][0], 4)
+        gs = sc.view(HKV, 4, T_CTX).float().sum(1)
+        top = torch.topk(gs[:, SINK:T_CTX - LOCAL], TOPK, dim=-1, sorted=False).indices + SINK
+        keep = torch.cat([top, sink_idx, local_idx], dim=-1).repeat_interleave(4, 0).unsqueeze(0)
+        kg, vg = gqa.gqa_gather_kv(L["keys"], L["vals"], keep, 4)
+        return F.scaled_dot_product_attention(L["q"].view(1, HQ, 1, D), kg, vg)
+
+    us = _time_calls(cfg3_layer, n_calls)
+    out["cfg3_layer_us"] = us
+    out["cfg3_tok_s_30_layers"] = 1e6 / (us * N_LAYERS)
+
+    def scorer_only(i):
+        L = layers[i % N_SIDE]
+        return gqa.aq_lut_gather_grouped(L["lut"], L["codes"][0], 4)
+
+    for L in layers:
+        L["lut"] = torch.bmm(L["q"][0].view(HKV, 4, D),
+                             L["C16"].view(HKV, M * K, D).transpose(1, 2)).view(HQ, M, K)
+    us = _time_calls(scorer_only, n_calls)
+    out["cfg3_grouped_scorer_us"] = us
+    out["cfg3_grouped_scorer_code_gbs"] = HKV * T_CTX * M / (us * 1e-6) / 1e9
+    del layers
+    torch.cuda.empty_cache()
+
+    hook = _side_layers(dev, 78, shared_codebook=True)
+    for L in hook:
+        L["C16"] = L["C"].to(torch.float16)
+        L["C"] = None
+
+    def hook_layer(i):
+        L = hook[i % N_SIDE]
+        q = L["q"][0]
+        lut = torch.matmul(q, L["C16"].reshape(M * K, D).t())
+        sc = gqa.aq_lut_gather_grouped(lut.view(HQ, M, K), L["codes"][0], 4).view(1, HQ, T_CTX)
+        top = torch.topk(sc[..., :T_CTX - LOCAL], HOOK_K, dim=-1, sorted=False).indices
+        kg, vg = gqa.gqa_gather_kv_with_tail(L["keys"], L["vals"], top, 4, T_CTX - LOCAL, LOCAL)
+        return F.scaled_dot_product_attention(L["q"].view(1, HQ, 1, D), kg, vg)
+
+    us = _time_calls(hook_layer, n_calls)
+    out["hook_layer_us"] = us
+    out["hook_tok_s_30_layers"] = 1e6 / (us * N_LAYERS)
+    del hook
+    torch.cuda.empty_cache()
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(79)
+    C = torch.randn((HKV, M, K, D), generator=g, device=dev) * 0.05
+    C16 = C.to(torch.float16)
+    wt = C16.transpose(2, 3).contiguous()
+    bias = (-0.5 * C16.float().pow(2).sum(-1)).to(torch.float16)
+
+    def enc_us(x, h):
+        return _time_calls(lambda i: enc(x, wt[h], bias[h], C16[h], True, 0), 20)
+
+    x512 = torch.randn((1 * HKV * 64, D), generator=g, device=dev).to(torch.float16)
+    x2048 = torch.randn((4 * HKV * 64, D), generator=g, device=dev).to(torch.float16)
+    x256 = x2048.view(HKV, 256, D)  # config 2 per KV head: 4 batches x 64 keys of one head
+    xpre = torch.randn((HKV * 4096, D), generator=g, device=dev).to(torch.float16)
+    out["encode_decode_512_shared_us"] = enc_us(x512, 0)
+    out["encode_cfg2_2048_shared_us"] = enc_us(x2048, 0)
+    out["encode_cfg2_per_kv_head_us"] = _time_calls(
+        lambda i: [enc(x256[h], wt[h], bias[h], C16[h], True, 0) for h in range(HKV)], 20)
+    out["encode_prefill_32768_shared_us"] = enc_us(xpre, 0)
+    return out
+
+
 def run_reference(args):
     ws, rank, _ = _dist_env()
     if rank != 0:
@@ -208,6 +350,16 @@ def run_reference(args):
                          "sample": SAMPLE_DESC},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_ref_cuda:
+        try:
+            import torch
+            from oracle import build_ref
+            if torch.cuda.is_available() and build_ref.available():
+                line["ref_cuda"] = ref_cuda_measurement()
+            else:
+                line["ref_cuda"] = {"unavailable": "no GPU or the reference extension is not built"}
+        except Exception as e:  # a side measurement: the CPU line above stands
+            line["ref_cuda"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -226,9 +378,19 @@ def encode_measurement(dev, reps: int = 20):
     tf32_peak = bf16 / 2
     c = syn.config2(0)
     C = c["C"].to(dev)
-    cases = {"cfg2_4x8x64": c["keys"].to(dev),
-             "prefill_1x8x4096": torch.randn((1, 8, 4096, 128), device=dev).to(torch.bfloat16)}
-    for name, keys in cases.items():
+    g = torch.Generator(device=dev)
+    g.manual_seed(79)
+    C1 = torch.randn((32, 256, 128), generator=g, device=dev) * 0.05
+    # per-KV-head codebooks (config 2) and one shared codebook (the shipped
+    # configuration): the decode batch (B=1: 8 heads x 64 keys, every 64
+    # tokens), config 2's 4 x 8 x 64 keys and a prefill chunk of 8 x 4096
+    cases = {"cfg2_4x8x64": (c["keys"].to(dev), C),
+             "prefill_1x8x4096": (torch.randn((1, 8, 4096, 128), device=dev).to(torch.bfloat16), C),
+             "decode_1x8x64_shared": (torch.randn((1, 8, 64, 128), generator=g, device=dev).to(torch.float16), C1),
+             "cfg2_4x8x64_shared": (torch.randn((4, 8, 64, 128), generator=g, device=dev).to(torch.float16), C1),
+             "prefill_1x8x4096_shared": (torch.randn((1, 8, 4096, 128), generator=g,
+                                                     device=dev).to(torch.float16), C1)}
+    for name, (keys, C) in cases.items():
         codes = ops.encode_keys(keys, C)
         for _ in range(3):
             ops.encode_keys(keys, C, codes=codes)
@@ -242,11 +404,50 @@ def encode_measurement(dev, reps: int = 20):
         us = e0.elapsed_time(e1) * 1e3 / reps
         nvec = keys.numel() // 128
         tflops = nvec * 32 * 2 * 256 * 128 / (us * 1e-6) / 1e12
-        out[name] = {"us": us, "vectors": nvec, "tensor_tflops": tflops,
-                     "frac_of_tf32_peak": tflops / tf32_peak}
+        out[name] = {"us": us, "vectors": nvec, "rows_per_cta": ops.encode_rows_per_cta(keys, C),
+                     "tensor_tflops": tflops, "frac_of_tf32_peak": tflops / tf32_peak}
     out["tf32_peak_tflops"] = tf32_peak
     out["tf32_peak_kind"] = "half of measured bf16" if p.exists() else "half of fallback bf16"
     return out
+
+
+def hook_measurement(dev, reps: int = 3):
+    """This package's layer step at the reference decode hook's shipped
+    settings (the configuration of ref_cuda_measurement's hook_layer): one
+    fp32 codebook for every head, fp16 K/V, top-2621 per QUERY head on
+    [0, T-64), the 64-token local window, attention of every query head over
+    its own set (LP_SELECT_QUERY_HEAD), 30 calls over N_SIDE resident layers.
+    Algorithmic bytes: the codebook (4.19 MB), the codes of the candidate
+    window and the K/V rows of every query head's set (32 x 2685 rows of
+    2 x 256 B, the reference's gather)."""
+    import ctypes
+    import torch
+    from laprune_b200 import _lib, ops
+    lib = _lib.load()
+    layers = _side_layers(dev, 78, shared_codebook=True)
+    for L in layers:
+        L["out"] = torch.empty((1, HQ, D), dtype=torch.float16, device=dev)
+        L["args"] = ops.build_args(L["q"], L["C"], L["codes"], L["keys"], L["vals"], topk=HOOK_K, sink=0,
+                                   local=LOCAL, select="query_head", out=L["out"])
+    need = max(lib.lp_sparse_decode_workspace_size(ctypes.byref(L["args"])) for L in layers)
+    ws = ops.workspace(need, dev, tag="bench_hook")
+    st = torch.cuda.current_stream(dev).cuda_stream
+
+    def call(i):
+        rc = lib.lp_sparse_decode(ctypes.byref(layers[i % N_SIDE]["args"]), ws.data_ptr(), ws.numel(), st)
+        if rc != 0:
+            _lib.check(rc)
+
+    us = _time_calls(call, reps * N_LAYERS)
+    peak, peak_kind = _peaks()
+    nbytes = M * K * D * 4 + HKV * (T_CTX - LOCAL) * M + HQ * (HOOK_K + LOCAL) * D * 2 * 2
+    res = {"layer_us": us, "tok_s_30_layers": 1e6 / (us * N_LAYERS),
+           "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (us * 1e-6) / 1e9,
+           "frac_of_peak": nbytes / (us * 1e-6) / 1e9 / peak, "peak_kind": peak_kind,
+           "device_error_bits": ops.device_errors(ws, dev)}
+    del layers
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---------------------------------------------------------------------------
@@ -490,8 +691,9 @@ def run_ours(args):
                                      "device_error_bits": graph_errs}},
             "gpu_launches": args.steps * N_LAYERS,
         }
-        if world == 1:
+        if world == 1 and not args.no_side:
             line["encode"] = encode_measurement(dev)
+            line["hook_layer"] = hook_measurement(dev)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -508,6 +710,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-cuda", action="store_true",
+                    help="reference arm: skip the timing of the reference's CUDA kernels")
+    ap.add_argument("--no-side", action="store_true",
+                    help="our arm: skip the side measurements (decode-hook layer, encoders)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="resident layer instances cycled over the 30 layer calls of a step "

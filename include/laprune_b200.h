@@ -209,6 +209,12 @@ size_t lp_encode_workspace_size(const lp_encode_args* a);
  * (AdditiveQuantizer._batch_icm_lut with 0 ICM iterations). */
 int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Vectors per CTA that lp_encode_keys uses for this geometry on the current
+ * device: 128 (one M=128 tensor-core tile per stage), 64 or 32 (smaller
+ * tiles while larger ones would leave SMs idle); 0 for invalid arguments.
+ * A diagnostic for tests that must cover every tile size. */
+int lp_encode_rows_per_cta(const lp_encode_args* a);
+
 /* ======================================================================
  * Building blocks behind the aq_kernels-named Python surface
  * ====================================================================== */
@@ -285,8 +291,11 @@ int lp_gqa_gather_kv(const lp_gqa_gather_args* a, void* stream);
  * kept until the process exits); it calls no cudaMalloc, cudaFree or other
  * allocating routine.  The caller still passes every input and output.
  *   - The first call on a device looks up the scratch's device address
- *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture starts on the device.
+ *     (cudaGetSymbolAddress) with that device current, and so does the first
+ *     call after the device's context was recreated (cudaDeviceReset unloads
+ *     the library's device code with the context, and the scratch comes back
+ *     zeroed at another address); make such a first call before any stream
+ *     capture starts on the device.
  *   - Geometries whose workspace exceeds LP_NOALLOC_SCRATCH_BYTES are
  *     rejected with LP_ERR_WORKSPACE (use lp_sparse_decode with a workspace
  *     of your own for those).

@@ -107,6 +107,7 @@ SIGNATURES = {
     "lp_sizeof_encode_args": (ctypes.c_size_t, []),
     "lp_encode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(EncodeArgs)]),
     "lp_encode_keys": (ctypes.c_int, [ctypes.POINTER(EncodeArgs), _c_p, ctypes.c_size_t, _c_p]),
+    "lp_encode_rows_per_cta": (ctypes.c_int, [ctypes.POINTER(EncodeArgs)]),
     "lp_lut_gather": (ctypes.c_int, [ctypes.POINTER(LutGatherArgs), _c_p]),
     "lp_lut_build": (ctypes.c_int, [ctypes.POINTER(LutBuildArgs), _c_p]),
     "lp_gqa_gather_kv": (ctypes.c_int, [ctypes.POINTER(GqaGatherArgs), _c_p]),

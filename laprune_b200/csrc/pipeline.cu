@@ -172,8 +172,15 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
 
     p.bm_words = (a->T_codes + 31) / 32 + 1;
 
-    // the fused single-kernel path (cooperative, one CTA per SM)
+    // the fused single-kernel path (cooperative, one CTA per SM).  Every
+    // fused launch on a device has this grid: a call's CTAs derive its epoch
+    // as (launch counter / grid size) from a counter that each CTA of every
+    // earlier call advanced by one, which is consistent only if all of them
+    // used the same grid size (the counter lives in the workspace, and a
+    // workspace is device memory of one device)
     p.fused_ctas = sms;
+    LP_CHECK(p.fused_ctas == sm_count(device) && p.fused_ctas > 0,
+             "internal: the fused grid must have one CTA per SM of the device");
     {
         const int cn_min = p.U > 0 ? p.fused_ctas / p.U : 0;
         const int nwu = p.ncand > 0 ? ((p.c1 + 31) >> 5) - (p.c0 >> 5) : 0;
@@ -634,6 +641,24 @@ static int encode_plan(const lp_encode_args* a, size_t* bytes, int64_t* nsets, i
     return LP_OK;
 }
 
+// Vectors per CTA of the encoder: fewer rows per CTA while that still
+// leaves SMs idle (the 32 stages are a serial chain per CTA, so more, smaller
+// CTAs finish sooner): 128 (one full UMMA tile), 64 or 32.
+static int encode_rows_per_cta(int64_t nsets, int64_t nvec_set, int sms) {
+    int rows = kEncRows;
+    while (rows > 32 && nsets * ((nvec_set + rows / 2 - 1) / (rows / 2)) <= sms) rows /= 2;
+    return rows;
+}
+
+int lp_encode_rows_per_cta(const lp_encode_args* a) {
+    size_t bytes = 0;
+    int64_t ns = 0, nv = 0;
+    if (encode_plan(a, &bytes, &ns, &nv) != LP_OK) return 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    return encode_rows_per_cta(ns, nv, sm_count(dev));
+}
+
 size_t lp_encode_workspace_size(const lp_encode_args* a) {
     size_t bytes = 0;
     int64_t ns = 0, nv = 0;
@@ -685,10 +710,7 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
     ep.cs_b = a->codes_stride_b;
     ep.cs_h = a->codes_stride_h;
     ep.cs_t = a->codes_stride_t;
-    // fewer rows per CTA while that still leaves SMs idle: the stages are a
-    // serial chain per CTA, so more, smaller CTAs finish sooner
-    int rows = kEncRows;
-    while (rows > 32 && nsets * ((nvec_set + rows / 2 - 1) / (rows / 2)) <= sm_count(dev)) rows /= 2;
+    const int rows = encode_rows_per_cta(nsets, nvec_set, sm_count(dev));
     ep.rows_per_cta = rows;
     ep.ctas_per_set = (int)((nvec_set + rows - 1) / rows);
     ep.force_exact = (a->flags & LP_ENCODE_FLAG_EXACT) ? 1 : 0;
@@ -878,19 +900,52 @@ namespace lp {
 // address once per device.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[LP_NOALLOC_SCRATCH_BYTES];
 
+// The identity of the device's current context (0 if the driver cannot say).
+// A device reset destroys the primary context and unloads this module with
+// it; the scratch then reappears at another address in the next context, so
+// the address looked up for a device is only valid while its context lives.
+static unsigned long long current_context_id() {
+    using GetCurrentFn = CUresult (*)(CUcontext*);
+    using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrentFn get_current = nullptr;
+    static GetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrentFn>(fn);
+        fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetIdFn>(fn);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current && get_id && get_current(&ctx) == CUDA_SUCCESS && ctx && get_id(ctx, &id) == CUDA_SUCCESS)
+        return id;
+    return 0;
+}
+
 static int noalloc_scratch(void** out) {
     static std::mutex mu;
     static void* addr[64] = {nullptr};
+    static unsigned long long ctx_of[64] = {0};
     int dev = 0;
     LP_CUDA(cudaGetDevice(&dev));
     LP_CHECK(dev >= 0 && dev < 64, "device ordinal out of range (at most 64 devices)");
+    // 0 before the device's first runtime call (no context yet): the lookup
+    // below then creates the context
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    if (!addr[dev] || ctx == 0 || ctx != ctx_of[dev]) {
         void* ptr = nullptr;
         LP_CUDA(cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch));
         LP_CHECK(ptr != nullptr && (reinterpret_cast<uintptr_t>(ptr) & 255u) == 0,
                  "built-in scratch has no 256-byte aligned device address");
         addr[dev] = ptr;
+        ctx_of[dev] = current_context_id();
     }
     *out = addr[dev];
     return LP_OK;

@@ -231,17 +231,9 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
     return SparseDecodeResult(out=o, topk=tk[:, :topk] if tk is not None else None, head_scores=hs)
 
 
-def encode_keys(x: torch.Tensor, codebooks: torch.Tensor, codes: Optional[torch.Tensor] = None, *,
-                exact: bool = False, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Greedy residual additive-quantization codes of vectors (lp_encode_keys).
-
-    x: [B,H,T,128] (bf16/fp16/fp32, any strides) or [N,128]; codebooks fp32
-    [H,32,256,128] (vector (b,h,t) uses set h) or [32,256,128] (one set).
-    ``codes``: optional uint8 [B,H,T,32] destination (e.g. a slice of a code
-    cache, rows of 32 contiguous bytes); allocated when omitted.  Returns it.
-    Every distance follows the CPU arithmetic exactly (first minimum on
-    ties); ``exact=True`` computes all of them on CUDA cores (testing).
-    """
+def _encode_args(x: torch.Tensor, codebooks: torch.Tensor, codes: Optional[torch.Tensor], exact: bool):
+    """Validate the encoder's tensors and fill lp_encode_args; allocates
+    ``codes`` when omitted.  Returns (args, codes)."""
     flat = x.dim() == 2
     x4 = x.view(1, 1, *x.shape) if flat else x
     if x4.dim() != 4:
@@ -275,6 +267,29 @@ def encode_keys(x: torch.Tensor, codebooks: torch.Tensor, codes: Optional[torch.
     a.codes_stride_b, a.codes_stride_h, a.codes_stride_t = c4.stride(0), c4.stride(1), c4.stride(2)
     a.B, a.H, a.T, a.D, a.M, a.K = B, H, T, D, M, K
     a.flags = _lib.LP_ENCODE_FLAG_EXACT if exact else 0
+    return a, codes
+
+
+def encode_rows_per_cta(x: torch.Tensor, codebooks: torch.Tensor) -> int:
+    """Vectors per CTA (128, 64 or 32) that :func:`encode_keys` uses for
+    these shapes on x's device (a diagnostic; lp_encode_rows_per_cta)."""
+    a, _ = _encode_args(x, codebooks, None, False)
+    with torch.cuda.device(x.device):
+        return int(_lib.load().lp_encode_rows_per_cta(ctypes.byref(a)))
+
+
+def encode_keys(x: torch.Tensor, codebooks: torch.Tensor, codes: Optional[torch.Tensor] = None, *,
+                exact: bool = False, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Greedy residual additive-quantization codes of vectors (lp_encode_keys).
+
+    x: [B,H,T,128] (bf16/fp16/fp32, any strides) or [N,128]; codebooks fp32
+    [H,32,256,128] (vector (b,h,t) uses set h) or [32,256,128] (one set).
+    ``codes``: optional uint8 [B,H,T,32] destination (e.g. a slice of a code
+    cache, rows of 32 contiguous bytes); allocated when omitted.  Returns it.
+    Every distance follows the CPU arithmetic exactly (first minimum on
+    ties); ``exact=True`` computes all of them on CUDA cores (testing).
+    """
+    a, codes = _encode_args(x, codebooks, codes, exact)
     lib = _lib.load()
     need = lib.lp_encode_workspace_size(ctypes.byref(a))
     if need == 0:

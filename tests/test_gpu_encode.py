@@ -102,3 +102,22 @@ def test_codes_written_into_a_cache_slice_score_like_the_reference(golden_dir):
     hs = r.head_scores.cpu().numpy()[:, :, fix["sample"]]
     ref = fix["scores"]
     assert np.abs(hs - ref).max() <= 1e-3 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("B,H,T,per_head,rows", [
+    (1, 8, 4096, True, 128),    # prefill chunk: 1 x 8 KV heads x 4096 keys, 256 CTAs of 128 vectors
+    (1, 1, 12288, False, 128),  # 12k vectors on one shared codebook, 96 CTAs of 128
+    (1, 8, 1024, True, 64),     # 8 x 1024: 128 CTAs of 64 vectors
+])
+def test_large_tiles_equal_the_oracle(B, H, T, per_head, rows):
+    """The 128- and 64-row CTA tiles (smaller batches run 32-row tiles), each
+    checked to be the tile the library picks and bit-exact with the oracle."""
+    g = torch.Generator().manual_seed(20 + rows + H)
+    C = torch.randn((H, 32, 256, 128) if per_head else (32, 256, 128), generator=g) * 0.05
+    keys = torch.randn((B, H, T, 128), generator=g).to(torch.bfloat16)
+    dev = _dev()
+    kd, cd = keys.to(dev), C.to(dev)
+    assert ops.encode_rows_per_cta(kd, cd) == rows
+    got = ops.encode_keys(kd, cd)
+    torch.cuda.synchronize()
+    assert np.array_equal(got.cpu().numpy(), _oracle_codes(keys, C))

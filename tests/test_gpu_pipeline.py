@@ -312,3 +312,67 @@ def test_wait_timeout_is_reported_and_the_next_call_recovers():
     torch.cuda.synchronize()
     assert ops.device_errors(ws, dev) == 0
     assert torch.equal(again.topk, ref.topk) and torch.equal(again.out, ref.out)
+
+
+@pytest.mark.parametrize("select,mode", [("kv_group", "auto"), ("kv_group", "exchange"), ("kv_group", "multi"),
+                                         ("query_head", "auto")])
+def test_batched_long_context_at_the_config5_unit_count(select, mode):
+    """B = 8 sequences x 8 KV heads = 64 selection units (256 per query
+    head) at T = 32768, the unit count of batched decode; checked against
+    the oracle whichever path the library takes for it."""
+    B, Hkv, G, T = 8, 8, 4, 32768
+    sink, local = 4, 64
+    k = ops.num_candidates(T, T, sink, local) // 50
+    C, codes, K, V, q = _rand_case(4242, B, Hkv, G, T)
+    dev = _dev()
+    r = ops.sparse_decode(q.to(dev), C.to(dev), codes.to(dev), K.to(dev), V.to(dev), topk=k, sink=sink,
+                          local=local, select=select, return_topk=True, out_dtype=torch.float32, **MODES[mode])
+    torch.cuda.synchronize()
+    top = r.topk.cpu().numpy()
+    top_ref, out_ref, s_ref = _oracle_step(C, codes, K, V, q, T, T, k, sink, local, True, select)
+    for u in range(top.shape[0]):
+        kth = np.sort(s_ref[u][top_ref[u]])[0]
+        assert _overlap(top[u], top_ref[u], s_ref[u], kth, 1e-4) >= 0.999, u
+    nu = top.shape[0] // B
+    for b in range(B):
+        keep = oracle.keep_positions(top[b * nu:(b + 1) * nu], T, sink, local)
+        idx_q = np.repeat(keep, G, axis=0) if select == "kv_group" else keep
+        want = oracle.sparse_attention(q[b].float().numpy(), K[b].float().numpy(), V[b].float().numpy(), idx_q, G)
+        assert np.abs(r.out[b].cpu().numpy() - want).max() <= 2e-3
+    assert np.abs(r.out.cpu().numpy() - out_ref).max() <= ATTN_ATOL
+    _check_errors()
+
+
+@pytest.mark.parametrize("kv_dtype", [torch.bfloat16, torch.float16])
+def test_query_head_selection_is_a_top_k_of_the_cache_dtype_scores(kv_dtype):
+    """The reference's decode hook casts its scores to the K/V cache dtype
+    before torch.topk (aq_evaluation.py:166, :199), so many tokens tie at the
+    k-th value and torch picks among them in an unspecified order.  This
+    package selects on the unrounded scores (exact fixed-point sums, ties by
+    lower index).  Rounding is monotone, so that choice is always one of the
+    reference's valid outcomes: every token whose rounded score lies strictly
+    above the k-th rounded score is selected, and every selected token rounds
+    to at least that value.  Keep-set tolerance: none (100 % of the tokens
+    above the tie value, and only tokens at or above it)."""
+    Hkv, G, T, sink, local = 8, 4, 131072, 0, 64
+    k = 2621  # the decode hook's keep size at 128k (mask_out 0.98)
+    C, codes, _, _, q = _rand_case(515, 1, Hkv, G, 8, cap=8)  # codebooks and queries only
+    g = torch.Generator().manual_seed(516)
+    codes = torch.randint(0, 256, (1, Hkv, T, 32), generator=g, dtype=torch.uint8)
+    dev = _dev()
+    r = ops.sparse_decode(q.to(dev), C[0].to(dev), codes.to(dev), topk=k, sink=sink, local=local,
+                          select="query_head", attention=False, return_topk=True, return_head_scores=True)
+    torch.cuda.synchronize()
+    lo, hi = ops._window(T, T, sink, local)
+    rounded = r.head_scores[0, :, lo:hi].to(torch.float16).to(kv_dtype).float()
+    sel = r.topk.long() - lo
+    ties_at_kth = 0
+    for h in range(Hkv * G):
+        kth = torch.topk(rounded[h], k).values.min()
+        mine = rounded[h][sel[h]]
+        assert (mine >= kth).all(), h
+        above = rounded[h] > kth
+        assert int(above.sum()) == int((mine > kth).sum()), h
+        ties_at_kth += int((rounded[h] == kth).sum()) - int((mine == kth).sum())
+    assert ties_at_kth > 0  # the rounded scores do tie at the threshold (the case this covers)
+    _check_errors()

@@ -37,9 +37,12 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls_in_a_row():
     ref = ops.sparse_decode(q, C, codes, K, V, topk=k, sink=sink, local=local, return_topk=True)
     lib = _lib.load()
     stream = ops._stream_handle(dev)
-    for _ in range(2):  # the second call runs on the scratch the first one left behind
-        out = torch.empty_like(ref.out)
-        top = torch.empty((8, k), dtype=torch.int32, device=dev)
+    # every output exists before the first call, so that device memory in use
+    # can only change through the entry point itself
+    outs = [(torch.empty_like(ref.out), torch.empty((8, k), dtype=torch.int32, device=dev)) for _ in range(2)]
+    torch.cuda.synchronize(dev)
+    free = []
+    for out, top in outs:  # the second call runs on the scratch the first one left behind
         a = ops.build_args(q, C, codes, K, V, topk=k, T_codes=None, T_total=None, sink=sink, local=local,
                            select="kv_group", scale=None, out=out, head_scores=None, topk_out=top,
                            prefetch=None)
@@ -47,9 +50,13 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls_in_a_row():
         with torch.cuda.device(dev):
             _lib.check(lib.lp_sparse_decode_noalloc(ctypes.byref(a), stream, ctypes.byref(bits)))
         torch.cuda.synchronize(dev)
+        free.append(torch.cuda.mem_get_info(dev)[0])
         assert bits.value & _lib.LP_DEVERR_WAIT_TIMEOUT == 0
         assert torch.equal(top, ref.topk)
         assert (out.float() - ref.out.float()).abs().max().item() <= ATTN_ATOL
+    # no device memory was taken by the second call (the first may have loaded
+    # the library's device code into the context)
+    assert free[1] == free[0]
 
 
 def test_noalloc_rejects_a_geometry_beyond_its_scratch():
