@@ -134,6 +134,12 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
+// Normal L2 priority, for streams that other CTAs read again soon after.
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
 
 // 16-byte asynchronous copy global -> shared (L2 only, bypassing L1).
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {

@@ -16,9 +16,10 @@
 // still building theirs.
 //
 // Phases (CTA c belongs to one selection unit u = (b, kv head)):
-//   A  LUT build: the unit's CTAs split its 32*256 codeword rows evenly,
-//      write LUT_sum[u][k][m] = q_sum . C_m[k] (fp32) to L2 and raise an
-//      epoch-tagged flag each.  The first code tiles of phase B are already
+//   A  LUT build: the CTAs of the units that read one codebook (a LUT
+//      group) split its 32*256 codeword rows evenly, write LUT_sum[u][k][m]
+//      = q_sum(u) . C_m[k] (fp32) of every unit u of the group to L2 and
+//      raise an epoch-tagged flag each.  The first code tiles of phase B are already
 //      streaming into the CTA's TMA ring; the rest follow once the codebook
 //      stream is done.                                     | the unit's flags
 //   B  score: the unit's table is staged as int32 fixed point (exact sums,
@@ -63,8 +64,15 @@ constexpr int kFMaxWords = 8192;                 // bitmap words per unit in sme
 constexpr int kFMaxRows = 192;                   // kept rows per attention chunk in phase E
 constexpr int kPubWin = 128;                     // bins in a CTA's published count window
 constexpr int kPubMaxCtas = 64;                  // CTAs per unit of the published-candidate path
-constexpr int kPubMaxCap = 1024;                 // published candidates per CTA (own copy in shared memory)
+constexpr int kPubMaxCap = 2048;                 // published candidates per CTA (own copy in shared memory)
 constexpr int kFastTieCap = 1024;                // tie-bin entries the fast selection path settles
+// spill mode (a CTA's share above kFScoreCap tokens): the scores go to the
+// L2-resident global buffer and the shared-memory score region holds the row
+// list and the CTA's selection bitmaps instead
+constexpr int kFSpillList = 5120;                // row list entries (above-threshold + tie winners <= k)
+constexpr int kFSpillWords = 2112;               // own bitmap words of a CTA (tokens <= 32 * 2110)
+constexpr int kFSpillMaxTok = 32 * (kFSpillWords - 2);
+static_assert((kFSpillList + 2 * kFSpillWords) * 4 <= kFScoreCap * 4, "spill overlays fit the score region");
 
 struct FusedParams {
     const void* q;
@@ -77,7 +85,10 @@ struct FusedParams {
     const void* vals;
     int64_t k_stride_b, k_stride_h, k_stride_t;
     int64_t v_stride_b, v_stride_h, v_stride_t;
-    int Hkv, G, U;
+    int Hkv, G, U;     // G: query heads attended per unit
+    int B;             // sequences
+    int Hu, upk;       // units per sequence, units per KV head (1: KV-group units, G: query-head units)
+    int spill;         // 1: the CTAs' shares exceed the shared-memory score buffer; scores live in sel_scores
     int c0, c1, k;
     int n_sink, local_start, n_local, n_rows, T_total;
     float scale_log2;
@@ -261,6 +272,29 @@ __device__ __forceinline__ void fused_cta_unit(int cta, int nctas, int U, int* u
         *u = extra + i / base; *j = i - (*u - extra) * base; *n = base;
     }
 }
+// first CTA of unit u (u == U: one past the last CTA)
+__device__ __forceinline__ int fused_unit_first_cta(int u, int nctas, int U) {
+    const int base = nctas / U, extra = nctas % U;
+    return u < extra ? u * (base + 1) : extra * (base + 1) + (u - extra) * base;
+}
+
+// Units are ordered KV head first (v = (hkv * B + b) * upk + g), so the units
+// that read one codebook -- every unit of a KV head with per-KV-head
+// codebooks, all of them with a shared one -- are consecutive, and so are
+// their CTAs.  A LUT group is such a run of at most kFLutGroup units; its
+// CTAs split the codebook's rows once and build every member's table.
+constexpr int kFLutGroup = 64;
+__device__ __forceinline__ void fused_lut_group(int v, int U, int cb_units, int* g0, int* g1) {
+    const int c0 = v / cb_units * cb_units;           // this codebook's run of units
+    const int cnt = min(cb_units, U - c0);
+    const int nsub = (cnt + kFLutGroup - 1) / kFLutGroup;
+    const int r = v - c0;
+    int s = r * nsub / cnt;                            // sub-run s covers [s*cnt/nsub, (s+1)*cnt/nsub)
+    while (s + 1 < nsub && (s + 1) * cnt / nsub <= r) ++s;
+    while (s > 0 && s * cnt / nsub > r) --s;
+    *g0 = c0 + s * cnt / nsub;
+    *g1 = c0 + (s + 1) * cnt / nsub;
+}
 
 // ---- warp-level tensor-core tiles for phase E (mma.sync m16n8k16, fp32
 //      accumulators; A row-major, B column-major; A and B of one type) ----
@@ -325,7 +359,13 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     unsigned long long* ubar = p.bar + u;
     int nbar = 0;  // unit barriers passed in this call (uniform over the unit's CTAs)
     __shared__ uint32_t s_epoch;
-    const int b = u / p.Hkv, hkv = u - b * p.Hkv;
+    // unit u = (KV head hkv, sequence b, unit head hu) in KV-head-major order;
+    // its codes, codebook and K/V rows are those of KV head hkv, its query
+    // rows hu*G .. hu*G + G - 1; ul is its index in the caller's (b, hu)
+    // order (rows of the top-k output)
+    const int gi = u % p.upk, hb = u / p.upk, hkv = hb / p.B, b = hb - hkv * p.B;
+    const int hu = hkv * p.upk + gi;
+    const int ul = b * p.Hu + hu;
     // the CTA's tokens: a run of whole bitmap words of the candidate window
     const int wlo = p.c0 >> 5, whi = (p.c1 + 31) >> 5;
     const int nwu = whi - wlo;
@@ -335,17 +375,24 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     const int t_end = min(p.c1, w_end * 32);
     const int ntok = max(0, t_end - t_begin);
     const int ntiles = (ntok + kFThreads - 1) / kFThreads;
-    const bool keep_smem = ntok <= kFScoreCap;
+    const bool keep_smem = !p.spill;  // the plan guarantees ntok <= kFScoreCap then
     const uint8_t* src = p.codes + (int64_t)b * p.codes_stride_b + (int64_t)hkv * p.codes_stride_h;
 
     uint64_t* s_empty = s_bar + kFStages;      // per-slot "all warps done" barriers
     uint64_t* s_abar = s_bar + 2 * kFStages;   // phase-A codebook stages
-    // phase A's share of the unit's 32*256 codeword rows, split evenly over
-    // its cn CTAs, streamed HBM -> shared memory in 64-row (32 KB) chunks
-    // through 3 stages
+    // phase A's share of the codebook's 32*256 rows: split evenly over the
+    // ncg CTAs of the unit's LUT group (units gv0 .. gv1-1, which read the
+    // same codebook), streamed HBM -> shared memory in 64-row (32 KB) chunks
+    // through 3 stages; each row is dotted with the summed query of every
+    // unit of the group
     constexpr int64_t kRows = 32 * 256;
-    const int64_t f_begin = (kRows * cj / cn) & ~(int64_t)7;
-    const int64_t f_end = cj + 1 == cn ? kRows : ((kRows * (cj + 1) / cn) & ~(int64_t)7);
+    int gv0, gv1;
+    fused_lut_group(u, p.U, p.cb_per_kv_head ? p.B * p.upk : p.U, &gv0, &gv1);
+    const int gc0 = fused_unit_first_cta(gv0, gridDim.x, p.U);
+    const int ncg = fused_unit_first_cta(gv1, gridDim.x, p.U) - gc0;
+    const int jg = blockIdx.x - gc0, nq = gv1 - gv0;
+    const int64_t f_begin = (kRows * jg / ncg) & ~(int64_t)7;
+    const int64_t f_end = jg + 1 == ncg ? kRows : ((kRows * (jg + 1) / ncg) & ~(int64_t)7);
     const int nchunk = (int)((f_end - f_begin + 63) / 64);
     const float* cbu = p.cb + (int64_t)(p.cb_per_kv_head ? hkv : 0) * (kRows * 128);
     auto abuf = [&](int c) -> unsigned char* {
@@ -364,7 +411,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     // the first 3 codebook chunks, then the first phase-B code tiles
     auto issue_inputs = [&]() {
         for (int c = 0; c < 3 && c < nchunk; ++c) issue_chunk(c);
-        policy = policy_evict_first();
+        policy = p.upk > 1 ? policy_evict_normal() : policy_evict_first();
         for (int i = 0; i < npre0; ++i) {
             const int t0 = t_begin + i * kFThreads;
             const int nn = min(kFThreads, t_end - t0);
@@ -410,21 +457,28 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
 
     for (int i = tid; i < p.G * 128; i += kFThreads) {
         const int g = i >> 7, d = i & 127;
-        s_qu[i] = to_f32(reinterpret_cast<const QT*>(p.q)[(int64_t)b * p.q_stride_b + (int64_t)(hkv * p.G + g) * p.q_stride_h + d]);
+        s_qu[i] = to_f32(reinterpret_cast<const QT*>(p.q)[(int64_t)b * p.q_stride_b + (int64_t)(hu * p.G + g) * p.q_stride_h + d]);
     }
 
-    // ================= phase A: LUT build of the CTA's unit =================
+    // ================= phase A: LUT build of the CTA's LUT group =================
     // The CTA's codeword rows arrive in the 3 chunk stages issued above;
-    // warp w dots rows 4w..4w+3 of a chunk with the summed query and reduces
-    // the 4 dot products with a 6-shuffle transpose.
+    // warp w dots rows 4w..4w+3 of a chunk with the summed query of each
+    // unit of the group and reduces the 4 dot products with a 6-shuffle
+    // transpose.
     {
-        // q_sum of the unit, summed over g in order (s_hist is free now)
-        float* s_qsum = reinterpret_cast<float*>(s_hist);
-        __syncthreads();  // s_qu complete
-        for (int d = tid; d < 128; d += kFThreads) {
+        // the summed query rows of the group's units (fp32, g in order), in
+        // the ring's slots 2.. (their code tiles are issued after phase A)
+        float* s_qs = reinterpret_cast<float*>(s_ring + kFPre0 * kFTile);  // [nq <= kFLutGroup][128]
+        static_assert(kFPre0 * kFTile + kFLutGroup * 128 * 4 <= FusedSmem::kRing, "group queries fit the ring");
+        for (int i = tid; i < nq * 128; i += kFThreads) {
+            const int jq = i >> 7, d = i & 127;
+            const int v = gv0 + jq;
+            const int vgi = v % p.upk, vhb = v / p.upk, vkv = vhb / p.B, vb = vhb - vkv * p.B;
+            const QT* qr = reinterpret_cast<const QT*>(p.q) + (int64_t)vb * p.q_stride_b +
+                           (int64_t)((vkv * p.upk + vgi) * p.G) * p.q_stride_h + d;
             float acc = 0.f;
-            for (int g = 0; g < p.G; ++g) acc += s_qu[g * 128 + d];
-            s_qsum[d] = acc;
+            for (int g = 0; g < p.G; ++g) acc += to_f32(qr[(int64_t)g * p.q_stride_h]);
+            s_qs[i] = acc;
         }
         __syncthreads();
         bool okA = true;
@@ -441,35 +495,42 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 const int m = (int)((fr >> 8) & 31);
                 const int k0 = (int)(fr & 255);
                 const float* rows = reinterpret_cast<const float*>(abuf(c)) + (warp * 4) * 128 + lane * 4;
-                const float4 qv = *reinterpret_cast<const float4*>(&s_qsum[lane * 4]);
-                float v[4];
+                float4 cv[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float4 cv = (fr + j < f_end) ? *reinterpret_cast<const float4*>(rows + j * 128)
-                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-                    float a = qv.x * cv.x;
-                    a = fmaf(qv.y, cv.y, a);
-                    a = fmaf(qv.z, cv.z, a);
-                    a = fmaf(qv.w, cv.w, a);
-                    v[j] = a;
-                }
-                // transpose-reduce of 4 values: lane l ends with row (l >> 3) & 3
-                const bool b4 = lane & 16, b3 = lane & 8;
-                float w2[2];
+                for (int j = 0; j < 4; ++j)
+                    cv[j] = (fr + j < f_end) ? *reinterpret_cast<const float4*>(rows + j * 128)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+                const int jr = (lane >> 3) & 3;  // the row whose total this lane ends with
+                float* dst = p.lut + ((int64_t)gv0 * 256 + k0 + jr) * 32 + m;
+#pragma unroll 4
+                for (int jq = 0; jq < nq; ++jq) {  // independent reductions: unrolled to overlap their shuffles
+                    const float4 qv = *reinterpret_cast<const float4*>(&s_qs[jq * 128 + lane * 4]);
+                    float v[4];
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const float keep = b4 ? v[2 + j] : v[j];
-                    const float send = b4 ? v[j] : v[2 + j];
-                    w2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                    for (int j = 0; j < 4; ++j) {
+                        float a = qv.x * cv[j].x;
+                        a = fmaf(qv.y, cv[j].y, a);
+                        a = fmaf(qv.z, cv[j].z, a);
+                        a = fmaf(qv.w, cv[j].w, a);
+                        v[j] = a;
+                    }
+                    // transpose-reduce of 4 values: lane l ends with row (l >> 3) & 3
+                    const bool b4 = lane & 16, b3 = lane & 8;
+                    float w2[2];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const float keep = b4 ? v[2 + j] : v[j];
+                        const float send = b4 ? v[j] : v[2 + j];
+                        w2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                    }
+                    const float keep = b3 ? w2[1] : w2[0];
+                    const float send = b3 ? w2[0] : w2[1];
+                    float tot = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                    tot += __shfl_xor_sync(0xffffffffu, tot, 4);
+                    tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+                    tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+                    if ((lane & 7) == 0 && fr + jr < f_end) dst[(int64_t)jq * 256 * 32] = tot;
                 }
-                const float keep = b3 ? w2[1] : w2[0];
-                const float send = b3 ? w2[0] : w2[1];
-                float tot = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-                tot += __shfl_xor_sync(0xffffffffu, tot, 4);
-                tot += __shfl_xor_sync(0xffffffffu, tot, 2);
-                tot += __shfl_xor_sync(0xffffffffu, tot, 1);
-                const int j = (lane >> 3) & 3;
-                if ((lane & 7) == 0 && fr + j < f_end) p.lut[((int64_t)u * 256 + k0 + j) * 32 + m] = tot;
             }
             __syncthreads();  // stage c fully consumed
             if (tid == 0 && c + 3 < nchunk) issue_chunk(c + 3);
@@ -509,8 +570,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         float4 v[4];
         {
             bool ok = true;
-            if (tid < cn) {
-                const unsigned long long* fl = p.lut_flag + (blockIdx.x - cj) + tid;  // the unit's CTAs
+            if (tid < ncg) {
+                const unsigned long long* fl = p.lut_flag + gc0 + tid;  // the LUT group's CTAs
                 const long long lim = p.test_timeout ? (1ll << 20) : kWaitCycles;
                 const long long t0 = clock64();
                 while (!tag_ok(ld_tag_acquire(fl), s_epoch)) {
@@ -747,14 +808,26 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             __syncthreads();
             if (pub_ok) {
                 unsigned long long* slot = p.pub + (int64_t)blockIdx.x * p.pub_cap * 2;
-                for (int lt = tid; lt < ntok; lt += kFThreads) {
-                    const float sc = s_scores[lt];
-                    const int bin = score_bin(sc, bp.lo, bp.inv_w, kNB);
-                    if (bin >= bj) {
-                        const int pos = (int)atomicAdd(&s_cur[min(bin - bj, kPubWin - 1)], 1u);
-                        st_tag(slot + 2 * pos, __float_as_uint(sc), s_epoch);
-                        st_tag(slot + 2 * pos + 1, (uint32_t)(t_begin + lt), s_epoch);
-                        s_own[pos] = make_float2(sc, __int_as_float(t_begin + lt));
+                // PU scores per thread per round, all loads issued before any
+                // is used (spilled scores come from L2)
+                constexpr int PU = 16;
+                for (int base = 0; base < ntok; base += kFThreads * PU) {
+                    float scv[PU];
+#pragma unroll
+                    for (int r = 0; r < PU; ++r) {
+                        const int lt = base + r * kFThreads + tid;
+                        scv[r] = lt < ntok ? (keep_smem ? s_scores[lt] : __ldcg(gsc + t_begin + lt)) : 0.f;
+                    }
+#pragma unroll
+                    for (int r = 0; r < PU; ++r) {
+                        const int lt = base + r * kFThreads + tid;
+                        const int bin = score_bin(scv[r], bp.lo, bp.inv_w, kNB);
+                        if (lt < ntok && bin >= bj) {
+                            const int pos = (int)atomicAdd(&s_cur[min(bin - bj, kPubWin - 1)], 1u);
+                            st_tag(slot + 2 * pos, __float_as_uint(scv[r]), s_epoch);
+                            st_tag(slot + 2 * pos + 1, (uint32_t)(t_begin + lt), s_epoch);
+                            s_own[pos] = make_float2(scv[r], __int_as_float(t_begin + lt));
+                        }
                     }
                 }
             }
@@ -771,7 +844,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     //      s_list holds the above-threshold tokens followed by the tie winners ----
     constexpr int D = 128;
     constexpr int R = kFMaxRows;
-    int* s_list = reinterpret_cast<int*>(s_scores);  // [<= kFScoreCap] (scores consumed by then)
+    int* s_list = reinterpret_cast<int*>(s_scores);  // [<= kFScoreCap | kFSpillList] (scores consumed by then)
     KT* s_k = reinterpret_cast<KT*>(s_ring);         // [R][128] (the ring is free after phase B)
     KT* s_v = s_k + R * D;                           // [R][128]
     const KT* kb = reinterpret_cast<const KT*>(p.keys) + (int64_t)b * p.k_stride_b + (int64_t)hkv * p.k_stride_h;
@@ -807,13 +880,34 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         cp_async_commit();
     };
     __shared__ int s_nabove, s_nwin;
+    using ListScan = cub::BlockScan<int, kFThreads>;
+    // s_list[pos0 ..] = tok0 + 32*i + j for every set bit j of words[i],
+    // i < nwords, in ascending order, 512 words per round; returns the count
+    // (every thread).  Ends with a block barrier.
+    auto list_bits = [&](const uint32_t* words, int nwords, int tok0, int pos0) -> int {
+        int run = 0;
+        for (int w0 = 0; w0 < nwords; w0 += kFThreads) {
+            const int w = w0 + tid;
+            const uint32_t bits = w < nwords ? words[w] : 0u;
+            int pos, total;
+            ListScan(scan_tmp).ExclusiveSum(__popc(bits), pos, total);
+            pos += pos0 + run;
+            for (uint32_t b2 = bits; b2; b2 &= b2 - 1) s_list[pos++] = tok0 + 32 * w + __ffs(b2) - 1;
+            run += total;
+            __syncthreads();  // scan_tmp is reused by the next round
+        }
+        return run;
+    };
 
     // ================= phase C: select =================
     uint32_t* bm = p.bitmap + (int64_t)u * p.bm_stride;
     const float* gsc_c = p.sel_scores + (int64_t)u * p.sel_stride;
     __shared__ int s_cnt_above, s_win_before, s_topk_off, s_ntie_loc, s_ntie, s_fast;
-    uint32_t* s_selw = s_hist + 1024;  // own words: selected bits (exchange path: above-threshold bits)
-    uint32_t* s_win = s_hist + 1536;   // exchange path: tie winners of the own range (bit lt)
+    // own words: selected bits (exchange path: above-threshold bits), and the
+    // tie winners of the own range (bit lt); spill mode keeps them after the
+    // row list in the (unused) score region
+    uint32_t* s_selw = keep_smem ? s_hist + 1024 : reinterpret_cast<uint32_t*>(s_scores) + kFSpillList;
+    uint32_t* s_win = keep_smem ? s_hist + 1536 : s_selw + kFSpillWords;
     const int nw_own = w_end - w_begin;
     const int ubase = blockIdx.x - cj;  // first CTA of the unit
     // ---- fast path: the unit's threshold bin from the published windows,
@@ -978,11 +1072,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 s_topk_off = c;
             }
             {
-                const uint32_t bits = tid < nw_own ? s_selw[tid] : 0u;
-                int pos, total;
-                Scan(scan_tmp).ExclusiveSum(__popc(bits), pos, total);
-                for (uint32_t b2 = bits; b2; b2 &= b2 - 1) s_list[pos++] = (w_begin + tid) * 32 + __ffs(b2) - 1;
-                if (tid == 0) s_nabove = total;
+                const int na = list_bits(s_selw, nw_own, w_begin * 32, 0);
+                if (tid == 0) s_nabove = na;
             }
             __syncthreads();
             // the unit's tie-bin entries: loads issued first (up to 2 per
@@ -1080,27 +1171,40 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         __syncthreads();
         const int bstar = s_bstar;
         int my_above = 0;
-        for (int w = w_begin + warp; w < w_end; w += NW) {
-            const int t = w * 32 + lane;
-            const bool valid = t >= p.c0 && t < p.c1;
-            float s = 0.f;
-            if (valid) s = keep_smem ? s_scores[t - t_begin] : __ldcg(gsc_c + t);
-            const int bin = score_bin(s, bp.lo, bp.inv_w, kNB);
-            const bool tie = valid && bin == bstar;
-            const uint32_t abv = __ballot_sync(0xffffffffu, valid && bin > bstar);
-            my_above += __popc(abv);
-            if (lane == 0) {
-                bm[w] = 0u;  // cleared for the exact slow path
-                s_selw[w - w_begin] = abv;
+        // 4 words per warp and round, their score loads issued first
+        // (spilled scores come from L2)
+        for (int w4 = w_begin + warp; w4 < w_end; w4 += 4 * NW) {
+            float sv4[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int t = (w4 + r * NW) * 32 + lane;
+                const bool valid = w4 + r * NW < w_end && t >= p.c0 && t < p.c1;
+                sv4[r] = valid ? (keep_smem ? s_scores[t - t_begin] : __ldcg(gsc_c + t)) : 0.f;
             }
-            const uint32_t tmask = __ballot_sync(0xffffffffu, tie);
-            if (tmask) {
-                int base = 0;
-                if (lane == 0) base = atomicAdd(&s_ntie_loc, __popc(tmask));
-                base = __shfl_sync(0xffffffffu, base, 0);
-                if (tie) {
-                    const int pos = base + __popc(tmask & ((1u << lane) - 1u));
-                    if (pos < kTieCap) s_tloc[pos] = make_float2(s, __int_as_float(t));
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int w = w4 + r * NW;
+                if (w >= w_end) break;  // warp-uniform
+                const int t = w * 32 + lane;
+                const bool valid = t >= p.c0 && t < p.c1;
+                const float s = sv4[r];
+                const int bin = score_bin(s, bp.lo, bp.inv_w, kNB);
+                const bool tie = valid && bin == bstar;
+                const uint32_t abv = __ballot_sync(0xffffffffu, valid && bin > bstar);
+                my_above += __popc(abv);
+                if (lane == 0) {
+                    bm[w] = 0u;  // cleared for the exact slow path
+                    s_selw[w - w_begin] = abv;
+                }
+                const uint32_t tmask = __ballot_sync(0xffffffffu, tie);
+                if (tmask) {
+                    int base = 0;
+                    if (lane == 0) base = atomicAdd(&s_ntie_loc, __popc(tmask));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (tie) {
+                        const int pos = base + __popc(tmask & ((1u << lane) - 1u));
+                        if (pos < kTieCap) s_tloc[pos] = make_float2(s, __int_as_float(t));
+                    }
                 }
             }
         }
@@ -1282,21 +1386,13 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         //      path), then the tie winners (bit lt of s_win = token t_begin + lt),
         //      each in ascending token order ----
         if (!s_fast) {
-            const uint32_t bits = tid < nw_own ? s_selw[tid] : 0u;
-            int pos, total;
-            Scan(scan_tmp).ExclusiveSum(__popc(bits), pos, total);
-            for (uint32_t b2 = bits; b2; b2 &= b2 - 1) s_list[pos++] = (w_begin + tid) * 32 + __ffs(b2) - 1;
-            if (tid == 0) s_nabove = total;
+            const int na = list_bits(s_selw, nw_own, w_begin * 32, 0);
+            if (tid == 0) s_nabove = na;
             __syncthreads();
         }
         {
-            const int nww = (ntok + 31) / 32;
-            const uint32_t bits = tid < nww ? s_win[tid] : 0u;
-            int pos, total;
-            Scan(scan_tmp).ExclusiveSum(__popc(bits), pos, total);
-            pos += s_nabove;
-            for (uint32_t b2 = bits; b2; b2 &= b2 - 1) s_list[pos++] = t_begin + tid * 32 + __ffs(b2) - 1;
-            if (tid == 0) s_nwin = total;
+            const int nwin = list_bits(s_win, (ntok + 31) / 32, t_begin, s_nabove);
+            if (tid == 0) s_nwin = nwin;
         }
         if (!s_fast && p.topk_out && tid == 0) s_topk_off = s_win_before;
         __syncthreads();
@@ -1309,33 +1405,39 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 if (c) atomicAdd(&s_topk_off, c);
             }
             const int shift0 = t_begin - w_begin * 32;  // 0 except for the first CTA (c0 % 32)
-            uint32_t wordsel = 0u;
-            const int w = tid;  // one own word per thread (nw_own <= kFScoreCap/32 + 2 <= 512)
-            if (w < nw_own) {
-                // winners of tokens 32*(w_begin+w) + i  <->  bit lt = 32*w + i - shift0
-                const int lt0 = 32 * w - shift0;
-                uint32_t r = 0u;
-                if (ntok > 0) {
-                    const int wl = lt0 >> 5, sh = lt0 & 31;  // lt0 may be negative for w = 0
-                    if (lt0 >= 0) {
-                        r = s_win[wl] >> sh;
-                        if (sh && wl + 1 < (ntok + 31) / 32) r |= s_win[wl + 1] << (32 - sh);
-                    } else {
-                        r = s_win[0] << (-lt0);
-                    }
-                }
-                wordsel = s_selw[w] | r;
-                const int tb = (w_begin + w) * 32;
-                if (tb < p.c0) wordsel &= ~0u << (p.c0 - tb);
-                if (tb + 32 > p.c1) wordsel &= (p.c1 - tb) >= 32 ? ~0u : ((1u << (p.c1 - tb)) - 1u);
-            }
-            int pos, total;
             __syncthreads();  // s_topk_off complete; scan_tmp free
-            Scan(scan_tmp).ExclusiveSum(__popc(wordsel), pos, total);
             const int off = s_topk_off;
-            for (uint32_t b2 = wordsel; b2; b2 &= b2 - 1) {
-                if (off + pos < p.k) p.topk_out[(int64_t)u * p.k + off + pos] = (w_begin + w) * 32 + __ffs(b2) - 1;
-                ++pos;
+            int run = 0;
+            for (int w0 = 0; w0 < nw_own; w0 += kFThreads) {  // 512 own words per round
+                uint32_t wordsel = 0u;
+                const int w = w0 + tid;
+                if (w < nw_own) {
+                    // winners of tokens 32*(w_begin+w) + i  <->  bit lt = 32*w + i - shift0
+                    const int lt0 = 32 * w - shift0;
+                    uint32_t r = 0u;
+                    if (ntok > 0) {
+                        const int wl = lt0 >> 5, sh = lt0 & 31;  // lt0 may be negative for w = 0
+                        if (lt0 >= 0) {
+                            r = s_win[wl] >> sh;
+                            if (sh && wl + 1 < (ntok + 31) / 32) r |= s_win[wl + 1] << (32 - sh);
+                        } else {
+                            r = s_win[0] << (-lt0);
+                        }
+                    }
+                    wordsel = s_selw[w] | r;
+                    const int tb = (w_begin + w) * 32;
+                    if (tb < p.c0) wordsel &= ~0u << (p.c0 - tb);
+                    if (tb + 32 > p.c1) wordsel &= (p.c1 - tb) >= 32 ? ~0u : ((1u << (p.c1 - tb)) - 1u);
+                }
+                int pos, total;
+                Scan(scan_tmp).ExclusiveSum(__popc(wordsel), pos, total);
+                pos += run;
+                for (uint32_t b2 = wordsel; b2; b2 &= b2 - 1) {
+                    if (off + pos < p.k) p.topk_out[(int64_t)ul * p.k + off + pos] = (w_begin + w) * 32 + __ffs(b2) - 1;
+                    ++pos;
+                }
+                run += total;
+                __syncthreads();  // scan_tmp is reused by the next round
             }
         }
         const int nabove = s_nabove;
@@ -1568,7 +1670,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 A = fmaf(aa[sl], f, A);
             }
             const int o = o0 + ol, g = o / D, d = o - g * D;
-            ob[(int64_t)(hkv * p.G + g) * p.out_stride_h + d] = from_f32<OT>(A / L);
+            ob[(int64_t)(hu * p.G + g) * p.out_stride_h + d] = from_f32<OT>(A / L);
         }
         if (p.phase_ns && tid == 0) atomicMax(&p.phase_ns[7], global_ns());
     }

@@ -69,6 +69,8 @@ struct Plan {
     int64_t bm_words;
     bool fused;       // single cooperative kernel path
     int fused_ctas, fused_max_split;
+    int fused_units;  // its units: (sequence, KV head), or (sequence, query head) for query-head selection
+    bool fused_spill; // its CTAs' shares exceed the shared-memory score buffer
     // workspace regions
     uint32_t* err;
     float* lut;
@@ -182,17 +184,28 @@ static int make_plan(const lp_sparse_decode_args* a, void* ws, Plan* P, int devi
     LP_CHECK(p.fused_ctas == sm_count(device) && p.fused_ctas > 0,
              "internal: the fused grid must have one CTA per SM of the device");
     {
-        const int cn_min = p.U > 0 ? p.fused_ctas / p.U : 0;
+        // per-KV-head selection: a unit is a (sequence, KV head) pair scoring
+        // with the summed query of its G heads; per-query-head selection: a
+        // unit is a (sequence, query head) pair, G units per KV head reading
+        // the same codes and K/V rows
+        p.fused_units = p.per_head ? p.Usel : p.U;
+        const int Uf = p.fused_units;
+        const int cn_min = Uf > 0 ? p.fused_ctas / Uf : 0;
         const int nwu = p.ncand > 0 ? ((p.c1 + 31) >> 5) - (p.c0 >> 5) : 0;
         const int ntok_max = cn_min > 0 ? (nwu + cn_min - 1) / cn_min * 32 : 0;
-        p.fused = !(a->flags & LP_FLAG_NO_FUSED) && !p.per_head && !p.heads && a->out != nullptr &&
-                  a->D == 128 && a->G <= kFusedMaxG && p.U <= p.fused_ctas && p.U <= kUnitBarWords && p.ncand > 0 && a->topk > 0 &&
-                  nwu <= kFMaxWords && cn_min >= 1 && ntok_max <= kFScoreCap;
+        // a CTA keeps the scores of up to kFScoreCap tokens in shared memory;
+        // above that (long contexts over few CTAs per unit) they spill to the
+        // L2-resident score buffer, with the row list bounded by kFSpillList
+        p.fused_spill = ntok_max > kFScoreCap;
+        p.fused = !(a->flags & LP_FLAG_NO_FUSED) && a->head_scores == nullptr && a->out != nullptr &&
+                  a->D == 128 && (p.per_head || a->G <= kFusedMaxG) && Uf <= p.fused_ctas && Uf <= kUnitBarWords &&
+                  p.ncand > 0 && a->topk > 0 && nwu <= kFMaxWords && cn_min >= 1 &&
+                  (!p.fused_spill || (ntok_max <= kFSpillMaxTok && a->topk <= kFSpillList));
         p.fused_max_split = cn_min + 1;
         // candidate publishing: each CTA aims at twice its even share of the
         // top-k plus a margin (slot capacity: that plus the population of
         // its threshold bin)
-        const int cn_max = p.U > 0 ? (p.fused_ctas + p.U - 1) / p.U : 1;
+        const int cn_max = Uf > 0 ? (p.fused_ctas + Uf - 1) / Uf : 1;
         p.pub_target = 2 * ((a->topk + cn_max - 1) / cn_max) + 32;
         p.pub_cap = p.pub_target + 64;
         if (p.pub_cap > kPubMaxCap || cn_max > kPubMaxCtas || (a->flags & LP_FLAG_EXCHANGE_SELECT)) p.pub_cap = 0;
@@ -349,8 +362,12 @@ static int launch_fused(const lp_sparse_decode_args* a, const Plan& p, cudaStrea
     fp.v_stride_h = a->v_stride_h;
     fp.v_stride_t = a->v_stride_t;
     fp.Hkv = a->Hkv;
-    fp.G = a->G;
-    fp.U = p.U;
+    fp.G = p.per_head ? 1 : a->G;
+    fp.U = p.fused_units;
+    fp.B = a->B;
+    fp.Hu = p.per_head ? a->Hkv * a->G : a->Hkv;
+    fp.upk = p.per_head ? a->G : 1;
+    fp.spill = p.fused_spill ? 1 : 0;
     fp.c0 = p.c0;
     fp.c1 = p.c1;
     fp.k = a->topk;

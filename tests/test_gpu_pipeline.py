@@ -376,3 +376,55 @@ def test_query_head_selection_is_a_top_k_of_the_cache_dtype_scores(kv_dtype):
         ties_at_kth += int((rounded[h] == kth).sum()) - int((mine == kth).sum())
     assert ties_at_kth > 0  # the rounded scores do tie at the threshold (the case this covers)
     _check_errors()
+
+
+@pytest.mark.parametrize("mode", ["auto", "exchange"])
+def test_query_head_units_on_the_fused_path_at_the_decode_hook_settings(mode):
+    """The reference decode hook's shipped settings: one codebook for every
+    head, fp16 K/V, T = 131072, top-2621 per QUERY head, sink 0, local 64.
+    The fused kernel runs one unit per query head (4.6 CTAs each, so their
+    scores spill to the L2-resident buffer); its selection must equal the
+    multi-kernel path's exactly and match the oracle."""
+    B, Hkv, G, T = 1, 8, 4, 131072
+    k, sink, local = 2621, 0, 64
+    C, codes, K, V, q = _rand_case(777, B, Hkv, G, T, per_kv=False, kv_dtype=torch.float16,
+                                   q_dtype=torch.float16)
+    dev = _dev()
+    args = [t.to(dev) for t in (q, C, codes, K, V)]
+    kw = dict(topk=k, sink=sink, local=local, select="query_head", return_topk=True, out_dtype=torch.float32)
+    ns = torch.zeros(8, dtype=torch.int64, device=dev)
+    r = ops.sparse_decode(*args, phase_ns=ns, **kw, **MODES[mode])
+    m = ops.sparse_decode(*args, fused=False, **kw)
+    torch.cuda.synchronize()
+    assert (ns.cpu().numpy() > 0).all(), "the fused kernel did not run"
+    assert torch.equal(r.topk, m.topk)
+    assert (r.out - m.out).abs().max().item() <= 2e-3
+    top_ref, out_ref, s_ref = _oracle_step(C, codes, K, V, q, T, T, k, sink, local, False, "query_head")
+    top = r.topk.cpu().numpy()
+    for u in range(top.shape[0]):
+        kth = np.sort(s_ref[u][top_ref[u]])[0]
+        assert _overlap(top[u], top_ref[u], s_ref[u], kth, 1e-4) >= 0.999, u
+    keep = oracle.keep_positions(top, T, sink, local)
+    want = oracle.sparse_attention(q[0].float().numpy(), K[0].float().numpy(), V[0].float().numpy(), keep, G)
+    assert np.abs(r.out[0].cpu().numpy() - want).max() <= 2e-3
+    assert np.abs(r.out.cpu().numpy() - out_ref).max() <= ATTN_ATOL
+    _check_errors()
+
+
+@pytest.mark.parametrize("B,Hkv,T,k", [(8, 8, 32768, 640), (2, 8, 131072, 2048), (4, 8, 65536, 1300)])
+def test_spilled_scores_select_like_the_multi_kernel_path(B, Hkv, T, k):
+    """KV-group selection with more tokens per CTA than its shared-memory
+    score buffer holds (B*Hkv units over 148 CTAs): the fused kernel keeps
+    its scores in the global buffer; selection equal to the multi-kernel
+    path's, attention within accumulation-order rounding."""
+    C, codes, K, V, q = _rand_case(900 + B, B, Hkv, 4, T)
+    dev = _dev()
+    args = [t.to(dev) for t in (q, C, codes, K, V)]
+    ns = torch.zeros(8, dtype=torch.int64, device=dev)
+    r = ops.sparse_decode(*args, topk=k, sink=4, local=64, return_topk=True, phase_ns=ns)
+    m = ops.sparse_decode(*args, topk=k, sink=4, local=64, return_topk=True, fused=False)
+    torch.cuda.synchronize()
+    assert (ns.cpu().numpy() > 0).all(), "the fused kernel did not run"
+    assert torch.equal(r.topk, m.topk)
+    assert (r.out.float() - m.out.float()).abs().max().item() <= 1e-2
+    _check_errors()
