@@ -185,7 +185,7 @@ typedef struct lp_encode_args {
     int64_t codes_stride_b, codes_stride_h, codes_stride_t;
     int32_t B, H, T, D, M, K;   /* D = 128, M = 32, K = 256 */
     int32_t flags;              /* LP_ENCODE_FLAG_* bits */
-    int32_t _pad0;
+    int32_t icm_iters;          /* ICM sweeps after the greedy pass (0: greedy codes only) */
 } lp_encode_args;
 
 #define LP_ENCODE_FLAG_EXACT 1 /* compute every distance on CUDA cores (testing) */
@@ -193,10 +193,18 @@ typedef struct lp_encode_args {
 /* sizeof(lp_encode_args), for bindings to verify their struct layout */
 size_t lp_sizeof_encode_args(void);
 /* Workspace bytes needed by lp_encode_keys (first 2048 bytes: error word
- * and reserved state, as for lp_sparse_decode). */
+ * and reserved state, as for lp_sparse_decode; with icm_iters > 0 also the
+ * vectors' reconstructions between sweeps, 512 bytes per vector). */
 size_t lp_encode_workspace_size(const lp_encode_args* a);
 
-/* Greedy residual encode: for m = 0..M-1, code_m = the first k minimising
+/* With icm_iters > 0 the greedy codes are then refined by up to icm_iters ICM
+ * sweeps (laprune/quantizer.py:356-370): each sweep re-chooses code m =
+ * 0..M-1 of every vector against the reconstruction without it
+ * (r = x - (full_recon - C_m[prev]), the same distance arithmetic), and a
+ * sweep that changes no code of the vectors sharing a codebook set ends that
+ * set's refinement.
+ *
+ * Greedy residual encode: for m = 0..M-1, code_m = the first k minimising
  * ||r||^2 + ||C_m[k]||^2 - 2 r.C_m[k] (fp32: the norms sequential chains of
  * fused multiply-adds in index order, r.C_m[k] 32 four-term chains over
  * dims 4l..4l+3 folded pairwise at strides 16, 8, 4, 2, 1), then

@@ -52,7 +52,7 @@ class EncodeArgs(ctypes.Structure):
         ("codebooks", _c_p), ("codes", _c_p),
         ("codes_stride_b", _c_i64), ("codes_stride_h", _c_i64), ("codes_stride_t", _c_i64),
         ("B", _c_i32), ("H", _c_i32), ("T", _c_i32), ("D", _c_i32), ("M", _c_i32), ("K", _c_i32),
-        ("flags", _c_i32), ("_pad0", _c_i32),
+        ("flags", _c_i32), ("icm_iters", _c_i32),
     ]
 
 

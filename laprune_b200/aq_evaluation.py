@@ -19,8 +19,8 @@ and cache dictionaries, the sparse path on this package's kernels:
 
 Dense attention (prefill, dense layers) stays the reference's torch SDPA
 call.  fp16 / bf16 K/V caches only (the reference's CUDA kernels take fp16; its
-fp32 path is its torch fallback).  Multi-token decode (Tq > 1), ICM
-refinement and key reconstruction are outside the decode path and raise.
+fp32 path is its torch fallback).  Multi-token decode (Tq > 1) and key
+reconstruction are outside the decode path and raise.
 """
 from __future__ import annotations
 
@@ -155,11 +155,13 @@ def _kv_cache_append(self_attn, k_new: torch.Tensor, v_new: torch.Tensor, total_
     return k_view, v_view, (k_view.data, v_view.data)
 
 
-def _encode_into(manager: AQLayerCodebookManager, layer_idx: int, keys: torch.Tensor, codes_dst: torch.Tensor) -> None:
+def _encode_into(manager: AQLayerCodebookManager, layer_idx: int, keys: torch.Tensor, codes_dst: torch.Tensor,
+                 icm_iters: int = 0) -> None:
     # keys [B, H, t, d] -> codes_dst [B, H, t, M] (a slice of the cache)
     if keys.shape[2] == 0:
         return
-    ops.encode_keys(keys, _encoding_codebooks(manager, layer_idx, keys.shape[1]), codes=codes_dst)
+    ops.encode_keys(keys, _encoding_codebooks(manager, layer_idx, keys.shape[1]), codes=codes_dst,
+                    icm_iters=icm_iters)
 
 
 def _prepare_aq_cache(self, manager: AQLayerCodebookManager, layer_idx: int, keys: torch.Tensor, need_recon: bool,
@@ -200,22 +202,18 @@ def _prepare_aq_cache(self, manager: AQLayerCodebookManager, layer_idx: int, key
                 return cache
             if pending > 0:
                 icm = int(conf.get("aq_encode_icm_iters_decode", 0))
-                if icm != 0:
-                    raise NotImplementedError(f"aq_encode_icm_iters_decode={icm}: ICM refinement is not on the decode path")
-                _encode_into(manager, layer_idx, keys[:, :, encoded:T], codes[:, :, encoded:T])
+                _encode_into(manager, layer_idx, keys[:, :, encoded:T], codes[:, :, encoded:T], icm)
             cache["seq_len"], cache["encoded_len"], cache["codes"] = T, T, codes
             self._aq_cache = cache
             return cache
     icm = int(conf.get("aq_encode_icm_iters_prefill", 0 if is_prefill else 2))
-    if icm != 0:
-        raise NotImplementedError(f"aq_encode_icm_iters_prefill={icm}: ICM refinement is not on the decode path")
     extra = max(0, int(conf.get("aq_code_extra_capacity", 0))) if is_prefill else 0
     codes = torch.empty((B, H, T + extra, M), dtype=torch.uint8, device=keys.device)
     group = int(conf.get("aq_prefill_group_size", 0))
     group = T if group <= 0 else group
     for t0 in range(0, T, group):
         t1 = min(T, t0 + group)
-        _encode_into(manager, layer_idx, keys[:, :, t0:t1], codes[:, :, t0:t1])
+        _encode_into(manager, layer_idx, keys[:, :, t0:t1], codes[:, :, t0:t1], icm)
     cache = {"seq_len": T, "encoded_len": T, "batch_size": B, "codes": codes, "approx": None}
     self._aq_cache = cache
     return cache

@@ -4,7 +4,8 @@ Mirrors ``AQLayerConfig`` / ``AQLayerCodebookManager`` of
 laprune/llm/aq_kv.py:79-699: the on-disk codebook format
 (``layer_{L}_group_{G}.pt`` holding ``{"M", "K", "d", "codebooks" [M,K,d]}``,
 aq_kv.py:251-342), greedy key encoding (``encode_keys`` /
-``encode_keys_batch`` with ``icm_iters=0``, aq_kv.py:348-429) and LUT
+``encode_keys_batch``, greedy with optional ICM refinement,
+aq_kv.py:348-429) and LUT
 scoring (``approx_inner_product*``, aq_kv.py:459-699), with every compute
 call on this package's sm_100a kernels:
 
@@ -15,9 +16,8 @@ call on this package's sm_100a kernels:
 
 Codebooks are held in fp32 on the manager's device whatever ``dtype`` says
 (``dtype`` is the dtype of returned scores, as the reference's manager dtype).
-There is no CPU fallback: a missing CUDA device or extension raises.  ICM
-refinement (``icm_iters > 0``) and codebook training are outside the decode
-path and raise ``NotImplementedError``.
+There is no CPU fallback: a missing CUDA device or extension raises.
+Codebook training is outside the decode path and is not provided.
 """
 from __future__ import annotations
 
@@ -41,13 +41,6 @@ class AQLayerConfig:
     d: int
     heads_per_group: int = 2
     num_heads: Optional[int] = None
-
-
-def _no_icm(icm_iters: int) -> None:
-    if int(icm_iters) != 0:
-        raise NotImplementedError(
-            f"icm_iters={icm_iters}: ICM refinement is not on the B200 decode path; "
-            "the decode configs encode greedily (aq_encode_icm_iters_decode: 0)")
 
 
 class AQLayerCodebookManager:
@@ -131,23 +124,24 @@ class AQLayerCodebookManager:
     @torch.no_grad()
     def encode_keys(self, layer_idx: int, head_idx: int, keys: torch.Tensor, batch_size: int = 3_000_000,
                     icm_iters: int = 2) -> torch.Tensor:
-        """Greedy codes ``[N, M]`` (uint8) of ``keys [N, d]`` with the codebook
-        of ``head_idx``'s group (aq_kv.py:348-388)."""
-        _no_icm(icm_iters)
+        """Codes ``[N, M]`` (uint8) of ``keys [N, d]`` with the codebook of
+        ``head_idx``'s group: greedy, then ``icm_iters`` ICM sweeps
+        (aq_kv.py:348-388)."""
         group_idx = self._group(layer_idx, head_idx)
         return self.encode_keys_batch(layer_idx, group_idx, keys, batch_size=batch_size, icm_iters=icm_iters)
 
     @torch.no_grad()
     def encode_keys_batch(self, layer_idx: int, group_idx: int, keys: torch.Tensor, batch_size: int = 3_000_000,
                           icm_iters: int = 2) -> torch.Tensor:
-        """Greedy codes ``[N_all, M]`` (uint8) of ``keys [N_all, d]`` with one
-        group's codebook (aq_kv.py:390-429).  fp32, fp16 and bf16 keys are
-        read as they are (the reference casts to the manager dtype first)."""
-        _no_icm(icm_iters)
+        """Codes ``[N_all, M]`` (uint8) of ``keys [N_all, d]`` with one group's
+        codebook: greedy, then ``icm_iters`` ICM sweeps (aq_kv.py:390-429,
+        quantizer.py:346-370).  fp32, fp16 and bf16 keys are read as they are
+        (the reference casts to the manager dtype first)."""
         x = keys.to(device=self.device)
         if x.dtype not in (torch.float32, torch.float16, torch.bfloat16):
             x = x.to(self.dtype)
-        return ops.encode_keys(x.contiguous() if x.stride(-1) != 1 else x, self.codebooks(layer_idx, group_idx))
+        return ops.encode_keys(x.contiguous() if x.stride(-1) != 1 else x, self.codebooks(layer_idx, group_idx),
+                               icm_iters=icm_iters)
 
     @torch.no_grad()
     def reconstruct(self, layer_idx: int, head_idx: int, codes: torch.Tensor) -> torch.Tensor:

@@ -6,6 +6,7 @@
 #include "attention.cuh"
 #include "compat.cuh"
 #include "encode.cuh"
+#include "icm.cuh"
 #include "fused_step.cuh"
 #include "lut_build.cuh"
 #include "score.cuh"
@@ -649,11 +650,16 @@ static int encode_plan(const lp_encode_args* a, size_t* bytes, int64_t* nsets, i
     *nsets = a->cb_per_kv_head ? a->H : 1;
     *nvec_set = a->cb_per_kv_head ? (int64_t)a->B * a->T : (int64_t)a->B * a->H * a->T;
     LP_CHECK(*nvec_set <= (int64_t)1 << 30, "too many vectors");
+    LP_CHECK(a->icm_iters >= 0 && a->icm_iters <= 1024, "icm_iters must be in [0, 1024]");
     Carver c(nullptr);
     c.take<unsigned char>(kPersistBytes);
     c.take<float>((size_t)*nsets * 32 * 256);
     c.take<float>((size_t)*nsets * 32 * 256);
     c.take<float>((size_t)*nsets * 32 * 4);
+    if (a->icm_iters > 0) {
+        c.take<float>((size_t)*nsets * *nvec_set * 128);
+        c.take<uint32_t>((size_t)a->icm_iters * *nsets);
+    }
     *bytes = c.used();
     return LP_OK;
 }
@@ -703,6 +709,8 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
     float* nrm = c.take<float>((size_t)nsets * 32 * 256);
     float* cnorm = c.take<float>((size_t)nsets * 32 * 256);
     float* smax = c.take<float>((size_t)nsets * 32 * 4);
+    float* icm_fr = a->icm_iters > 0 ? c.take<float>((size_t)nsets * nvec_set * 128) : nullptr;
+    uint32_t* icm_changed = a->icm_iters > 0 ? c.take<uint32_t>((size_t)a->icm_iters * nsets) : nullptr;
     const int64_t ncw = nsets * 32 * 256;
     encode_norms_kernel<<<(unsigned)((ncw + 255) / 256), 256, 0, st>>>(a->codebooks, ncw, nrm, cnorm);
     rc = check_launch("encode_norms_kernel");
@@ -782,7 +790,44 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
             encode_keys_kernel<float><<<grid, kEncThreads, EncSmem::kTotal, st>>>(cmap, ep);
             break;
     }
-    return check_launch("encode_keys_kernel");
+    rc = check_launch("encode_keys_kernel");
+    if (rc != LP_OK || a->icm_iters == 0) return rc;
+
+    // ICM sweeps, one launch each (a sweep reads the previous one's count of
+    // changed codes of its set and returns when it is zero)
+    LP_CUDA(cudaMemsetAsync(icm_changed, 0, sizeof(uint32_t) * (size_t)a->icm_iters * nsets, st));
+    IcmParams ip{};
+    ip.x = a->x;
+    ip.xs_b = a->x_stride_b;
+    ip.xs_h = a->x_stride_h;
+    ip.xs_t = a->x_stride_t;
+    ip.B = a->B;
+    ip.H = a->H;
+    ip.T = a->T;
+    ip.per_head = a->cb_per_kv_head ? 1 : 0;
+    ip.cb = a->codebooks;
+    ip.nrm = nrm;
+    ip.codes = a->codes;
+    ip.cs_b = a->codes_stride_b;
+    ip.cs_h = a->codes_stride_h;
+    ip.cs_t = a->codes_stride_t;
+    ip.fr = icm_fr;
+    ip.changed = icm_changed;
+    ip.ctas_per_set = (int)((nvec_set + kIcmVec - 1) / kIcmVec);
+    ip.err = err;
+    const dim3 igrid((unsigned)(nsets * ip.ctas_per_set));
+    for (int sweep = 0; sweep < a->icm_iters; ++sweep) {
+        ip.sweep = sweep;
+        ip.last = sweep + 1 == a->icm_iters ? 1 : 0;
+        switch (a->x_dtype) {
+            case LP_BF16: icm_sweep_kernel<__nv_bfloat16><<<igrid, kIcmThreads, 0, st>>>(ip); break;
+            case LP_F16: icm_sweep_kernel<__half><<<igrid, kIcmThreads, 0, st>>>(ip); break;
+            default: icm_sweep_kernel<float><<<igrid, kIcmThreads, 0, st>>>(ip); break;
+        }
+        rc = check_launch("icm_sweep_kernel");
+        if (rc != LP_OK) return rc;
+    }
+    return LP_OK;
 }
 
 int lp_lut_gather(const lp_lut_gather_args* a, void* stream) {

@@ -279,7 +279,7 @@ def encode_rows_per_cta(x: torch.Tensor, codebooks: torch.Tensor) -> int:
 
 
 def encode_keys(x: torch.Tensor, codebooks: torch.Tensor, codes: Optional[torch.Tensor] = None, *,
-                exact: bool = False, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+                icm_iters: int = 0, exact: bool = False, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Greedy residual additive-quantization codes of vectors (lp_encode_keys).
 
     x: [B,H,T,128] (bf16/fp16/fp32, any strides) or [N,128]; codebooks fp32
@@ -288,8 +288,14 @@ def encode_keys(x: torch.Tensor, codebooks: torch.Tensor, codes: Optional[torch.
     cache, rows of 32 contiguous bytes); allocated when omitted.  Returns it.
     Every distance follows the CPU arithmetic exactly (first minimum on
     ties); ``exact=True`` computes all of them on CUDA cores (testing).
+    ``icm_iters`` > 0 refines the greedy codes by up to that many ICM sweeps
+    (quantizer.py:356-370; the sweeps stop early for the vectors of a
+    codebook set once a sweep changes none of their codes).
     """
     a, codes = _encode_args(x, codebooks, codes, exact)
+    if int(icm_iters) < 0:
+        raise RuntimeError(f"icm_iters must be non-negative, got {icm_iters}")
+    a.icm_iters = int(icm_iters)
     lib = _lib.load()
     need = lib.lp_encode_workspace_size(ctypes.byref(a))
     if need == 0:

@@ -1,12 +1,13 @@
 """Drop-in for the encode surface of the reference's ``AdditiveQuantizer``
 (laprune/quantizer.py:319-374) with pretrained codebooks.
 
-``encode(X, method="icm", icm_iters=0)`` returns the reference's tuple
+``encode(X, method="icm", icm_iters=2)`` returns the reference's tuple
 ``(codes int64 [N, M], average loss, None)``: greedy residual codes from
-this package's tcgen05 encoder (equal to the CPU arithmetic's), and, with
-``return_loss``, the mean L2 norm of the final residual
-(``sqrt(sum((X - recon)^2, 1)).mean()``, quantizer.py:372-373).  Codebook
-training (``fit``) and ICM refinement are outside the decode path and raise.
+this package's tcgen05 encoder, refined by up to ``icm_iters`` ICM sweeps
+(both equal to the CPU arithmetic's), and, with ``return_loss``, the mean L2
+norm of the final residual (``sqrt(sum((X - recon)^2, 1)).mean()``,
+quantizer.py:372-373).  Codebook training (``fit``) is outside the decode
+path and is not provided.
 """
 from __future__ import annotations
 
@@ -40,14 +41,12 @@ class AdditiveQuantizer:
         """``(codes, avg_loss, None)`` for ``X [N, d]`` (quantizer.py:319-344)."""
         if method != "icm":
             raise NotImplementedError("Only ICM method is implemented in this LUT version.")
-        if int(icm_iters) != 0:
-            raise NotImplementedError(f"icm_iters={icm_iters}: ICM refinement is not on the decode path")
         X = X.to(self.device)
         if X.dtype not in (torch.float32, torch.float16, torch.bfloat16):
             X = X.to(self.dtype)
         if X.stride(-1) != 1:
             X = X.contiguous()
-        codes = ops.encode_keys(X, self.codebooks).long()
+        codes = ops.encode_keys(X, self.codebooks, icm_iters=int(icm_iters)).long()
         if not return_loss or X.shape[0] == 0:
             return codes, 0.0, None
         recon = torch.zeros((X.shape[0], self.d), dtype=torch.float32, device=self.device)

@@ -53,6 +53,7 @@ def _load():
         lib.orc_topk_rows.argtypes = [_f32p, ci, ci, ci, ci, ci, _i32p]
         lib.orc_encode_greedy.argtypes = [_f32p, _f32p, _i32p, ci, ci, ci, ci, _u8p]
         lib.orc_encode_stage_dists.argtypes = [_f32p, _f32p, _u8p, ci, ci, ci, _f64p]
+        lib.orc_encode_icm.argtypes = [_f32p, _f32p, _i32p, ci, ci, ci, ci, ci, _u8p, _i32p]
         lib.orc_sparse_attention.argtypes = [_f32p, _f32p, _f32p, i64, i64, _i32p,
                                              ci, ci, ci, ci, ctypes.c_float, _f32p]
         lib.orc_num_threads.restype = ci
@@ -204,6 +205,32 @@ def encode_greedy(x, codebooks, cb_index=None) -> np.ndarray:
     _load().orc_encode_greedy(_p(x, _f32p), _p(cb, _f32p), idxp, N, M, K, d,
                               out.ctypes.data_as(_u8p))
     return out
+
+
+def encode_icm(x, codebooks, icm_iters: int, cb_index=None, return_sweeps: bool = False):
+    """Greedy codes refined by up to ``icm_iters`` ICM sweeps (uint8 [N,M]).
+    quantizer.py:346-370: after the greedy pass, each sweep re-chooses code m
+    = 0..M-1 of every vector against the reconstruction without it, and a
+    sweep that changes no code of the batch ends the refinement.  The batch
+    is the set of vectors sharing a codebook set (the reference runs one
+    quantizer per codebook group).  With ``return_sweeps`` also the number
+    of sweeps each set ran."""
+    x = _f32(x)
+    cb = _f32(codebooks)
+    codes = encode_greedy(x, cb, cb_index)
+    N, d = x.shape
+    M, K = cb.shape[-3], cb.shape[-2]
+    cbi = None
+    idxp = None
+    if cb_index is not None:
+        cbi = np.ascontiguousarray(np.asarray(cb_index, dtype=np.int32))
+        idxp = _p(cbi, _i32p)
+    nsets = int(cbi.max()) + 1 if cbi is not None and cbi.size else 1
+    sweeps = np.zeros(nsets, dtype=np.int32)
+    if N and icm_iters > 0:
+        _load().orc_encode_icm(_p(x, _f32p), _p(cb, _f32p), idxp, N, M, K, d, int(icm_iters),
+                               codes.ctypes.data_as(_u8p), _p(sweeps, _i32p))
+    return (codes, sweeps) if return_sweeps else codes
 
 
 def encode_stage_dists(x_row, codebooks, prefix_codes, m: int) -> np.ndarray:

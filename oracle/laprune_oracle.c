@@ -215,6 +215,107 @@ void orc_encode_greedy(const float* x, const float* cb, const int32_t* cb_index,
     free(norms);
 }
 
+/* ICM refinement after the greedy codes (quantizer.py:356-370, the loop of
+ * _batch_icm_lut after its greedy pass): full_recon = x - r_greedy; then up
+ * to `iters` sweeps over m = 0..M-1 of
+ *     recon_wo = full_recon - C_m[prev];  r = x - recon_wo;
+ *     new = first argmin_k ||r||^2 + ||C_m[k]||^2 - 2 r.C_m[k];
+ *     full_recon = recon_wo + C_m[new]
+ * (elementwise fp32; the norms and r.c in enc_dot's order, as in
+ * orc_encode_greedy).  A sweep that changes no code of the batch ends the
+ * refinement (quantizer.py:368-369).  The reference runs one quantizer per
+ * codebook group, so "the batch" is the set of vectors sharing a codebook
+ * set: the early exit is decided per set.  codes [N][M] hold the greedy codes
+ * on entry (orc_encode_greedy) and the refined ones on return; sweeps_run
+ * [nsets] (optional) receives the number of sweeps each set ran. */
+void orc_encode_icm(const float* x, const float* cb, const int32_t* cb_index,
+                    int N, int M, int K, int d, int iters, uint8_t* codes, int32_t* sweeps_run) {
+    int nsets = 1;
+    if (cb_index) {
+        for (int n = 0; n < N; ++n) if (cb_index[n] + 1 > nsets) nsets = cb_index[n] + 1;
+    }
+    for (int s = 0; s < nsets; ++s) if (sweeps_run) sweeps_run[s] = 0;
+    if (iters <= 0 || N == 0) return;
+    float* norms = (float*)malloc(sizeof(float) * (size_t)nsets * M * K);
+    for (int s = 0; s < nsets; ++s) {
+        for (int mk = 0; mk < M * K; ++mk) {
+            const float* c = cb + ((int64_t)s * M * K + mk) * d;
+            float acc = 0.f;
+            for (int j = 0; j < d; ++j) acc = fmaf(c[j], c[j], acc);
+            norms[(int64_t)s * M * K + mk] = acc;
+        }
+    }
+    /* full reconstruction x - r, r the greedy residual (r -= C_m[code_m]) */
+    float* fr = (float*)malloc(sizeof(float) * (size_t)N * d);
+    #pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+        const int s = cb_index ? cb_index[n] : 0;
+        const float* cbs = cb + (int64_t)s * M * K * d;
+        const float* xn = x + (int64_t)n * d;
+        float* f = fr + (int64_t)n * d;
+        for (int j = 0; j < d; ++j) f[j] = xn[j];
+        for (int m = 0; m < M; ++m) {
+            const float* cw = cbs + ((int64_t)m * K + codes[(int64_t)n * M + m]) * d;
+            for (int j = 0; j < d; ++j) f[j] -= cw[j];
+        }
+        for (int j = 0; j < d; ++j) f[j] = xn[j] - f[j];
+    }
+    int* active = (int*)malloc(sizeof(int) * (size_t)nsets);
+    long long* changed = (long long*)malloc(sizeof(long long) * (size_t)nsets);
+    for (int s = 0; s < nsets; ++s) active[s] = 1;
+    for (int it = 0; it < iters; ++it) {
+        for (int s = 0; s < nsets; ++s) changed[s] = 0;
+        #pragma omp parallel
+        {
+            float* rw = (float*)malloc(sizeof(float) * (size_t)d);
+            float* r = (float*)malloc(sizeof(float) * (size_t)d);
+            #pragma omp for schedule(static)
+            for (int n = 0; n < N; ++n) {
+                const int s = cb_index ? cb_index[n] : 0;
+                if (!active[s]) continue;
+                const float* cbs = cb + (int64_t)s * M * K * d;
+                const float* nrm = norms + (int64_t)s * M * K;
+                const float* xn = x + (int64_t)n * d;
+                float* f = fr + (int64_t)n * d;
+                long long ch = 0;
+                for (int m = 0; m < M; ++m) {
+                    const int prev = codes[(int64_t)n * M + m];
+                    const float* cp = cbs + ((int64_t)m * K + prev) * d;
+                    for (int j = 0; j < d; ++j) { rw[j] = f[j] - cp[j]; r[j] = xn[j] - rw[j]; }
+                    float rn = 0.f;
+                    for (int j = 0; j < d; ++j) rn = fmaf(r[j], r[j], rn);
+                    float best = INFINITY;
+                    int best_k = 0;
+                    for (int k = 0; k < K; ++k) {
+                        const float dot = enc_dot(r, cbs + ((int64_t)m * K + k) * d, d);
+                        const float dist = fmaf(-2.f, dot, rn + nrm[(int64_t)m * K + k]);
+                        if (dist < best) { best = dist; best_k = k; }
+                    }
+                    if (best_k != prev) ++ch;
+                    codes[(int64_t)n * M + m] = (uint8_t)best_k;
+                    const float* cw = cbs + ((int64_t)m * K + best_k) * d;
+                    for (int j = 0; j < d; ++j) f[j] = rw[j] + cw[j];
+                }
+                if (ch) {
+                    #pragma omp atomic
+                    changed[s] += ch;
+                }
+            }
+            free(rw);
+            free(r);
+        }
+        for (int s = 0; s < nsets; ++s) {
+            if (!active[s]) continue;
+            if (sweeps_run) sweeps_run[s] += 1;
+            if (changed[s] == 0) active[s] = 0;
+        }
+    }
+    free(changed);
+    free(active);
+    free(fr);
+    free(norms);
+}
+
 /* Double-precision distances of one vector at one stage, for near-tie
  * classification of encode disagreements: dist[k] = ||r - C_m[k]||^2 with r
  * the residual after the given prefix of codes. */

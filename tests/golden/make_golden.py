@@ -11,7 +11,8 @@ public functions on its CPU/PyTorch path:
                (laprune/llm/aq_kv.py:633), one manager per KV head for the
                per-KV-head codebooks of the benchmark configs;
 * encoding  -- AQLayerCodebookManager.encode_keys_batch(icm_iters=0)
-               (laprune/llm/aq_kv.py:390 -> laprune/quantizer.py:346);
+               (laprune/llm/aq_kv.py:390 -> laprune/quantizer.py:346), and
+               with the reference's default icm_iters=2 (quantizer.py:346-370);
 * selection -- torch.topk over the candidate window (as
                laprune/llm/modifiers/aq_evaluation.py:185-201);
 * attention -- torch SDPA over the kept rows (aq_evaluation.py:251);
@@ -54,7 +55,13 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference LAPrune checkout")
     ap.add_argument("--threads", type=int, default=0)
+    ap.add_argument("--only", default="", help="comma-separated fixtures to (re)generate: "
+                    "cfg1,cfg2,cfg3,small,hook,icm (default: all)")
     args = ap.parse_args()
+    only = set(x for x in args.only.split(",") if x)
+
+    def want(name):
+        return not only or name in only
     if args.threads:
         torch.set_num_threads(args.threads)
     sys.path.insert(0, str(Path(args.reference).resolve()))
@@ -75,6 +82,21 @@ def main():
         return torch.cat(outs, 0)
 
     # ---------------- config 1: scoring op (T=4096) ----------------
+    if want("cfg1"):
+        cfg1(per_kv_scores)
+    if want("cfg2"):
+        cfg2(mgr_for, per_kv_scores)
+    if want("cfg3"):
+        cfg3(per_kv_scores)
+    if want("small"):
+        small(mgr_for)
+    if want("hook"):
+        hook(mgr_for, aqe)
+    if want("icm"):
+        icm(mgr_for)
+
+
+def cfg1(per_kv_scores):
     c1 = syn.config1(0)
     s1 = per_kv_scores(c1["C"], c1["q"], c1["codes"], c1["G"])          # [32,4096] fp32
     gs1 = s1.reshape(8, 4, -1).sum(1)
@@ -86,6 +108,8 @@ def main():
         scores=s1.numpy(), topk=top1.numpy().astype(np.int32), kth=kth1.numpy())
     print("cfg1 done", s1.shape)
 
+
+def cfg2(mgr_for, per_kv_scores):
     # ---------------- config 2: encode + scoring (B=4) ----------------
     c2 = syn.config2(0)
     B, Hkv, Tn, D = c2["keys"].shape
@@ -110,6 +134,8 @@ def main():
         codes=codes2.numpy(), sample=sample.numpy().astype(np.int32), scores=s2.numpy())
     print("cfg2 done")
 
+
+def cfg3(per_kv_scores):
     # ---------------- config 3: sparse decode step (T=131072) ----------------
     c3 = syn.config3(0)
     T = c3["codes"].shape[1]
@@ -136,6 +162,8 @@ def main():
         out=out3.reshape(32, 128).numpy())
     print("cfg3 done")
 
+
+def small(mgr_for):
     # ---------------- small cases: shared codebook, ragged, strided ----------------
     sm = syn.small_shared(7)
     codes_s = sm["codes_full"][:, :sm["T"]]          # strided prefix like the decode cache
@@ -149,6 +177,8 @@ def main():
         scores=s_small.numpy(), codes_enc=codes_enc.numpy())
     print("small done")
 
+
+def hook(mgr_for, aqe):
     # ---------------- the reference decode hook on fp32 inputs ----------------
     dh = syn.decode_hook_case(11)
     mgr = mgr_for(dh["cb"], dh["Hq"])
@@ -168,6 +198,28 @@ def main():
                             syn.checksum(dh["q"])]),
         **outs)
     print("decode hook done")
+
+
+def icm(mgr_for):
+    # ---------------- encoding with the reference's default ICM refinement ----------------
+    # config 2's keys per KV head (one quantizer per head, as the reference
+    # would run per-KV-head codebooks) and the small shared-codebook case
+    c2 = syn.config2(0)
+    B, Hkv, Tn, D = c2["keys"].shape
+    codes = torch.empty((B, Hkv, Tn, 32), dtype=torch.uint8)
+    for h in range(Hkv):
+        mgr = mgr_for(c2["C"][h], 4)
+        x = c2["keys"][:, h].reshape(B * Tn, D).float()
+        codes[:, h] = mgr.encode_keys_batch(0, 0, x, icm_iters=2).reshape(B, Tn, 32).to(torch.uint8)
+    sm = syn.small_shared(7)
+    mgr = mgr_for(sm["cb"], 8)
+    codes_small = mgr.encode_keys_batch(0, 0, sm["x"], icm_iters=2).to(torch.uint8)
+    np.savez_compressed(
+        OUT / "icm_encode.npz",
+        checksums=np.array([syn.checksum(c2["C"]), syn.checksum(c2["keys"]),
+                            syn.checksum(sm["cb"]), syn.checksum(sm["x"])]),
+        codes_cfg2=codes.numpy(), codes_small=codes_small.numpy())
+    print("icm done")
 
 
 if __name__ == "__main__":

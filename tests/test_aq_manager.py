@@ -47,13 +47,16 @@ def test_load_skips_stale_groups_and_unknown_layers_and_adopts_file_shapes(tmp_p
         m.load(str(tmp_path / "missing"))
 
 
-def test_icm_refinement_is_refused_before_any_compute():
+def test_encoding_has_no_cpu_fallback():
+    # greedy or with the reference's default ICM sweeps, the codes come from
+    # the CUDA kernels only: host tensors are an error, not a slow path
     m = _mgr()
     m.set_codebooks(0, 0, torch.zeros(32, 256, 128))
-    with pytest.raises(NotImplementedError):
-        m.encode_keys(0, 0, torch.zeros(4, 128), icm_iters=2)
-    with pytest.raises(NotImplementedError):
-        m.encode_keys_batch(0, 0, torch.zeros(4, 128), icm_iters=1)
+    for icm in (0, 2):
+        with pytest.raises(RuntimeError, match="CUDA"):
+            m.encode_keys(0, 0, torch.zeros(4, 128), icm_iters=icm)
+        with pytest.raises(RuntimeError, match="CUDA"):
+            m.encode_keys_batch(0, 0, torch.zeros(4, 128), icm_iters=icm)
 
 
 def test_group_stacks_follow_heads_per_group():
@@ -107,18 +110,18 @@ def test_sharded_manager_loads_one_copy_per_device_on_first_use(tmp_path):
     assert sh.for_device("cpu") is sh.for_device(torch.device("cpu"))
     assert torch.equal(sh.codebooks(0, 0), cb)
     assert sh._on(torch.zeros(1)) is sh.for_device("cpu")
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(RuntimeError, match="CUDA"):
         sh.encode_keys(0, 0, torch.zeros(4, 128), icm_iters=2)
 
 
-def test_quantizer_encode_surface_refuses_training_and_icm():
+def test_quantizer_encode_surface_refuses_training_and_host_tensors():
     from laprune_b200.quantizer import AdditiveQuantizer
     with pytest.raises(NotImplementedError):
         AdditiveQuantizer(M=32, K=256, d=128, init="random", device="cpu")
     with pytest.raises(ValueError):
         AdditiveQuantizer(M=32, K=256, d=128, device="cpu", codebooks=torch.zeros(16, 256, 128))
     aq = AdditiveQuantizer(M=32, K=256, d=128, device="cpu", codebooks=torch.zeros(32, 256, 128))
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(RuntimeError, match="CUDA"):
         aq.encode(torch.zeros(4, 128), icm_iters=2)
     with pytest.raises(NotImplementedError):
         aq.encode(torch.zeros(4, 128), method="beam", icm_iters=0)

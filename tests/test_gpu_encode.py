@@ -121,3 +121,63 @@ def test_large_tiles_equal_the_oracle(B, H, T, per_head, rows):
     got = ops.encode_keys(kd, cd)
     torch.cuda.synchronize()
     assert np.array_equal(got.cpu().numpy(), _oracle_codes(keys, C))
+
+
+def test_icm_codes_equal_the_oracle_and_the_reference(golden_dir):
+    """ICM refinement with the reference's default two sweeps
+    (quantizer.py:356-370): config 2 on per-KV-head codebooks and the small
+    shared-codebook case, bit-exact with the oracle and agreeing with the
+    reference's own codes (golden fixture)."""
+    fix = np.load(golden_dir / "icm_encode.npz")
+    c = syn.config2(0)
+    dev = _dev()
+    got = ops.encode_keys(c["keys"].to(dev), c["C"].to(dev), icm_iters=2).cpu().numpy()
+    B, H, T, D = c["keys"].shape
+    x = c["keys"].permute(1, 0, 2, 3).reshape(H * B * T, D).float().numpy()
+    cbi = np.repeat(np.arange(H, dtype=np.int32), B * T)
+    want = oracle.encode_icm(x, c["C"].numpy(), 2, cbi).reshape(H, B, T, 32).transpose(1, 0, 2, 3)
+    assert np.array_equal(got, want)
+    assert (got == fix["codes_cfg2"]).all(-1).mean() >= 0.99
+    sm = syn.small_shared(7)
+    got_s = ops.encode_keys(sm["x"].to(dev), sm["cb"].to(dev), icm_iters=2).cpu().numpy()
+    assert np.array_equal(got_s, oracle.encode_icm(sm["x"].float().numpy(), sm["cb"].numpy(), 2))
+    assert (got_s == fix["codes_small"]).all(-1).mean() >= 0.99
+
+
+def test_icm_sets_stop_at_their_own_sweep():
+    """Many sweeps: each codebook set stops after its first sweep without a
+    change (the sets converge after different numbers of sweeps), exactly as
+    the oracle's per-set early exit."""
+    g = torch.Generator().manual_seed(61)
+    H = 3
+    C = torch.randn((H, 32, 256, 128), generator=g) * 0.05
+    keys = torch.randn((1, H, 50, 128), generator=g) * torch.tensor([0.3, 1.0, 2.0]).view(1, H, 1, 1)
+    dev = _dev()
+    got = ops.encode_keys(keys.to(dev), C.to(dev), icm_iters=40).cpu().numpy()
+    x = keys[0].reshape(H * 50, 128).numpy()
+    cbi = np.repeat(np.arange(H, dtype=np.int32), 50)
+    want, sweeps = oracle.encode_icm(x, C.numpy(), 40, cbi, return_sweeps=True)
+    assert np.array_equal(got[0].reshape(H * 50, 32), want)
+    assert (sweeps < 40).all() and len(set(sweeps.tolist())) > 1, sweeps
+
+
+def test_reference_default_arguments_refine_with_icm():
+    """The manager's encode_keys(_batch) and AdditiveQuantizer.encode default
+    to icm_iters=2 (aq_kv.py:354, 396; quantizer.py:319): called with the
+    reference's defaults they now return the ICM-refined codes."""
+    from laprune_b200.aq_kv import AQLayerCodebookManager, AQLayerConfig
+    from laprune_b200.quantizer import AdditiveQuantizer
+    g = torch.Generator().manual_seed(62)
+    C = torch.randn((32, 256, 128), generator=g) * 0.05
+    x = torch.randn((300, 128), generator=g)
+    dev = _dev()
+    want = oracle.encode_icm(x.numpy(), C.numpy(), 2)
+    m = AQLayerCodebookManager({0: AQLayerConfig(M=32, K=256, d=128, heads_per_group=8, num_heads=8)}, device=dev)
+    m.set_codebooks(0, 0, C)
+    assert np.array_equal(m.encode_keys(0, 3, x).cpu().numpy(), want)
+    assert np.array_equal(m.encode_keys_batch(0, 0, x).cpu().numpy(), want)
+    aq = AdditiveQuantizer(M=32, K=256, d=128, device=dev, codebooks=C)
+    codes, loss, _ = aq.encode(x)
+    assert codes.dtype == torch.int64 and np.array_equal(codes.cpu().numpy(), want.astype(np.int64))
+    recon = sum(C[m_][torch.from_numpy(want[:, m_]).long()] for m_ in range(32))
+    assert abs(loss - float(torch.sqrt(((x - recon) ** 2).sum(1)).mean())) <= 1e-4
