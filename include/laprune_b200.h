@@ -282,6 +282,38 @@ typedef struct lp_gqa_gather_args {
 int lp_gqa_gather_kv(const lp_gqa_gather_args* a, void* stream);
 
 /* ======================================================================
+ * Decode-token rotary embedding fused with the K/V cache append
+ * ====================================================================== */
+
+/* One decode token of B sequences: q_out[b][h] = rope(q[b][h]) for the Hq
+ * query rows; k_cache[b][h][pos] = rope(k[b][h]) and v_cache[b][h][pos] =
+ * v[b][h] for the Hkv KV rows, rope(x) = x * cos[b] + rotate_half(x) *
+ * sin[b] with rotate_half(x) = [-x[D/2:], x[:D/2]] and every product and the
+ * sum rounded to the dtype (as HF apply_rotary_pos_emb on bf16/fp16
+ * tensors).  Replaces laprune/llm/modifiers/aq_evaluation.py:296-308 (RoPE of
+ * the new token, then _kv_cache_append's slice copies, :65-112) for a static
+ * cache with room at `pos`.  Strides in elements; every tensor of `dtype`. */
+typedef struct lp_rope_append_args {
+    const void* q;            /* [B][Hq][D] at q + b*q_stride_b + h*q_stride_h */
+    const void* k;            /* [B][Hkv][D] */
+    const void* v;            /* [B][Hkv][D] */
+    int64_t q_stride_b, q_stride_h, k_stride_b, k_stride_h, v_stride_b, v_stride_h;
+    const void* cos;          /* [B][D]: the token's rotary rows */
+    const void* sin;
+    int64_t cos_stride_b, sin_stride_b;
+    void* q_out;              /* [B][Hq][D] */
+    int64_t q_out_stride_b, q_out_stride_h;
+    void* k_cache;            /* [B][Hkv][cap][D] */
+    void* v_cache;
+    int64_t kc_stride_b, kc_stride_h, kc_stride_t, vc_stride_b, vc_stride_h, vc_stride_t;
+    int32_t dtype;            /* LP_BF16 | LP_F16 */
+    int32_t B, Hq, Hkv, D;    /* D even, <= 1024 */
+    int32_t pos;              /* cache slot of the token (< cap) */
+} lp_rope_append_args;
+size_t lp_sizeof_rope_append_args(void);
+int lp_rope_append(const lp_rope_append_args* a, void* stream);
+
+/* ======================================================================
  * Allocation-free variant (no counterpart in the reference)
  * ====================================================================== */
 

@@ -94,6 +94,21 @@ class GqaGatherArgs(ctypes.Structure):
         ("tail_count", _c_i32), ("out_k", _c_p), ("out_v", _c_p),
     ]
 
+class RopeAppendArgs(ctypes.Structure):
+    """Mirror of lp_rope_append_args."""
+    _fields_ = [
+        ("q", _c_p), ("k", _c_p), ("v", _c_p),
+        ("q_stride_b", _c_i64), ("q_stride_h", _c_i64), ("k_stride_b", _c_i64), ("k_stride_h", _c_i64),
+        ("v_stride_b", _c_i64), ("v_stride_h", _c_i64),
+        ("cos", _c_p), ("sin", _c_p), ("cos_stride_b", _c_i64), ("sin_stride_b", _c_i64),
+        ("q_out", _c_p), ("q_out_stride_b", _c_i64), ("q_out_stride_h", _c_i64),
+        ("k_cache", _c_p), ("v_cache", _c_p),
+        ("kc_stride_b", _c_i64), ("kc_stride_h", _c_i64), ("kc_stride_t", _c_i64),
+        ("vc_stride_b", _c_i64), ("vc_stride_h", _c_i64), ("vc_stride_t", _c_i64),
+        ("dtype", _c_i32), ("B", _c_i32), ("Hq", _c_i32), ("Hkv", _c_i32), ("D", _c_i32), ("pos", _c_i32),
+    ]
+
+
 # name -> (restype, argtypes) of every exported entry point
 SIGNATURES = {
     "lp_last_error": (ctypes.c_char_p, []),
@@ -111,6 +126,8 @@ SIGNATURES = {
     "lp_lut_gather": (ctypes.c_int, [ctypes.POINTER(LutGatherArgs), _c_p]),
     "lp_lut_build": (ctypes.c_int, [ctypes.POINTER(LutBuildArgs), _c_p]),
     "lp_gqa_gather_kv": (ctypes.c_int, [ctypes.POINTER(GqaGatherArgs), _c_p]),
+    "lp_sizeof_rope_append_args": (ctypes.c_size_t, []),
+    "lp_rope_append": (ctypes.c_int, [ctypes.POINTER(RopeAppendArgs), _c_p]),
 }
 LP_NOALLOC_SCRATCH_BYTES = 32 << 20
 
@@ -138,6 +155,8 @@ def load() -> ctypes.CDLL:
             raise ImportError("lp_sparse_decode_args layout mismatch between the binding and the library")
         if lib.lp_sizeof_encode_args() != ctypes.sizeof(EncodeArgs):
             raise ImportError("lp_encode_args layout mismatch between the binding and the library")
+        if lib.lp_sizeof_rope_append_args() != ctypes.sizeof(RopeAppendArgs):
+            raise ImportError("lp_rope_append_args layout mismatch between the binding and the library")
         _lib = lib
     return _lib
 

@@ -111,48 +111,84 @@ def _decode_attention(self_attn, manager: AQLayerCodebookManager, layer_idx: int
     return self_attn.o_proj(attn_output)
 
 
-def _kv_cache_append(self_attn, k_new: torch.Tensor, v_new: torch.Tensor, total_len: int, input_kv_cache=None):
-    """Append ``k_new`` / ``v_new`` ``[B, H, Tn, D]`` to the growable K/V
-    buffers on ``self_attn`` (capacity doubling, ``aq_kv_extra_capacity``
-    spare slots; aq_evaluation.py:65-112).  Returns the ``[B, H, total, D]``
-    views and ``(K_view.data, V_view.data)``."""
-    k_buf = getattr(self_attn, "k_cache", None)
-    v_buf = getattr(self_attn, "v_cache", None)
-    k_len = int(getattr(self_attn, "k_cache_len", 0))
-    k_cap = int(getattr(self_attn, "k_cache_capacity", 0))
-    B, H, Tn, D = k_new.shape
+# ---- the layer's K/V cache --------------------------------------------------
+# Observable contract (aq_evaluation.py:65-112): buffers self_attn.k_cache /
+# v_cache [B, Hkv, cap, D] of which k_cache_len tokens are valid and
+# k_cache_capacity slots exist; callers get [B, Hkv, total, D] views of them.
+# Capacity policy (it fixes the views' strides): the first buffers hold
+# total + aq_kv_extra_capacity slots (at least 16), or max(total, 2 max(16, L))
+# when they start from an input cache of L tokens; a full buffer doubles (at
+# least to total).  Decode tokens land in place: with the slots reserved,
+# the fused rotary + append kernel writes each token's rotated key and value
+# straight into its slot, so the buffers are static between doublings.
+
+
+def _kv_slots(total_len: int, have: int, prefix_len: Optional[int], extra: int) -> int:
+    """Slots the buffers need for ``total_len`` tokens when they hold ``have``
+    (0: not allocated yet; ``prefix_len`` is the input cache's length then)."""
+    if have > 0:
+        return have if total_len <= have else max(total_len, 2 * have)
+    if prefix_len is not None:
+        return max(total_len, 2 * max(16, prefix_len))
+    return max(total_len + extra, 16)
+
+
+def _kv_reserve(self_attn, like_k: torch.Tensor, like_v: torch.Tensor, total_len: int, input_kv_cache=None):
+    """Buffers on ``self_attn`` with room for ``total_len`` tokens, allocated
+    or grown as the policy above says; returns ``(k_buf, v_buf, valid)``."""
+    k_buf, v_buf = getattr(self_attn, "k_cache", None), getattr(self_attn, "v_cache", None)
+    have = int(getattr(self_attn, "k_cache_capacity", 0)) if k_buf is not None and v_buf is not None else 0
+    valid = int(getattr(self_attn, "k_cache_len", 0)) if have > 0 else 0
     conf = getattr(self_attn, "draft_kwargs", {}) or {}
     extra = max(0, int(conf.get("aq_kv_extra_capacity", 0)))
-    if k_buf is None or v_buf is None or k_cap <= 0:
-        if input_kv_cache is not None:
-            k_prefix, v_prefix = input_kv_cache
-            k_len = int(k_prefix.shape[-2])
-            k_cap = max(total_len, max(16, k_len) * 2)
-            k_buf = k_prefix.new_empty((B, H, k_cap, D))
-            v_buf = v_prefix.new_empty((B, H, k_cap, D))
-            if k_len > 0:
-                k_buf[:, :, :k_len] = k_prefix
-                v_buf[:, :, :k_len] = v_prefix
-        else:
-            k_len = 0
-            k_cap = max(total_len + extra, 16)
-            k_buf = k_new.new_empty((B, H, k_cap, D))
-            v_buf = v_new.new_empty((B, H, k_cap, D))
-    if total_len > k_cap:
-        new_cap = max(total_len, k_cap * 2)
-        k2 = k_buf.new_empty((B, H, new_cap, D))
-        v2 = v_buf.new_empty((B, H, new_cap, D))
-        if k_len > 0:
-            k2[:, :, :k_len] = k_buf[:, :, :k_len]
-            v2[:, :, :k_len] = v_buf[:, :, :k_len]
-        k_buf, v_buf, k_cap = k2, v2, new_cap
-    end = k_len + Tn
-    k_buf[:, :, k_len:end] = k_new
-    v_buf[:, :, k_len:end] = v_new
-    self_attn.k_cache, self_attn.v_cache = k_buf, v_buf
-    self_attn.k_cache_len, self_attn.k_cache_capacity = end, k_cap
-    k_view, v_view = k_buf[:, :, :end], v_buf[:, :, :end]
+    B, H, _, D = like_k.shape
+    prefix = None
+    if have == 0 and input_kv_cache is not None:
+        prefix = input_kv_cache
+        valid = int(prefix[0].shape[-2])
+    need = _kv_slots(total_len, have, None if prefix is None else valid, extra)
+    if need != have:
+        src_k, src_v = (prefix if prefix is not None else (k_buf, v_buf))
+        proto_k = src_k if src_k is not None else like_k
+        proto_v = src_v if src_v is not None else like_v
+        new_k = proto_k.new_empty((B, H, need, D))
+        new_v = proto_v.new_empty((B, H, need, D))
+        if valid > 0:
+            new_k[:, :, :valid].copy_(src_k[:, :, :valid])
+            new_v[:, :, :valid].copy_(src_v[:, :, :valid])
+        k_buf, v_buf = new_k, new_v
+        self_attn.k_cache, self_attn.v_cache, self_attn.k_cache_capacity = k_buf, v_buf, need
+    return k_buf, v_buf, valid
+
+
+def _kv_publish(self_attn, end: int):
+    """Record ``end`` valid tokens; the [B, Hkv, end, D] views and their data."""
+    self_attn.k_cache_len = end
+    k_view, v_view = self_attn.k_cache[:, :, :end], self_attn.v_cache[:, :, :end]
     return k_view, v_view, (k_view.data, v_view.data)
+
+
+def _kv_cache_append(self_attn, k_new: torch.Tensor, v_new: torch.Tensor, total_len: int, input_kv_cache=None):
+    """Append ``k_new`` / ``v_new`` ``[B, H, Tn, D]`` (post-RoPE keys) to the
+    layer's K/V buffers (aq_evaluation.py:65-112).  Returns the
+    ``[B, H, total, D]`` views and ``(K_view.data, V_view.data)``."""
+    k_buf, v_buf, valid = _kv_reserve(self_attn, k_new, v_new, total_len, input_kv_cache)
+    end = valid + int(k_new.shape[2])
+    k_buf[:, :, valid:end].copy_(k_new)
+    v_buf[:, :, valid:end].copy_(v_new)
+    return _kv_publish(self_attn, end)
+
+
+def _rope_append_decode(self_attn, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor,
+                        sin: torch.Tensor, total_len: int, input_kv_cache=None):
+    """One decode token: rotary embedding of q and k fused with the append of
+    the rotated key and the value into their reserved slot (ops.rope_append),
+    replacing apply_rotary_pos_emb + _kv_cache_append (aq_evaluation.py:
+    296-308).  Returns ``(Q_rope, K_view, V_view, (K_view.data, V_view.data))``."""
+    k_buf, v_buf, valid = _kv_reserve(self_attn, k, v, total_len, input_kv_cache)
+    q_rot = ops.rope_append(q, k, v, cos, sin, k_buf, v_buf, valid)
+    k_view, v_view, data = _kv_publish(self_attn, valid + 1)
+    return q_rot.unsqueeze(2), k_view, v_view, data
 
 
 def _encode_into(manager: AQLayerCodebookManager, layer_idx: int, keys: torch.Tensor, codes_dst: torch.Tensor,
@@ -261,49 +297,72 @@ def do_sdpa_attn(query, key, value, cos=None, sin=None, out_proj=None, query_dow
     return out_proj(o) if out_proj is not None else o
 
 
+def _rope_rows(self, manager, q: torch.Tensor, past: int, n_new: int):
+    """HF rotary rows (cos, sin) ``[B, n_new, D]`` of positions past .. past +
+    n_new - 1, computed once per step and shared by the layers: they depend
+    only on the positions, the batch size, the device and the dtype, which
+    together key the copy kept on the manager."""
+    key = (q.device, q.dtype, int(past), int(n_new), int(q.shape[0]))
+    held = getattr(manager, "_lp_rope_rows", None)
+    if held is None or held[0] != key:
+        pos = _cached_position_ids(manager, q.device, past + n_new)[past:past + n_new]
+        cos, sin = self.rotary_emb(q, pos.unsqueeze(0).expand(q.shape[0], -1))
+        held = (key, cos, sin)
+        manager._lp_rope_rows = held
+    return held[1], held[2]
+
+
+def _sparse_layer(self, manager, conf: dict, is_prefill: bool) -> bool:
+    """Whether the layer runs the AQ path (aq_evaluation.py:310-314): AQ on
+    and encoding on, not a fixed / dense (full-KV) layer, a configured layer,
+    and not a prefill with aq_disable_prefill."""
+    if not conf.get("enable", True) or conf.get("aq_disable_encode", False):
+        return False
+    if self.is_fix_layer or getattr(self, "full_kv_layer", False) or self.layer_idx not in manager.layer_cfgs:
+        return False
+    return not (is_prefill and conf.get("aq_disable_prefill", False))
+
+
 def self_attn_forward(self, hidden_states: torch.Tensor, kv_cache=None):
     """The reference's replacement Llama attention forward (aq_evaluation.py:279-322), bound to a
     ``LlamaAttention`` that carries ``aq_manager``, ``layer_idx``, ``draft_kwargs``,
-    ``is_fix_layer``, ``rotary_emb`` and ``config``: projections, RoPE (cos/sin computed once per
-    step and shared by the layers), K/V append, code cache; prefill and dense layers attend
-    densely, a sparse layer's decode token goes through ``_decode_attention``.  Returns
-    ``(attn_output, kv_cache_out, None, None)``."""
-    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
-    manager = self.aq_manager
-    layer_idx = self.layer_idx
-    conf = self.draft_kwargs
-    H = self.config.num_attention_heads
-    Hkv = self.config.num_key_value_heads
-    D = self.config.hidden_size // H
-    B, T_new = hidden_states.shape[0], hidden_states.shape[-2]
-    is_prefill = T_new > 1 and kv_cache is None
-    q = self.q_proj(hidden_states).unflatten(-1, (H, D)).transpose(1, 2)
-    k = self.k_proj(hidden_states).unflatten(-1, (Hkv, D)).transpose(1, 2)
-    v = self.v_proj(hidden_states).unflatten(-1, (Hkv, D)).transpose(1, 2)
+    ``is_fix_layer``, ``rotary_emb`` and ``config``.  Returns ``(attn_output, kv_cache_out, None,
+    None)``.
+
+    A decode token (one new position) goes through one fused kernel for the rotary embedding of
+    its query and key and the append of its key and value to the layer's static cache
+    (``_rope_append_decode``); longer inputs take HF ``apply_rotary_pos_emb`` and
+    ``_kv_cache_append``.  Prefill and dense layers attend densely (torch SDPA); a sparse
+    layer's decode token goes through ``_decode_attention`` after ``_prepare_aq_cache`` has
+    brought its code cache up to date."""
+    manager, conf = self.aq_manager, self.draft_kwargs
+    n_q, n_kv = self.config.num_attention_heads, self.config.num_key_value_heads
+    d = self.config.hidden_size // n_q
+    n_new = hidden_states.shape[-2]
+    is_prefill = n_new > 1 and kv_cache is None
+
+    def heads(proj, n):  # [B, T, n*d] -> [B, n, T, d]
+        return proj(hidden_states).unflatten(-1, (n, d)).transpose(1, 2)
+
+    q, k, v = heads(self.q_proj, n_q), heads(self.k_proj, n_kv), heads(self.v_proj, n_kv)
     past = int(getattr(self, "total_seq_len", 0))
-    total = past + T_new
-    pos = _cached_position_ids(manager, q.device, total)[past:total][None, :].expand(B, -1)
-    key = (str(q.device), past, int(T_new), int(B), q.dtype)
-    cached = getattr(manager, "_laprune_rope_step", None)
-    if layer_idx == 0 or cached is None or cached[0] != key:
-        cos, sin = self.rotary_emb(q, pos)
-        manager._laprune_rope_step = (key, cos, sin)
+    total = past + n_new
+    cos, sin = _rope_rows(self, manager, q, past, n_new)
+    if n_new == 1 and q.is_cuda and q.dtype in (torch.float16, torch.bfloat16) and d % 2 == 0:
+        q_rope, k_all, v_all, kv_out = _rope_append_decode(self, q, k, v, cos, sin, total, kv_cache)
     else:
-        cos, sin = cached[1], cached[2]
-    Q_rope, K_new = apply_rotary_pos_emb(q, k, cos, sin)
-    if layer_idx + 1 == int(self.config.num_hidden_layers):
-        manager._laprune_rope_step = None
-    K_rope, vals_full, kv_out = _kv_cache_append(self, K_new, v, total, kv_cache)
+        from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+        q_rope, k_rope = apply_rotary_pos_emb(q, k, cos, sin)
+        k_all, v_all, kv_out = _kv_cache_append(self, k_rope, v, total, kv_cache)
     self.total_seq_len = total
-    sparse = (conf.get("enable", True) and not conf.get("aq_disable_encode", False) and not self.is_fix_layer
-              and not getattr(self, "full_kv_layer", False) and layer_idx in manager.layer_cfgs)
-    if is_prefill and conf.get("aq_disable_prefill", False):
-        sparse = False
-    if not sparse:
-        return do_sdpa_attn(Q_rope, K_rope, vals_full, out_proj=self.o_proj, already_rope=True), kv_out, None, None
-    aq_cache = _prepare_aq_cache(self, manager, layer_idx, K_rope,
+
+    if not _sparse_layer(self, manager, conf, is_prefill):
+        return do_sdpa_attn(q_rope, k_all, v_all, out_proj=self.o_proj, already_rope=True), kv_out, None, None
+    aq_cache = _prepare_aq_cache(self, manager, self.layer_idx, k_all,
                                  need_recon=not conf.get("aq_use_exact_true_score", True),
-                                 decode_group_size=int(conf.get("aq_decode_group_size", 1)), is_prefill=is_prefill)
+                                 decode_group_size=int(conf.get("aq_decode_group_size", 1)),
+                                 is_prefill=is_prefill)
     if is_prefill:
-        return do_sdpa_attn(Q_rope, K_rope, vals_full, out_proj=self.o_proj, already_rope=True), kv_out, None, None
-    return _decode_attention(self, manager, layer_idx, Q_rope, K_rope, vals_full, aq_cache, conf), kv_out, None, None
+        return do_sdpa_attn(q_rope, k_all, v_all, out_proj=self.o_proj, already_rope=True), kv_out, None, None
+    out = _decode_attention(self, manager, self.layer_idx, q_rope, k_all, v_all, aq_cache, conf)
+    return out, kv_out, None, None

@@ -7,6 +7,7 @@
 #include "compat.cuh"
 #include "encode.cuh"
 #include "icm.cuh"
+#include "rope_append.cuh"
 #include "fused_step.cuh"
 #include "lut_build.cuh"
 #include "score.cuh"
@@ -928,6 +929,54 @@ int lp_gqa_gather_kv(const lp_gqa_gather_args* a, void* stream) {
     p.out_v = static_cast<uint16_t*>(a->out_v);
     gqa_gather_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
     return check_launch("gqa_gather_kernel");
+}
+
+size_t lp_sizeof_rope_append_args(void) { return sizeof(lp_rope_append_args); }
+
+int lp_rope_append(const lp_rope_append_args* a, void* stream) {
+    LP_CHECK(a != nullptr, "args must not be NULL");
+    LP_CHECK(a->dtype == LP_BF16 || a->dtype == LP_F16, "dtype must be LP_BF16 or LP_F16");
+    LP_CHECK(a->B >= 0 && a->Hq > 0 && a->Hkv > 0 && a->D > 0 && a->D % 2 == 0 && a->D <= 1024,
+             "need B >= 0, Hq > 0, Hkv > 0 and an even D <= 1024");
+    LP_CHECK(a->pos >= 0, "pos must be non-negative");
+    if (a->B == 0) return LP_OK;
+    LP_CHECK(a->q && a->k && a->v && a->cos && a->sin && a->q_out && a->k_cache && a->v_cache,
+             "tensors must not be NULL");
+    RopeAppendParams p{};
+    p.q = a->q;
+    p.k = a->k;
+    p.v = a->v;
+    p.q_sb = a->q_stride_b;
+    p.q_sh = a->q_stride_h;
+    p.k_sb = a->k_stride_b;
+    p.k_sh = a->k_stride_h;
+    p.v_sb = a->v_stride_b;
+    p.v_sh = a->v_stride_h;
+    p.cos = a->cos;
+    p.sin = a->sin;
+    p.cos_sb = a->cos_stride_b;
+    p.sin_sb = a->sin_stride_b;
+    p.q_out = a->q_out;
+    p.qo_sb = a->q_out_stride_b;
+    p.qo_sh = a->q_out_stride_h;
+    p.k_cache = a->k_cache;
+    p.v_cache = a->v_cache;
+    p.kc_sb = a->kc_stride_b;
+    p.kc_sh = a->kc_stride_h;
+    p.kc_st = a->kc_stride_t;
+    p.vc_sb = a->vc_stride_b;
+    p.vc_sh = a->vc_stride_h;
+    p.vc_st = a->vc_stride_t;
+    p.Hq = a->Hq;
+    p.Hkv = a->Hkv;
+    p.D = a->D;
+    p.pos = a->pos;
+    const dim3 grid((unsigned)(a->Hq + 2 * a->Hkv), (unsigned)a->B);
+    const unsigned threads = (unsigned)((a->D / 2 + 31) / 32 * 32);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (a->dtype == LP_BF16) rope_append_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>(p);
+    else rope_append_kernel<__half><<<grid, threads, 0, st>>>(p);
+    return check_launch("rope_append_kernel");
 }
 
 int lp_read_device_errors(void* workspace, size_t workspace_bytes, void* stream, uint32_t* bits_out) {

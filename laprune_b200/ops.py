@@ -307,6 +307,64 @@ def encode_keys(x: torch.Tensor, codebooks: torch.Tensor, codes: Optional[torch.
     return codes
 
 
+def rope_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                k_cache: torch.Tensor, v_cache: torch.Tensor, pos: int,
+                q_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One decode token (lp_rope_append): rotary embedding of its query rows
+    (returned, or written to ``q_out``) and key rows, the rotated key and the
+    value written to slot ``pos`` of the static caches.
+
+    q ``[B, Hq, 1, D]`` or ``[B, Hq, D]``; k / v ``[B, Hkv, 1, D]`` or
+    ``[B, Hkv, D]``; cos / sin ``[B, 1, D]`` or ``[B, D]`` (HF rotary rows of
+    the token); k_cache / v_cache ``[B, Hkv, cap, D]``.  All of one dtype
+    (bf16 or fp16), rows contiguous.  The rotation rounds like HF
+    apply_rotary_pos_emb on these dtypes."""
+    def rows(t, name):
+        if t.dim() == 4:
+            if t.shape[2] != 1:
+                raise RuntimeError(f"{name}: one token expected, got {tuple(t.shape)}")
+            t = t[:, :, 0]
+        if t.dim() != 3 or t.stride(-1) != 1:
+            raise RuntimeError(f"{name} must be [B, H, D] with contiguous rows")
+        return t
+    q3, k3, v3 = rows(q, "q"), rows(k, "k"), rows(v, "v")
+    c2 = cos.reshape(cos.shape[0], -1) if cos.dim() == 3 else cos
+    s2 = sin.reshape(sin.shape[0], -1) if sin.dim() == 3 else sin
+    B, Hq, D = q3.shape
+    Hkv = k3.shape[1]
+    dt = q3.dtype
+    for name, t in (("k", k3), ("v", v3), ("cos", c2), ("sin", s2), ("k_cache", k_cache), ("v_cache", v_cache)):
+        if t.dtype != dt or not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor of the query's dtype {dt}")
+    if dt not in (torch.bfloat16, torch.float16):
+        raise RuntimeError("rope_append takes bf16 or fp16 tensors")
+    if k3.shape != (B, Hkv, D) or v3.shape != (B, Hkv, D) or c2.shape != (B, D) or s2.shape != (B, D):
+        raise RuntimeError("shape mismatch between q, k, v, cos and sin")
+    if k_cache.dim() != 4 or k_cache.shape[:2] != (B, Hkv) or k_cache.shape[3] != D or v_cache.shape != k_cache.shape:
+        raise RuntimeError("k_cache / v_cache must be [B, Hkv, cap, D]")
+    if not 0 <= int(pos) < k_cache.shape[2]:
+        raise RuntimeError(f"pos={pos} outside the cache capacity {k_cache.shape[2]}")
+    if c2.stride(-1) != 1 or s2.stride(-1) != 1 or k_cache.stride(-1) != 1 or v_cache.stride(-1) != 1:
+        raise RuntimeError("cos, sin and the caches must have contiguous rows")
+    out = torch.empty((B, Hq, D), dtype=dt, device=q3.device) if q_out is None else q_out
+    o3 = rows(out, "q_out")
+    a = _lib.RopeAppendArgs()
+    a.q, a.k, a.v = q3.data_ptr(), k3.data_ptr(), v3.data_ptr()
+    a.q_stride_b, a.q_stride_h = q3.stride(0), q3.stride(1)
+    a.k_stride_b, a.k_stride_h = k3.stride(0), k3.stride(1)
+    a.v_stride_b, a.v_stride_h = v3.stride(0), v3.stride(1)
+    a.cos, a.sin, a.cos_stride_b, a.sin_stride_b = c2.data_ptr(), s2.data_ptr(), c2.stride(0), s2.stride(0)
+    a.q_out, a.q_out_stride_b, a.q_out_stride_h = o3.data_ptr(), o3.stride(0), o3.stride(1)
+    a.k_cache, a.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+    a.kc_stride_b, a.kc_stride_h, a.kc_stride_t = k_cache.stride(0), k_cache.stride(1), k_cache.stride(2)
+    a.vc_stride_b, a.vc_stride_h, a.vc_stride_t = v_cache.stride(0), v_cache.stride(1), v_cache.stride(2)
+    a.dtype = _DTYPE[dt]
+    a.B, a.Hq, a.Hkv, a.D, a.pos = B, Hq, Hkv, D, int(pos)
+    with torch.cuda.device(q3.device):
+        _lib.check(_lib.load().lp_rope_append(ctypes.byref(a), _stream_handle(q3.device)))
+    return out
+
+
 def event_array(events) -> ctypes.Array:
     """ctypes array of raw cudaEvent_t handles of torch.cuda.Event objects
     (each event is created on the current device if it was not yet)."""

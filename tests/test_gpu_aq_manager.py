@@ -192,3 +192,78 @@ def test_quantizer_encode_matches_the_oracle_and_its_loss():
     assert abs(loss - ref) <= 1e-4 * ref
     codes2, loss2, _ = aq.encode(x.to(_dev()), icm_iters=0, return_loss=False)
     assert torch.equal(codes2, codes) and loss2 == 0.0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_decode_token_rope_append_equals_hf_rotation_and_slice_copy(dtype):
+    """lp_rope_append against HF apply_rotary_pos_emb + the slice copies of
+    the reference's _kv_cache_append (aq_evaluation.py:296-308, 65-112):
+    rotated query, rotated key and value in slot `pos`, bit for bit, with
+    Llama-3.1's rope scaling; every other cache slot untouched."""
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding, apply_rotary_pos_emb
+    from laprune_b200 import ops
+    dev = _dev()
+    cfg = LlamaConfig(hidden_size=4096, num_attention_heads=32, num_key_value_heads=8, rope_theta=500000.0,
+                      max_position_embeddings=131072,
+                      rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                    "high_freq_factor": 4.0, "original_max_position_embeddings": 8192})
+    rot = LlamaRotaryEmbedding(cfg, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(21)
+    B, Hq, Hkv, D, cap, pos = 2, 32, 8, 128, 300, 257
+    q = torch.randn((B, Hq, 1, D), generator=g, device=dev).to(dtype)
+    k = torch.randn((B, Hkv, 1, D), generator=g, device=dev).to(dtype)
+    v = torch.randn((B, Hkv, 1, D), generator=g, device=dev).to(dtype)
+    kc = torch.randn((B, Hkv, cap, D), generator=g, device=dev).to(dtype)
+    vc = torch.randn((B, Hkv, cap, D), generator=g, device=dev).to(dtype)
+    kc0, vc0 = kc.clone(), vc.clone()
+    cos, sin = rot(q, torch.full((B, 1), 100000, device=dev))
+    q_rot = ops.rope_append(q, k, v, cos, sin, kc, vc, pos)
+    q_ref, k_ref = apply_rotary_pos_emb(q, k, cos, sin)
+    torch.cuda.synchronize()
+    assert torch.equal(q_rot, q_ref[:, :, 0])
+    assert torch.equal(kc[:, :, pos], k_ref[:, :, 0]) and torch.equal(vc[:, :, pos], v[:, :, 0])
+    keep = torch.ones(cap, dtype=torch.bool)
+    keep[pos] = False
+    assert torch.equal(kc[:, :, keep], kc0[:, :, keep]) and torch.equal(vc[:, :, keep], vc0[:, :, keep])
+
+
+@torch.no_grad()
+def test_attention_forward_keeps_the_cache_contract():
+    """The rewritten attention forward against the reference's contract: the
+    cache views it returns, the buffers' capacity policy (first buffers
+    total + aq_kv_extra_capacity, doubling when full) and the rotated keys
+    in the cache (HF rotation) through prefill and decode tokens."""
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaAttention, LlamaRotaryEmbedding, apply_rotary_pos_emb
+    dev = _dev()
+    cfg = LlamaConfig(hidden_size=512, num_attention_heads=4, num_key_value_heads=1, num_hidden_layers=4,
+                      intermediate_size=1024, rope_theta=500000.0, max_position_embeddings=4096)
+    g = torch.Generator().manual_seed(31)
+    attn = LlamaAttention(cfg, layer_idx=0)
+    for prm in attn.parameters():
+        prm.copy_(torch.randn(prm.shape, generator=g) * 0.02)
+    attn = attn.to(dev, torch.bfloat16)
+    attn.rotary_emb = LlamaRotaryEmbedding(cfg, device=dev)
+    attn.aq_manager = _mgr(torch.randn((32, 256, 128), generator=g) * 0.05, 4, layer=0)
+    attn.draft_kwargs = {"aq_kv_extra_capacity": 3, "enable": False}
+    attn.is_fix_layer = False
+    fwd = types.MethodType(aqe.self_attn_forward, attn)
+    T0 = 20
+    hs = (torch.randn((1, T0, 512), generator=g) * 0.5).to(dev, torch.bfloat16)
+    _, kv, _, _ = fwd(hs)
+    assert attn.k_cache_capacity == T0 + 3 and attn.k_cache_len == T0
+    for step in range(6):  # 3 tokens fill the extra slots, the 4th doubles the buffers
+        h1 = (torch.randn((1, 1, 512), generator=g) * 0.5).to(dev, torch.bfloat16)
+        _, kv, _, _ = fwd(h1, kv_cache=kv)
+        total = T0 + step + 1
+        assert attn.k_cache_len == total and kv[0].shape[2] == total
+        assert attn.k_cache_capacity == (T0 + 3 if total <= T0 + 3 else 2 * (T0 + 3))
+        assert kv[0].data_ptr() == attn.k_cache.data_ptr() and kv[0].stride(1) == attn.k_cache_capacity * 128
+        k = attn.k_proj(h1).unflatten(-1, (1, 128)).transpose(1, 2)
+        q = attn.q_proj(h1).unflatten(-1, (4, 128)).transpose(1, 2)
+        cos, sin = attn.rotary_emb(q, torch.tensor([[total - 1]], device=dev))
+        _, k_ref = apply_rotary_pos_emb(q, k, cos, sin)
+        assert torch.equal(attn.k_cache[:, :, total - 1], k_ref[:, :, 0])
+        assert torch.equal(attn.v_cache[:, :, total - 1], attn.v_proj(h1).unflatten(-1, (1, 128)).transpose(1, 2)[:, :, 0])
