@@ -414,18 +414,21 @@ def encode_measurement(dev, reps: int = 20):
 def hook_measurement(dev, reps: int = 3):
     """This package's layer step at the reference decode hook's shipped
     settings (the configuration of ref_cuda_measurement's hook_layer): one
-    fp32 codebook for every head, fp16 K/V, top-2621 per QUERY head on
-    [0, T-64), the 64-token local window, attention of every query head over
-    its own set (LP_SELECT_QUERY_HEAD), 30 calls over N_SIDE resident layers.
-    Algorithmic bytes: the codebook (4.19 MB), the codes of the candidate
-    window and the K/V rows of every query head's set (32 x 2685 rows of
-    2 x 256 B, the reference's gather)."""
+    fp16 codebook for every head (the fp16 manager's copy), fp16 K/V,
+    top-2621 per QUERY head on [0, T-64), the 64-token local window,
+    attention of every query head over its own set (LP_SELECT_QUERY_HEAD),
+    30 calls over N_SIDE resident layers.  Algorithmic bytes: the codebook
+    (2.10 MB), the codes of the candidate window and the K/V rows of every
+    query head's set (32 x 2685 rows of 2 x 256 B, the reference's gather)."""
     import ctypes
     import torch
     from laprune_b200 import _lib, ops
     lib = _lib.load()
     layers = _side_layers(dev, 78, shared_codebook=True)
     for L in layers:
+        # the fp16 codebook copy an fp16 manager scores from (the reference's
+        # aq_manager_dtype fp16 reads fp16 codebooks too)
+        L["C"] = L["C"].to(torch.float16)
         L["out"] = torch.empty((1, HQ, D), dtype=torch.float16, device=dev)
         L["args"] = ops.build_args(L["q"], L["C"], L["codes"], L["keys"], L["vals"], topk=HOOK_K, sink=0,
                                    local=LOCAL, select="query_head", out=L["out"])
@@ -440,7 +443,7 @@ def hook_measurement(dev, reps: int = 3):
 
     us = _time_calls(call, reps * N_LAYERS)
     peak, peak_kind = _peaks()
-    nbytes = M * K * D * 4 + HKV * (T_CTX - LOCAL) * M + HQ * (HOOK_K + LOCAL) * D * 2 * 2
+    nbytes = M * K * D * 2 + HKV * (T_CTX - LOCAL) * M + HQ * (HOOK_K + LOCAL) * D * 2 * 2
     res = {"layer_us": us, "tok_s_30_layers": 1e6 / (us * N_LAYERS),
            "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (us * 1e-6) / 1e9,
            "frac_of_peak": nbytes / (us * 1e-6) / 1e9 / peak, "peak_kind": peak_kind,

@@ -79,11 +79,13 @@ typedef struct lp_sparse_decode_args {
     int32_t q_dtype; /* LP_BF16 | LP_F16 | LP_F32 */
     int32_t _pad0;
     int64_t q_stride_b, q_stride_h;
-    /* fp32 codebooks, contiguous [Hkv][M][K][D] (cb_per_kv_head=1) or
-     * [M][K][D] shared by every KV head (cb_per_kv_head=0) */
-    const float* codebooks;
+    /* codebooks, contiguous [Hkv][M][K][D] (cb_per_kv_head=1) or [M][K][D]
+     * shared by every KV head (cb_per_kv_head=0), of cb_dtype: LP_F32 (0, the
+     * default), or LP_F16 / LP_BF16 copies (half the bytes; the tables are
+     * still built in fp32 from their exactly widened elements) */
+    const void* codebooks;
     int32_t cb_per_kv_head;
-    int32_t _pad1;
+    int32_t cb_dtype;
     /* uint8 codes[b][hkv][t][m] at codes + b*sb + hkv*sh + t*st + m (bytes) */
     const uint8_t* codes;
     int64_t codes_stride_b, codes_stride_h, codes_stride_t;

@@ -27,7 +27,7 @@ class SparseDecodeArgs(ctypes.Structure):
     _fields_ = [
         ("q", _c_p), ("q_dtype", _c_i32), ("_pad0", _c_i32),
         ("q_stride_b", _c_i64), ("q_stride_h", _c_i64),
-        ("codebooks", _c_p), ("cb_per_kv_head", _c_i32), ("_pad1", _c_i32),
+        ("codebooks", _c_p), ("cb_per_kv_head", _c_i32), ("cb_dtype", _c_i32),
         ("codes", _c_p), ("codes_stride_b", _c_i64), ("codes_stride_h", _c_i64), ("codes_stride_t", _c_i64),
         ("keys", _c_p), ("vals", _c_p), ("kv_dtype", _c_i32), ("_pad2", _c_i32),
         ("k_stride_b", _c_i64), ("k_stride_h", _c_i64), ("k_stride_t", _c_i64),

@@ -45,18 +45,21 @@ def decode_keep_size(num_candidate: int, mask_out: float = 0.98, min_remain: int
 
 
 def _scoring_codebooks(manager: AQLayerCodebookManager, layer_idx: int, Hq: int, Hkv: int) -> torch.Tensor:
-    """The decode hook's codebooks: one for every head when heads_per_group
-    covers the Hq query heads (aq_evaluation.py:161-167), else query head h
-    uses group h // heads_per_group (:169-176) -- stacked per KV head, which
-    needs the G query heads of a KV head in one group."""
+    """The decode hook's codebooks, in the manager's scoring dtype (a
+    half-precision copy for an fp16 / bf16 manager, as the reference scores
+    from its manager-dtype codebooks): one for every head when
+    heads_per_group covers the Hq query heads (aq_evaluation.py:161-167),
+    else query head h uses group h // heads_per_group (:169-176) -- stacked
+    per KV head, which needs the G query heads of a KV head in one group."""
     cfg = manager.layer_cfgs.get(layer_idx)
+    dt = manager.scoring_dtype
     if cfg is None or cfg.heads_per_group <= 0 or cfg.heads_per_group >= Hq:
-        return manager.codebooks(layer_idx, 0)
+        return manager.codebooks(layer_idx, 0, dt)
     G, hpg = Hq // Hkv, cfg.heads_per_group
     groups = [(kv * G) // hpg for kv in range(Hkv)]
     if any((kv * G + G - 1) // hpg != groups[kv] for kv in range(Hkv)):
         raise NotImplementedError(f"heads_per_group={hpg} splits the {G} query heads of a KV head over codebooks")
-    return manager.group_codebooks(layer_idx, groups)
+    return manager.group_codebooks(layer_idx, groups, dt)
 
 
 def _encoding_codebooks(manager: AQLayerCodebookManager, layer_idx: int, Hkv: int) -> torch.Tensor:

@@ -172,6 +172,34 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
     return __float2bfloat16_rn(v);
 }
 
+// 4 consecutive codebook elements (fp32, or fp16 / bf16 widened exactly to
+// fp32) at element index idx of a codebook of dtype dt (LP_F32 | LP_F16 |
+// LP_BF16); idx a multiple of 4
+__device__ __forceinline__ float4 cb_load4(const void* base, int64_t idx, int dt) {
+    if (dt == LP_F32) return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(base) + idx));
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + idx));
+    if (dt == LP_F16) {
+        const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
+        return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+    }
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+    return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+}
+// the same from shared memory (a row staged by a bulk copy)
+__device__ __forceinline__ float4 cb_lds4(const unsigned char* row, int i4, int dt) {
+    if (dt == LP_F32) return reinterpret_cast<const float4*>(row)[i4];
+    const uint2 raw = reinterpret_cast<const uint2*>(row)[i4];
+    if (dt == LP_F16) {
+        const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
+        return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+    }
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+    return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+}
+__host__ __device__ __forceinline__ int cb_elem_bytes(int dt) { return dt == LP_F32 ? 4 : 2; }
+
 // Order-preserving map of an fp32 score into a histogram bin in [0, nb):
 // bin = clamp(floor((s - lo) * inv_w)).  Monotone non-decreasing in s, so a
 // token in a higher bin never has a lower score.  Written with explicit

@@ -77,7 +77,8 @@ static_assert((kFSpillList + 2 * kFSpillWords) * 4 <= kFScoreCap * 4, "spill ove
 struct FusedParams {
     const void* q;
     int64_t q_stride_b, q_stride_h;
-    const float* cb;
+    const void* cb;      // codebooks of cb_dtype (LP_F32 | LP_F16 | LP_BF16)
+    int cb_dtype;
     int cb_per_kv_head;
     const uint8_t* codes;
     int64_t codes_stride_b, codes_stride_h;
@@ -394,7 +395,9 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     const int64_t f_begin = (kRows * jg / ncg) & ~(int64_t)7;
     const int64_t f_end = jg + 1 == ncg ? kRows : ((kRows * (jg + 1) / ncg) & ~(int64_t)7);
     const int nchunk = (int)((f_end - f_begin + 63) / 64);
-    const float* cbu = p.cb + (int64_t)(p.cb_per_kv_head ? hkv : 0) * (kRows * 128);
+    const uint32_t row_bytes = 128u * (uint32_t)cb_elem_bytes(p.cb_dtype);  // one codeword row
+    const unsigned char* cbu = static_cast<const unsigned char*>(p.cb) +
+                               (int64_t)(p.cb_per_kv_head ? hkv : 0) * kRows * row_bytes;
     auto abuf = [&](int c) -> unsigned char* {
         const int b3 = c % 3;
         return b3 == 2 ? reinterpret_cast<unsigned char*>(s_scores) : s_lut + b3 * 32768;
@@ -402,8 +405,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     auto issue_chunk = [&](int c) {
         const int64_t r0 = f_begin + (int64_t)c * 64;
         const int64_t r1 = min(f_end, r0 + 64);
-        mbar_arrive_expect_tx(&s_abar[c % 3], (uint32_t)((r1 - r0) * 512));
-        bulk_g2s(abuf(c), cbu + r0 * 128, (uint32_t)((r1 - r0) * 512), &s_abar[c % 3]);
+        mbar_arrive_expect_tx(&s_abar[c % 3], (uint32_t)(r1 - r0) * row_bytes);
+        bulk_g2s(abuf(c), cbu + r0 * row_bytes, (uint32_t)(r1 - r0) * row_bytes, &s_abar[c % 3]);
     };
     uint64_t policy = 0;
     const int npre = ntiles < kFStages ? ntiles : kFStages;
@@ -494,11 +497,11 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             if (fr < f_end) {
                 const int m = (int)((fr >> 8) & 31);
                 const int k0 = (int)(fr & 255);
-                const float* rows = reinterpret_cast<const float*>(abuf(c)) + (warp * 4) * 128 + lane * 4;
+                const unsigned char* rows = abuf(c) + (warp * 4) * row_bytes;
                 float4 cv[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                    cv[j] = (fr + j < f_end) ? *reinterpret_cast<const float4*>(rows + j * 128)
+                    cv[j] = (fr + j < f_end) ? cb_lds4(rows + j * row_bytes, lane, p.cb_dtype)
                                              : make_float4(0.f, 0.f, 0.f, 0.f);
                 const int jr = (lane >> 3) & 3;  // the row whose total this lane ends with
                 float* dst = p.lut + ((int64_t)gv0 * 256 + k0 + jr) * 32 + m;

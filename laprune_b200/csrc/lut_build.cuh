@@ -1,8 +1,9 @@
 // lut_build.cuh -- per-query lookup tables LUT[m][k] = q . C_m[k] (fp32).
 //
 // Reference: laprune/llm/aq_kv.py:681-682 (cuBLAS q @ C^T, fp16) and the CPU
-// path aq_kv.py:620 (einsum, fp32).  Here the table is built in fp32 from
-// fp32 codebooks on CUDA cores.  The work is a skinny GEMV that is bound by
+// path aq_kv.py:620 (einsum, fp32).  Here the table is built in fp32 on CUDA
+// cores from fp32 codebooks, or from fp16 / bf16 copies (the reference's
+// fp16 manager dtype; their elements widen to fp32 exactly).  The work is a skinny GEMV that is bound by
 // the codebook bytes (33.5 MB for per-KV-head fp32 codebooks at Llama-3.1-8B
 // geometry), so the kernel is organised for memory-level parallelism: one
 // CTA per (codebook m, quarter of the K codewords, unit), each warp keeps 8
@@ -33,7 +34,8 @@ constexpr int kLutThreads = 128; // 4 warps
 struct LutBuildParams {
     const void* q;
     int64_t q_stride_b, q_stride_h;
-    const float* cb;
+    const void* cb;    // [Hkv or 1][M][K][D] of cb_dtype
+    int cb_dtype;      // LP_F32 | LP_F16 | LP_BF16
     int cb_per_kv_head;
     int Hkv, G, D, M, K;
     float* lut;      // GROUP: [U][K][M]; HEADS: [U][K][M][4]
@@ -92,16 +94,17 @@ __global__ void __launch_bounds__(kLutThreads) lut_build_kernel(LutBuildParams p
         for (int64_t i = start; i < p.zero_words; i += nthreads) p.zero[i] = 0u;
     }
 
-    const float* cbm = p.cb + (int64_t)(p.cb_per_kv_head ? hkv : 0) * p.M * p.K * p.D +
-                       (int64_t)m * p.K * p.D;
+    const int esz = cb_elem_bytes(p.cb_dtype);
+    const unsigned char* cbm = static_cast<const unsigned char*>(p.cb) +
+                               ((int64_t)(p.cb_per_kv_head ? hkv : 0) * p.M * p.K * p.D + (int64_t)m * p.K * p.D) * esz;
     const int kper = (p.K + kLutParts - 1) / kLutParts;
     const int kbeg = part * kper, kend = min(p.K, kbeg + kper);
     // pull this CTA's whole codebook slice toward L2 before anything else
     if (tid == 0 && kend > kbeg) {
-        const uint32_t bytes = (uint32_t)((kend - kbeg) * p.D * sizeof(float));
-        if ((bytes & 15u) == 0 && (((uintptr_t)(cbm + (int64_t)kbeg * p.D)) & 15u) == 0)
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(cbm + (int64_t)kbeg * p.D), "r"(bytes)
-                         : "memory");
+        const uint32_t bytes = (uint32_t)((kend - kbeg) * p.D * esz);
+        const unsigned char* src = cbm + (int64_t)kbeg * p.D * esz;
+        if ((bytes & 15u) == 0 && (((uintptr_t)src) & 15u) == 0)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
     }
 
     const QT* qb = reinterpret_cast<const QT*>(p.q) + (int64_t)b * p.q_stride_b;
@@ -138,7 +141,7 @@ __global__ void __launch_bounds__(kLutThreads) lut_build_kernel(LutBuildParams p
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const int k = k0 + j;
-                    cv[j] = k < kend ? __ldg(reinterpret_cast<const float4*>(cbm + (int64_t)k * p.D + d))
+                    cv[j] = k < kend ? cb_load4(cbm, (int64_t)k * p.D + d, p.cb_dtype)
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll

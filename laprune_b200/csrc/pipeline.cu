@@ -264,6 +264,7 @@ static int launch_lut(const lp_sparse_decode_args* a, const Plan& p, cudaStream_
     lp_.q_stride_b = a->q_stride_b;
     lp_.q_stride_h = a->q_stride_h;
     lp_.cb = a->codebooks;
+    lp_.cb_dtype = a->cb_dtype;
     lp_.cb_per_kv_head = a->cb_per_kv_head;
     lp_.Hkv = a->Hkv;
     lp_.G = a->G;
@@ -351,6 +352,7 @@ static int launch_fused(const lp_sparse_decode_args* a, const Plan& p, cudaStrea
     fp.q_stride_b = a->q_stride_b;
     fp.q_stride_h = a->q_stride_h;
     fp.cb = a->codebooks;
+    fp.cb_dtype = a->cb_dtype;
     fp.cb_per_kv_head = a->cb_per_kv_head;
     fp.codes = a->codes;
     fp.codes_stride_b = a->codes_stride_b;
@@ -486,6 +488,8 @@ int lp_sparse_decode(const lp_sparse_decode_args* a, void* workspace, size_t wor
     LP_CHECK(a->q_dtype == LP_BF16 || a->q_dtype == LP_F16 || a->q_dtype == LP_F32,
              "q_dtype must be LP_BF16, LP_F16 or LP_F32");
     LP_CHECK(aligned16(a->codebooks), "codebooks must be 16-byte aligned");
+    LP_CHECK(a->cb_dtype == LP_F32 || a->cb_dtype == LP_F16 || a->cb_dtype == LP_BF16,
+             "cb_dtype must be LP_F32, LP_F16 or LP_BF16");
     LP_CHECK(aligned16(a->codes) && a->codes_stride_b % 16 == 0 && a->codes_stride_h % 16 == 0,
              "codes base and batch/head strides must be 16-byte aligned");
     LP_CHECK(a->codes_stride_t == 32, "codes rows must be contiguous 32-byte rows (stride_t == M == 32)");

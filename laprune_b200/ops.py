@@ -101,8 +101,8 @@ def build_args(q, codebooks, codes, keys=None, vals=None, *, topk: int, T_codes=
     if Hq % Hkv != 0:
         raise RuntimeError(f"Invalid GQA score heads: Hq={Hq}, Hkv={Hkv}")
     G = Hq // Hkv
-    if codebooks.dtype != torch.float32 or not codebooks.is_contiguous():
-        raise RuntimeError("codebooks must be contiguous fp32 [Hkv,M,K,D] or [M,K,D]")
+    if codebooks.dtype not in (torch.float32, torch.float16, torch.bfloat16) or not codebooks.is_contiguous():
+        raise RuntimeError("codebooks must be contiguous fp32 / fp16 / bf16 [Hkv,M,K,D] or [M,K,D]")
     per_kv = codebooks.dim() == 4
     if per_kv and codebooks.shape[0] != Hkv:
         raise RuntimeError("per-KV-head codebooks must have Hkv sets")
@@ -125,6 +125,7 @@ def build_args(q, codebooks, codes, keys=None, vals=None, *, topk: int, T_codes=
     a.q_stride_b, a.q_stride_h = q.stride(0), q.stride(1)
     a.codebooks = codebooks.data_ptr()
     a.cb_per_kv_head = int(per_kv)
+    a.cb_dtype = _DTYPE[codebooks.dtype]
     a.codes = codes.data_ptr()
     a.codes_stride_b, a.codes_stride_h, a.codes_stride_t = codes.stride(0), codes.stride(1), codes.stride(2)
     if keys is not None:
@@ -174,7 +175,8 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
                   prefetch=None, exchange_select: bool = False) -> SparseDecodeResult:
     """One sparse decode step of one layer (see lp_sparse_decode).
 
-    q [B,Hq,D] (or [Hq,D]); codebooks fp32 [Hkv,M,K,D] or [M,K,D]; codes uint8
+    q [B,Hq,D] (or [Hq,D]); codebooks [Hkv,M,K,D] or [M,K,D] (fp32, or an fp16 / bf16
+    copy: half the bytes, tables built in fp32 from its elements); codes uint8
     [B,Hkv,cap,M]; keys/vals [B,Hkv,cap,D] bf16/fp16.  Returns the attention
     output [B,Hq,D] (``out_dtype``, default the K/V dtype), and optionally the
     selected indices ([B*Hkv, topk] or [B*Hq, topk], ascending int32) and the

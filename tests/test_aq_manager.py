@@ -125,3 +125,45 @@ def test_quantizer_encode_surface_refuses_training_and_host_tensors():
         aq.encode(torch.zeros(4, 128), icm_iters=2)
     with pytest.raises(NotImplementedError):
         aq.encode(torch.zeros(4, 128), method="beam", icm_iters=0)
+
+
+def test_codebook_copies_round_trip_and_stale_copies_are_ignored(tmp_path):
+    from laprune_b200.aq_kv import codebook_file_index
+    src = _mgr(layers=(0, 1), hpg=8, num_heads=8)
+    g = torch.Generator().manual_seed(8)
+    cbs = {(l, 0): torch.randn((32, 256, 128), generator=g) * 0.05 for l in (0, 1)}
+    for (l, gr), cb in cbs.items():
+        src.set_codebooks(l, gr, cb)
+    src.save(str(tmp_path))
+    assert src.write_codebook_copies(str(tmp_path)) == 2
+    names = sorted(p.name for p in tmp_path.iterdir())
+    assert names == ["layer_0_group_0.lpcopies.pt", "layer_0_group_0.pt",
+                     "layer_1_group_0.lpcopies.pt", "layer_1_group_0.pt"]
+    # only the codebook files themselves name a (layer, group), as for the
+    # reference's loader (its group field must parse as an integer)
+    assert codebook_file_index("layer_1_group_0.pt") == (1, 0)
+    assert codebook_file_index("layer_1_group_0.lpcopies.pt") is None
+    blob = torch.load(tmp_path / "layer_1_group_0.lpcopies.pt", weights_only=True)
+    c16 = cbs[(1, 0)].to(torch.float16)
+    assert torch.equal(blob["codebooks_fp16"], c16)
+    assert torch.equal(blob["weight_t_fp16"], c16.transpose(1, 2))
+    assert torch.equal(blob["bias_fp16"], (-0.5 * c16.float().pow(2).sum(-1)).to(torch.float16))
+    # loaded copies are the persisted tensors
+    blob["codebooks_fp16"][0, 0, 0] = 1.0  # marker: a copy from the file, not a fresh conversion
+    torch.save(blob, tmp_path / "layer_1_group_0.lpcopies.pt")
+    m = _mgr(layers=(0, 1), hpg=8, num_heads=8)
+    m.dtype = torch.float16
+    m.load(str(tmp_path))
+    assert m.scoring_dtype == torch.float16
+    assert m.codebooks(1, 0, torch.float16)[0, 0, 0].item() == 1.0
+    assert torch.equal(m.codebooks(1, 0), cbs[(1, 0)])
+    # a copy file made from other codebooks is ignored: converted afresh
+    torch.save(src._cb[(0, 0)] * 2, tmp_path / "unused.pt")
+    other = dict(blob, source_sha256="0" * 64)
+    torch.save(other, tmp_path / "layer_1_group_0.lpcopies.pt")
+    m2 = _mgr(layers=(0, 1), hpg=8, num_heads=8)
+    m2.load(str(tmp_path))
+    assert torch.equal(m2.codebooks(1, 0, torch.float16), c16)
+    m3 = _mgr(layers=(0, 1), hpg=8, num_heads=8)
+    m3.load(str(tmp_path), use_copies=False)
+    assert torch.equal(m3.codebooks(0, 0, torch.bfloat16), cbs[(0, 0)].to(torch.bfloat16))

@@ -117,20 +117,29 @@ def test_code_cache_follows_prefill_and_grouped_decode():
         assert np.array_equal(got[h], want)
 
 
-def test_sharded_manager_drives_the_decode_hook(golden_dir, tmp_path):
+@pytest.mark.parametrize("mgr_dtype,tol", [(torch.float32, 2e-2), (torch.float16, 5e-2)])
+def test_sharded_manager_drives_the_decode_hook(golden_dir, tmp_path, mgr_dtype, tol):
+    """The per-device manager through the decode hook against the
+    reference's own hook output (made with an fp32 manager).  An fp16
+    manager scores from the fp16 codebook copy, as the reference's fp16
+    manager does: the rounded codebooks move scores by about 1e-3 of their
+    range, which can swap tokens at the selection threshold, so its bound is
+    the looser 5e-2 (the kernels themselves are exact on the rounded values:
+    test_half_precision_codebooks_select_like_their_fp32_values)."""
     from laprune_b200.aq_kv import ShardedAQLayerCodebookManager
     fix = np.load(golden_dir / "decode_hook.npz")
     dh = syn.decode_hook_case(11)
     _mgr(dh["cb"], dh["Hq"]).save(str(tmp_path))
     sh = ShardedAQLayerCodebookManager({0: AQLayerConfig(M=32, K=256, d=128, heads_per_group=dh["Hq"],
-                                                         num_heads=dh["Hq"])}, str(tmp_path), devices=[_dev()])
+                                                         num_heads=dh["Hq"])}, str(tmp_path), devices=[_dev()],
+                                       dtype=mgr_dtype)
     dev = _dev()
     conf = {"mask_out": 0.98, "min_remain": 20, "sink_size": 4, "local_window": 64, "aq_scoring_m": 32}
     self_attn = types.SimpleNamespace(total_seq_len=dh["T"], o_proj=torch.nn.Identity())
     out = aqe._decode_attention(self_attn, sh, 0, dh["q"].to(dev).half(), dh["keys"].to(dev).half(),
                                 dh["vals"].to(dev).half(), {"codes": dh["codes"].to(dev), "seq_len": dh["T"]}, conf)
     torch.cuda.synchronize()
-    assert np.abs(out.float().cpu().numpy() - fix["out_sink4"]).max() <= 2e-2
+    assert np.abs(out.float().cpu().numpy() - fix["out_sink4"]).max() <= tol
 
 
 @torch.no_grad()

@@ -428,3 +428,30 @@ def test_spilled_scores_select_like_the_multi_kernel_path(B, Hkv, T, k):
     assert torch.equal(r.topk, m.topk)
     assert (r.out.float() - m.out.float()).abs().max().item() <= 1e-2
     _check_errors()
+
+
+@pytest.mark.parametrize("cbdt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("select,mode", [("kv_group", "auto"), ("kv_group", "multi"), ("query_head", "auto"),
+                                         ("query_head", "multi")])
+def test_half_precision_codebooks_select_like_their_fp32_values(cbdt, select, mode):
+    """Scoring from an fp16 / bf16 codebook copy (half the bytes of the
+    table build): its elements widen to fp32 exactly, so the tables, the
+    selection and the attention equal those of the fp32 tensor holding the
+    same values, bit for bit, on every path."""
+    C, codes, K, V, q = _rand_case(1313, 1, 8, 4, 20000, per_kv=(select == "kv_group"))
+    dev = _dev()
+    Ch = C.to(cbdt).to(dev)
+    args = [t.to(dev) for t in (codes, K, V)]
+    kw = dict(topk=400, sink=4, local=64, select=select, return_topk=True, **MODES[mode])
+    r = ops.sparse_decode(q.to(dev), Ch, *args, **kw)
+    w = ops.sparse_decode(q.to(dev), Ch.float(), *args, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(r.topk, w.topk) and torch.equal(r.out, w.out)
+    if mode == "multi":
+        hs = ops.sparse_decode(q.to(dev), Ch, *args, topk=400, sink=4, local=64, select=select,
+                               return_head_scores=True, attention=False).head_scores
+        hw = ops.sparse_decode(q.to(dev), Ch.float(), *args, topk=400, sink=4, local=64, select=select,
+                               return_head_scores=True, attention=False).head_scores
+        torch.cuda.synchronize()
+        assert torch.equal(hs, hw)
+    _check_errors()
