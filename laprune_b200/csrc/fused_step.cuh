@@ -66,6 +66,7 @@ constexpr int kPubWin = 128;                     // bins in a CTA's published co
 constexpr int kPubMaxCtas = 64;                  // CTAs per unit of the published-candidate path
 constexpr int kPubMaxCap = 2048;                 // published candidates per CTA (own copy in shared memory)
 constexpr int kFastTieCap = 1024;                // tie-bin entries the fast selection path settles
+constexpr int kFusedQMaxG = 8;                   // query heads per unit summed into a LUT query
 // spill mode (a CTA's share above kFScoreCap tokens): the scores go to the
 // L2-resident global buffer and the shared-memory score region holds the row
 // list and the CTA's selection bitmaps instead
@@ -157,6 +158,22 @@ __device__ __forceinline__ unsigned long long global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+
+// Fine-grained timeline for kernel development: built with -DLP_FUSED_TRACE,
+// thread 0 of CTA 0 and of the grid's last CTA stamp step i into
+// phase_ns[8 + i] and phase_ns[40 + i] (the caller then passes 72 words).
+// Off in the library build.
+#ifdef LP_FUSED_TRACE
+#define LP_FTRACE(i)                                                                          \
+    do {                                                                                      \
+        if (p.phase_ns && threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1)) \
+            p.phase_ns[8 + (blockIdx.x ? 32 : 0) + (i)] = global_ns();                        \
+    } while (0)
+#else
+#define LP_FTRACE(i) \
+    do {             \
+    } while (0)
+#endif
 
 
 // Words exchanged between the CTAs of a unit carry the call's epoch in their
@@ -440,6 +457,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const bool stamp = p.phase_ns != nullptr && blockIdx.x == 0 && tid == 0;
     if (stamp) p.phase_ns[0] = global_ns();
+    LP_FTRACE(0);
     if (tid == 0) {
         // the input streams first: the epoch's round trip below overlaps them
         issue_inputs();
@@ -458,9 +476,17 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         for (int j = from; j < issued; ++j) mbar_wait(&s_bar[j % kFStages], (uint32_t)(j / kFStages) & 1u, nullptr);
     };
 
-    for (int i = tid; i < p.G * 128; i += kFThreads) {
-        const int g = i >> 7, d = i & 127;
-        s_qu[i] = to_f32(reinterpret_cast<const QT*>(p.q)[(int64_t)b * p.q_stride_b + (int64_t)(hu * p.G + g) * p.q_stride_h + d]);
+    // the unit's own query rows (G * 128 <= 1024 values, at most 2 per
+    // thread): loaded into registers here, stored after the group's rows
+    // below have been issued, so that all query loads share one round trip
+    float qown[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int i = tid + r * kFThreads;
+        qown[r] = i < p.G * 128
+                      ? to_f32(reinterpret_cast<const QT*>(p.q)[(int64_t)b * p.q_stride_b +
+                                                                (int64_t)(hu * p.G + (i >> 7)) * p.q_stride_h + (i & 127)])
+                      : 0.f;
     }
 
     // ================= phase A: LUT build of the CTA's LUT group =================
@@ -473,17 +499,28 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         // the ring's slots 2.. (their code tiles are issued after phase A)
         float* s_qs = reinterpret_cast<float*>(s_ring + kFPre0 * kFTile);  // [nq <= kFLutGroup][128]
         static_assert(kFPre0 * kFTile + kFLutGroup * 128 * 4 <= FusedSmem::kRing, "group queries fit the ring");
+        // every head's value loaded before any is added (the G <= 8 loads of
+        // an entry are independent), then summed in g order
         for (int i = tid; i < nq * 128; i += kFThreads) {
             const int jq = i >> 7, d = i & 127;
             const int v = gv0 + jq;
             const int vgi = v % p.upk, vhb = v / p.upk, vkv = vhb / p.B, vb = vhb - vkv * p.B;
             const QT* qr = reinterpret_cast<const QT*>(p.q) + (int64_t)vb * p.q_stride_b +
                            (int64_t)((vkv * p.upk + vgi) * p.G) * p.q_stride_h + d;
+            float x[kFusedQMaxG];
+#pragma unroll
+            for (int g = 0; g < kFusedQMaxG; ++g) x[g] = g < p.G ? to_f32(qr[(int64_t)g * p.q_stride_h]) : 0.f;
             float acc = 0.f;
-            for (int g = 0; g < p.G; ++g) acc += to_f32(qr[(int64_t)g * p.q_stride_h]);
+#pragma unroll
+            for (int g = 0; g < kFusedQMaxG; ++g)
+                if (g < p.G) acc += x[g];
             s_qs[i] = acc;
         }
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+            if (tid + r * kFThreads < p.G * 128) s_qu[tid + r * kFThreads] = qown[r];
         __syncthreads();
+        LP_FTRACE(1);
         bool okA = true;
         for (int c = 0; c < nchunk; ++c) {
             if (!mbar_wait(&s_abar[c % 3], (uint32_t)(c / 3) & 1u, p.err)) okA = false;
@@ -492,6 +529,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 drain(0);
                 return;
             }
+            if (c == 0) LP_FTRACE(2);
             const int64_t r0 = f_begin + (int64_t)c * 64;
             const int64_t fr = r0 + warp * 4;  // first row of this warp (4 rows of the same m)
             if (fr < f_end) {
@@ -547,6 +585,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         st_tag(p.lut_flag + blockIdx.x, 1u, s_epoch);
     }
     if (stamp) p.phase_ns[1] = global_ns();
+    LP_FTRACE(3);
     // the ring's other slots: issued once phase A's codebook stream is done,
     // so that the two streams do not share HBM while the LUT is built
     if (tid == 0) {
@@ -591,6 +630,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             for (int j = 0; j < 4; ++j) v[j] = __ldcg(gl + tid + j * kFThreads);
         }
         if (stamp) p.phase_ns[2] = global_ns();
+        LP_FTRACE(4);
         // thread's m group is (tid & 7); reduce min/max per m over k
         // (scratch in the score buffer, which is not written yet)
         float (*s_mmin)[32] = reinterpret_cast<float (*)[32]>(s_scores);
@@ -679,6 +719,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         __shared__ int s_abort;
         if (tid == 0) s_abort = 0;
         __syncthreads();
+        LP_FTRACE(5);
         // two tiles per iteration: two independent gather chains per thread
         auto score_row = [&](int slot, int lt) {
             const uint32_t* row = reinterpret_cast<const uint32_t*>(s_ring + slot * kFTile + tid * 32);
@@ -707,6 +748,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             if (!mbar_wait(&s_bar[s0], (uint32_t)(i / kFStages) & 1u, p.err)) s_abort = 1;
             if (two && !mbar_wait(&s_bar[s1], (uint32_t)((i + 1) / kFStages) & 1u, p.err)) s_abort = 1;
             if (*((volatile int*)&s_abort)) break;
+            if (i == 0) LP_FTRACE(6);
             const int lt0 = i * kFThreads + tid, lt1 = lt0 + kFThreads;
             const bool v0 = t_begin + lt0 < t_end, v1 = two && t_begin + lt1 < t_end;
             if (v1) {
@@ -742,8 +784,10 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             }
         }
         if (__syncthreads_or(s_abort)) { drain(0); return; }
+        LP_FTRACE(7);
         // the local histogram, for the exchange path (read after a unit barrier)
         for (int i = tid; i < kNB; i += kFThreads) p.chist[(int64_t)blockIdx.x * kNB + i] = s_hist[i];
+        LP_FTRACE(19);
         // ---- publish the CTA's candidates for the unit's selection: every
         //      own token whose bin is at or above b_j, the CTA's threshold
         //      bin for pub_target tokens (all tokens if it has fewer), sorted
@@ -754,8 +798,15 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         //      exchange path. ----
         if (p.pub_cap > 0) {
             __shared__ int s_bj;
-            uint32_t* s_suf = reinterpret_cast<uint32_t*>(s_lut);    // [kNB + 1] suffix counts (table is dead)
-            uint32_t* s_cur = s_suf + kNB + 1;                        // [kPubWin] scatter cursors
+            // s_suf: [kNB + 1] suffix counts (the table is dead now).  The
+            // scatter cursors s_cur stay in use until a thread's last slot
+            // atomic, while threads that are done already copy the unit's
+            // windows into the front of the table region in phase C (no
+            // barrier in between): they sit in its last 512 bytes, which
+            // phase C does not touch before its first barrier.
+            uint32_t* s_suf = reinterpret_cast<uint32_t*>(s_lut);
+            uint32_t* s_cur = reinterpret_cast<uint32_t*>(s_lut + FusedSmem::kLut - kPubWin * 4);
+            static_assert((kNB + 1) * 4 <= FusedSmem::kLut - kPubWin * 4, "suffix counts end before the cursors");
             float2* s_own = reinterpret_cast<float2*>(s_ring + 64 * 1024);  // own published entries
             // suffix counts s_suf[b] = tokens in bins >= b: thread t owns bins
             // [kNB - 4(t+1), kNB - 4t), the top bins first
@@ -783,10 +834,12 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 }
             }
             __syncthreads();
+            LP_FTRACE(20);
             // b_j: the highest bin whose suffix reaches pub_target
             for (int bb = tid; bb < kNB; bb += kFThreads)
                 if ((int)s_suf[bb] >= p.pub_target && (int)s_suf[bb + 1] < p.pub_target) s_bj = bb;
             __syncthreads();
+            LP_FTRACE(21);
             const int bj = s_bj;
             const int npub = (int)s_suf[bj];
             const bool pub_ok = npub <= p.pub_cap;
@@ -809,6 +862,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 st_tag(pw + kPubWin + 1, pub_ok ? (uint32_t)bj : (uint32_t)kNB, s_epoch);
             }
             __syncthreads();
+            LP_FTRACE(22);
             if (pub_ok) {
                 unsigned long long* slot = p.pub + (int64_t)blockIdx.x * p.pub_cap * 2;
                 // PU scores per thread per round, all loads issued before any
@@ -837,6 +891,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         }
     }
     if (stamp) p.phase_ns[3] = global_ns();
+    LP_FTRACE(8);
     if (tid == kFThreads - 32) {  // a lane off the select critical path
         prefetch_share(p.pf_ptr[0], p.pf_bytes[0], p.pf_count[0], p.pf_stride[0]);
         prefetch_share(p.pf_ptr[1], p.pf_bytes[1], p.pf_count[1], p.pf_stride[1]);
@@ -935,6 +990,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             __syncthreads();
         }
         if (stamp) p.phase_ns[4] = global_ns();
+        LP_FTRACE(9);
         for (int i = tid; i < nw_own; i += kFThreads) s_selw[i] = 0u;
         for (int i = tid; i < (ntok + 31) / 32; i += kFThreads) s_win[i] = 0u;
         if (pub) {
@@ -1019,6 +1075,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             }
         }
         __syncthreads();
+        LP_FTRACE(10);
         if (s_fast) {
             const int bs = s_bstar;
             const int need = p.k - s_above;
@@ -1048,6 +1105,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 }
             }
             __syncthreads();
+            LP_FTRACE(23);
             // offsets of the slots' tie entries (warp 0); the own
             // above-threshold tokens in ascending order -> s_list (all)
             if (warp == 0) {
@@ -1079,6 +1137,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 if (tid == 0) s_nabove = na;
             }
             __syncthreads();
+            LP_FTRACE(24);
             // the unit's tie-bin entries: loads issued first (up to 2 per
             // thread), then the K/V rows known now (own above-threshold
             // tokens, sink and local shares), while the tie bin is settled
@@ -1104,6 +1163,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 }
             }
             issue_rows(0, 0, min(s_nabove + n_sink_here + n_loc_here, R), s_nabove);
+            LP_FTRACE(25);
             {
                 bool ok = true;
                 const long long t0 = clock64();
@@ -1135,6 +1195,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                     return;
                 }
             }
+            LP_FTRACE(11);
             // rank (score desc, index asc) of the own tie entries (all of them
             // when the top-k indices are requested): the first `need` win
             const int i0 = p.topk_out ? 0 : s_toff[cj];
@@ -1156,6 +1217,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         }
     }
     if (stamp) p.phase_ns[5] = global_ns();
+    LP_FTRACE(12);
     if (!s_fast) {
         // ---- exchange path: threshold bin of the unit histogram, ballots,
         //      tie-bin tokens through the tie slots, one more barrier ----
@@ -1443,6 +1505,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 __syncthreads();  // scan_tmp is reused by the next round
             }
         }
+        LP_FTRACE(13);
         const int nabove = s_nabove;
         const int n_early = nabove + n_sink_here + n_loc_here;
         const int nrows = n_early + s_nwin;
@@ -1551,6 +1614,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 __syncthreads();
                 attend(0, n_issued);
                 r_ready = n_issued;
+                LP_FTRACE(14);
             } else {
                 issue_rows(c0r, 0, nr, nabove);
             }
@@ -1559,6 +1623,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             attend(r_ready, nr);
             __syncthreads();  // staging rows consumed before the next chunk lands
         }
+        LP_FTRACE(15);
         // ---- combine the warps' states into the CTA's slice state ----
         {
             float* s_wacc = reinterpret_cast<float*>(s_lut);  // [NW][G][128]
@@ -1621,6 +1686,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             }
         }
     }
+    LP_FTRACE(16);
 
     // ================= merge: each CTA of the unit finalises a slice of its G*128 outputs =================
     {
@@ -1659,6 +1725,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         }
         if (__syncthreads_or(!ok)) return;
         if (stamp) p.phase_ns[6] = global_ns();
+        LP_FTRACE(17);
         OT* ob = reinterpret_cast<OT*>(p.out) + (int64_t)b * p.out_stride_b;
         for (int ol = tid; ol < o1 - o0; ol += kFThreads) {
             const float* mm = s_mm + ol * cn;
@@ -1676,6 +1743,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             ob[(int64_t)(hu * p.G + g) * p.out_stride_h + d] = from_f32<OT>(A / L);
         }
         if (p.phase_ns && tid == 0) atomicMax(&p.phase_ns[7], global_ns());
+        LP_FTRACE(18);
     }
 }
 
