@@ -865,8 +865,51 @@ int lp_lut_gather(const lp_lut_gather_args* a, void* stream) {
     p.out = a->out;
     p.out_f16 = a->out_dtype == LP_F16;
     p.os_q = a->out_stride_q;
-    const int smem = (a->m1 - a->m0) * a->K * 4;
-    lut_gather_kernel<<<dim3((a->N + 255) / 256, a->Q), 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = sm_count(dev);
+    const int mr = a->m1 - a->m0;
+    // 16-byte code-row loads: rows of at most 32 used bytes, 16-byte aligned
+    const bool vec = a->m1 <= 32 && (reinterpret_cast<uintptr_t>(a->codes) & 15u) == 0 &&
+                     a->codes_stride_h % 16 == 0 && a->codes_stride_t % 16 == 0;
+    const bool f16 = a->lut_dtype == LP_F16;
+    p.lut_vec = f16 && (reinterpret_cast<uintptr_t>(a->lut) & 15u) == 0 && a->lut_stride_q % 8 == 0 &&
+                ((int64_t)a->m0 * a->K) % 8 == 0 && ((int64_t)mr * a->K) % 8 == 0;
+    if (vec && a->indices == nullptr && a->G > 1 && a->Q % a->G == 0 && a->G <= (f16 ? kScanMaxG : kScanMaxG32) &&
+        a->N == a->T) {
+        // dense scan: each code row read once for the G rows that share it
+        const int H = a->Q / a->G;
+        const int64_t smem64 = (int64_t)(f16 ? (a->G + 1) / 2 : a->G) * mr * a->K * 4;
+        if (smem64 <= 200 * 1024) {
+            const int smem = (int)smem64;
+            // about 3 CTAs per SM (the fp16 G=4 table, 64 KB, allows 3)
+            int64_t tile = ((int64_t)a->T * H + 3ll * sms - 1) / (3ll * sms);
+            tile = std::min<int64_t>(16384, std::max<int64_t>(kScanThreads, (tile + kScanThreads - 1) / kScanThreads * kScanThreads));
+            const dim3 grid((unsigned)((a->T + tile - 1) / tile), (unsigned)H);
+            static bool opt16[64] = {false}, opt32[64] = {false};
+            if (f16) {
+                int rc = smem_opt_in(lut_scan_group_kernel<true>, 200 * 1024, dev, opt16);
+                if (rc != LP_OK) return rc;
+                lut_scan_group_kernel<true><<<grid, kScanThreads, smem, st>>>(p, (int)tile);
+            } else {
+                int rc = smem_opt_in(lut_scan_group_kernel<false>, 200 * 1024, dev, opt32);
+                if (rc != LP_OK) return rc;
+                lut_scan_group_kernel<false><<<grid, kScanThreads, smem, st>>>(p, (int)tile);
+            }
+            return check_launch("lut_scan_group_kernel");
+        }
+    }
+    const int smem = mr * a->K * 4;
+    if (vec) {
+        // per-row tables, `tile` tokens per CTA so that a table is staged
+        // once for many tokens
+        int64_t tile = ((int64_t)a->N * a->Q + 2ll * sms - 1) / (2ll * sms);
+        tile = std::min<int64_t>(8192, std::max<int64_t>(256, (tile + 255) / 256 * 256));
+        lut_gather_rows_kernel<<<dim3((unsigned)((a->N + tile - 1) / tile), a->Q), 256, smem, st>>>(p, (int)tile);
+        return check_launch("lut_gather_rows_kernel");
+    }
+    lut_gather_kernel<<<dim3((a->N + 255) / 256, a->Q), 256, smem, st>>>(p);
     return check_launch("lut_gather_kernel");
 }
 
@@ -876,21 +919,34 @@ int lp_lut_build(const lp_lut_build_args* a, void* stream) {
     if (a->Q == 0) return LP_OK;
     LP_CHECK(a->q && a->codebooks && a->lut, "q, codebooks and lut must not be NULL");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const dim3 grid(a->M, a->Q);
-    const int smem = a->D * 4;
+    LP_CHECK(a->D <= 320, "lut build: D must be at most 320");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const dim3 grid((a->K + 31) / 32, a->M, (a->Q + 31) / 32);
+    const int smem = 2 * 32 * (a->D + 1) * 4;
+    static bool opt[3][64] = {};
     switch (a->q_dtype) {
-        case LP_BF16:
+        case LP_BF16: {
+            int rc = smem_opt_in(lut_build_rows_kernel<__nv_bfloat16>, smem, dev, opt[0]);
+            if (rc != LP_OK) return rc;
             lut_build_rows_kernel<__nv_bfloat16><<<grid, 256, smem, st>>>(
-                reinterpret_cast<const __nv_bfloat16*>(a->q), a->q_stride, a->codebooks, a->M, a->K, a->D, a->lut);
+                reinterpret_cast<const __nv_bfloat16*>(a->q), a->q_stride, a->codebooks, a->M, a->K, a->D, a->Q, a->lut);
             break;
-        case LP_F16:
+        }
+        case LP_F16: {
+            int rc = smem_opt_in(lut_build_rows_kernel<__half>, smem, dev, opt[1]);
+            if (rc != LP_OK) return rc;
             lut_build_rows_kernel<__half><<<grid, 256, smem, st>>>(
-                reinterpret_cast<const __half*>(a->q), a->q_stride, a->codebooks, a->M, a->K, a->D, a->lut);
+                reinterpret_cast<const __half*>(a->q), a->q_stride, a->codebooks, a->M, a->K, a->D, a->Q, a->lut);
             break;
-        case LP_F32:
+        }
+        case LP_F32: {
+            int rc = smem_opt_in(lut_build_rows_kernel<float>, smem, dev, opt[2]);
+            if (rc != LP_OK) return rc;
             lut_build_rows_kernel<float><<<grid, 256, smem, st>>>(
-                reinterpret_cast<const float*>(a->q), a->q_stride, a->codebooks, a->M, a->K, a->D, a->lut);
+                reinterpret_cast<const float*>(a->q), a->q_stride, a->codebooks, a->M, a->K, a->D, a->Q, a->lut);
             break;
+        }
         default:
             return fail(LP_ERR_INVALID, "q_dtype must be LP_BF16, LP_F16 or LP_F32");
     }
@@ -931,7 +987,20 @@ int lp_gqa_gather_kv(const lp_gqa_gather_args* a, void* stream) {
     p.N = (int)N;
     p.out_k = static_cast<uint16_t*>(a->out_k);
     p.out_v = static_cast<uint16_t*>(a->out_v);
-    gqa_gather_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+    if (a->D % 8 == 0 && al16(a->keys) && al16(a->vals) && al16(a->out_k) && al16(a->out_v) &&
+        a->k_stride_b % 8 == 0 && a->k_stride_h % 8 == 0 && a->k_stride_t % 8 == 0 && a->v_stride_b % 8 == 0 &&
+        a->v_stride_h % 8 == 0 && a->v_stride_t % 8 == 0) {
+        // 16-byte units: every K and V row is D/8 of them
+        int dev = 0;
+        cudaGetDevice(&dev);
+        (void)dev;
+        const dim3 grid((unsigned)((N + 8 * kKvRowsPerWarp - 1) / (8 * kKvRowsPerWarp)), (unsigned)(a->B * a->Hkv * a->G));
+        gqa_gather_vec_kernel<<<grid, 256, 0, st>>>(p);
+        return check_launch("gqa_gather_vec_kernel");
+    }
+    gqa_gather_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(p);
     return check_launch("gqa_gather_kernel");
 }
 
