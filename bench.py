@@ -201,6 +201,86 @@ def _side_layers(dev, seed: int, shared_codebook: bool):
     return layers
 
 
+def _time_graph(fn, n_calls: int = 30, warmup: int = 3):
+    """Mean µs per call of fn() over n_calls calls captured in one CUDA graph
+    and replayed (kernel time, no host gaps between the calls)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for _ in range(n_calls):
+            fn()
+    gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del gr
+    return e0.elapsed_time(e1) * 1e3 / n_calls
+
+
+def _drop_in_inputs(dev):
+    """Seeded inputs of the aq_kernels op timings (both arms use the same):
+    cfg3-sized fp16 LUTs [32,32,256] and code caches [8,131072,32] (six
+    copies, 201 MB, cycled), index lists [32,8192], fp16 K/V caches
+    [1,8,131072,128] (three copies, 1.6 GB) with the decode hook's top-2621
+    lists and 64-token tail, and the aq_lut.cu shapes (q [32,128], C
+    [32,256,128], per-query codes [32,4096,32])."""
+    import torch
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    T = T_CTX
+    d = {"luts": [torch.randn((HQ, M, K), generator=g, device=dev).to(torch.float16) for _ in range(6)],
+         "codes": [torch.randint(0, 256, (HKV, T, M), generator=g, device=dev, dtype=torch.uint8) for _ in range(6)]}
+    d["idx"] = torch.randint(0, T, (HQ, 8192), generator=g, device=dev)
+    d["K"] = [torch.randn((1, HKV, T, D), generator=g, device=dev).to(torch.float16) for _ in range(3)]
+    d["V"] = [torch.randn((1, HKV, T, D), generator=g, device=dev).to(torch.float16) for _ in range(3)]
+    d["kidx"] = torch.randint(0, T - LOCAL, (1, HQ, HOOK_K), generator=g, device=dev)
+    d["q"] = torch.randn((HQ, D), generator=g, device=dev).to(torch.float16)
+    d["C"] = torch.randn((M, K, D), generator=g, device=dev).to(torch.float16)
+    d["cq"] = torch.randint(0, 256, (HQ, 4096, M), generator=g, device=dev, dtype=torch.uint8)
+    d["lut2"] = torch.randn((HQ, M * K), generator=g, device=dev).to(torch.float16)
+    return d
+
+
+def _drop_in_timings(ops_, d, graph_ok: bool):
+    """µs per call of the seven aq_kernels ops (on module `ops_`, this
+    package's drop-ins or the reference extension's functions).  Kernel
+    time from CUDA-graph replays where the ops launch on the current stream;
+    the reference's aq_lut.cu ops launch on the legacy default stream, which
+    a capture does not record, so those are timed eagerly (graph_ok False)."""
+    it = {"i": 0, "j": 0}
+
+    def nl():
+        it["i"] = (it["i"] + 1) % 6
+        return it["i"]
+
+    def nk():
+        it["j"] = (it["j"] + 1) % 3
+        return it["j"]
+
+    tg = _time_graph
+    grouped, gather = ops_["grouped"], ops_["gather"]
+    kv_tail, kv = ops_["kv_tail"], ops_["kv"]
+    res = {
+        "aq_lut_gather_grouped_cfg3": tg(lambda: grouped(d["luts"][nl()], d["codes"][it["i"]], 4)),
+        "aq_lut_gather_gqa_dense_cfg3": tg(lambda: gather(d["luts"][nl()], d["codes"][it["i"]], 4, 0, M)),
+        "aq_lut_gather_gqa_index_8192_m16": tg(lambda: gather(d["luts"][nl()], d["codes"][it["i"]], 4, 0, 16, d["idx"])),
+        "gqa_gather_kv_with_tail_hook": tg(lambda: kv_tail(d["K"][nk()], d["V"][it["j"]], d["kidx"], 4, T_CTX - LOCAL, LOCAL)),
+        "gqa_gather_kv_hook": tg(lambda: kv(d["K"][nk()], d["V"][it["j"]], d["kidx"], 4)),
+    }
+    t2 = tg if graph_ok else (lambda fn: _time_calls(lambda i: fn(), 30))
+    res["aq_lut_forward_32x4096"] = t2(lambda: ops_["lut_forward"](d["q"], d["C"], d["cq"]))
+    res["aq_lut_gather_forward_32x4096"] = t2(lambda: ops_["gather_forward"](d["lut2"], d["cq"]))
+    res["timing"] = ("CUDA-graph replay (kernel time)" if graph_ok else
+                     "CUDA-graph replay; aq_lut_* eager (legacy-stream launches)")
+    return res
+
+
 def _time_calls(fn, n_calls: int, warmup: int = 3):
     """Mean µs per call of fn(i) over n_calls calls (CUDA events)."""
     import torch
@@ -319,6 +399,16 @@ def ref_cuda_measurement(reps: int = 3):
     out["encode_cfg2_per_kv_head_us"] = _time_calls(
         lambda i: [enc(x256[h], wt[h], bias[h], C16[h], True, 0) for h in range(HKV)], 20)
     out["encode_prefill_32768_shared_us"] = enc_us(xpre, 0)
+    del C, C16, wt, bias, x512, x2048, x256, xpre
+    torch.cuda.empty_cache()
+    lut_mod = build_ref.load("aq_lut")
+    d = _drop_in_inputs(dev)
+    out["aq_kernels_us"] = _drop_in_timings(
+        {"grouped": gqa.aq_lut_gather_grouped, "gather": gqa.aq_lut_gather, "kv_tail": gqa.gqa_gather_kv_with_tail,
+         "kv": gqa.gqa_gather_kv, "lut_forward": lut_mod.aq_lut_forward,
+         "gather_forward": lut_mod.aq_lut_gather_forward}, d, graph_ok=False)
+    del d
+    torch.cuda.empty_cache()
     return out
 
 
@@ -449,6 +539,21 @@ def hook_measurement(dev, reps: int = 3):
            "frac_of_peak": nbytes / (us * 1e-6) / 1e9 / peak, "peak_kind": peak_kind,
            "device_error_bits": ops.device_errors(ws, dev)}
     del layers
+    torch.cuda.empty_cache()
+    return res
+
+
+def aq_kernels_measurement(dev):
+    """This package's aq_kernels drop-ins on the shapes the reference arm
+    times the reference extension on (_drop_in_inputs), kernel time."""
+    import torch
+    from laprune_b200 import aq_kernels as aqk
+    d = _drop_in_inputs(dev)
+    res = _drop_in_timings({"grouped": aqk.aq_lut_gather_grouped, "gather": aqk.aq_lut_gather_gqa,
+                            "kv_tail": aqk.gqa_gather_kv_with_tail, "kv": aqk.gqa_gather_kv,
+                            "lut_forward": aqk.aq_lut_forward, "gather_forward": aqk.aq_lut_gather_forward},
+                           d, graph_ok=True)
+    del d
     torch.cuda.empty_cache()
     return res
 
@@ -697,6 +802,7 @@ def run_ours(args):
         if world == 1 and not args.no_side:
             line["encode"] = encode_measurement(dev)
             line["hook_layer"] = hook_measurement(dev)
+            line["aq_kernels_us"] = aq_kernels_measurement(dev)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         print(json.dumps(line), flush=True)
