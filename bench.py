@@ -558,6 +558,85 @@ def aq_kernels_measurement(dev):
     return res
 
 
+def cfg5_measurement(dev, world: int, rank: int, layers: int = 4, reps: int = 3):
+    """BASELINE config 5's attention path: B = 8 sequences x T = 131072 with
+    the 8 KV heads sharded over the N ranks (strong scaling: the job is
+    fixed, each GPU holds 64/N (sequence, KV head) units), and for N >= 2
+    the weak-scaled variant B = 16 x 65536 (16 x 8/N units per GPU).  Per
+    layer: top-2048 per KV head + 4 sink + 64 local, bf16 K/V, fp32
+    per-KV-head codebooks; one step = the 30 sparse layers (`layers`
+    resident instances cycled), captured in a CUDA graph and replayed, timed
+    between barriers as the max over ranks.  tok/s counts every sequence's
+    token of the step (B per step).  Every rank calls this (collectives)."""
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from laprune_b200 import _lib, ops, tp
+    lib = _lib.load()
+    out = {}
+    cases = [("strong_B8_T131072", 8, 131072)]
+    if world >= 2:
+        cases.append(("weak_B16_T65536", 16, 65536))
+    h0, h1 = tp.kv_head_range(HKV, world, rank)
+    hkv = h1 - h0
+    for name, B, T in cases:
+        g = torch.Generator(device=dev)
+        g.manual_seed(4321 + rank)
+        Ls = []
+        for _ in range(layers):
+            L = {"C": torch.randn((hkv, M, K, D), generator=g, device=dev) * 0.05,
+                 "codes": torch.randint(0, 256, (B, hkv, T, M), generator=g, device=dev, dtype=torch.uint8),
+                 "keys": torch.randn((B, hkv, T, D), generator=g, device=dev).to(torch.bfloat16),
+                 "vals": torch.randn((B, hkv, T, D), generator=g, device=dev).to(torch.bfloat16),
+                 "q": torch.randn((B, hkv * 4, D), generator=g, device=dev).to(torch.bfloat16)}
+            L["out"] = torch.empty_like(L["q"])
+            L["args"] = ops.build_args(L["q"], L["C"], L["codes"], L["keys"], L["vals"], topk=TOPK, sink=SINK,
+                                       local=LOCAL, out=L["out"])
+            Ls.append(L)
+        need = max(lib.lp_sparse_decode_workspace_size(ctypes.byref(L["args"])) for L in Ls)
+        ws = ops.workspace(need, dev, tag=f"bench_{name}")
+
+        def step():
+            st = torch.cuda.current_stream(dev).cuda_stream
+            for li in range(N_LAYERS):
+                rc = lib.lp_sparse_decode(ctypes.byref(Ls[li % layers]["args"]), ws.data_ptr(), ws.numel(), st)
+                if rc != 0:
+                    _lib.check(rc)
+
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, capture_error_mode="thread_local"):
+            step()
+        gr.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.barrier()
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms = float(t[0])
+        units = B * hkv
+        nbytes = hkv * M * K * D * 4 + units * (T - SINK - LOCAL) * M + units * (TOPK + SINK + LOCAL) * D * 2 * 2
+        peak, peak_kind = _peaks()
+        out[name] = {"tok_s": B / (step_ms / 1e3), "step_ms": step_ms, "layer_us": step_ms * 1e3 / N_LAYERS,
+                     "units_per_gpu": units, "kv_heads_per_gpu": hkv,
+                     "hbm_frac_per_gpu": nbytes / (step_ms / 1e3 / N_LAYERS) / 1e9 / peak, "peak_kind": peak_kind,
+                     "device_error_bits": ops.device_errors(ws, dev)}
+        del gr, Ls, ws
+        torch.cuda.empty_cache()
+    out["scaling"] = "strong (B=8 x 131072 fixed) and weak (B=16 x 65536, 8/N KV heads per GPU)"
+    return out
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -737,6 +816,9 @@ def run_ours(args):
     del graph
     graph_errs = ops.device_errors(ws, dev)
 
+    # BASELINE config 5 (all ranks take part), outside the timed region
+    cfg5 = None if args.no_cfg5 else cfg5_measurement(dev, world, rank)
+
     # max over ranks
     t = torch.tensor([elapsed_ms, e2e_ms, kernel_ms, launch_ms, graph_ms, eager_ms] + stage_ms, device=dev,
                      dtype=torch.float64)
@@ -799,6 +881,8 @@ def run_ours(args):
                                      "device_error_bits": graph_errs}},
             "gpu_launches": args.steps * N_LAYERS,
         }
+        if cfg5 is not None:
+            line["config5"] = cfg5
         if world == 1 and not args.no_side:
             line["encode"] = encode_measurement(dev)
             line["hook_layer"] = hook_measurement(dev)
@@ -824,6 +908,9 @@ def main():
     ap.add_argument("--no-side", action="store_true",
                     help="our arm: skip the side measurements (decode-hook layer, encoders)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cfg5", action="store_true", help="our arm: skip the config-5 (B=8 x 131072) measurement")
+    ap.add_argument("--only", choices=["aq_kernels", "encode", "hook", "cfg5"],
+                    help="run one side measurement on one GPU, print its JSON and exit (small cases for profiling)")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="resident layer instances cycled over the 30 layer calls of a step "
                          "(default 30; fewer only to profile a small case)")
@@ -832,6 +919,13 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.only:
+        import torch
+        dev = torch.device("cuda", 0)
+        fn = {"aq_kernels": aq_kernels_measurement, "encode": encode_measurement, "hook": hook_measurement,
+              "cfg5": lambda d: cfg5_measurement(d, 1, 0, layers=2, reps=1)}[args.only]
+        print(json.dumps({args.only: fn(dev)}), flush=True)
+        return 0
     return run_ours(args)
 
 
