@@ -870,7 +870,9 @@ def run_ours(args):
                          "algorithmic_bytes_per_launch": launch_bytes,
                          "bytes_split": {"codebooks_fp32": lut_bytes, "codes_u8": score_bytes,
                                          "kv_rows_bf16": gather_bytes},
-                         "traffic": _profile_traffic()},
+                         # the committed capture is of the N = 1 launch (8 KV heads); at N > 1 a
+                         # GPU's launch holds another split of the work, so no figure applies
+                         "traffic": _profile_traffic() if world == 1 else None},
             "clocks": clocks,
             "e2e": {"value": e2e_tok_s, "unit": UNIT,
                     "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
