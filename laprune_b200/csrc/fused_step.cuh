@@ -19,14 +19,14 @@
 //   A  LUT build: the CTAs of the units that read one codebook (a LUT
 //      group) split its 32*256 codeword rows evenly, write LUT_sum[u][k][m]
 //      = q_sum(u) . C_m[k] (fp32) of every unit u of the group to L2 and
-//      raise an epoch-tagged flag each.  The first code tiles of phase B are already
-//      streaming into the CTA's TMA ring; the rest follow once the codebook
-//      stream is done.                                     | the unit's flags
+//      raise an epoch-tagged flag each.                   | the unit's flags
 //   B  score: the unit's table is staged as int32 fixed point (exact sums,
 //      order-independent), the per-m bounds are recomputed from the table in
 //      shared memory (identical in every CTA of the unit), the CTA's code
-//      words stream through the ring, scores stay in shared memory (and go
-//      to global for the rare exact slow path), histogram -> global.  | barrier
+//      rows come straight from global memory into registers (one 256-bit
+//      load per token, the next step's rows in flight), scores stay in
+//      shared memory (or the L2-resident score buffer for long shares),
+//      histogram -> global.                                            | barrier
 //   C  select: bin b* of the k-th score from the unit histogram; ballots give
 //      the CTA's above-threshold tokens (row list in shared memory) and its
 //      tie-bin tokens (written to its own slot of the tie buffer).  The K/V
@@ -57,7 +57,7 @@ namespace lp {
 
 constexpr int kFThreads = 512;
 constexpr int kFStages = 6;
-constexpr int kFPre0 = 2;                        // code tiles issued before phase A
+constexpr int kFPre0 = 2;                        // ring slots kept free ahead of phase A's group queries
 constexpr int kFTile = kFThreads * 32;           // 16 KB of code rows per stage
 constexpr int kFScoreCap = 11264;                // tokens per CTA kept in smem
 constexpr int kFMaxWords = 8192;                 // bitmap words per unit in smem overlay
@@ -425,19 +425,9 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
         mbar_arrive_expect_tx(&s_abar[c % 3], (uint32_t)(r1 - r0) * row_bytes);
         bulk_g2s(abuf(c), cbu + r0 * row_bytes, (uint32_t)(r1 - r0) * row_bytes, &s_abar[c % 3]);
     };
-    uint64_t policy = 0;
-    const int npre = ntiles < kFStages ? ntiles : kFStages;
-    const int npre0 = npre < kFPre0 ? npre : kFPre0;  // the rest after phase A
-    // the first 3 codebook chunks, then the first phase-B code tiles
+    // the first 3 codebook chunks
     auto issue_inputs = [&]() {
         for (int c = 0; c < 3 && c < nchunk; ++c) issue_chunk(c);
-        policy = p.upk > 1 ? policy_evict_normal() : policy_evict_first();
-        for (int i = 0; i < npre0; ++i) {
-            const int t0 = t_begin + i * kFThreads;
-            const int nn = min(kFThreads, t_end - t0);
-            mbar_arrive_expect_tx(&s_bar[i], (uint32_t)nn * 32u);
-            bulk_g2s_stream(s_ring + i * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[i], policy);
-        }
     };
     if (tid == 0) {
         for (int s = 0; s < kFStages; ++s) {
@@ -471,7 +461,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     // (the epoch stays in shared memory, s_epoch: a register held across the
     // scorer would spill; the mbarrier inits and s_epoch are visible to all
     // threads after the barrier that completes s_qu below)
-    int issued = npre0;
+    int issued = 0;  // TMA transfers into the ring (none: the ring is staging space only)
     auto drain = [&](int from) {
         for (int j = from; j < issued; ++j) mbar_wait(&s_bar[j % kFStages], (uint32_t)(j / kFStages) & 1u, nullptr);
     };
@@ -496,7 +486,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     // transpose.
     {
         // the summed query rows of the group's units (fp32, g in order), in
-        // the ring's slots 2.. (their code tiles are issued after phase A)
+        // the ring's slots 2.. (free until phase B's publish)
         float* s_qs = reinterpret_cast<float*>(s_ring + kFPre0 * kFTile);  // [nq <= kFLutGroup][128]
         static_assert(kFPre0 * kFTile + kFLutGroup * 128 * 4 <= FusedSmem::kRing, "group queries fit the ring");
         // every head's value loaded before any is added (the G <= 8 loads of
@@ -588,15 +578,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     LP_FTRACE(3);
     // the ring's other slots: issued once phase A's codebook stream is done,
     // so that the two streams do not share HBM while the LUT is built
-    if (tid == 0) {
-        for (int i = npre0; i < npre; ++i) {
-            const int t0 = t_begin + i * kFThreads;
-            const int nn = min(kFThreads, t_end - t0);
-            mbar_arrive_expect_tx(&s_bar[i], (uint32_t)nn * 32u);
-            bulk_g2s_stream(s_ring + i * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[i], policy);
-        }
-    }
-    issued = npre;
+
 
     using Scan = cub::BlockScan<int, kFThreads>;
     __shared__ typename Scan::TempStorage scan_tmp;
@@ -742,45 +724,79 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             else gsc[t_begin + lt] = sc;
             atomicAdd(&s_hist[score_bin(sc, bp.lo, bp.inv_w, kNB)], 1u);
         };
+        // codes straight from global memory into registers: each thread's
+        // token rows (two 16-byte loads each), the next step's rows loaded
+        // before this step's lookups; a lane's 8 code words are rotated by L
+        // in registers, so the table reads stay bank-conflict free
+        const uint4* g4 = reinterpret_cast<const uint4*>(src) + (int64_t)t_begin * 2;
+        const bool shared_codes = p.upk > 1;  // the G query-head units of a KV head read the same rows
+        // 32-byte rows: one 256-bit load each when the rows are 32-byte
+        // aligned (evict-first in L2 unless other units read them too)
+        const bool v8ok = (reinterpret_cast<uintptr_t>(g4) & 31u) == 0;
+        auto load_row = [&](int lt, uint32_t* c) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) c[j] = 0u;
+            if (t_begin + lt < t_end) {
+                const uint4* pp = g4 + (int64_t)lt * 2;
+                if (v8ok && !shared_codes) {
+                    asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                                 : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]), "=r"(c[4]), "=r"(c[5]), "=r"(c[6]),
+                                   "=r"(c[7])
+                                 : "l"(pp));
+                } else if (v8ok) {
+                    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                                 : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]), "=r"(c[4]), "=r"(c[5]), "=r"(c[6]),
+                                   "=r"(c[7])
+                                 : "l"(pp));
+                } else {
+                    const uint4 a = __ldg(pp), b2 = __ldg(pp + 1);
+                    c[0] = a.x; c[1] = a.y; c[2] = a.z; c[3] = a.w;
+                    c[4] = b2.x; c[5] = b2.y; c[6] = b2.z; c[7] = b2.w;
+                }
+            }
+        };
+        auto score_regs = [&](const uint32_t* c) {
+            // r[w] = c[(w + L) & 7]: rotate by 1, 2, 4 as L's bits say
+            uint32_t r1[8], r2[8], r[8];
+#pragma unroll
+            for (int w = 0; w < 8; ++w) r1[w] = (L & 1u) ? c[(w + 1) & 7] : c[w];
+#pragma unroll
+            for (int w = 0; w < 8; ++w) r2[w] = (L & 2u) ? r1[(w + 2) & 7] : r1[w];
+#pragma unroll
+            for (int w = 0; w < 8; ++w) r[w] = (L & 4u) ? r2[(w + 4) & 7] : r2[w];
+            int iacc = 0;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    const uint32_t a = __byte_perm(r[w], off[s], sel[s]);
+                    iacc += *reinterpret_cast<const int*>(s_lut + a + 16 * w);
+                }
+            }
+            return __fmul_rn(__int2float_rn(iacc), from_fx);
+        };
+        uint32_t c0[8], c1[8];
+        load_row(tid, c0);
+        load_row(tid + kFThreads, c1);
+        LP_FTRACE(6);
         for (int i = 0; i < ntiles; i += 2) {
-            const bool two = i + 1 < ntiles;
-            const int s0 = i % kFStages, s1 = (i + 1) % kFStages;
-            if (!mbar_wait(&s_bar[s0], (uint32_t)(i / kFStages) & 1u, p.err)) s_abort = 1;
-            if (two && !mbar_wait(&s_bar[s1], (uint32_t)((i + 1) / kFStages) & 1u, p.err)) s_abort = 1;
-            if (*((volatile int*)&s_abort)) break;
-            if (i == 0) LP_FTRACE(6);
             const int lt0 = i * kFThreads + tid, lt1 = lt0 + kFThreads;
-            const bool v0 = t_begin + lt0 < t_end, v1 = two && t_begin + lt1 < t_end;
+            uint32_t n0[8], n1[8];
+            load_row(lt0 + 2 * kFThreads, n0);
+            load_row(lt1 + 2 * kFThreads, n1);
+            const bool v0 = t_begin + lt0 < t_end, v1 = t_begin + lt1 < t_end;
             if (v1) {
-                const float a0 = score_row(s0, lt0);
-                const float a1 = score_row(s1, lt1);
+                const float a0 = score_regs(c0);
+                const float a1 = score_regs(c1);
                 commit_score(lt0, a0);
                 commit_score(lt1, a1);
             } else if (v0) {
-                commit_score(lt0, score_row(s0, lt0));
+                commit_score(lt0, score_regs(c0));
             }
-            __syncwarp();
-            if (lane == 0) {
-                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_empty[s0])) : "memory");
-                if (two) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_empty[s1])) : "memory");
-            }
-            if (tid == 0) {
-                // refill the slots of the two tiles just consumed
-                for (int pi = i; pi < i + 2; ++pi) {
-                    if (pi + kFStages >= ntiles) continue;
-                    const int ps = pi % kFStages;
-                    if (!mbar_wait(&s_empty[ps], (uint32_t)(pi / kFStages) & 1u, p.err)) {
-                        s_abort = 1;
-                        break;
-                    }
-                    const int j = pi + kFStages;
-                    const int t0 = t_begin + j * kFThreads;
-                    const int nn = min(kFThreads, t_end - t0);
-                    mbar_arrive_expect_tx(&s_bar[ps], (uint32_t)nn * 32u);
-                    bulk_g2s_stream(s_ring + ps * kFTile, src + (int64_t)t0 * 32, (uint32_t)nn * 32u, &s_bar[ps],
-                                    policy);
-                    ++issued;
-                }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c0[j] = n0[j];
+                c1[j] = n1[j];
             }
         }
         if (__syncthreads_or(s_abort)) { drain(0); return; }
