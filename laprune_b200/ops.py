@@ -27,8 +27,53 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream_handle(device: torch.device) -> int:
+    """The current torch stream of ``device`` as a raw handle (the same value
+    as ``torch.cuda.current_stream(device).cuda_stream``, read without
+    creating a Stream object when torch offers that)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
     return torch.cuda.current_stream(device).cuda_stream
+
+
+class _OnDevice:
+    """``torch.cuda.device(dev)`` only when ``dev`` is not current already
+    (entering the guard costs a few microseconds per call)."""
+    __slots__ = ("dev", "guard")
+
+    def __init__(self, dev: torch.device):
+        self.dev = dev
+        self.guard = None
+
+    def __enter__(self):
+        if self.dev.index is not None and self.dev.index != torch.cuda.current_device():
+            self.guard = torch.cuda.device(self.dev)
+            self.guard.__enter__()
+        return self
+
+    def __exit__(self, *exc):
+        if self.guard is not None:
+            self.guard.__exit__(*exc)
+        return False
+
+
+# Filled argument structs of recent sparse_decode calls, keyed by everything
+# but the token counts: a decode loop calls with the same buffers every token,
+# so the validation and the struct filling run once per buffer set.  A hit
+# hands out a copy (callers on several threads never share one), whose
+# T_codes / T_total are then checked and set.
+_args_cache: dict = {}
+_ARGS_CACHE_MAX = 1024
+
+
+def _tensor_key(t: Optional[torch.Tensor]):
+    if t is None:
+        return None
+    return (t.data_ptr(), t.dtype, tuple(t.shape), t.stride(), t.device.index, t.is_cuda)
 
 
 def workspace(nbytes: int, device: torch.device, tag: str = "decode") -> torch.Tensor:
@@ -207,9 +252,30 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
     units = B * Hkv if select == "kv_group" else B * Hq
     tk = torch.empty((units, max(topk, 1)), dtype=torch.int32, device=dev) if return_topk else None
     hs = torch.zeros((B, Hq, T_codes_v), dtype=torch.float32, device=dev) if return_head_scores else None
-    a = build_args(q3, codebooks, codes, keys, vals, topk=topk, T_codes=T_codes, T_total=T_total,
-                   sink=sink, local=local, select=select, scale=scale, out=o, head_scores=hs,
-                   topk_out=tk, prefetch=prefetch)
+    key = (_tensor_key(q3), _tensor_key(codebooks), _tensor_key(codes), _tensor_key(keys), _tensor_key(vals),
+           _tensor_key(o), _tensor_key(tk), _tensor_key(hs), int(topk), int(sink), int(local), select,
+           None if scale is None else float(scale),
+           None if prefetch is None else tuple(tuple(int(x) for x in r) for r in prefetch[:2]))
+    base = _args_cache.get(key)
+    if base is None:
+        a = build_args(q3, codebooks, codes, keys, vals, topk=topk, T_codes=T_codes, T_total=T_total,
+                       sink=sink, local=local, select=select, scale=scale, out=o, head_scores=hs,
+                       topk_out=tk, prefetch=prefetch)
+        if len(_args_cache) >= _ARGS_CACHE_MAX:
+            _args_cache.clear()
+        _args_cache[key] = SparseDecodeArgs.from_buffer_copy(a)
+    else:
+        # the same buffers as an earlier call: only the token counts change
+        a = SparseDecodeArgs.from_buffer_copy(base)
+        cap = codes.shape[-2]
+        T_codes_i = cap if T_codes is None else int(T_codes)
+        # K/V are [B,Hkv,cap,D] or [Hkv,cap,D]: the token axis is the second to last
+        T_total_i = (keys.shape[-2] if keys is not None else T_codes_i) if T_total is None else int(T_total)
+        if not 0 <= T_codes_i <= cap:
+            raise RuntimeError(f"T_codes={T_codes_i} exceeds the code cache capacity {cap}")
+        if keys is not None and (T_total_i > keys.shape[-2] or T_total_i > vals.shape[-2]):
+            raise RuntimeError(f"T_total={T_total_i} exceeds the K/V cache capacity {keys.shape[-2]}")
+        a.T_codes, a.T_total = T_codes_i, T_total_i
     if fused is False:
         a.flags |= _lib.LP_FLAG_NO_FUSED
     if exchange_select:
@@ -221,12 +287,14 @@ def sparse_decode(q: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
         ev_arr = event_array(stage_events)
         a.stage_events = ctypes.cast(ev_arr, ctypes.c_void_p)
     lib = _lib.load()
-    need = lib.lp_sparse_decode_workspace_size(ctypes.byref(a))
-    if need == 0:
-        _lib.check(_lib.LP_ERR_INVALID)
     if ws is None:
+        # a caller-given workspace is checked against the geometry by the
+        # library itself (LP_ERR_WORKSPACE when it is too small)
+        need = lib.lp_sparse_decode_workspace_size(ctypes.byref(a))
+        if need == 0:
+            _lib.check(_lib.LP_ERR_INVALID)
         ws = workspace(need, dev)
-    with torch.cuda.device(dev):
+    with _OnDevice(dev):
         _lib.check(lib.lp_sparse_decode(ctypes.byref(a), ws.data_ptr(), ws.numel(), _stream_handle(dev)))
     if o is not None and squeeze:
         o = o[0]

@@ -196,6 +196,29 @@ def test_repeat_calls_deterministic(mode):
     _check_errors()
 
 
+def test_calls_on_the_same_buffers_follow_the_token_counts():
+    # a decode loop calls sparse_decode on the same caches with growing token
+    # counts: calls that reuse an earlier call's argument struct (same
+    # buffers) must equal calls on fresh copies of the buffers, whatever
+    # T_codes / T_total they pass, for [Hkv,T,.] and [B,Hkv,T,.] tensors
+    C, codes, K, V, q = _rand_case(13, 1, 8, 4, 12000)
+    dev = _dev()
+    q, C, codes, K, V = (t.to(dev) for t in (q, C, codes, K, V))
+    for T_codes, T_total in ((9000, 9100), (11936, 12000), (9000, 9100)):
+        for dims in (4, 3):
+            cd, kk, vv, qq = (codes, K, V, q) if dims == 4 else (codes[0], K[0], V[0], q[0])
+            same = ops.sparse_decode(qq, C, cd, kk, vv, topk=300, T_codes=T_codes, T_total=T_total, sink=4,
+                                     local=64, return_topk=True)
+            fresh = ops.sparse_decode(qq.clone(), C.clone(), cd.clone(), kk.clone(), vv.clone(), topk=300,
+                                      T_codes=T_codes, T_total=T_total, sink=4, local=64, return_topk=True)
+            torch.cuda.synchronize()
+            assert torch.equal(same.topk, fresh.topk)
+            assert torch.equal(same.out, fresh.out)
+    with pytest.raises(RuntimeError, match="T_total"):
+        ops.sparse_decode(q, C, codes, K, V, topk=300, T_codes=9000, T_total=12001, sink=4, local=64)
+    _check_errors()
+
+
 def test_candidate_union_and_tie_exchange_select_the_same_set():
     # both fused selection paths are exact: identical index sets, and the
     # attention outputs agree to accumulation-order rounding
