@@ -451,20 +451,23 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         const int code = total > 1 ? (int)(s_best[row] & 0xffu)
                                    : max(max(max(s_bk[0][row], s_bk[1][row]), max(s_bk[2][row], s_bk[3][row])), 0);
         if (cg == 0) s_codes[row][m] = (uint8_t)code;
-        // r -= C_m[code]: the row's 4 column groups take 32 dims each
+        // r - C_m[code] into registers (the row's 4 column groups take 32
+        // dims each): the subtractions consume the codeword loads before the
+        // barrier, after which the next stage's copies overwrite the
+        // codewords; the stores follow the copies' issue
+        float4 nr[8];
         {
             const unsigned char* bh = sB + (code >> 7) * EncSmem::kBHalf;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int d = (8 * cg + j) * 4;
                 const float4 cv = *reinterpret_cast<const float4*>(bh + enc_off(code & 127, d));
-                float4* r4p = reinterpret_cast<float4*>(sA + enc_off(row, d));
-                float4 r4 = *r4p;
-                r4.x = __fsub_rn(r4.x, cv.x);
-                r4.y = __fsub_rn(r4.y, cv.y);
-                r4.z = __fsub_rn(r4.z, cv.z);
-                r4.w = __fsub_rn(r4.w, cv.w);
-                *r4p = r4;
+                const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(row, d));
+                nr[j] = make_float4(__fsub_rn(r4.x, cv.x), __fsub_rn(r4.y, cv.y), __fsub_rn(r4.z, cv.z),
+                                    __fsub_rn(r4.w, cv.w));
+                // the differences exist before the barrier (the compiler may
+                // not sink them, and with them the wait for the loads, past it)
+                asm volatile("" : "+f"(nr[j].x), "+f"(nr[j].y), "+f"(nr[j].z), "+f"(nr[j].w));
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -473,6 +476,9 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             if (tid == 0) issue_stage(m + 1);
             load_norms(m + 1);
         }
+        // (visible to the next stage's MMA after the barrier that starts it)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(sA + enc_off(row, (8 * cg + j) * 4)) = nr[j];
     }
     cp_async_wait<0>();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
