@@ -61,7 +61,8 @@ constexpr int kFPre0 = 2;                        // ring slots kept free ahead o
 constexpr int kFTile = kFThreads * 32;           // 16 KB of code rows per stage
 constexpr int kFScoreCap = 11264;                // tokens per CTA kept in smem
 constexpr int kFMaxWords = 8192;                 // bitmap words per unit in smem overlay
-constexpr int kFMaxRows = 192;                   // kept rows per attention chunk in phase E
+constexpr int kFMaxRows = 192;                   // K/V staging rows in the ring (phase C's early rows)
+constexpr int kFLutRows = 128;                   // more staging rows in the table region (phase E only)
 constexpr int kPubWin = 128;                     // bins in a CTA's published count window
 constexpr int kPubMaxCtas = 64;                  // CTAs per unit of the published-candidate path
 constexpr int kPubMaxCap = 2048;                 // published candidates per CTA (own copy in shared memory)
@@ -921,6 +922,14 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
     int* s_list = reinterpret_cast<int*>(s_scores);  // [<= kFScoreCap | kFSpillList] (scores consumed by then)
     KT* s_k = reinterpret_cast<KT*>(s_ring);         // [R][128] (the ring is free after phase B)
     KT* s_v = s_k + R * D;                           // [R][128]
+    // phase E's chunks take RE rows: rows R.. sit in the table region, which
+    // is free from the start of phase E until the warps' states are combined
+    constexpr int RE = R + kFLutRows;
+    static_assert(2 * kFLutRows * 128 * sizeof(KT) <= FusedSmem::kLut, "staging rows fit the table region");
+    KT* s_k2 = reinterpret_cast<KT*>(s_lut);         // [kFLutRows][128]
+    KT* s_v2 = s_k2 + kFLutRows * D;                 // [kFLutRows][128]
+    auto stg_k = [&](int r) { return r < R ? s_k + r * D : s_k2 + (r - R) * D; };
+    auto stg_v = [&](int r) { return r < R ? s_v + r * D : s_v2 + (r - R) * D; };
     const KT* kb = reinterpret_cast<const KT*>(p.keys) + (int64_t)b * p.k_stride_b + (int64_t)hkv * p.k_stride_h;
     const KT* vb = reinterpret_cast<const KT*>(p.vals) + (int64_t)b * p.v_stride_b + (int64_t)hkv * p.v_stride_h;
     constexpr int CH = D * (int)sizeof(KT) / 16;
@@ -948,8 +957,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             const int r = c / CH, part = c - r * CH;
             const int64_t t = min(max(row_token(c0r + r, nabove), 0), p.T_total - 1);
             const int sw = (part ^ (r & 7)) * EPC;
-            cp_async16(s_k + r * D + sw, kb + t * p.k_stride_t + part * EPC);
-            cp_async16(s_v + r * D + sw, vb + t * p.v_stride_t + part * EPC);
+            cp_async16(stg_k(r) + sw, kb + t * p.k_stride_t + part * EPC);
+            cp_async16(stg_v(r) + sw, vb + t * p.v_stride_t + part * EPC);
         }
         cp_async_commit();
     };
@@ -1562,7 +1571,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 // rows past r_hi read row r_lo instead (finite data, masked below)
                 int krow = r0 + (mi & 1) * 8 + rr;
                 if (krow >= r_hi) krow = r_lo;
-                const uint32_t kbase = smem_u32(s_k + krow * D);
+                const uint32_t kbase = smem_u32(stg_k(krow));
                 float sv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
@@ -1610,7 +1619,7 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 pb[1] = __byte_perm(xa23, xb23, selp);
                 int vrow = r0 + (mi >> 1) * 8 + rr;
                 if (vrow >= r_hi) vrow = r_lo;
-                const uint32_t vbase = smem_u32(s_v + vrow * D);
+                const uint32_t vbase = smem_u32(stg_v(vrow));
 #pragma unroll
                 for (int mb = 0; mb < 8; ++mb) {
                     uint32_t af[4];
@@ -1619,8 +1628,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
                 }
             }
         };
-        for (int c0r = 0; c0r < nrows; c0r += R) {
-            const int nr = min(R, nrows - c0r);
+        for (int c0r = 0; c0r < nrows; c0r += RE) {
+            const int nr = min(RE, nrows - c0r);
             int r_ready = 0;
             if (c0r == 0 && n_issued > 0) {
                 // the chunk's first n_issued rows were issued in phase C; the
@@ -1649,8 +1658,8 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             float* s_cm = s_wf + NW * 8;                       // [8] slice max
             float* s_cl = s_cm + 8;                            // [8] slice sum
             // warps past nwu never had a tile (16 rows per tile, at most
-            // min(nrows, R) rows per chunk): they hold no state
-            const int nwu = min(NW, (min(nrows, R) + 15) / 16);
+            // min(nrows, RE) rows per chunk): they hold no state
+            const int nwu = min(NW, (min(nrows, RE) + 15) / 16);
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int h = 2 * tq + e;
