@@ -22,12 +22,12 @@
 // that set has one member it is the code, otherwise its members are
 // recomputed exactly on CUDA cores.
 //
-// Shared memory holds the residuals (A operand, 64 KB) and the stage's
-// codewords in two halves of 128 (B operands, 64 KB each), both in the UMMA
-// K-major SWIZZLE_128B layout: per 32-dim K chunk (16 KB), 8-row atoms of
-// 1024 B, rows 128 B apart, 16-byte units XOR-swizzled with the row.  The
-// codewords arrive by 2-D TMA tensor copies (box 32 dims x 128 rows, the
-// same swizzle).  The exact recomputation and the residual update read the
+// Shared memory holds the residuals (A operand, 64 KB) and the stage's 256
+// codewords (B operand, 128 KB, one N = 256 MMA per K step), both in the
+// UMMA K-major SWIZZLE_128B layout: per 32-dim K chunk (16 KB of residual
+// rows, 32 KB of codeword rows), 8-row atoms of 1024 B, rows 128 B apart,
+// 16-byte units XOR-swizzled with the row.  The codewords arrive by 2-D TMA
+// tensor copies (box 32 dims x 128 rows, the same swizzle).  The exact recomputation and the residual update read the
 // codeword rows from there, so the next stage's copies start once the
 // residual update is done.  Rows with several candidates put their (row,
 // codeword) pairs on a CTA-wide list, one pair per thread, so that the
@@ -78,6 +78,14 @@ __device__ __forceinline__ uint32_t enc_off(int n, int d) {
     return (uint32_t)(((d >> 5) << 14) + ((n >> 3) << 10) + ((n & 7) << 7) + (u << 4) + (b & 15));
 }
 
+// byte offset of (codeword k < 256, dim d) of the stage's [256][128] fp32
+// codewords: the same layout with K chunks of 256 rows at 32 KB steps
+__device__ __forceinline__ uint32_t enc_off_cb(int k, int d) {
+    const int b = (d & 31) << 2;
+    const int u = (b >> 4) ^ (k & 7);
+    return (uint32_t)(((d >> 5) << 15) + ((k >> 3) << 10) + ((k & 7) << 7) + (u << 4) + (b & 15));
+}
+
 // UMMA shared-memory descriptor: K-major SWIZZLE_128B, SBO 1024 B (8-row
 // atoms), LBO unused (1); the start address may step inside an atom by the
 // 32 bytes of one K step (the swizzle works on absolute address bits)
@@ -98,49 +106,21 @@ __device__ __forceinline__ void enc_tma_2d(void* dst, const CUtensorMap* map, in
         : "memory");
 }
 
-// instruction descriptors: D fp32, A/B tf32, both K-major, M = 128 and
-// N = 128 (128 residual rows x 128 codewords of a half) or N = 32 (128
-// codewords of a half x 32 residual rows: CTAs of 32 vectors)
-constexpr uint32_t kEncIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
-constexpr uint32_t kEncIdescT = (1u << 4) | (2u << 7) | (2u << 10) | ((32u >> 3) << 17) | ((128u >> 4) << 24);
+// instruction descriptor: D fp32, A/B tf32, both K-major, N = 256, M = 128
+constexpr uint32_t kEncIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((256u >> 3) << 17) | ((128u >> 4) << 24);
 
-__device__ __forceinline__ void enc_mma(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t accum,
-                                        uint32_t idesc = kEncIdesc) {
+__device__ __forceinline__ void enc_mma(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t accum) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtmem),
-        "l"(da), "l"(db), "r"(idesc), "r"(accum)
+        "l"(da), "l"(db), "r"(kEncIdesc), "r"(accum)
         : "memory");
 }
 
 __device__ __forceinline__ void enc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
-}
-
-// 16 fp32 columns of this thread's TMEM lane
-__device__ __forceinline__ void enc_tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// float order as unsigned order (+0 and -0 apart; NaN-free inputs)
-__device__ __forceinline__ uint32_t enc_okey(float x) {
-    const uint32_t b = __float_as_uint(x);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-__device__ __forceinline__ float enc_okey_inv(uint32_t k) {
-    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
 // 64 fp32 columns of this thread's TMEM lane
@@ -206,11 +186,7 @@ __global__ void __launch_bounds__(256) encode_norms_kernel(const float* cb, int6
     cnorm[i] = __fmul_ru(__fsqrt_ru(acc), 1.0000001f);
 }
 
-// TR: CTAs of 32 vectors put the codewords on the MMA's M side (128 per
-// half) and the 32 residual rows on its N side -- a quarter of the tensor
-// work of the 128-row tile, 16 accumulator columns per thread -- with the
-// same filter, bound and exact recomputation.
-template <typename XT, bool TR>
+template <typename XT>
 __global__ void __launch_bounds__(kEncThreads, 1)
     encode_keys_kernel(const __grid_constant__ CUtensorMap cmap, EncodeParams p) {
     extern __shared__ unsigned char smem_raw[];
@@ -255,7 +231,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) enc_tma_2d(sB + hf * EncSmem::kBHalf + c * 16384, &cmap, 32 * c, row0 + 128 * hf, s_tbar);
+            for (int c = 0; c < 4; ++c) enc_tma_2d(sB + c * 32768 + hf * 16384, &cmap, 32 * c, row0 + 128 * hf, s_tbar);
     };
     // stage m's norms (cp.async, one group per thread)
     auto load_norms = [&](int m) {
@@ -323,14 +299,6 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     __shared__ float s_u[4][kEncRows];
     __shared__ int s_cnt[4][kEncRows];
     __shared__ int s_bk[4][kEncRows];               // the group's first candidate (-1: none)
-    // TR: per row the ordered key of the smallest approximation, the bound,
-    // the candidate count and a candidate (reset at the start of each stage)
-    __shared__ uint32_t s_umin[TR ? kEncRows : 1];
-    __shared__ float s_bnd[TR ? kEncRows : 1];
-    __shared__ int s_cnt1[TR ? kEncRows : 1];
-    __shared__ int s_bk1[TR ? kEncRows : 1];
-    // TR: this thread's codeword (TMEM lane) and its 16 rows (columns)
-    const int j0t = 16 * (cg & 1), kkt = 128 * (cg >> 1) + 32 * q4 + lane;
     __shared__ unsigned long long s_best[kEncRows];  // (ordered exact distance, codeword), minimum
     __shared__ uint32_t s_list[kEncListCap];         // (row << 8) | codeword
     __shared__ int s_nlist[2];
@@ -348,18 +316,14 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         }
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a0 = smem_u32(sA);
+            const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+            // K step s: 32 bytes into K chunk s / 4 (16 KB of residual rows,
+            // 32 KB of codeword rows); all 256 codewords in one N = 256 MMA
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                const uint32_t b0 = smem_u32(sB + hf * EncSmem::kBHalf);
-#pragma unroll
-                for (int s = 0; s < kEncD / 8; ++s) {
-                    const uint32_t ko = (uint32_t)((s >> 2) * 16384 + (s & 3) * 32);
-                    if constexpr (TR)
-                        enc_mma(tmem + hf * 32, enc_desc(b0 + ko), enc_desc(a0 + ko), s > 0 ? 1u : 0u, kEncIdescT);
-                    else
-                        enc_mma(tmem + hf * 128, enc_desc(a0 + ko), enc_desc(b0 + ko), s > 0 ? 1u : 0u);
-                }
+            for (int s = 0; s < kEncD / 8; ++s) {
+                const uint32_t koa = (uint32_t)((s >> 2) * 16384 + (s & 3) * 32);
+                const uint32_t kob = (uint32_t)((s >> 2) * 32768 + (s & 3) * 32);
+                enc_mma(tmem, enc_desc(a0 + koa), enc_desc(b0 + kob), s > 0 ? 1u : 0u);
             }
             enc_commit(s_mbar);
         }
@@ -375,11 +339,6 @@ __global__ void __launch_bounds__(kEncThreads, 1)
                 rn = __fmaf_rn(r4.w, r4.w, rn);
             }
             s_rn[row] = rn;
-            if constexpr (TR) {
-                s_umin[row] = ~0u;
-                s_cnt1[row] = 0;
-                s_bk1[row] = -1;
-            }
         }
         const bool done = mbar_wait(s_mbar, par, p.err);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -396,91 +355,44 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         const float slack = kAbs * (rn + 2.f * (nb[kEncK] + rnorm * nb[kEncK + 1]));
         // the row's bound for every codeword of the stage: kEps ||r|| max ||c|| + slack
         const float bnd = __fmaf_ru(kEps * rnorm, nb[kEncK + 1], slack);
-        int total;
-        uint64_t pend;
-        if constexpr (!TR) {
-            const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + 64 * cg;
-            float v[64];
-            enc_tmem_ld64(taddr, v);
-            // pass 1: the row's smallest approximate distance A (less ||r||^2)
-            float u = INFINITY;
-    #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                const float ap = fmaf(-2.f, v[i], nb[64 * cg + i]);
-                v[i] = ap;
-                u = fminf(u, ap);
-            }
-            s_u[cg][row] = u;
-            __syncthreads();
-            // pass 2: candidates approx_k <= A + 2 bnd -- the winner's exact
-            // distance is at most A + bnd and its approximation at most bnd below
-            // that (bit i of the mask = column 64cg + i)
-            const float thr = __fmaf_ru(2.f, bnd, fminf(fminf(s_u[0][row], s_u[1][row]), fminf(s_u[2][row], s_u[3][row])));
-            uint32_t cm0 = 0u, cm1 = 0u;
-    #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                const bool c = p.force_exact || v[i] <= thr;
-                if (i < 32) cm0 |= (uint32_t)c << i;
-                else cm1 |= (uint32_t)c << (i - 32);
-            }
-            s_cnt[cg][row] = __popc(cm0) + __popc(cm1);
-            s_bk[cg][row] = cm0 ? __ffs(cm0) - 1 + 64 * cg : (cm1 ? __ffs(cm1) + 31 + 64 * cg : -1);
-            if (cg == 0) s_best[row] = ~0ull;
-            if (tid == 0) {
-                s_nlist[0] = 0;
-                s_nlist[1] = 0;
-            }
-            __syncthreads();
-            total = s_cnt[0][row] + s_cnt[1][row] + s_cnt[2][row] + s_cnt[3][row];
-            // a row with several candidates: their exact distances, one (row,
-            // codeword) pair per 8 lanes through a CTA-wide list (rounds of at most
-            // kEncListCap pairs); the smallest (distance, codeword) key is the
-            // first minimum of the CPU scan
-            pend = total > 1 ? ((uint64_t)cm1 << 32) | cm0 : 0ull;
-        } else {
-            // codeword kkt (TMEM lane) against rows j0t .. j0t + 15 (columns)
-            if (cg == 0) s_bnd[row] = bnd;
-            float v[16];
-            enc_tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + 16 * cg, v);
-            const float nk = nb[kkt];
-            // pass 1: per row the smallest approximate distance A (less
-            // ||r||^2): over the warp's 32 codewords, then over the 8 warps
-            // that hold the row (ordered keys)
+        const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + 64 * cg;
+        float v[64];
+        enc_tmem_ld64(taddr, v);
+        // pass 1: the row's smallest approximate distance A (less ||r||^2)
+        float u = INFINITY;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const float ap = fmaf(-2.f, v[j], nk);
-                v[j] = ap;
-                const uint32_t mk = __reduce_min_sync(0xffffffffu, enc_okey(ap));
-                if (lane == j) atomicMin(&s_umin[j0t + j], mk);
-            }
-            __syncthreads();
-            // pass 2: candidates approx_k <= A + 2 bnd of their row (bit j of
-            // cm = row j0t + j); per row the count and one candidate
-            uint32_t cm = 0u;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const float thr = __fmaf_ru(2.f, s_bnd[j0t + j], enc_okey_inv(s_umin[j0t + j]));
-                const bool c = p.force_exact || v[j] <= thr;
-                cm |= (uint32_t)c << j;
-                const uint32_t bal = __ballot_sync(0xffffffffu, c);
-                if (lane == j && bal) {
-                    atomicAdd(&s_cnt1[j0t + j], __popc(bal));
-                    s_bk1[j0t + j] = 128 * (cg >> 1) + 32 * q4 + __ffs(bal) - 1;
-                }
-            }
-            if (cg == 0) s_best[row] = ~0ull;
-            if (tid == 0) {
-                s_nlist[0] = 0;
-                s_nlist[1] = 0;
-            }
-            __syncthreads();
-            total = s_cnt1[row];
-            uint32_t pm = 0u;
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (((cm >> j) & 1u) && s_cnt1[j0t + j] > 1) pm |= 1u << j;
-            pend = pm;
+        for (int i = 0; i < 64; ++i) {
+            const float ap = fmaf(-2.f, v[i], nb[64 * cg + i]);
+            v[i] = ap;
+            u = fminf(u, ap);
         }
+        s_u[cg][row] = u;
+        __syncthreads();
+        // pass 2: candidates approx_k <= A + 2 bnd -- the winner's exact
+        // distance is at most A + bnd and its approximation at most bnd below
+        // that (bit i of the mask = column 64cg + i)
+        const float thr = __fmaf_ru(2.f, bnd, fminf(fminf(s_u[0][row], s_u[1][row]), fminf(s_u[2][row], s_u[3][row])));
+        uint32_t cm0 = 0u, cm1 = 0u;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            const bool c = p.force_exact || v[i] <= thr;
+            if (i < 32) cm0 |= (uint32_t)c << i;
+            else cm1 |= (uint32_t)c << (i - 32);
+        }
+        s_cnt[cg][row] = __popc(cm0) + __popc(cm1);
+        s_bk[cg][row] = cm0 ? __ffs(cm0) - 1 + 64 * cg : (cm1 ? __ffs(cm1) + 31 + 64 * cg : -1);
+        if (cg == 0) s_best[row] = ~0ull;
+        if (tid == 0) {
+            s_nlist[0] = 0;
+            s_nlist[1] = 0;
+        }
+        __syncthreads();
+        const int total = s_cnt[0][row] + s_cnt[1][row] + s_cnt[2][row] + s_cnt[3][row];
+        // a row with several candidates: their exact distances, one (row,
+        // codeword) pair per 8 lanes through a CTA-wide list (rounds of at most
+        // kEncListCap pairs); the smallest (distance, codeword) key is the
+        // first minimum of the CPU scan
+        uint64_t pend = total > 1 ? ((uint64_t)cm1 << 32) | cm0 : 0ull;
         for (int round = 0;; ++round) {
             int* nl = &s_nlist[round & 1];
             const bool had = pend != 0ull;
@@ -496,9 +408,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             if (lane == 31 && incl > 0) base = atomicAdd(nl, incl);
             base = __shfl_sync(0xffffffffu, base, 31);
             for (int i = base + incl - mine; pend && i < kEncListCap; ++i) {
-                const int bit = __ffsll((long long)pend) - 1;
-                s_list[i] = TR ? ((uint32_t)(j0t + bit) << 8) | (uint32_t)kkt
-                               : ((uint32_t)row << 8) | (uint32_t)(bit + 64 * cg);
+                s_list[i] = ((uint32_t)row << 8) | (uint32_t)(__ffsll((long long)pend) - 1 + 64 * cg);
                 pend &= pend - 1;
             }
             if (!__syncthreads_or(had)) break;
@@ -519,12 +429,11 @@ __global__ void __launch_bounds__(kEncThreads, 1)
                     const uint32_t it = s_list[e];
                     r = (int)(it >> 8);
                     k = (int)(it & 255u);
-                    const unsigned char* bh = sB + (k >> 7) * EncSmem::kBHalf;
                     float pj[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(r, 32 * j + 4 * l8));
-                        const float4 cv = *reinterpret_cast<const float4*>(bh + enc_off(k & 127, 32 * j + 4 * l8));
+                        const float4 cv = *reinterpret_cast<const float4*>(sB + enc_off_cb(k, 32 * j + 4 * l8));
                         float a = __fmaf_rn(r4.x, cv.x, 0.f);
                         a = __fmaf_rn(r4.y, cv.y, a);
                         a = __fmaf_rn(r4.z, cv.z, a);
@@ -546,7 +455,6 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         }
         // the code: the refined minimum, else the one candidate (one group has it)
         const int code = total > 1 ? (int)(s_best[row] & 0xffu)
-                         : TR      ? max(s_bk1[row], 0)
                                    : max(max(max(s_bk[0][row], s_bk[1][row]), max(s_bk[2][row], s_bk[3][row])), 0);
         if (cg == 0) s_codes[row][m] = (uint8_t)code;
         // r - C_m[code] into registers (the row's 4 column groups take 32
@@ -555,11 +463,10 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         // codewords; the stores follow the copies' issue
         float4 nr[8];
         {
-            const unsigned char* bh = sB + (code >> 7) * EncSmem::kBHalf;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int d = (8 * cg + j) * 4;
-                const float4 cv = *reinterpret_cast<const float4*>(bh + enc_off(code & 127, d));
+                const float4 cv = *reinterpret_cast<const float4*>(sB + enc_off_cb(code, d));
                 const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(row, d));
                 nr[j] = make_float4(__fsub_rn(r4.x, cv.x), __fsub_rn(r4.y, cv.y), __fsub_rn(r4.z, cv.z),
                                     __fsub_rn(r4.w, cv.w));
