@@ -186,7 +186,9 @@ __global__ void __launch_bounds__(256) encode_norms_kernel(const float* cb, int6
     cnorm[i] = __fmul_ru(__fsqrt_ru(acc), 1.0000001f);
 }
 
-template <typename XT>
+// PART: CTAs of fewer than 128 vectors (the warps past them skip the
+// per-row steps); the full-tile instantiation has no such branches.
+template <typename XT, bool PART>
 __global__ void __launch_bounds__(kEncThreads, 1)
     encode_keys_kernel(const __grid_constant__ CUtensorMap cmap, EncodeParams p) {
     extern __shared__ unsigned char smem_raw[];
@@ -275,6 +277,10 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     // epilogue: warp w reads TMEM lane quarter q = w & 3 (vector rows
     // 32q .. 32q+31) and the 64 columns of group cg = w >> 2
     const int q4 = warp & 3, cg = warp >> 2;
+    // warps whose 32 rows all lie past the CTA's vectors (CTAs of 32 or 64)
+    // skip the per-row steps; they still take part in every barrier and in
+    // the CTA-wide exact recomputation
+    const bool live_w = !PART || q4 * 32 < p.rows_per_cta;
     const int row = q4 * 32 + lane;
     const bool row_valid = row < p.rows_per_cta && v0 + row < nvec_set;
     __shared__ uint8_t* s_cptr[kEncRows];         // the row's 32 codes in the output (null: no vector)
@@ -328,7 +334,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             enc_commit(s_mbar);
         }
         // meanwhile: ||r||^2 of each row, exactly (sequential fma in d order)
-        if (cg == 0) {
+        if (cg == 0 && live_w) {
             float rn = 0.f;
 #pragma unroll 4
             for (int d4 = 0; d4 < kEncD / 4; ++d4) {
@@ -348,46 +354,52 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             break;
         }
         const float* nb = sNorm + (m & 1) * EncSmem::kNormStride;
-        const float rn = s_rn[row];
-        const float rnorm = __fmul_ru(__fsqrt_ru(rn), 1.0000001f);
-        // the bound's absolute part, one upper bound per row: |approx| <=
-        // ||c||^2 + 2 ||r|| ||c|| <= nmax + 2 rnorm cmax
-        const float slack = kAbs * (rn + 2.f * (nb[kEncK] + rnorm * nb[kEncK + 1]));
-        // the row's bound for every codeword of the stage: kEps ||r|| max ||c|| + slack
-        const float bnd = __fmaf_ru(kEps * rnorm, nb[kEncK + 1], slack);
-        const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + 64 * cg;
         float v[64];
-        enc_tmem_ld64(taddr, v);
-        // pass 1: the row's smallest approximate distance A (less ||r||^2)
-        float u = INFINITY;
+        float bnd = 0.f;
+        if (live_w) {
+            const float rn = s_rn[row];
+            const float rnorm = __fmul_ru(__fsqrt_ru(rn), 1.0000001f);
+            // the bound's absolute part, one upper bound per row: |approx| <=
+            // ||c||^2 + 2 ||r|| ||c|| <= nmax + 2 rnorm cmax
+            const float slack = kAbs * (rn + 2.f * (nb[kEncK] + rnorm * nb[kEncK + 1]));
+            // the row's bound for every codeword of the stage: kEps ||r|| max ||c|| + slack
+            bnd = __fmaf_ru(kEps * rnorm, nb[kEncK + 1], slack);
+            const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + 64 * cg;
+            enc_tmem_ld64(taddr, v);
+            // pass 1: the row's smallest approximate distance A (less ||r||^2)
+            float u = INFINITY;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-            const float ap = fmaf(-2.f, v[i], nb[64 * cg + i]);
-            v[i] = ap;
-            u = fminf(u, ap);
+            for (int i = 0; i < 64; ++i) {
+                const float ap = fmaf(-2.f, v[i], nb[64 * cg + i]);
+                v[i] = ap;
+                u = fminf(u, ap);
+            }
+            s_u[cg][row] = u;
         }
-        s_u[cg][row] = u;
         __syncthreads();
-        // pass 2: candidates approx_k <= A + 2 bnd -- the winner's exact
-        // distance is at most A + bnd and its approximation at most bnd below
-        // that (bit i of the mask = column 64cg + i)
-        const float thr = __fmaf_ru(2.f, bnd, fminf(fminf(s_u[0][row], s_u[1][row]), fminf(s_u[2][row], s_u[3][row])));
         uint32_t cm0 = 0u, cm1 = 0u;
+        if (live_w) {
+            // pass 2: candidates approx_k <= A + 2 bnd -- the winner's exact
+            // distance is at most A + bnd and its approximation at most bnd
+            // below that (bit i of the mask = column 64cg + i)
+            const float thr =
+                __fmaf_ru(2.f, bnd, fminf(fminf(s_u[0][row], s_u[1][row]), fminf(s_u[2][row], s_u[3][row])));
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-            const bool c = p.force_exact || v[i] <= thr;
-            if (i < 32) cm0 |= (uint32_t)c << i;
-            else cm1 |= (uint32_t)c << (i - 32);
+            for (int i = 0; i < 64; ++i) {
+                const bool c = p.force_exact || v[i] <= thr;
+                if (i < 32) cm0 |= (uint32_t)c << i;
+                else cm1 |= (uint32_t)c << (i - 32);
+            }
+            s_cnt[cg][row] = __popc(cm0) + __popc(cm1);
+            s_bk[cg][row] = cm0 ? __ffs(cm0) - 1 + 64 * cg : (cm1 ? __ffs(cm1) + 31 + 64 * cg : -1);
+            if (cg == 0) s_best[row] = ~0ull;
         }
-        s_cnt[cg][row] = __popc(cm0) + __popc(cm1);
-        s_bk[cg][row] = cm0 ? __ffs(cm0) - 1 + 64 * cg : (cm1 ? __ffs(cm1) + 31 + 64 * cg : -1);
-        if (cg == 0) s_best[row] = ~0ull;
         if (tid == 0) {
             s_nlist[0] = 0;
             s_nlist[1] = 0;
         }
         __syncthreads();
-        const int total = s_cnt[0][row] + s_cnt[1][row] + s_cnt[2][row] + s_cnt[3][row];
+        const int total = live_w ? s_cnt[0][row] + s_cnt[1][row] + s_cnt[2][row] + s_cnt[3][row] : 0;
         // a row with several candidates: their exact distances, one (row,
         // codeword) pair per 8 lanes through a CTA-wide list (rounds of at most
         // kEncListCap pairs); the smallest (distance, codeword) key is the
@@ -453,26 +465,28 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             }
             if (!__syncthreads_or(pend != 0ull)) break;
         }
-        // the code: the refined minimum, else the one candidate (one group has it)
-        const int code = total > 1 ? (int)(s_best[row] & 0xffu)
-                                   : max(max(max(s_bk[0][row], s_bk[1][row]), max(s_bk[2][row], s_bk[3][row])), 0);
-        if (cg == 0) s_codes[row][m] = (uint8_t)code;
-        // r - C_m[code] into registers (the row's 4 column groups take 32
-        // dims each): the subtractions consume the codeword loads before the
-        // barrier, after which the next stage's copies overwrite the
-        // codewords; the stores follow the copies' issue
         float4 nr[8];
-        {
+        if (live_w) {
+            // the code: the refined minimum, else the one candidate (one group has it)
+            const int code = total > 1 ? (int)(s_best[row] & 0xffu)
+                                       : max(max(max(s_bk[0][row], s_bk[1][row]), max(s_bk[2][row], s_bk[3][row])), 0);
+            if (cg == 0) s_codes[row][m] = (uint8_t)code;
+            // r - C_m[code] into registers (the row's 4 column groups take 32
+            // dims each): the subtractions consume the codeword loads before the
+            // barrier, after which the next stage's copies overwrite the
+            // codewords; the stores follow the copies' issue
+            {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int d = (8 * cg + j) * 4;
-                const float4 cv = *reinterpret_cast<const float4*>(sB + enc_off_cb(code, d));
-                const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(row, d));
-                nr[j] = make_float4(__fsub_rn(r4.x, cv.x), __fsub_rn(r4.y, cv.y), __fsub_rn(r4.z, cv.z),
-                                    __fsub_rn(r4.w, cv.w));
-                // the differences exist before the barrier (the compiler may
-                // not sink them, and with them the wait for the loads, past it)
-                asm volatile("" : "+f"(nr[j].x), "+f"(nr[j].y), "+f"(nr[j].z), "+f"(nr[j].w));
+                for (int j = 0; j < 8; ++j) {
+                    const int d = (8 * cg + j) * 4;
+                    const float4 cv = *reinterpret_cast<const float4*>(sB + enc_off_cb(code, d));
+                    const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(row, d));
+                    nr[j] = make_float4(__fsub_rn(r4.x, cv.x), __fsub_rn(r4.y, cv.y), __fsub_rn(r4.z, cv.z),
+                                        __fsub_rn(r4.w, cv.w));
+                    // the differences exist before the barrier (the compiler may
+                    // not sink them, and with them the wait for the loads, past it)
+                    asm volatile("" : "+f"(nr[j].x), "+f"(nr[j].y), "+f"(nr[j].z), "+f"(nr[j].w));
+                }
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -482,8 +496,10 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             load_norms(m + 1);
         }
         // (visible to the next stage's MMA after the barrier that starts it)
+        if (live_w) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(sA + enc_off(row, (8 * cg + j) * 4)) = nr[j];
+            for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(sA + enc_off(row, (8 * cg + j) * 4)) = nr[j];
+        }
     }
     cp_async_wait<0>();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

@@ -777,24 +777,30 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
         if (cr != CUDA_SUCCESS) return fail(LP_ERR_CUDA, "cuTensorMapEncodeTiled failed for the codebooks");
     }
     const dim3 grid((unsigned)(nsets * ep.ctas_per_set));
-    static bool opt_enc[3][64] = {{false}};
+    static bool opt_enc[6][64] = {{false}};
+    auto launch_enc = [&](auto kern, int slot) {
+        const int r = smem_opt_in(kern, EncSmem::kTotal, dev, opt_enc[slot]);
+        if (r != LP_OK) return r;
+        kern<<<grid, kEncThreads, EncSmem::kTotal, st>>>(cmap, ep);
+        return (int)LP_OK;
+    };
+    // CTAs of fewer than 128 vectors: the instantiation whose idle warps skip
+    // the per-row steps
+    const bool part = rows < kEncRows;
     switch (a->x_dtype) {
         case LP_BF16:
-            rc = smem_opt_in(encode_keys_kernel<__nv_bfloat16>, EncSmem::kTotal, dev, opt_enc[0]);
-            if (rc != LP_OK) return rc;
-            encode_keys_kernel<__nv_bfloat16><<<grid, kEncThreads, EncSmem::kTotal, st>>>(cmap, ep);
+            rc = part ? launch_enc(encode_keys_kernel<__nv_bfloat16, true>, 3)
+                      : launch_enc(encode_keys_kernel<__nv_bfloat16, false>, 0);
             break;
         case LP_F16:
-            rc = smem_opt_in(encode_keys_kernel<__half>, EncSmem::kTotal, dev, opt_enc[1]);
-            if (rc != LP_OK) return rc;
-            encode_keys_kernel<__half><<<grid, kEncThreads, EncSmem::kTotal, st>>>(cmap, ep);
+            rc = part ? launch_enc(encode_keys_kernel<__half, true>, 4)
+                      : launch_enc(encode_keys_kernel<__half, false>, 1);
             break;
         default:
-            rc = smem_opt_in(encode_keys_kernel<float>, EncSmem::kTotal, dev, opt_enc[2]);
-            if (rc != LP_OK) return rc;
-            encode_keys_kernel<float><<<grid, kEncThreads, EncSmem::kTotal, st>>>(cmap, ep);
+            rc = part ? launch_enc(encode_keys_kernel<float, true>, 5) : launch_enc(encode_keys_kernel<float, false>, 2);
             break;
     }
+    if (rc != LP_OK) return rc;
     rc = check_launch("encode_keys_kernel");
     if (rc != LP_OK || a->icm_iters == 0) return rc;
 
