@@ -123,6 +123,30 @@ __device__ __forceinline__ void enc_commit(uint64_t* bar) {
                  : "memory");
 }
 
+// 16 fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void enc_tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// float order as unsigned order (NaN-free inputs)
+__device__ __forceinline__ uint32_t enc_okey(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float enc_okey_inv(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 // 64 fp32 columns of this thread's TMEM lane
 __device__ __forceinline__ void enc_tmem_ld64(uint32_t taddr, float* v) {
     uint32_t r[64];
@@ -186,9 +210,13 @@ __global__ void __launch_bounds__(256) encode_norms_kernel(const float* cb, int6
     cnorm[i] = __fmul_ru(__fsqrt_ru(acc), 1.0000001f);
 }
 
-// PART: CTAs of fewer than 128 vectors (the warps past them skip the
-// per-row steps); the full-tile instantiation has no such branches.
-template <typename XT, bool PART>
+// REP = 128 / vectors per CTA.  CTAs of 32 or 64 vectors hold REP copies of
+// their residual rows in the MMA's 128 rows (rows otherwise computed on
+// zeros), so that every TMEM lane quarter, and with it every warp, holds
+// rows: each thread filters 64 / REP of a row's 256 columns, and the
+// per-row steps spread over all warps (and schedulers) instead of the
+// quarter-0 warps.
+template <typename XT, int REP>
 __global__ void __launch_bounds__(kEncThreads, 1)
     encode_keys_kernel(const __grid_constant__ CUtensorMap cmap, EncodeParams p) {
     extern __shared__ unsigned char smem_raw[];
@@ -260,9 +288,10 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     for (int e = tid; e < kEncRows * (kEncD / 4); e += kEncThreads) {
         const int n = e >> 5, d = (e & 31) * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (n < p.rows_per_cta && v0 + n < nvec_set) {
+        const int nv = REP > 1 ? n % (kEncRows / REP) : n;  // the vector of row n
+        if (nv < p.rows_per_cta && v0 + nv < nvec_set) {
             int b, h, t;
-            vec_bht(v0 + n, &b, &h, &t);
+            vec_bht(v0 + nv, &b, &h, &t);
             const XT* xr = reinterpret_cast<const XT*>(p.x) + (int64_t)b * p.xs_b + (int64_t)h * p.xs_h + (int64_t)t * p.xs_t;
             v = make_float4(to_f32(xr[d]), to_f32(xr[d + 1]), to_f32(xr[d + 2]), to_f32(xr[d + 3]));
         }
@@ -277,11 +306,13 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     // epilogue: warp w reads TMEM lane quarter q = w & 3 (vector rows
     // 32q .. 32q+31) and the 64 columns of group cg = w >> 2
     const int q4 = warp & 3, cg = warp >> 2;
-    // warps whose 32 rows all lie past the CTA's vectors (CTAs of 32 or 64)
-    // skip the per-row steps; they still take part in every barrier and in
-    // the CTA-wide exact recomputation
-    const bool live_w = !PART || q4 * 32 < p.rows_per_cta;
     const int row = q4 * 32 + lane;
+    // REP > 1: the thread's copy rep, vector row rr (row of copy 0) and
+    // first of its W columns
+    constexpr int QPR = 4 / REP, W = 64 / REP;
+    const int rep = q4 / QPR;
+    const int rr = (q4 % QPR) * 32 + lane;
+    const int c0 = 64 * cg + W * rep;
     const bool row_valid = row < p.rows_per_cta && v0 + row < nvec_set;
     __shared__ uint8_t* s_cptr[kEncRows];         // the row's 32 codes in the output (null: no vector)
     __shared__ __align__(16) uint8_t s_codes[kEncRows][kEncM];
@@ -305,6 +336,11 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     __shared__ float s_u[4][kEncRows];
     __shared__ int s_cnt[4][kEncRows];
     __shared__ int s_bk[4][kEncRows];               // the group's first candidate (-1: none)
+    // REP > 1: per vector row the ordered key of the smallest approximation,
+    // the candidate count and the smallest candidate (reset every stage)
+    __shared__ uint32_t s_umin[REP > 1 ? kEncRows / REP : 1];
+    __shared__ int s_cnt1[REP > 1 ? kEncRows / REP : 1];
+    __shared__ int s_bk1[REP > 1 ? kEncRows / REP : 1];
     __shared__ unsigned long long s_best[kEncRows];  // (ordered exact distance, codeword), minimum
     __shared__ uint32_t s_list[kEncListCap];         // (row << 8) | codeword
     __shared__ int s_nlist[2];
@@ -334,7 +370,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             enc_commit(s_mbar);
         }
         // meanwhile: ||r||^2 of each row, exactly (sequential fma in d order)
-        if (cg == 0 && live_w) {
+        if (cg == 0 && rep == 0) {
             float rn = 0.f;
 #pragma unroll 4
             for (int d4 = 0; d4 < kEncD / 4; ++d4) {
@@ -345,6 +381,11 @@ __global__ void __launch_bounds__(kEncThreads, 1)
                 rn = __fmaf_rn(r4.w, r4.w, rn);
             }
             s_rn[row] = rn;
+            if constexpr (REP > 1) {
+                s_umin[row] = ~0u;
+                s_cnt1[row] = 0;
+                s_bk1[row] = 0x7fffffff;
+            }
         }
         const bool done = mbar_wait(s_mbar, par, p.err);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -354,37 +395,35 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             break;
         }
         const float* nb = sNorm + (m & 1) * EncSmem::kNormStride;
-        float v[64];
-        float bnd = 0.f;
-        if (live_w) {
+        int total;
+        uint64_t pend;
+        if constexpr (REP == 1) {
             const float rn = s_rn[row];
             const float rnorm = __fmul_ru(__fsqrt_ru(rn), 1.0000001f);
             // the bound's absolute part, one upper bound per row: |approx| <=
             // ||c||^2 + 2 ||r|| ||c|| <= nmax + 2 rnorm cmax
             const float slack = kAbs * (rn + 2.f * (nb[kEncK] + rnorm * nb[kEncK + 1]));
             // the row's bound for every codeword of the stage: kEps ||r|| max ||c|| + slack
-            bnd = __fmaf_ru(kEps * rnorm, nb[kEncK + 1], slack);
+            const float bnd = __fmaf_ru(kEps * rnorm, nb[kEncK + 1], slack);
             const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + 64 * cg;
+            float v[64];
             enc_tmem_ld64(taddr, v);
             // pass 1: the row's smallest approximate distance A (less ||r||^2)
             float u = INFINITY;
-#pragma unroll
+    #pragma unroll
             for (int i = 0; i < 64; ++i) {
                 const float ap = fmaf(-2.f, v[i], nb[64 * cg + i]);
                 v[i] = ap;
                 u = fminf(u, ap);
             }
             s_u[cg][row] = u;
-        }
-        __syncthreads();
-        uint32_t cm0 = 0u, cm1 = 0u;
-        if (live_w) {
+            __syncthreads();
             // pass 2: candidates approx_k <= A + 2 bnd -- the winner's exact
-            // distance is at most A + bnd and its approximation at most bnd
-            // below that (bit i of the mask = column 64cg + i)
-            const float thr =
-                __fmaf_ru(2.f, bnd, fminf(fminf(s_u[0][row], s_u[1][row]), fminf(s_u[2][row], s_u[3][row])));
-#pragma unroll
+            // distance is at most A + bnd and its approximation at most bnd below
+            // that (bit i of the mask = column 64cg + i)
+            const float thr = __fmaf_ru(2.f, bnd, fminf(fminf(s_u[0][row], s_u[1][row]), fminf(s_u[2][row], s_u[3][row])));
+            uint32_t cm0 = 0u, cm1 = 0u;
+    #pragma unroll
             for (int i = 0; i < 64; ++i) {
                 const bool c = p.force_exact || v[i] <= thr;
                 if (i < 32) cm0 |= (uint32_t)c << i;
@@ -393,18 +432,54 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             s_cnt[cg][row] = __popc(cm0) + __popc(cm1);
             s_bk[cg][row] = cm0 ? __ffs(cm0) - 1 + 64 * cg : (cm1 ? __ffs(cm1) + 31 + 64 * cg : -1);
             if (cg == 0) s_best[row] = ~0ull;
+            if (tid == 0) {
+                s_nlist[0] = 0;
+                s_nlist[1] = 0;
+            }
+            __syncthreads();
+            total = s_cnt[0][row] + s_cnt[1][row] + s_cnt[2][row] + s_cnt[3][row];
+            // a row with several candidates: their exact distances, one (row,
+            // codeword) pair per 8 lanes through a CTA-wide list (rounds of at most
+            // kEncListCap pairs); the smallest (distance, codeword) key is the
+            // first minimum of the CPU scan
+            pend = total > 1 ? ((uint64_t)cm1 << 32) | cm0 : 0ull;
+        } else {
+            // the same bound and passes over the thread's W columns of row
+            // rr; per-row minimum, count and first candidate by shared atomics
+            const float rn = s_rn[rr];
+            const float rnorm = __fmul_ru(__fsqrt_ru(rn), 1.0000001f);
+            const float slack = kAbs * (rn + 2.f * (nb[kEncK] + rnorm * nb[kEncK + 1]));
+            const float bnd = __fmaf_ru(kEps * rnorm, nb[kEncK + 1], slack);
+            const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + c0;
+            float v[W];
+            enc_tmem_ld16(taddr, v);
+            if constexpr (W == 32) enc_tmem_ld16(taddr + 16, v + 16);
+            float u = INFINITY;
+#pragma unroll
+            for (int i = 0; i < W; ++i) {
+                const float ap = fmaf(-2.f, v[i], nb[c0 + i]);
+                v[i] = ap;
+                u = fminf(u, ap);
+            }
+            atomicMin(&s_umin[rr], enc_okey(u));
+            __syncthreads();
+            const float thr = __fmaf_ru(2.f, bnd, enc_okey_inv(s_umin[rr]));
+            uint32_t cm = 0u;
+#pragma unroll
+            for (int i = 0; i < W; ++i) cm |= (uint32_t)(p.force_exact || v[i] <= thr) << i;
+            if (cm) {
+                atomicAdd(&s_cnt1[rr], __popc(cm));
+                atomicMin(&s_bk1[rr], c0 + __ffs(cm) - 1);
+            }
+            if (cg == 0 && rep == 0) s_best[rr] = ~0ull;
+            if (tid == 0) {
+                s_nlist[0] = 0;
+                s_nlist[1] = 0;
+            }
+            __syncthreads();
+            total = s_cnt1[rr];
+            pend = total > 1 ? (uint64_t)cm : 0ull;
         }
-        if (tid == 0) {
-            s_nlist[0] = 0;
-            s_nlist[1] = 0;
-        }
-        __syncthreads();
-        const int total = live_w ? s_cnt[0][row] + s_cnt[1][row] + s_cnt[2][row] + s_cnt[3][row] : 0;
-        // a row with several candidates: their exact distances, one (row,
-        // codeword) pair per 8 lanes through a CTA-wide list (rounds of at most
-        // kEncListCap pairs); the smallest (distance, codeword) key is the
-        // first minimum of the CPU scan
-        uint64_t pend = total > 1 ? ((uint64_t)cm1 << 32) | cm0 : 0ull;
         for (int round = 0;; ++round) {
             int* nl = &s_nlist[round & 1];
             const bool had = pend != 0ull;
@@ -420,7 +495,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             if (lane == 31 && incl > 0) base = atomicAdd(nl, incl);
             base = __shfl_sync(0xffffffffu, base, 31);
             for (int i = base + incl - mine; pend && i < kEncListCap; ++i) {
-                s_list[i] = ((uint32_t)row << 8) | (uint32_t)(__ffsll((long long)pend) - 1 + 64 * cg);
+                s_list[i] = ((uint32_t)rr << 8) | (uint32_t)(__ffsll((long long)pend) - 1 + c0);
                 pend &= pend - 1;
             }
             if (!__syncthreads_or(had)) break;
@@ -465,28 +540,27 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             }
             if (!__syncthreads_or(pend != 0ull)) break;
         }
+        // the code: the refined minimum, else the one candidate (one group has it)
+        const int code = total > 1 ? (int)(s_best[rr] & 0xffu)
+                         : REP > 1 ? min(s_bk1[rr], kEncK - 1)
+                                   : max(max(max(s_bk[0][row], s_bk[1][row]), max(s_bk[2][row], s_bk[3][row])), 0);
+        if (cg == 0 && rep == 0) s_codes[rr][m] = (uint8_t)code;
+        // r - C_m[code] into registers (the row's 4 column groups take 32
+        // dims each): the subtractions consume the codeword loads before the
+        // barrier, after which the next stage's copies overwrite the
+        // codewords; the stores follow the copies' issue
         float4 nr[8];
-        if (live_w) {
-            // the code: the refined minimum, else the one candidate (one group has it)
-            const int code = total > 1 ? (int)(s_best[row] & 0xffu)
-                                       : max(max(max(s_bk[0][row], s_bk[1][row]), max(s_bk[2][row], s_bk[3][row])), 0);
-            if (cg == 0) s_codes[row][m] = (uint8_t)code;
-            // r - C_m[code] into registers (the row's 4 column groups take 32
-            // dims each): the subtractions consume the codeword loads before the
-            // barrier, after which the next stage's copies overwrite the
-            // codewords; the stores follow the copies' issue
-            {
+        {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int d = (8 * cg + j) * 4;
-                    const float4 cv = *reinterpret_cast<const float4*>(sB + enc_off_cb(code, d));
-                    const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(row, d));
-                    nr[j] = make_float4(__fsub_rn(r4.x, cv.x), __fsub_rn(r4.y, cv.y), __fsub_rn(r4.z, cv.z),
-                                        __fsub_rn(r4.w, cv.w));
-                    // the differences exist before the barrier (the compiler may
-                    // not sink them, and with them the wait for the loads, past it)
-                    asm volatile("" : "+f"(nr[j].x), "+f"(nr[j].y), "+f"(nr[j].z), "+f"(nr[j].w));
-                }
+            for (int j = 0; j < 8; ++j) {
+                const int d = (8 * cg + j) * 4;
+                const float4 cv = *reinterpret_cast<const float4*>(sB + enc_off_cb(code, d));
+                const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(row, d));
+                nr[j] = make_float4(__fsub_rn(r4.x, cv.x), __fsub_rn(r4.y, cv.y), __fsub_rn(r4.z, cv.z),
+                                    __fsub_rn(r4.w, cv.w));
+                // the differences exist before the barrier (the compiler may
+                // not sink them, and with them the wait for the loads, past it)
+                asm volatile("" : "+f"(nr[j].x), "+f"(nr[j].y), "+f"(nr[j].z), "+f"(nr[j].w));
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -496,10 +570,8 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             load_norms(m + 1);
         }
         // (visible to the next stage's MMA after the barrier that starts it)
-        if (live_w) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(sA + enc_off(row, (8 * cg + j) * 4)) = nr[j];
-        }
+        for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(sA + enc_off(row, (8 * cg + j) * 4)) = nr[j];
     }
     cp_async_wait<0>();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

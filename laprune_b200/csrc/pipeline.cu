@@ -777,27 +777,31 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
         if (cr != CUDA_SUCCESS) return fail(LP_ERR_CUDA, "cuTensorMapEncodeTiled failed for the codebooks");
     }
     const dim3 grid((unsigned)(nsets * ep.ctas_per_set));
-    static bool opt_enc[6][64] = {{false}};
+    static bool opt_enc[9][64] = {{false}};
     auto launch_enc = [&](auto kern, int slot) {
         const int r = smem_opt_in(kern, EncSmem::kTotal, dev, opt_enc[slot]);
         if (r != LP_OK) return r;
         kern<<<grid, kEncThreads, EncSmem::kTotal, st>>>(cmap, ep);
         return (int)LP_OK;
     };
-    // CTAs of fewer than 128 vectors: the instantiation whose idle warps skip
-    // the per-row steps
-    const bool part = rows < kEncRows;
+    // CTAs of 64 or 32 vectors: the instantiation with 2 or 4 copies of the
+    // residual rows in the MMA tile
+    const int ri = rows == kEncRows ? 0 : (rows == kEncRows / 2 ? 1 : 2);
     switch (a->x_dtype) {
         case LP_BF16:
-            rc = part ? launch_enc(encode_keys_kernel<__nv_bfloat16, true>, 3)
-                      : launch_enc(encode_keys_kernel<__nv_bfloat16, false>, 0);
+            rc = ri == 0 ? launch_enc(encode_keys_kernel<__nv_bfloat16, 1>, 0)
+                 : ri == 1 ? launch_enc(encode_keys_kernel<__nv_bfloat16, 2>, 1)
+                           : launch_enc(encode_keys_kernel<__nv_bfloat16, 4>, 2);
             break;
         case LP_F16:
-            rc = part ? launch_enc(encode_keys_kernel<__half, true>, 4)
-                      : launch_enc(encode_keys_kernel<__half, false>, 1);
+            rc = ri == 0 ? launch_enc(encode_keys_kernel<__half, 1>, 3)
+                 : ri == 1 ? launch_enc(encode_keys_kernel<__half, 2>, 4)
+                           : launch_enc(encode_keys_kernel<__half, 4>, 5);
             break;
         default:
-            rc = part ? launch_enc(encode_keys_kernel<float, true>, 5) : launch_enc(encode_keys_kernel<float, false>, 2);
+            rc = ri == 0 ? launch_enc(encode_keys_kernel<float, 1>, 6)
+                 : ri == 1 ? launch_enc(encode_keys_kernel<float, 2>, 7)
+                           : launch_enc(encode_keys_kernel<float, 4>, 8);
             break;
     }
     if (rc != LP_OK) return rc;
