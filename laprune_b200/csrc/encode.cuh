@@ -546,14 +546,16 @@ __global__ void __launch_bounds__(kEncThreads, 1)
                                    : max(max(max(s_bk[0][row], s_bk[1][row]), max(s_bk[2][row], s_bk[3][row])), 0);
         if (cg == 0 && rep == 0) s_codes[rr][m] = (uint8_t)code;
         // r - C_m[code] into registers (the row's 4 column groups take 32
-        // dims each): the subtractions consume the codeword loads before the
-        // barrier, after which the next stage's copies overwrite the
-        // codewords; the stores follow the copies' issue
-        float4 nr[8];
+        // dims each, split over the REP copies' threads): the subtractions
+        // consume the codeword loads before the barrier, after which the next
+        // stage's copies overwrite the codewords; the stores (into every copy
+        // of the row) follow the copies' issue
+        constexpr int NF = 8 / REP;  // float4 slices of the thread
+        float4 nr[NF];
         {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int d = (8 * cg + j) * 4;
+            for (int j = 0; j < NF; ++j) {
+                const int d = (8 * cg + NF * rep + j) * 4;
                 const float4 cv = *reinterpret_cast<const float4*>(sB + enc_off_cb(code, d));
                 const float4 r4 = *reinterpret_cast<const float4*>(sA + enc_off(row, d));
                 nr[j] = make_float4(__fsub_rn(r4.x, cv.x), __fsub_rn(r4.y, cv.y), __fsub_rn(r4.z, cv.z),
@@ -571,7 +573,10 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         }
         // (visible to the next stage's MMA after the barrier that starts it)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(sA + enc_off(row, (8 * cg + j) * 4)) = nr[j];
+        for (int j = 0; j < NF; ++j)
+#pragma unroll
+            for (int c = 0; c < REP; ++c)
+                *reinterpret_cast<float4*>(sA + enc_off(c * (kEncRows / REP) + rr, (8 * cg + NF * rep + j) * 4)) = nr[j];
     }
     cp_async_wait<0>();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
