@@ -55,7 +55,7 @@ struct EncodeParams {
     uint8_t* codes;
     int64_t cs_b, cs_h, cs_t;  // bytes
     int ctas_per_set;          // ceil(vectors of a set / rows_per_cta)
-    int rows_per_cta;          // 128, or 64 / 32 when the sets have too few vectors to fill the GPU
+    int rows_per_cta;          // 128, or 64 / 32 / 16 when the sets have too few vectors to fill the GPU
                                // (the MMA still runs 128 rows; the others are zero)
     int force_exact;           // recompute every codeword exactly (testing)
     uint32_t* err;
@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(256) encode_norms_kernel(const float* cb, int6
     cnorm[i] = __fmul_ru(__fsqrt_ru(acc), 1.0000001f);
 }
 
-// REP = 128 / vectors per CTA.  CTAs of 32 or 64 vectors hold REP copies of
+// REP = 128 / vectors per CTA.  CTAs of 16, 32 or 64 vectors hold REP copies of
 // their residual rows in the MMA's 128 rows (rows otherwise computed on
 // zeros), so that every TMEM lane quarter, and with it every warp, holds
 // rows: each thread filters 64 / REP of a row's 256 columns, and the
@@ -309,9 +309,9 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     const int row = q4 * 32 + lane;
     // REP > 1: the thread's copy rep, vector row rr (row of copy 0) and
     // first of its W columns
-    constexpr int QPR = 4 / REP, W = 64 / REP;
-    const int rep = q4 / QPR;
-    const int rr = (q4 % QPR) * 32 + lane;
+    constexpr int RP = kEncRows / REP, W = 64 / REP;
+    const int rep = row / RP;
+    const int rr = row % RP;
     const int c0 = 64 * cg + W * rep;
     const bool row_valid = row < p.rows_per_cta && v0 + row < nvec_set;
     __shared__ uint8_t* s_cptr[kEncRows];         // the row's 32 codes in the output (null: no vector)
@@ -452,8 +452,18 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             const float bnd = __fmaf_ru(kEps * rnorm, nb[kEncK + 1], slack);
             const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + c0;
             float v[W];
-            enc_tmem_ld16(taddr, v);
-            if constexpr (W == 32) enc_tmem_ld16(taddr + 16, v + 16);
+            if constexpr (W == 8) {
+                // two copies per lane quarter: the warp loads their 16
+                // columns at one (warp-uniform) address, each half-warp keeps
+                // its own 8
+                float w[16];
+                enc_tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + 64 * cg + 16 * q4, w);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = (lane & 16) ? w[8 + i] : w[i];
+            } else {
+                enc_tmem_ld16(taddr, v);
+                if constexpr (W == 32) enc_tmem_ld16(taddr + 16, v + 16);
+            }
             float u = INFINITY;
 #pragma unroll
             for (int i = 0; i < W; ++i) {

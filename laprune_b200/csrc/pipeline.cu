@@ -671,10 +671,10 @@ static int encode_plan(const lp_encode_args* a, size_t* bytes, int64_t* nsets, i
 
 // Vectors per CTA of the encoder: fewer rows per CTA while that still
 // leaves SMs idle (the 32 stages are a serial chain per CTA, so more, smaller
-// CTAs finish sooner): 128 (one full UMMA tile), 64 or 32.
+// CTAs finish sooner): 128 (one full UMMA tile), 64, 32 or 16.
 static int encode_rows_per_cta(int64_t nsets, int64_t nvec_set, int sms) {
     int rows = kEncRows;
-    while (rows > 32 && nsets * ((nvec_set + rows / 2 - 1) / (rows / 2)) <= sms) rows /= 2;
+    while (rows > 16 && nsets * ((nvec_set + rows / 2 - 1) / (rows / 2)) <= sms) rows /= 2;
     return rows;
 }
 
@@ -777,31 +777,34 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
         if (cr != CUDA_SUCCESS) return fail(LP_ERR_CUDA, "cuTensorMapEncodeTiled failed for the codebooks");
     }
     const dim3 grid((unsigned)(nsets * ep.ctas_per_set));
-    static bool opt_enc[9][64] = {{false}};
+    static bool opt_enc[12][64] = {{false}};
     auto launch_enc = [&](auto kern, int slot) {
         const int r = smem_opt_in(kern, EncSmem::kTotal, dev, opt_enc[slot]);
         if (r != LP_OK) return r;
         kern<<<grid, kEncThreads, EncSmem::kTotal, st>>>(cmap, ep);
         return (int)LP_OK;
     };
-    // CTAs of 64 or 32 vectors: the instantiation with 2 or 4 copies of the
-    // residual rows in the MMA tile
-    const int ri = rows == kEncRows ? 0 : (rows == kEncRows / 2 ? 1 : 2);
+    // CTAs of 64, 32 or 16 vectors: the instantiation with 2, 4 or 8 copies
+    // of the residual rows in the MMA tile
+    const int ri = rows == kEncRows ? 0 : rows == kEncRows / 2 ? 1 : rows == kEncRows / 4 ? 2 : 3;
     switch (a->x_dtype) {
         case LP_BF16:
-            rc = ri == 0 ? launch_enc(encode_keys_kernel<__nv_bfloat16, 1>, 0)
+            rc = ri == 0   ? launch_enc(encode_keys_kernel<__nv_bfloat16, 1>, 0)
                  : ri == 1 ? launch_enc(encode_keys_kernel<__nv_bfloat16, 2>, 1)
-                           : launch_enc(encode_keys_kernel<__nv_bfloat16, 4>, 2);
+                 : ri == 2 ? launch_enc(encode_keys_kernel<__nv_bfloat16, 4>, 2)
+                           : launch_enc(encode_keys_kernel<__nv_bfloat16, 8>, 3);
             break;
         case LP_F16:
-            rc = ri == 0 ? launch_enc(encode_keys_kernel<__half, 1>, 3)
-                 : ri == 1 ? launch_enc(encode_keys_kernel<__half, 2>, 4)
-                           : launch_enc(encode_keys_kernel<__half, 4>, 5);
+            rc = ri == 0   ? launch_enc(encode_keys_kernel<__half, 1>, 4)
+                 : ri == 1 ? launch_enc(encode_keys_kernel<__half, 2>, 5)
+                 : ri == 2 ? launch_enc(encode_keys_kernel<__half, 4>, 6)
+                           : launch_enc(encode_keys_kernel<__half, 8>, 7);
             break;
         default:
-            rc = ri == 0 ? launch_enc(encode_keys_kernel<float, 1>, 6)
-                 : ri == 1 ? launch_enc(encode_keys_kernel<float, 2>, 7)
-                           : launch_enc(encode_keys_kernel<float, 4>, 8);
+            rc = ri == 0   ? launch_enc(encode_keys_kernel<float, 1>, 8)
+                 : ri == 1 ? launch_enc(encode_keys_kernel<float, 2>, 9)
+                 : ri == 2 ? launch_enc(encode_keys_kernel<float, 4>, 10)
+                           : launch_enc(encode_keys_kernel<float, 8>, 11);
             break;
     }
     if (rc != LP_OK) return rc;

@@ -107,11 +107,13 @@ def test_codes_written_into_a_cache_slice_score_like_the_reference(golden_dir):
 @pytest.mark.parametrize("B,H,T,per_head,rows", [
     (1, 8, 4096, True, 128),    # prefill chunk: 1 x 8 KV heads x 4096 keys, 256 CTAs of 128 vectors
     (1, 1, 12288, False, 128),  # 12k vectors on one shared codebook, 96 CTAs of 128
-    (1, 8, 1024, True, 64),     # 8 x 1024: 128 CTAs of 64 vectors
+    (1, 8, 1024, True, 64),     # 8 x 1024: 128 CTAs of 64 vectors (2 copies of the rows in the MMA tile)
+    (1, 8, 512, True, 32),      # 8 x 512: 128 CTAs of 32 vectors (4 copies)
+    (1, 8, 256, True, 16),      # 8 x 256: 128 CTAs of 16 vectors (8 copies)
 ])
 def test_large_tiles_equal_the_oracle(B, H, T, per_head, rows):
-    """The 128- and 64-row CTA tiles (smaller batches run 32-row tiles), each
-    checked to be the tile the library picks and bit-exact with the oracle."""
+    """Every CTA tile (128, 64, 32 and 16 vectors), each checked to be the
+    tile the library picks and bit-exact with the oracle."""
     g = torch.Generator().manual_seed(20 + rows + H)
     C = torch.randn((H, 32, 256, 128) if per_head else (32, 256, 128), generator=g) * 0.05
     keys = torch.randn((B, H, T, 128), generator=g).to(torch.bfloat16)
