@@ -220,8 +220,9 @@ size_t lp_encode_workspace_size(const lp_encode_args* a);
 int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Vectors per CTA that lp_encode_keys uses for this geometry on the current
- * device: 128 (one M=128 tensor-core tile per stage), 64 or 32 (smaller
- * tiles while larger ones would leave SMs idle); 0 for invalid arguments.
+ * device: 128 (one M=128 tensor-core tile per stage), 64, 32 or 16
+ * (smaller CTAs, their rows copied 2, 4 or 8 times into the tile, while
+ * larger ones would leave SMs idle); 0 for invalid arguments.
  * A diagnostic for tests that must cover every tile size. */
 int lp_encode_rows_per_cta(const lp_encode_args* a);
 

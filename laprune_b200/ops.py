@@ -341,7 +341,7 @@ def _encode_args(x: torch.Tensor, codebooks: torch.Tensor, codes: Optional[torch
 
 
 def encode_rows_per_cta(x: torch.Tensor, codebooks: torch.Tensor) -> int:
-    """Vectors per CTA (128, 64 or 32) that :func:`encode_keys` uses for
+    """Vectors per CTA (128, 64, 32 or 16) that :func:`encode_keys` uses for
     these shapes on x's device (a diagnostic; lp_encode_rows_per_cta)."""
     a, _ = _encode_args(x, codebooks, None, False)
     with torch.cuda.device(x.device):
