@@ -695,29 +695,10 @@ __global__ void __launch_bounds__(kFThreads, 1) sparse_decode_fused_kernel(Fused
             sel[s] = 0x5504u | (bs << 4);
         }
         float* gsc = p.sel_scores + (int64_t)u * p.sel_stride;
-        // Ring protocol: full[s] completes when tile bytes land; every warp
-        // arrives on empty[s] once it has read its rows of the tile; thread 0
-        // refills slot (i-1)%S with tile i-1+S one iteration later, after
-        // empty[(i-1)%S] completed.  No block-wide barrier per tile.
         __shared__ int s_abort;
         if (tid == 0) s_abort = 0;
         __syncthreads();
         LP_FTRACE(5);
-        // two tiles per iteration: two independent gather chains per thread
-        auto score_row = [&](int slot, int lt) {
-            const uint32_t* row = reinterpret_cast<const uint32_t*>(s_ring + slot * kFTile + tid * 32);
-            int iacc = 0;
-#pragma unroll
-            for (int w = 0; w < 8; ++w) {
-                const uint32_t cw = row[(w + L) & 7u];
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const uint32_t a = __byte_perm(cw, off[s], sel[s]);
-                    iacc += *reinterpret_cast<const int*>(s_lut + a + 16 * w);
-                }
-            }
-            return __fmul_rn(__int2float_rn(iacc), from_fx);
-        };
         // scores stay in shared memory (the plan keeps every CTA's share
         // there); global memory gets them only on the exact slow path
         auto commit_score = [&](int lt, float sc) {
