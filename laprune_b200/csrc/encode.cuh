@@ -50,8 +50,6 @@ struct EncodeParams {
     int B, H, T;               // vectors x[b][h][t][0..128)
     int per_head;              // codebook set of vector (b, h, t) is h (else 0)
     const float* cb;           // [S][32][256][128] fp32
-    const float* nrm;          // [S][32][256]  ||C||^2 (sequential fma)
-    const float* smax;         // [S][32][4]    per stage: max ||C||^2, max ||C||, 0, 0
     uint8_t* codes;
     int64_t cs_b, cs_h, cs_t;  // bytes
     int ctas_per_set;          // ceil(vectors of a set / rows_per_cta)
@@ -64,7 +62,7 @@ struct EncodeParams {
 struct EncSmem {
     static constexpr int kA = kEncRows * kEncD * 4;          // 64 KB
     static constexpr int kBHalf = 128 * kEncD * 4;           // 64 KB
-    static constexpr int kNormStride = kEncK + 4;           // nrm[256] nmax cmax . .
+    static constexpr int kNormStride = kEncK + 4;           // the stage's ||C||^2 [256] (+ 4 spare)
     static constexpr int kNorm = 2 * kNormStride * 4;        // double buffered
     static constexpr int kTotal = kA + 2 * kBHalf + kNorm + 64 + 1024;  // + alignment slack
 };
@@ -171,29 +169,8 @@ __device__ __forceinline__ void enc_tmem_ld64(uint32_t taddr, float* v) {
     for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// per stage (set, m): the largest ||C||^2 and ||C|| of its 256 codewords
-__global__ void __launch_bounds__(256) encode_stage_max_kernel(const float* nrm, const float* cnorm, float* smax) {
-    __shared__ float s_a[8], s_b[8];
-    const int st = blockIdx.x, k = threadIdx.x;
-    float a = nrm[(int64_t)st * kEncK + k], b = cnorm[(int64_t)st * kEncK + k];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
-    }
-    if ((k & 31) == 0) { s_a[k >> 5] = a; s_b[k >> 5] = b; }
-    __syncthreads();
-    if (k == 0) {
-        for (int w = 1; w < 8; ++w) { a = fmaxf(a, s_a[w]); b = fmaxf(b, s_b[w]); }
-        smax[st * 4 + 0] = a;
-        smax[st * 4 + 1] = b;
-        smax[st * 4 + 2] = 0.f;
-        smax[st * 4 + 3] = 0.f;
-    }
-}
-
-// ||C||^2 of every codeword (sequential fma over d) and ||C|| rounded up.
-__global__ void __launch_bounds__(256) encode_norms_kernel(const float* cb, int64_t n, float* nrm, float* cnorm) {
+// ||C||^2 of every codeword (sequential fma over d), for the ICM sweeps.
+__global__ void __launch_bounds__(256) encode_norms_kernel(const float* cb, int64_t n, float* nrm) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const float4* c = reinterpret_cast<const float4*>(cb + i * kEncD);
@@ -207,7 +184,6 @@ __global__ void __launch_bounds__(256) encode_norms_kernel(const float* cb, int6
         acc = __fmaf_rn(v.w, v.w, acc);
     }
     nrm[i] = acc;
-    cnorm[i] = __fmul_ru(__fsqrt_ru(acc), 1.0000001f);
 }
 
 // REP = 128 / vectors per CTA.  CTAs of 16, 32 or 64 vectors hold REP copies of
@@ -226,7 +202,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* sA = smem;
     unsigned char* sB = smem + EncSmem::kA;  // half hf, K chunk c at hf * 64 KB + c * 16 KB
-    float* sNorm = reinterpret_cast<float*>(sB + 2 * EncSmem::kBHalf);  // [2][nrm 256 | nmax cmax . .]
+    float* sNorm = reinterpret_cast<float*>(sB + 2 * EncSmem::kBHalf);  // [2][||C||^2 of 256 codewords | . .]
     uint64_t* s_mbar = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(sNorm) + EncSmem::kNorm);
     uint64_t* s_tbar = s_mbar + 1;
     __shared__ uint32_t s_tmem;
@@ -237,8 +213,6 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     const int tile = blockIdx.x - set * p.ctas_per_set;
     const int nvec_set = p.per_head ? p.B * p.T : p.B * p.H * p.T;  // vectors of this set
     const int v0 = tile * p.rows_per_cta;
-    const float* nrms = p.nrm + (int64_t)set * kEncM * kEncK;
-    const float* smx = p.smax + (int64_t)set * kEncM * 4;
 
     // vector i of the set -> (b, h, t)
     auto vec_bht = [&](int i, int* b, int* h, int* t) {
@@ -262,13 +236,6 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
             for (int c = 0; c < 4; ++c) enc_tma_2d(sB + c * 32768 + hf * 16384, &cmap, 32 * c, row0 + 128 * hf, s_tbar);
-    };
-    // stage m's norms (cp.async, one group per thread)
-    auto load_norms = [&](int m) {
-        float* nb = sNorm + (m & 1) * EncSmem::kNormStride;
-        if (tid < 64) cp_async16(nb + tid * 4, nrms + (int64_t)m * kEncK + tid * 4);
-        else if (tid == 64) cp_async16(nb + kEncK, smx + m * 4);
-        cp_async_commit();
     };
 
     if (warp == 0) {
@@ -297,7 +264,6 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         }
         *reinterpret_cast<float4*>(sA + enc_off(n, d)) = v;
     }
-    load_norms(0);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -333,6 +299,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     constexpr float kEps = 1.0f / 128.0f;
     constexpr float kAbs = 1.0f / 1048576.0f;
     __shared__ float s_rn[kEncRows];
+    __shared__ float s_wmx[kEncK / 32][2];  // per warp of the norm threads: max ||c||^2, max ||c||
     __shared__ float s_u[4][kEncRows];
     __shared__ int s_cnt[4][kEncRows];
     __shared__ int s_bk[4][kEncRows];               // the group's first candidate (-1: none)
@@ -387,6 +354,33 @@ __global__ void __launch_bounds__(kEncThreads, 1)
                 s_bk1[row] = 0x7fffffff;
             }
         }
+        // meanwhile: the stage's codeword norms ||c||^2 from its copies in
+        // shared memory (threads 256..511, one codeword each; the sequential
+        // fma chain in d order of the CPU arithmetic) and, per warp, the
+        // largest ||c||^2 and ||c|| (rounded up)
+        if (tid >= kEncThreads - kEncK) {
+            const int k = tid - (kEncThreads - kEncK);
+            float acc = 0.f;
+#pragma unroll 8
+            for (int d4 = 0; d4 < kEncD / 4; ++d4) {
+                const float4 c = *reinterpret_cast<const float4*>(sB + enc_off_cb(k, d4 * 4));
+                acc = __fmaf_rn(c.x, c.x, acc);
+                acc = __fmaf_rn(c.y, c.y, acc);
+                acc = __fmaf_rn(c.z, c.z, acc);
+                acc = __fmaf_rn(c.w, c.w, acc);
+            }
+            sNorm[(m & 1) * EncSmem::kNormStride + k] = acc;
+            float a = acc, cn = __fmul_ru(__fsqrt_ru(acc), 1.0000001f);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+                cn = fmaxf(cn, __shfl_xor_sync(0xffffffffu, cn, o));
+            }
+            if (lane == 0) {
+                s_wmx[warp - (kEncThreads - kEncK) / 32][0] = a;
+                s_wmx[warp - (kEncThreads - kEncK) / 32][1] = cn;
+            }
+        }
         const bool done = mbar_wait(s_mbar, par, p.err);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (__syncthreads_or(!done)) {
@@ -395,6 +389,13 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             break;
         }
         const float* nb = sNorm + (m & 1) * EncSmem::kNormStride;
+        // the stage's largest ||c||^2 and ||c||
+        float nmax = s_wmx[0][0], cmax = s_wmx[0][1];
+#pragma unroll
+        for (int w = 1; w < kEncK / 32; ++w) {
+            nmax = fmaxf(nmax, s_wmx[w][0]);
+            cmax = fmaxf(cmax, s_wmx[w][1]);
+        }
         int total;
         uint64_t pend;
         if constexpr (REP == 1) {
@@ -402,9 +403,9 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             const float rnorm = __fmul_ru(__fsqrt_ru(rn), 1.0000001f);
             // the bound's absolute part, one upper bound per row: |approx| <=
             // ||c||^2 + 2 ||r|| ||c|| <= nmax + 2 rnorm cmax
-            const float slack = kAbs * (rn + 2.f * (nb[kEncK] + rnorm * nb[kEncK + 1]));
+            const float slack = kAbs * (rn + 2.f * (nmax + rnorm * cmax));
             // the row's bound for every codeword of the stage: kEps ||r|| max ||c|| + slack
-            const float bnd = __fmaf_ru(kEps * rnorm, nb[kEncK + 1], slack);
+            const float bnd = __fmaf_ru(kEps * rnorm, cmax, slack);
             const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + 64 * cg;
             float v[64];
             enc_tmem_ld64(taddr, v);
@@ -448,8 +449,8 @@ __global__ void __launch_bounds__(kEncThreads, 1)
             // rr; per-row minimum, count and first candidate by shared atomics
             const float rn = s_rn[rr];
             const float rnorm = __fmul_ru(__fsqrt_ru(rn), 1.0000001f);
-            const float slack = kAbs * (rn + 2.f * (nb[kEncK] + rnorm * nb[kEncK + 1]));
-            const float bnd = __fmaf_ru(kEps * rnorm, nb[kEncK + 1], slack);
+            const float slack = kAbs * (rn + 2.f * (nmax + rnorm * cmax));
+            const float bnd = __fmaf_ru(kEps * rnorm, cmax, slack);
             const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + c0;
             float v[W];
             if constexpr (W == 8) {
@@ -579,7 +580,6 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         __syncthreads();  // the stage's codewords are no longer read: the next stage's copies start
         if (m + 1 < kEncM) {
             if (tid == 0) issue_stage(m + 1);
-            load_norms(m + 1);
         }
         // (visible to the next stage's MMA after the barrier that starts it)
 #pragma unroll

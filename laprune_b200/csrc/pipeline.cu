@@ -659,8 +659,6 @@ static int encode_plan(const lp_encode_args* a, size_t* bytes, int64_t* nsets, i
     Carver c(nullptr);
     c.take<unsigned char>(kPersistBytes);
     c.take<float>((size_t)*nsets * 32 * 256);
-    c.take<float>((size_t)*nsets * 32 * 256);
-    c.take<float>((size_t)*nsets * 32 * 4);
     if (a->icm_iters > 0) {
         c.take<float>((size_t)*nsets * *nvec_set * 128);
         c.take<uint32_t>((size_t)a->icm_iters * *nsets);
@@ -711,18 +709,17 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     Carver c(workspace);
     uint32_t* err = c.take<uint32_t>(kPersistBytes / 4);
-    float* nrm = c.take<float>((size_t)nsets * 32 * 256);
-    float* cnorm = c.take<float>((size_t)nsets * 32 * 256);
-    float* smax = c.take<float>((size_t)nsets * 32 * 4);
+    float* nrm = c.take<float>((size_t)nsets * 32 * 256);  // ||C||^2 for the ICM sweeps
     float* icm_fr = a->icm_iters > 0 ? c.take<float>((size_t)nsets * nvec_set * 128) : nullptr;
     uint32_t* icm_changed = a->icm_iters > 0 ? c.take<uint32_t>((size_t)a->icm_iters * nsets) : nullptr;
-    const int64_t ncw = nsets * 32 * 256;
-    encode_norms_kernel<<<(unsigned)((ncw + 255) / 256), 256, 0, st>>>(a->codebooks, ncw, nrm, cnorm);
-    rc = check_launch("encode_norms_kernel");
-    if (rc != LP_OK) return rc;
-    encode_stage_max_kernel<<<(unsigned)(nsets * 32), 256, 0, st>>>(nrm, cnorm, smax);
-    rc = check_launch("encode_stage_max_kernel");
-    if (rc != LP_OK) return rc;
+    // the ICM sweeps read the codeword norms from the workspace (the greedy
+    // kernel computes its own, stage by stage, from its shared-memory copies)
+    if (a->icm_iters > 0) {
+        const int64_t ncw = nsets * 32 * 256;
+        encode_norms_kernel<<<(unsigned)((ncw + 255) / 256), 256, 0, st>>>(a->codebooks, ncw, nrm);
+        rc = check_launch("encode_norms_kernel");
+        if (rc != LP_OK) return rc;
+    }
 
     EncodeParams ep{};
     ep.x = a->x;
@@ -734,8 +731,6 @@ int lp_encode_keys(const lp_encode_args* a, void* workspace, size_t workspace_by
     ep.T = a->T;
     ep.per_head = a->cb_per_kv_head ? 1 : 0;
     ep.cb = a->codebooks;
-    ep.nrm = nrm;
-    ep.smax = smax;
     ep.codes = a->codes;
     ep.cs_b = a->codes_stride_b;
     ep.cs_h = a->codes_stride_h;
