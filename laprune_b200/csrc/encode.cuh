@@ -27,12 +27,15 @@
 // UMMA K-major SWIZZLE_128B layout: per 32-dim K chunk (16 KB of residual
 // rows, 32 KB of codeword rows), 8-row atoms of 1024 B, rows 128 B apart,
 // 16-byte units XOR-swizzled with the row.  The codewords arrive by 2-D TMA
-// tensor copies (box 32 dims x 128 rows, the same swizzle).  The exact recomputation and the residual update read the
-// codeword rows from there, so the next stage's copies start once the
-// residual update is done.  Rows with several candidates put their (row,
-// codeword) pairs on a CTA-wide list, one pair per thread, so that the
-// sequential 128-term chains run side by side; the codes collect in shared
-// memory and leave once, 32 bytes per vector.
+// tensor copies (box 32 dims x 128 rows, the same swizzle); while the MMA
+// runs, warps 8-15 compute the stage's ||c||^2 from them.  The exact
+// recomputation and the residual update read the codeword rows from there,
+// so the next stage's copies start once the chosen codewords are in
+// registers.  Rows with several candidates put their (row, codeword) pairs
+// on a CTA-wide list, one pair per 8 lanes, so that the sequential 128-term
+// chains run side by side; the codes collect in shared memory and leave
+// once, 32 bytes per vector.  CTAs of 64, 32 or 16 vectors hold 2, 4 or 8
+// copies of their rows in the MMA's 128 rows (see encode_keys_kernel).
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
